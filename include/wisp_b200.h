@@ -1,0 +1,290 @@
+/*
+ * wisp_b200.h -- C ABI of the B200-native WISP MoE-block library
+ * (libwisp_b200.so, built for sm_100a).
+ *
+ * Three groups of entry points:
+ *
+ *  1. The reference's kernel-launcher ABI for the MoE path, with identical C
+ *     signatures (reference: csrc/core/wisp_engine.h:549-665).  Each
+ *     declaration names the reference launcher it replaces.
+ *  2. The fused MoE block (new): router + top-k + int4 gate/up/SwiGLU +
+ *     int4 down + gate-weighted combine for T tokens, with no host
+ *     synchronisation, on caller-owned device buffers.  The stacked form
+ *     adds the RMSNorm + residual between blocks (the FFN half of
+ *     decode_step, csrc/core/wisp_engine.c:1563-1570, attention = identity).
+ *  3. The engine ABI (reference: csrc/core/wisp_engine.h:472-543): engine
+ *     lifecycle on a converted model directory, the 3-tier expert fetch,
+ *     cache statistics, the expert access log, prefetch hints, self-tests
+ *     and the byte-layout probe; plus the new wisp_moe_forward.
+ *
+ * Conventions (same as the reference): functions that can fail return
+ * WispError and fill a caller-provided WispErrCtx; device buffers are owned
+ * by the caller; every launcher takes the stream it runs on.  No entry point
+ * falls back to the CPU: without a CUDA device they return WISP_ERR_CUDA.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+typedef __half wisp_half;
+#else
+typedef uint16_t wisp_half; /* raw fp16 bits; same size/layout as __half */
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------- *
+ * Errors -- same codes and context struct as the reference
+ * (csrc/core/wisp_engine.h:50-67).
+ * ---------------------------------------------------------------------- */
+typedef enum {
+    WISP_OK = 0,
+    WISP_ERR_OOM = 1,
+    WISP_ERR_IO = 2,
+    WISP_ERR_CUDA = 3,
+    WISP_ERR_INVALID_ARG = 4,
+    WISP_ERR_EXPERT_MISS = 5,
+    WISP_ERR_MODEL = 6,
+    WISP_ERR_TIMEOUT = 7,
+} WispError;
+
+typedef struct {
+    WispError code;
+    char message[512];
+    const char* file;
+    int line;
+} WispErrCtx;
+
+/* Expert blob layout, parsed from the 120-byte .bin header
+ * (reference: csrc/core/wisp_engine.h:241-251). */
+#define WISP_EXPERT_NMATS 3
+typedef struct {
+    size_t packed_off[WISP_EXPERT_NMATS];
+    size_t scales_off[WISP_EXPERT_NMATS];
+    size_t zeros_off[WISP_EXPERT_NMATS];
+    uint32_t rows[WISP_EXPERT_NMATS];
+    uint32_t cols[WISP_EXPERT_NMATS];
+    uint32_t group_size;
+    size_t total_bytes;
+    int valid;
+} WispExpertMeta;
+
+/* Replaces wisp_expert_parse_header (csrc/core/wisp_engine.c:268-303). */
+WispError wisp_expert_parse_header(const void* blob, size_t blob_size,
+                                   WispExpertMeta* meta, WispErrCtx* err);
+
+/* ====================================================================== *
+ * 1. Reference kernel-launcher ABI (identical signatures)
+ * ====================================================================== */
+
+/* Replaces csrc/cuda/matmul.cu:56-62 (wisp_engine.h:552). y = W x. */
+void wisp_gpu_gemv_f16(const wisp_half* W, const float* x, float* y,
+                       int rows, int cols, cudaStream_t s);
+/* Replaces matmul.cu:80-86 (wisp_engine.h:554). y = W^T x. */
+void wisp_gpu_gemv_t_f16(const wisp_half* W, const float* x, float* y,
+                         int rows, int cols, cudaStream_t s);
+/* Replaces matmul.cu:112-117 (wisp_engine.h:556). In-place safe. */
+void wisp_gpu_rmsnorm(const float* x, const wisp_half* w, float* y, int n,
+                      float eps, cudaStream_t s);
+/* Replaces matmul.cu:125-130 (wisp_engine.h:558). x += d. */
+void wisp_gpu_residual_add(float* x, const float* delta, int n,
+                           cudaStream_t s);
+/* Replaces matmul.cu:144-148 (wisp_engine.h:560). out = silu(g)*u. */
+void wisp_gpu_swiglu(const float* gate, const float* up, float* out, int n,
+                     cudaStream_t s);
+/* Replaces matmul.cu:207-213 (wisp_engine.h:562). h = silu(Wg x)*(Wu x). */
+void wisp_gpu_swiglu_ffn(const wisp_half* Wg, const wisp_half* Wu,
+                         const float* x, float* h, int inter, int cols,
+                         cudaStream_t s);
+/* Replaces matmul.cu:157-161 (wisp_engine.h:565). acc += w*x. */
+void wisp_gpu_scale_accum(float* acc, const float* x, float w, int n,
+                          cudaStream_t s);
+/* Replaces csrc/cuda/router.cu:140-171 (wisp_engine.h:587).  logits = W x +
+ * bias, softmax, k strict-argmax passes, renormalised weights.  out_idx /
+ * out_w are HOST pointers, valid after the caller synchronises `s`. */
+void wisp_gpu_router_topk(const wisp_half* W, const wisp_half* bias,
+                          const float* x, float* logits_scratch,
+                          int n_experts, int hidden, int top_k,
+                          int* out_idx, float* out_w, cudaStream_t s);
+/* Replaces csrc/cuda/expert_loader.cu:46-63 (wisp_engine.h:598).
+ * out[i] = fp16((nib(i)-8)*scale[i/gs] + zero[i/gs]). */
+cudaError_t launch_dequant_expert(const uint8_t* d_packed,
+                                  const wisp_half* d_scales,
+                                  const wisp_half* d_zeros,
+                                  wisp_half* d_output, int n_elements,
+                                  int group_size, cudaStream_t stream);
+/* Replaces expert_loader.cu:67-97 (wisp_engine.h:604): 3 H2D copies on
+ * `stream`, then dequant. */
+cudaError_t async_load_expert(const uint8_t* h_packed,
+                              const wisp_half* h_scales,
+                              const wisp_half* h_zeros, uint8_t* d_packed_tmp,
+                              wisp_half* d_scales_tmp, wisp_half* d_zeros_tmp,
+                              wisp_half* d_output, int n_elements,
+                              int group_size, cudaStream_t stream);
+
+/* ====================================================================== *
+ * 2. Fused MoE block (new; no reference counterpart -- replaces the body of
+ *    run_moe, csrc/core/wisp_engine.c:1411-1522, for the all-resident case)
+ * ====================================================================== */
+
+/* One MoE layer as the kernels see it.  All pointers are DEVICE pointers
+ * except where noted.  Every expert blob of the layer has the same layout,
+ * described by `meta` (host copy, parsed from any blob's header).  The
+ * packed, scales and zeros sections of every blob must start 16-byte
+ * aligned (true for a .bin blob placed at an address = 8 mod 16 when all
+ * section sizes are multiples of 16; the engine's VRAM slots do this).
+ * Shape limits: hidden and inter multiples of 32; group_size a multiple of
+ * 32 that divides hidden and inter; rows multiples of 8. */
+typedef struct {
+    WispExpertMeta meta;               /* host copy                        */
+    const void* const* expert_blobs;   /* device array [n_experts]         */
+    const wisp_half* router_w;         /* [n_experts, hidden] fp16         */
+    const wisp_half* router_bias;      /* [n_experts] fp16 or NULL         */
+    const wisp_half* norm_w;           /* [hidden] RMSNorm weight (stacks) */
+    const void* shared_blob;           /* int4 shared expert blob or NULL  */
+    WispExpertMeta shared_meta;        /* host copy; used when shared_blob */
+    int n_experts;
+    int top_k;
+} WispMoeLayer;
+
+/* Bytes of device workspace wisp_moe_block_forward / wisp_moe_stack_forward
+ * need for T tokens (max over the layers passed). */
+size_t wisp_moe_workspace_bytes(const WispMoeLayer* layers, int n_layers,
+                                int T);
+
+/* y[T,H] = MoE(x[T,H]) for one layer.  x is the block input (the
+ * reference's buf_norm); y may not alias x.  topk_idx / topk_w (device,
+ * [T, top_k], optional) receive the routing.  workspace: device, at least
+ * wisp_moe_workspace_bytes(); contents need no initialisation. */
+WispError wisp_moe_block_forward(const WispMoeLayer* layer, const float* x,
+                                 float* y, int T, int* topk_idx,
+                                 float* topk_w, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream,
+                                 WispErrCtx* err);
+
+/* The two halves of wisp_moe_block_forward, for callers that must see the
+ * routing on the host between them (e.g. to fetch the routed experts into
+ * the table first): _route quantises x and runs router + top-k + the
+ * expert-tile plan; _experts runs gate/up, down and the combine on the plan
+ * the preceding _route left in the SAME workspace (same x, T, layer shape,
+ * stream; topk_idx/topk_w the same buffers or both NULL). */
+WispError wisp_moe_block_route(const WispMoeLayer* layer, const float* x,
+                               int T, int* topk_idx, float* topk_w,
+                               void* workspace, size_t workspace_bytes,
+                               cudaStream_t stream, WispErrCtx* err);
+WispError wisp_moe_block_experts(const WispMoeLayer* layer, const float* x,
+                                 float* y, int T, int* topk_idx,
+                                 float* topk_w, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream,
+                                 WispErrCtx* err);
+
+/* Stack of n_layers blocks: per layer l, x <- x + MoE_l(rmsnorm(x; norm_w_l,
+ * eps)).  x [T,H] is updated in place.  topk_idx/topk_w optional, device
+ * [n_layers, T, top_k].  Launch-only (capturable into a CUDA graph). */
+WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_layers,
+                                 float eps, float* x, int T, int* topk_idx,
+                                 float* topk_w, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream,
+                                 WispErrCtx* err);
+
+/* Device-side status word the kernels set instead of faulting (bit 0: a
+ * weight section was not 16-byte aligned; bit 1: an expert index was out of
+ * range; bit 2: a plan overflowed).  Synchronises `stream`. */
+int wisp_moe_status(const void* workspace, cudaStream_t stream);
+
+/* Profiling hook (new): while `events` is set, the calling thread's
+ * block/stack forwards record events[i] on the launch stream before each
+ * kernel they launch and one after the last (so n kernels -> n+1 events,
+ * durations by cudaEventElapsedTime of neighbours).  The records sit between
+ * launches and remove the programmatic overlap, so time the headline
+ * without them.  NULL turns the hook off; the count restarts at 0. */
+void wisp_moe_profile_events(void* events, int n_events);
+/* Events recorded since the hook was set. */
+int wisp_moe_profile_count(void);
+
+/* ====================================================================== *
+ * 3. Engine ABI (reference: csrc/core/wisp_engine.h:472-543)
+ * ====================================================================== */
+typedef struct WispEngine WispEngine;
+
+/* Replaces wisp_engine_create (wisp_engine.c:1914-2094).  Loads
+ * manifest.json and dense/model_dense.safetensors from model_path; expert
+ * blobs stream from experts/ through the RAM and VRAM LRU tiers.  Requires
+ * a GPU (gpu_count >= 1); the first index is the device used. */
+WispEngine* wisp_engine_create(const char* model_path,
+                               size_t vram_expert_budget_bytes,
+                               size_t ram_expert_budget_bytes,
+                               const int* gpu_indices, int gpu_count,
+                               int omp_threads, WispErrCtx* err);
+/* Replaces wisp_engine_destroy (wisp_engine.c:2096-2187). */
+void wisp_engine_destroy(WispEngine* eng);
+
+/* Replaces wisp_expert_fetch (wisp_engine.c:920-1078): returns a device
+ * pointer to the expert's blob (VRAM tier, or a scratch-ring slot for
+ * experts that have not earned a VRAM slot), NULL + err on failure
+ * (WISP_ERR_IO = file missing/short; callers skip the expert). */
+void* wisp_expert_fetch(WispEngine* eng, uint32_t layer_id,
+                        uint32_t expert_id, WispErrCtx* err);
+/* Replaces wisp_expert_prefetch_hint (wisp_engine.c:1162-1177). */
+void wisp_expert_prefetch_hint(WispEngine* eng, int layer_idx,
+                               const int* expert_ids, int n);
+
+/* New: one MoE layer on device buffers x/y [T,H] on the engine's compute
+ * stream (or `stream` when non-NULL).  If every expert of the layer is
+ * VRAM-resident the whole block runs without a host sync; otherwise the
+ * router runs first, the host fetches the routed experts through the
+ * tiers, then the expert kernels run. */
+WispError wisp_moe_forward(WispEngine* eng, int layer, const float* x,
+                           float* y, int T, cudaStream_t stream,
+                           WispErrCtx* err);
+/* New: x <- x + MoE_l(rmsnorm(x)) for layers [layer0, layer0+n). */
+WispError wisp_moe_stack(WispEngine* eng, int layer0, int n_layers, float* x,
+                         int T, cudaStream_t stream, WispErrCtx* err);
+/* New: load every expert of layers [layer0, layer0+n) into the VRAM tier
+ * (until the budget is full).  Returns the number of experts resident. */
+int wisp_engine_pin_experts(WispEngine* eng, int layer0, int n_layers,
+                            WispErrCtx* err);
+/* New: the device stream the engine computes on. */
+cudaStream_t wisp_engine_stream(WispEngine* eng);
+/* New: hidden size, experts per layer, top-k, layers (for callers). */
+void wisp_engine_dims(WispEngine* eng, int* hidden, int* n_experts,
+                      int* top_k, int* n_layers);
+
+/* Replace wisp_cache_stats / wisp_cache_clear_all / wisp_ram_trim /
+ * wisp_drain_expert_log / wisp_vram_used / wisp_ram_used / wisp_tok_per_sec
+ * (wisp_engine.c:872-889, 2305-2367), same semantics. */
+void wisp_cache_stats(WispEngine* eng, uint64_t* vram_hits,
+                      uint64_t* ram_hits, uint64_t* ssd_hits,
+                      double* hit_rate);
+void wisp_cache_clear_all(WispEngine* eng);
+int wisp_ram_trim(WispEngine* eng, int count);
+int wisp_drain_expert_log(WispEngine* eng, uint32_t* out, int max_out,
+                          uint64_t* dropped_out);
+size_t wisp_vram_used(WispEngine* eng);
+size_t wisp_ram_used(WispEngine* eng);
+double wisp_tok_per_sec(WispEngine* eng);
+
+/* Replace the self-tests (lru_cache.c:213-270, double_buffer.c:184-229):
+ * host-only, return 1 on success. */
+int wisp_selftest_lru(void);
+int wisp_selftest_double_buffer(void);
+
+/* Replaces wisp_debug_expert_probe (wisp_engine.c:311-349): parse a .bin
+ * and dequantise the first n values of matrix `mat` (host arithmetic, the
+ * byte-layout cross-check the reference's tests call). */
+WispError wisp_debug_expert_probe(const char* path, int mat, int n,
+                                  float* out_values, WispExpertMeta* out_meta,
+                                  WispErrCtx* err);
+
+/* Library identity: "wisp_b200 <version> sm_100a". */
+const char* wisp_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif

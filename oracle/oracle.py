@@ -1,0 +1,246 @@
+"""ctypes front-end of the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline legs
+use this module.  Two checkers:
+
+* ``Port*`` -- ``moe_oracle.c``, the C restatement (works on in-memory blobs);
+* ``RefEngine`` -- the reference engine's own CPU ``run_moe`` built from its
+  sources (``oracle/_ref/libwisp_ref.so``); it reads a converted model directory.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+from pathlib import Path
+
+import numpy as np
+
+from . import build as _build
+
+_port = None
+_ref = None
+
+
+def port_lib() -> C.CDLL:
+    global _port
+    if _port is None:
+        _port = C.CDLL(str(_build.build_port()))
+        f = _port.oracle_moe_block
+        f.restype = C.c_int
+        f.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        f = _port.oracle_stack
+        f.restype = C.c_int
+        f.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_int, C.c_int,
+                      C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                      C.c_void_p, C.c_int]
+        _port.oracle_router_topk.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                             C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        _port.oracle_rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float]
+        _port.oracle_dequant.argtypes = [C.c_void_p, C.c_int, C.c_long, C.c_void_p]
+    return _port
+
+
+def ref_lib() -> C.CDLL | None:
+    global _ref
+    if _ref is None:
+        so = _build.build_ref()
+        if so is None or not Path(so).exists():
+            return None
+        _ref = C.CDLL(str(so))
+        _ref.ref_open.restype = C.c_void_p
+        _ref.ref_open.argtypes = [C.c_char_p, C.c_ulonglong, C.c_int, C.c_char_p, C.c_int]
+        _ref.ref_close.argtypes = [C.c_void_p]
+        _ref.ref_moe.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                 C.c_void_p, C.c_void_p]
+        _ref.ref_stack.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                   C.c_void_p, C.c_void_p]
+        _ref.ref_probe.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_void_p]
+        _ref.ref_cache_stats.argtypes = [C.c_void_p, C.c_void_p]
+    return _ref
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+def _ptr_array(arrs) -> np.ndarray:
+    return np.array([0 if a is None else a.ctypes.data for a in arrs], dtype=np.uint64)
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+class Model:
+    """A converted model directory held in host memory."""
+
+    def __init__(self, path: str | Path):
+        from safetensors.numpy import load_file
+        self.path = Path(path)
+        man = json.loads((self.path / "manifest.json").read_text())
+        a = man["architecture"]
+        self.n_layers = int(a["num_layers"])
+        self.E = int(a["num_experts_per_layer"])
+        self.k = int(a["top_k_routing"])
+        self.H = int(a["hidden_size"])
+        self.eps = float(a.get("rms_norm_eps", 1e-6))
+        self.dense = {k: v.view(np.uint16) for k, v in
+                      load_file(str(self.path / "dense" / "model_dense.safetensors")).items()}
+        self.blobs = [[np.fromfile(self.path / "experts" / f"L{l:03d}_E{e:05d}.bin", dtype=np.uint8)
+                       for e in range(self.E)] for l in range(self.n_layers)]
+
+    def d(self, name: str):
+        return self.dense.get(name)
+
+
+def port_moe_block(m: Model, layer: int, x: np.ndarray, threads: int | None = None,
+                   with_shared: bool = True):
+    """The restated block on x [T,H] fp32 -> (y [T,H], idx [T,k], w [T,k])."""
+    lib = port_lib()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    y = np.zeros((T, m.H), np.float32)
+    idx = np.zeros((T, m.k), np.int32)
+    w = np.zeros((T, m.k), np.float32)
+    blobs = _ptr_array(m.blobs[layer])
+    sg, su, sd = (m.d(f"layers.{layer}.shared.{n}") for n in ("gate", "up", "down"))
+    si = sg.shape[0] if (sg is not None and with_shared) else 0
+    rc = lib.oracle_moe_block(_ptr(m.d(f"layers.{layer}.router")),
+                              _ptr(m.d(f"layers.{layer}.router_bias")), m.E, m.H, m.k,
+                              _ptr(blobs), _ptr(sg) if si else None, _ptr(su) if si else None,
+                              _ptr(sd) if si else None, si, _ptr(x), T, _ptr(y), _ptr(idx),
+                              _ptr(w), threads or host_threads())
+    if rc:
+        raise RuntimeError(f"oracle_moe_block failed: {rc}")
+    return y, idx, w
+
+
+def port_moe_block_arrays(router_w: np.ndarray, router_bias: np.ndarray | None, blobs: list,
+                          k: int, x: np.ndarray, threads: int | None = None):
+    """Same as ``port_moe_block`` on explicit arrays (fp16 bits as uint16, blob bytes)."""
+    lib = port_lib()
+    E, H = router_w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    y = np.zeros((T, H), np.float32)
+    idx = np.zeros((T, k), np.int32)
+    w = np.zeros((T, k), np.float32)
+    bp = _ptr_array(blobs)
+    rc = lib.oracle_moe_block(_ptr(router_w), _ptr(router_bias), E, H, k, _ptr(bp), None, None,
+                              None, 0, _ptr(x), T, _ptr(y), _ptr(idx), _ptr(w),
+                              threads or host_threads())
+    if rc:
+        raise RuntimeError(f"oracle_moe_block failed: {rc}")
+    return y, idx, w
+
+
+def port_stack(m: Model, x: np.ndarray, layers: int | None = None, threads: int | None = None):
+    """x <- x + moe_l(rmsnorm(x)) for l < layers -> (x_out, idx [T,L,k], w [T,L,k])."""
+    lib = port_lib()
+    L = layers or m.n_layers
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    out = np.empty_like(x)
+    idx = np.zeros((T, L, m.k), np.int32)
+    w = np.zeros((T, L, m.k), np.float32)
+    rw = _ptr_array([m.d(f"layers.{l}.router") for l in range(L)])
+    rb = [m.d(f"layers.{l}.router_bias") for l in range(L)]
+    rbp = _ptr_array(rb) if any(b is not None for b in rb) else None
+    nw = _ptr_array([m.d(f"layers.{l}.post_norm") for l in range(L)])
+    bl = _ptr_array([b for l in range(L) for b in m.blobs[l]])
+    rc = lib.oracle_stack(L, _ptr(rw), _ptr(rbp), _ptr(nw), m.eps, m.E, m.H, m.k, _ptr(bl),
+                          _ptr(x), _ptr(out), T, _ptr(idx), _ptr(w), threads or host_threads())
+    if rc:
+        raise RuntimeError(f"oracle_stack failed: {rc}")
+    return out, idx, w
+
+
+def port_router(router_w: np.ndarray, bias: np.ndarray | None, x: np.ndarray, k: int):
+    """Router on one token -> (idx [k], w [k], probs [E])."""
+    lib = port_lib()
+    E, H = router_w.shape
+    idx = np.zeros(k, np.int32)
+    w = np.zeros(k, np.float32)
+    p = np.zeros(E, np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lib.oracle_router_topk(_ptr(router_w), _ptr(bias), _ptr(x), E, H, k, _ptr(idx), _ptr(w), _ptr(p))
+    return idx, w, p
+
+
+def port_dequant(blob: np.ndarray, mat: int, n: int) -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    rc = port_lib().oracle_dequant(_ptr(blob), mat, n, _ptr(out))
+    if rc:
+        raise RuntimeError("oracle_dequant: bad blob")
+    return out
+
+
+class RefEngine:
+    """The reference engine's CPU MoE path on a model directory."""
+
+    def __init__(self, path: str | Path, threads: int | None = None, ram_budget: int | None = None):
+        lib = ref_lib()
+        if lib is None:
+            raise RuntimeError("reference harness not built (oracle/_ref/libwisp_ref.so missing)")
+        self.lib = lib
+        man = json.loads((Path(path) / "manifest.json").read_text())
+        a = man["architecture"]
+        self.H = int(a["hidden_size"])
+        self.k = int(a["top_k_routing"])
+        if ram_budget is None:
+            n = int(a["num_layers"]) * int(a["num_experts_per_layer"])
+            ram_budget = (n + 1) * int(man["performance"]["expert_size_bytes"]) * 2
+        err = C.create_string_buffer(600)
+        self.h = lib.ref_open(str(path).encode(), ram_budget, threads or host_threads(), err, 600)
+        if not self.h:
+            raise RuntimeError(f"reference engine_create failed: {err.value.decode()}")
+
+    def moe(self, layer: int, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        y = np.zeros((T, self.H), np.float32)
+        idx = np.zeros((T, self.k), np.int32)
+        w = np.zeros((T, self.k), np.float32)
+        rc = self.lib.ref_moe(self.h, layer, _ptr(x), T, _ptr(y), _ptr(idx), _ptr(w))
+        if rc:
+            raise RuntimeError(f"reference run_moe failed: {rc}")
+        return y, idx, w
+
+    def stack(self, x: np.ndarray, n_layers: int, layer0: int = 0):
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        T = x.shape[0]
+        idx = np.zeros((T, n_layers, self.k), np.int32)
+        w = np.zeros((T, n_layers, self.k), np.float32)
+        rc = self.lib.ref_stack(self.h, layer0, n_layers, _ptr(x), T, _ptr(idx), _ptr(w))
+        if rc:
+            raise RuntimeError(f"reference stack failed: {rc}")
+        return x, idx, w
+
+    def cache_stats(self):
+        out = np.zeros(3, np.uint64)
+        self.lib.ref_cache_stats(self.h, _ptr(out))
+        return tuple(int(v) for v in out)
+
+    def close(self):
+        if self.h:
+            self.lib.ref_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ref_probe(path: str | Path, mat: int, n: int) -> np.ndarray:
+    lib = ref_lib()
+    out = np.zeros(n, np.float32)
+    rc = lib.ref_probe(str(path).encode(), mat, n, _ptr(out))
+    if rc:
+        raise RuntimeError(f"reference probe failed: {rc}")
+    return out

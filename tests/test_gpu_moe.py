@@ -1,0 +1,120 @@
+"""Parity of the fused CUDA MoE path with the CPU oracle (GPU tests).
+
+Tolerances (from the build's north star): routed expert indices bit-exact except
+where the competing router logits tie within 1e-5; outputs within max-abs 2e-2 and
+rel-L2 1e-2 of the reference's fp32 computation.  A tighter regression bound
+(rel-L2 <= 2e-3) guards the int4 arithmetic itself: the kernels' only deviations
+from the oracle are fp32 summation order and the 2-digit int8 activation split
+(error <= 1.6e-5 * max|x| per element).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from wisp_b200 import converter as cv
+from wisp_b200.moe import MoEStack
+
+pytestmark = pytest.mark.gpu
+
+from parity import check_outputs, check_routing  # noqa: E402
+
+
+CONFIGS = [
+    # H, I, E, k, gs, bias, T
+    (128, 256, 8, 2, 64, "random", 1),
+    (128, 256, 8, 2, 64, "random", 5),
+    (256, 512, 16, 4, 64, None, 16),
+    (192, 96, 4, 2, 32, None, 3),
+    (512, 256, 64, 8, 128, "zipf", 24),
+    (1024, 2048, 8, 2, 64, None, 1),
+]
+
+
+@pytest.mark.parametrize("H,I,E,k,gs,bias,T", CONFIGS)
+def test_block_matches_oracle(cuda, H, I, E, k, gs, bias, T):
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=E, top_k=k, group_size=gs)
+    st = MoEStack(shape, seed=H + I + E + T, device=cuda, zipf_s=1.1 if bias == "zipf" else None,
+                  random_bias=bias == "random")
+    x = (torch.randn(T, H, generator=torch.Generator().manual_seed(T)) * 1.5).half().float()
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy())
+    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
+    if nd == 0:
+        np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-6)
+        check_outputs(y.cpu().numpy(), yr)
+
+
+@pytest.mark.parametrize("T", [1, 4, 16])
+def test_stack_matches_oracle(cuda, T, tmp_path):
+    shape = cv.MoEShape(hidden=256, inter=512, n_experts=8, top_k=2, n_layers=4)
+    st = MoEStack(shape, seed=11, device=cuda, random_bias=True)
+    x0 = (torch.randn(T, 256, generator=torch.Generator().manual_seed(3))).half().float()
+    x = x0.clone().to(cuda)
+    _, idx, w = st.stack(x, routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    # oracle: same per-layer recipe on the host copies
+    xr = x0.numpy().copy()
+    xs = []
+    for l in range(shape.n_layers):
+        Wb, bb = st.host_router(l)
+        ones = np.ones(256, np.float16).view(np.uint16)
+        xn = np.empty_like(xr)
+        for t in range(T):
+            orc.port_lib().oracle_rmsnorm(xr[t].ctypes.data, ones.ctypes.data, xn[t].ctypes.data,
+                                          256, np.float32(shape.rms_eps))
+        yl, il, wl = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(l), 2, xn)
+        check_routing(idx[l].cpu().numpy(), il, Wb, bb, xn)
+        xr = xr + yl
+    check_outputs(x.cpu().numpy(), xr)
+
+
+def test_stack_graph_capture_replays(cuda):
+    shape = cv.MoEShape(hidden=256, inter=256, n_experts=8, top_k=2, n_layers=3)
+    st = MoEStack(shape, seed=5, device=cuda)
+    x0 = torch.randn(4, 256, device=cuda)
+    x = x0.clone()
+    st.workspace(4)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        st.stack(x)  # warm-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    eager = x.clone()
+    g = torch.cuda.CUDAGraph()
+    x.copy_(x0)
+    with torch.cuda.graph(g):
+        st.stack(x)
+    x.copy_(x0)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(x, eager)
+
+
+def test_repeated_calls_deterministic(cuda):
+    shape = cv.MoEShape(hidden=512, inter=1024, n_experts=8, top_k=2)
+    st = MoEStack(shape, seed=2, device=cuda)
+    x = torch.randn(3, 512, device=cuda)
+    a = st.block(0, x).clone()
+    b = st.block(0, x).clone()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("T", [1, 4])
+def test_mixtral_block_matches_oracle(cuda, T):
+    st = MoEStack(cv.MIXTRAL, seed=2024, device=cuda)
+    x = cv.make_input(cv.MIXTRAL, T, 2024)
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 2, x.numpy())
+    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
+    if nd == 0:
+        check_outputs(y.cpu().numpy(), yr)

@@ -1,0 +1,1016 @@
+// engine.cpp -- the engine ABI (reference: csrc/core/wisp_engine.h:472-543,
+// wisp_engine.c:851-1177 and 1601-2367) over the fused B200 MoE kernels.
+//
+// Model directory: manifest.json (keys found by name anywhere in the file,
+// as the reference's strstr scan does, wisp_engine.c:1601-1657),
+// dense/model_dense.safetensors (fp16: layers.i.router, router_bias,
+// post_norm; wisp_engine.c:1698-1813) and experts/L%03u_E%05u.bin blobs.  An
+// int4 shared expert is read from experts/L%03u_shared.bin (same layout).
+//
+// Expert tiers (policy of wisp_engine.c:920-1078): VRAM LRU (fixed slots in
+// one device arena), RAM LRU (pinned host blobs), SSD files.  A RAM hit is
+// served through a small scratch ring of device slots until it has been hit
+// WISP_PROMOTE_HITS (3) times, then it earns a VRAM slot (evicting the VRAM
+// LRU back to RAM).  A cold SSD read takes a VRAM slot only if one is free.
+// Each layer keeps a device table [E] of blob pointers that the fused
+// kernels read; when every expert of a layer is VRAM-resident the whole MoE
+// block runs with no host synchronisation.
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include <algorithm>
+#include <chrono>
+#include <condition_variable>
+#include <deque>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "internal.h"
+#include "tiers.h"
+
+namespace {
+
+constexpr uint32_t kMagic = 0x57455850u;
+constexpr int kPromoteHits = 3;
+constexpr int kPrefetchRing = 1024;
+
+uint64_t now_ns() {
+    return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+bool read_file(const std::string& path, std::vector<char>& out) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) return false;
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (n < 0) {
+        fclose(f);
+        return false;
+    }
+    out.resize((size_t)n + 1);
+    size_t got = fread(out.data(), 1, (size_t)n, f);
+    fclose(f);
+    if (got != (size_t)n) return false;
+    out[(size_t)n] = 0;
+    out.resize((size_t)n);
+    return true;
+}
+
+// Value after "key": anywhere in a JSON text (the reference's lookup rule).
+const char* json_find(const char* js, const char* key) {
+    std::string pat = std::string("\"") + key + "\"";
+    const char* p = strstr(js, pat.c_str());
+    if (!p) return nullptr;
+    p += pat.size();
+    while (*p && *p != ':') ++p;
+    if (*p != ':') return nullptr;
+    ++p;
+    while (*p == ' ' || *p == '\n' || *p == '\t' || *p == '\r') ++p;
+    return p;
+}
+double json_num(const char* js, const char* key, double dflt) {
+    const char* p = json_find(js, key);
+    return p ? strtod(p, nullptr) : dflt;
+}
+
+// Minimal safetensors reader: locate a tensor by exact name in the header.
+struct StTensor {
+    uint64_t off = 0, bytes = 0;
+    std::vector<int64_t> shape;
+    bool f16 = false;
+};
+struct StFile {
+    FILE* f = nullptr;
+    std::string header;
+    uint64_t data_start = 0;
+    ~StFile() {
+        if (f) fclose(f);
+    }
+    bool open(const std::string& path) {
+        f = fopen(path.c_str(), "rb");
+        if (!f) return false;
+        uint8_t le[8];
+        if (fread(le, 1, 8, f) != 8) return false;
+        uint64_t n = 0;
+        for (int i = 7; i >= 0; --i) n = (n << 8) | le[i];
+        if (n == 0 || n > (1ull << 31)) return false;
+        header.resize(n);
+        if (fread(&header[0], 1, n, f) != n) return false;
+        data_start = 8 + n;
+        return true;
+    }
+    bool find(const std::string& name, StTensor* t) const {
+        std::string pat = "\"" + name + "\":";
+        size_t p = header.find(pat);
+        if (p == std::string::npos) return false;
+        size_t ob = header.find('{', p + pat.size());
+        size_t cb = header.find('}', ob);
+        if (ob == std::string::npos || cb == std::string::npos) return false;
+        std::string obj = header.substr(ob, cb - ob + 1);
+        t->f16 = obj.find("\"F16\"") != std::string::npos;
+        size_t sp = obj.find("\"shape\"");
+        if (sp != std::string::npos) {
+            size_t lb = obj.find('[', sp), rb = obj.find(']', lb);
+            const char* c = obj.c_str() + lb + 1;
+            const char* end = obj.c_str() + rb;
+            while (c < end) {
+                char* nx;
+                long long v = strtoll(c, &nx, 10);
+                if (nx == c) break;
+                t->shape.push_back(v);
+                c = nx;
+                while (c < end && (*c == ',' || *c == ' ')) ++c;
+            }
+        }
+        size_t dp = obj.find("\"data_offsets\"");
+        if (dp == std::string::npos) return false;
+        const char* c = obj.c_str() + obj.find('[', dp) + 1;
+        char* nx;
+        unsigned long long a = strtoull(c, &nx, 10);
+        while (*nx == ',' || *nx == ' ') ++nx;
+        unsigned long long b = strtoull(nx, nullptr, 10);
+        t->off = a;
+        t->bytes = b - a;
+        return true;
+    }
+    bool read(const StTensor& t, void* dst) const {
+        if (fseeko(f, (off_t)(data_start + t.off), SEEK_SET) != 0) return false;
+        return fread(dst, 1, t.bytes, f) == t.bytes;
+    }
+};
+
+struct LayerDev {
+    wisp_half* router = nullptr;
+    wisp_half* router_bias = nullptr;
+    wisp_half* post_norm = nullptr;
+    void* shared_blob = nullptr;
+    WispExpertMeta shared_meta{};
+    void** d_table = nullptr;     // device [E]
+    std::vector<void*> h_table;   // host mirror
+    std::vector<uint8_t> in_vram; // expert is VRAM-resident (not ring-served)
+    int n_vram = 0;
+};
+
+}  // namespace
+
+struct WispEngine {
+    std::string path;
+    int n_layers = 0, E = 0, K = 0, H = 0, inter = 0, gs = 64;
+    float eps = 1e-6f;
+    size_t expert_bytes = 0, max_expert_bytes = 0;
+    int device = 0;
+    cudaStream_t compute = nullptr, transfer = nullptr;
+    std::vector<LayerDev> L;
+    std::vector<WispExpertMeta> meta;
+    wb::Lru ram, vram;
+    wb::SlotArena arena, ring_arena;
+    size_t vram_budget = 0;
+    std::vector<void*> ring;
+    int ring_pos = 0;
+    void* staging = nullptr;  // pinned SSD staging (one expert)
+    std::mutex fetch_mu;
+    // workspace of the fused kernels
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    // prefetch worker
+    std::thread worker;
+    std::mutex q_mu;
+    std::condition_variable q_cv;
+    std::deque<std::pair<uint32_t, uint32_t>> q;
+    bool stop = false;
+    // stats
+    std::mutex stats_mu;
+    uint64_t hits[3] = {0, 0, 0};
+    std::vector<uint32_t> log;
+    int log_head = 0, log_count = 0;
+    uint64_t log_dropped = 0;
+    uint64_t tok_ns[32] = {0};
+    int tok_head = 0, tok_count = 0;
+};
+
+namespace {
+
+void stat_hit(WispEngine* e, int tier, uint32_t layer, uint32_t expert) {
+    std::lock_guard<std::mutex> g(e->stats_mu);
+    e->hits[tier]++;
+    if (!e->log.empty()) {
+        e->log[e->log_head] = ((layer & 0xFFFFu) << 16) | (expert & 0xFFFFu);
+        e->log_head = (e->log_head + 1) % (int)e->log.size();
+        if (e->log_count < (int)e->log.size())
+            e->log_count++;
+        else
+            e->log_dropped++;
+    }
+}
+
+std::string expert_path(const WispEngine* e, uint32_t layer, uint32_t expert) {
+    char buf[64];
+    snprintf(buf, sizeof buf, "/experts/L%03u_E%05u.bin", layer, expert);
+    return e->path + buf;
+}
+
+// Read an expert file into `dst` (capacity cap). Returns bytes, 0 on error.
+size_t read_expert(const std::string& p, void* dst, size_t cap, WispErrCtx* err) {
+    FILE* f = fopen(p.c_str(), "rb");
+    if (!f) {
+        WB_SET_ERR(err, WISP_ERR_IO, "expert file missing: %s", p.c_str());
+        return 0;
+    }
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (n <= 0 || (size_t)n > cap) {
+        fclose(f);
+        WB_SET_ERR(err, WISP_ERR_IO, "expert file %s size %ld exceeds staging %zu", p.c_str(),
+                   n, cap);
+        return 0;
+    }
+    size_t got = fread(dst, 1, (size_t)n, f);
+    fclose(f);
+    if (got != (size_t)n) {
+        WB_SET_ERR(err, WISP_ERR_IO, "short read on %s: %zu of %ld", p.c_str(), got, n);
+        return 0;
+    }
+    return got;
+}
+
+bool sections_aligned(const WispExpertMeta& m) {
+    for (int i = 0; i < 3; ++i)
+        if ((m.packed_off[i] - 120) % 16 || (m.scales_off[i] - 120) % 16 ||
+            (m.zeros_off[i] - 120) % 16)
+            return false;
+    return (m.total_bytes - 120) % 16 == 0;
+}
+
+void set_table(WispEngine* e, uint32_t layer, uint32_t expert, void* ptr, bool vram) {
+    LayerDev& d = e->L[layer];
+    if (d.in_vram[expert] && !vram) d.n_vram--;
+    if (!d.in_vram[expert] && vram) d.n_vram++;
+    d.in_vram[expert] = vram ? 1 : 0;
+    d.h_table[expert] = ptr;
+    cudaMemcpyAsync(d.d_table + expert, &d.h_table[expert], sizeof(void*),
+                    cudaMemcpyHostToDevice, e->compute);
+}
+
+void ram_put(WispEngine* e, uint32_t layer, uint32_t expert, void* data, size_t n) {
+    if (n > e->ram.capacity()) {
+        cudaFreeHost(data);
+        return;
+    }
+    wb::Lru::Entry v;
+    while (e->ram.would_overflow(n) && e->ram.evict(&v)) cudaFreeHost(v.data);
+    e->ram.put(layer, expert, data, n);
+}
+
+// H2D copy into a ring slot (cool experts: no cache insert, no eviction).
+void* scratch_serve(WispEngine* e, const void* src, size_t n, WispErrCtx* err) {
+    void* slot = e->ring[e->ring_pos];
+    e->ring_pos = (e->ring_pos + 1) % (int)e->ring.size();
+    cudaError_t ce = cudaMemcpyAsync(slot, src, n, cudaMemcpyHostToDevice, e->transfer);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "scratch H2D failed: %s", cudaGetErrorString(ce));
+        return nullptr;
+    }
+    return slot;
+}
+
+// A VRAM slot, evicting the VRAM LRU (copied back to the RAM tier) until
+// one is free.  `keep` lists keys that must not be evicted (sorted).
+void* vram_alloc_evicting(WispEngine* e, size_t n, const std::vector<uint64_t>& keep) {
+    if (e->arena.n_slots() == 0) return nullptr;
+    for (;;) {
+        if (!e->vram.would_overflow(n)) {
+            void* p = e->arena.alloc();
+            if (p) return p;
+        }
+        wb::Lru::Entry v;
+        if (!e->vram.evict_except(keep, &v)) return nullptr;
+        // in-flight kernels may still read the victim's slot
+        cudaStreamSynchronize(e->compute);
+        if (!e->ram.get(v.layer, v.expert, nullptr)) {
+            void* host = nullptr;
+            if (cudaHostAlloc(&host, v.bytes, cudaHostAllocDefault) == cudaSuccess) {
+                if (cudaMemcpy(host, v.data, v.bytes, cudaMemcpyDeviceToHost) == cudaSuccess)
+                    ram_put(e, v.layer, v.expert, host, v.bytes);
+                else
+                    cudaFreeHost(host);
+            }
+        }
+        set_table(e, v.layer, v.expert, nullptr, false);
+        e->arena.release(v.data);
+    }
+}
+
+WispError ensure_meta(WispEngine* e, uint32_t layer, const void* blob, size_t n,
+                      WispErrCtx* err) {
+    if (e->meta[layer].valid) return WISP_OK;
+    WispError r = wisp_expert_parse_header(blob, n, &e->meta[layer], err);
+    if (r != WISP_OK) return r;
+    return WISP_OK;
+}
+
+// Parse a layer's blob layout from the first readable expert file's header
+// (no tier insertion, no statistics).
+WispError meta_from_file(WispEngine* e, uint32_t layer, WispErrCtx* err) {
+    for (int x = 0; x < e->E; ++x) {
+        FILE* f = fopen(expert_path(e, layer, (uint32_t)x).c_str(), "rb");
+        if (!f) continue;
+        char head[120];
+        size_t got = fread(head, 1, sizeof head, f);
+        fseek(f, 0, SEEK_END);
+        long n = ftell(f);
+        fclose(f);
+        if (got != sizeof head || n <= 0) continue;
+        return wisp_expert_parse_header(head, (size_t)n, &e->meta[layer], err);
+    }
+    WB_SET_ERR(err, WISP_ERR_IO, "layer %u: no readable expert file", layer);
+    return WISP_ERR_IO;
+}
+
+void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
+                   const std::vector<uint64_t>& keep, WispErrCtx* err) {
+    wb::Lru::Entry ent;
+    // 1. VRAM hit
+    if (e->vram.get(layer, expert, &ent)) {
+        e->vram.touch(layer, expert);
+        stat_hit(e, 0, layer, expert);
+        return ent.data;
+    }
+    // 2. RAM hit: promote after kPromoteHits, else serve through the ring
+    if (e->ram.get(layer, expert, &ent)) {
+        uint32_t h = e->ram.touch(layer, expert);
+        stat_hit(e, 1, layer, expert);
+        if (ensure_meta(e, layer, ent.data, ent.bytes, err) != WISP_OK) return nullptr;
+        if (h < (uint32_t)kPromoteHits) {
+            void* p = scratch_serve(e, ent.data, ent.bytes, err);
+            if (p) set_table(e, layer, expert, p, false);
+            return p;
+        }
+        void* slot = vram_alloc_evicting(e, ent.bytes, keep);
+        if (!slot) {
+            void* p = scratch_serve(e, ent.data, ent.bytes, err);
+            if (p) set_table(e, layer, expert, p, false);
+            return p;
+        }
+        cudaError_t ce = cudaMemcpyAsync(slot, ent.data, ent.bytes, cudaMemcpyHostToDevice,
+                                         e->transfer);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
+        if (ce != cudaSuccess) {
+            e->arena.release(slot);
+            WB_SET_ERR(err, WISP_ERR_CUDA, "RAM->VRAM promote failed: %s",
+                       cudaGetErrorString(ce));
+            return nullptr;
+        }
+        e->vram.put(layer, expert, slot, ent.bytes);
+        set_table(e, layer, expert, slot, true);
+        return slot;
+    }
+    // 3. SSD miss
+    size_t n = read_expert(expert_path(e, layer, expert), e->staging, e->max_expert_bytes, err);
+    if (n == 0) return nullptr;
+    stat_hit(e, 2, layer, expert);
+    if (ensure_meta(e, layer, e->staging, n, err) != WISP_OK) return nullptr;
+    void* host = nullptr;
+    if (cudaHostAlloc(&host, n, cudaHostAllocDefault) == cudaSuccess) {
+        memcpy(host, e->staging, n);
+        ram_put(e, layer, expert, host, n);
+    }
+    void* slot = nullptr;
+    if (!e->vram.would_overflow(n)) slot = e->arena.alloc();
+    if (!slot) {
+        void* p = scratch_serve(e, e->staging, n, err);
+        if (p) set_table(e, layer, expert, p, false);
+        return p;
+    }
+    cudaError_t ce = cudaMemcpyAsync(slot, e->staging, n, cudaMemcpyHostToDevice, e->transfer);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
+    if (ce != cudaSuccess) {
+        e->arena.release(slot);
+        WB_SET_ERR(err, WISP_ERR_CUDA, "expert H2D failed: %s", cudaGetErrorString(ce));
+        return nullptr;
+    }
+    e->vram.put(layer, expert, slot, n);
+    set_table(e, layer, expert, slot, true);
+    return slot;
+}
+
+void prefetch_loop(WispEngine* e) {
+    std::vector<char> buf;
+    for (;;) {
+        std::pair<uint32_t, uint32_t> item;
+        {
+            std::unique_lock<std::mutex> g(e->q_mu);
+            e->q_cv.wait(g, [&] { return e->stop || !e->q.empty(); });
+            if (e->stop && e->q.empty()) return;
+            item = e->q.front();
+            e->q.pop_front();
+        }
+        if (e->vram.get(item.first, item.second, nullptr) ||
+            e->ram.get(item.first, item.second, nullptr))
+            continue;
+        WispErrCtx err{};
+        if (!read_file(expert_path(e, item.first, item.second), buf) || buf.empty()) continue;
+        void* host = nullptr;
+        if (cudaHostAlloc(&host, buf.size(), cudaHostAllocDefault) != cudaSuccess) continue;
+        memcpy(host, buf.data(), buf.size());
+        std::lock_guard<std::mutex> g(e->fetch_mu);
+        if (!e->meta[item.first].valid)
+            wisp_expert_parse_header(host, buf.size(), &e->meta[item.first], &err);
+        if (e->ram.get(item.first, item.second, nullptr))
+            cudaFreeHost(host);
+        else
+            ram_put(e, item.first, item.second, host, buf.size());
+    }
+}
+
+WispError load_half(WispEngine* e, const StFile& st, const std::string& name, wisp_half** out,
+                    bool required, WispErrCtx* err) {
+    StTensor t;
+    if (!st.find(name, &t)) {
+        if (required) {
+            WB_SET_ERR(err, WISP_ERR_MODEL, "dense file missing tensor %s", name.c_str());
+            return WISP_ERR_MODEL;
+        }
+        return WISP_OK;
+    }
+    if (!t.f16) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "tensor %s is not F16", name.c_str());
+        return WISP_ERR_MODEL;
+    }
+    std::vector<char> host(t.bytes);
+    if (!st.read(t, host.data())) {
+        WB_SET_ERR(err, WISP_ERR_IO, "short read for tensor %s", name.c_str());
+        return WISP_ERR_IO;
+    }
+    WB_CUDA_RET(cudaMalloc(out, t.bytes), err);
+    WB_CUDA_RET(cudaMemcpy(*out, host.data(), t.bytes, cudaMemcpyHostToDevice), err);
+    (void)e;
+    return WISP_OK;
+}
+
+WispError ensure_ws(WispEngine* e, const std::vector<WispMoeLayer>& layers, int T,
+                    WispErrCtx* err) {
+    size_t need = wisp_moe_workspace_bytes(layers.data(), (int)layers.size(), T);
+    if (need <= e->ws_bytes) return WISP_OK;
+    if (e->ws) {
+        cudaStreamSynchronize(e->compute);
+        cudaFree(e->ws);
+        e->ws = nullptr;
+    }
+    WB_CUDA_RET(cudaMalloc(&e->ws, need), err);
+    e->ws_bytes = need;
+    return WISP_OK;
+}
+
+WispMoeLayer layer_desc(WispEngine* e, int l) {
+    WispMoeLayer d{};
+    d.meta = e->meta[l];
+    d.expert_blobs = const_cast<const void* const*>(e->L[l].d_table);
+    d.router_w = e->L[l].router;
+    d.router_bias = e->L[l].router_bias;
+    d.norm_w = e->L[l].post_norm;
+    d.shared_blob = e->L[l].shared_blob;
+    d.shared_meta = e->L[l].shared_meta;
+    d.n_experts = e->E;
+    d.top_k = e->K;
+    return d;
+}
+
+bool layer_resident(WispEngine* e, int l) {
+    return e->meta[l].valid && e->L[l].n_vram == e->E;
+}
+
+WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
+    char buf[64];
+    snprintf(buf, sizeof buf, "/experts/L%03d_shared.bin", l);
+    std::vector<char> blob;
+    if (!read_file(e->path + buf, blob)) return WISP_OK;  // no int4 shared expert
+    WispExpertMeta m{};
+    WispError r = wisp_expert_parse_header(blob.data(), blob.size(), &m, err);
+    if (r != WISP_OK) return r;
+    // place at (256-aligned) + 8 so the sections are 16-byte aligned
+    char* base = nullptr;
+    WB_CUDA_RET(cudaMalloc(&base, blob.size() + 264), err);
+    void* dst = base + 8;
+    WB_CUDA_RET(cudaMemcpy(dst, blob.data(), blob.size(), cudaMemcpyHostToDevice), err);
+    e->L[l].shared_blob = dst;
+    e->L[l].shared_meta = m;
+    return WISP_OK;
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+
+extern "C" WispError wisp_expert_parse_header(const void* blob, size_t blob_size,
+                                              WispExpertMeta* meta, WispErrCtx* err) {
+    if (!blob || !meta) {
+        WB_SET_ERR(err, WISP_ERR_OOM, "NULL pointer: expert_parse_header");
+        return WISP_ERR_OOM;
+    }
+    if (blob_size < 120) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob too small: %zu bytes", blob_size);
+        return WISP_ERR_MODEL;
+    }
+    uint32_t h[6];
+    memcpy(h, blob, sizeof h);
+    if (h[0] != kMagic || h[1] != 1u || h[5] != 3u) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob corrupt: magic=%08x version=%u n_mats=%u",
+                   h[0], h[1], h[5]);
+        return WISP_ERR_MODEL;
+    }
+    const uint8_t* b = static_cast<const uint8_t*>(blob);
+    size_t off = 120;
+    for (int m = 0; m < 3; ++m) {
+        uint32_t rc[2];
+        uint64_t sz[3];
+        memcpy(rc, b + 24 + 32 * m, 8);
+        memcpy(sz, b + 24 + 32 * m + 8, 24);
+        meta->rows[m] = rc[0];
+        meta->cols[m] = rc[1];
+        meta->packed_off[m] = off;
+        off += sz[0];
+        meta->scales_off[m] = off;
+        off += sz[1];
+        meta->zeros_off[m] = off;
+        off += sz[2];
+    }
+    meta->group_size = h[4];
+    meta->total_bytes = off;
+    meta->valid = 1;
+    if (off > blob_size) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob truncated: needs %zu, have %zu", off,
+                   blob_size);
+        meta->valid = 0;
+        return WISP_ERR_MODEL;
+    }
+    return WISP_OK;
+}
+
+extern "C" WispError wisp_debug_expert_probe(const char* path, int mat, int n, float* out,
+                                             WispExpertMeta* out_meta, WispErrCtx* err) {
+    if (!path || !out) {
+        WB_SET_ERR(err, WISP_ERR_OOM, "NULL pointer: debug_probe");
+        return WISP_ERR_OOM;
+    }
+    if (mat < 0 || mat >= 3 || n <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "debug_probe: mat=%d n=%d", mat, n);
+        return WISP_ERR_INVALID_ARG;
+    }
+    std::vector<char> blob;
+    if (!read_file(path, blob)) {
+        WB_SET_ERR(err, WISP_ERR_IO, "debug_probe: cannot read %s", path);
+        return WISP_ERR_IO;
+    }
+    WispExpertMeta m{};
+    WispError r = wisp_expert_parse_header(blob.data(), blob.size(), &m, err);
+    if (r != WISP_OK) return r;
+    size_t total = (size_t)m.rows[mat] * m.cols[mat];
+    if ((size_t)n > total) n = (int)total;
+    const uint8_t* packed = reinterpret_cast<const uint8_t*>(blob.data() + m.packed_off[mat]);
+    const __half* sc = reinterpret_cast<const __half*>(blob.data() + m.scales_off[mat]);
+    const __half* ze = reinterpret_cast<const __half*>(blob.data() + m.zeros_off[mat]);
+    for (int i = 0; i < n; ++i) {
+        int code = (i & 1) ? (packed[i >> 1] >> 4) : (packed[i >> 1] & 0xF);
+        size_t g = (size_t)i / m.group_size;
+        out[i] = (float)(code - 8) * __half2float(sc[g]) + __half2float(ze[g]);
+    }
+    if (out_meta) *out_meta = m;
+    return WISP_OK;
+}
+
+extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_budget,
+                                          size_t ram_budget, const int* gpu_indices,
+                                          int gpu_count, int omp_threads, WispErrCtx* err) {
+    (void)omp_threads;  // no CPU compute path in this engine
+    if (!model_path || !err) return nullptr;
+    err->code = WISP_OK;
+    if (gpu_count <= 0 || !gpu_indices) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "engine_create: this engine runs on a GPU only (gpu_count=%d)", gpu_count);
+        return nullptr;
+    }
+    std::unique_ptr<WispEngine> e(new WispEngine());
+    e->path = model_path;
+    e->device = gpu_indices[0];
+    cudaError_t ce = cudaSetDevice(e->device);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "cudaSetDevice(%d): %s", e->device, cudaGetErrorString(ce));
+        return nullptr;
+    }
+    std::vector<char> js;
+    if (!read_file(e->path + "/manifest.json", js)) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "cannot read %s/manifest.json", model_path);
+        return nullptr;
+    }
+    js.push_back(0);
+    const char* j = js.data();
+    e->n_layers = (int)json_num(j, "num_layers", 0);
+    e->E = (int)json_num(j, "num_experts_per_layer", 0);
+    e->K = (int)json_num(j, "top_k_routing", 8);
+    e->H = (int)json_num(j, "hidden_size", 0);
+    e->inter = (int)json_num(j, "moe_intermediate_size", 2048);
+    e->eps = (float)json_num(j, "rms_norm_eps", 1e-6);
+    e->gs = (int)json_num(j, "group_size", 64);
+    e->expert_bytes = (size_t)json_num(j, "expert_size_bytes", 18350080);
+    if (e->n_layers <= 0 || e->H <= 0 || e->E <= 0 || e->K <= 0 || e->K > e->E) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "manifest invalid: layers=%d hidden=%d experts=%d top_k=%d",
+                   e->n_layers, e->H, e->E, e->K);
+        return nullptr;
+    }
+    e->max_expert_bytes = e->expert_bytes + e->expert_bytes / 4 + 4096;
+    ce = cudaStreamCreateWithFlags(&e->compute, cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->transfer, cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaHostAlloc(&e->staging, e->max_expert_bytes, 0);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "stream/staging setup: %s", cudaGetErrorString(ce));
+        wisp_engine_destroy(e.release());
+        return nullptr;
+    }
+    // dense weights
+    StFile st;
+    if (!st.open(e->path + "/dense/model_dense.safetensors")) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "cannot open dense weights: %s/dense/model_dense.safetensors",
+                   model_path);
+        wisp_engine_destroy(e.release());
+        return nullptr;
+    }
+    e->L.resize(e->n_layers);
+    e->meta.assign(e->n_layers, WispExpertMeta{});
+    for (int l = 0; l < e->n_layers; ++l) {
+        std::string p = "layers." + std::to_string(l) + ".";
+        LayerDev& d = e->L[l];
+        if (load_half(e.get(), st, p + "router", &d.router, true, err) != WISP_OK ||
+            load_half(e.get(), st, p + "router_bias", &d.router_bias, false, err) != WISP_OK ||
+            load_half(e.get(), st, p + "post_norm", &d.post_norm, false, err) != WISP_OK ||
+            load_shared(e.get(), l, err) != WISP_OK) {
+            wisp_engine_destroy(e.release());
+            return nullptr;
+        }
+        d.h_table.assign(e->E, nullptr);
+        d.in_vram.assign(e->E, 0);
+        ce = cudaMalloc(&d.d_table, (size_t)e->E * sizeof(void*));
+        if (ce == cudaSuccess) ce = cudaMemset(d.d_table, 0, (size_t)e->E * sizeof(void*));
+        if (ce != cudaSuccess) {
+            WB_SET_ERR(err, WISP_ERR_CUDA, "expert table alloc: %s", cudaGetErrorString(ce));
+            wisp_engine_destroy(e.release());
+            return nullptr;
+        }
+    }
+    // tiers
+    e->ram.set_capacity(ram_budget);
+    e->vram_budget = vram_budget;
+    e->vram.set_capacity(vram_budget);
+    size_t n_slots = e->max_expert_bytes ? vram_budget / e->max_expert_bytes : 0;
+    ce = e->arena.init(e->max_expert_bytes, n_slots);
+    int ring_n = std::min(e->E, std::max(e->K + 2, 16));
+    if (ce == cudaSuccess) ce = e->ring_arena.init(e->max_expert_bytes, (size_t)ring_n);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_OOM, "VRAM expert arena (%zu slots): %s", n_slots,
+                   cudaGetErrorString(ce));
+        wisp_engine_destroy(e.release());
+        return nullptr;
+    }
+    for (int i = 0; i < ring_n; ++i) e->ring.push_back(e->ring_arena.alloc());
+    int cap = e->K * e->n_layers * 16;
+    cap = std::max(4096, std::min(cap, 1 << 20));
+    e->log.assign((size_t)cap, 0);
+    WispEngine* raw = e.release();
+    raw->worker = std::thread(prefetch_loop, raw);
+    return raw;
+}
+
+extern "C" void wisp_engine_destroy(WispEngine* e) {
+    if (!e) return;
+    if (e->worker.joinable()) {
+        {
+            std::lock_guard<std::mutex> g(e->q_mu);
+            e->stop = true;
+        }
+        e->q_cv.notify_all();
+        e->worker.join();
+    }
+    if (e->compute) cudaStreamSynchronize(e->compute);
+    if (e->transfer) cudaStreamSynchronize(e->transfer);
+    e->ram.clear([](const wb::Lru::Entry& v) { cudaFreeHost(v.data); });
+    e->vram.clear([](const wb::Lru::Entry&) {});
+    for (auto& d : e->L) {
+        cudaFree(d.router);
+        cudaFree(d.router_bias);
+        cudaFree(d.post_norm);
+        if (d.shared_blob) cudaFree(static_cast<char*>(d.shared_blob) - 8);
+        cudaFree(d.d_table);
+    }
+    if (e->ws) cudaFree(e->ws);
+    if (e->staging) cudaFreeHost(e->staging);
+    if (e->compute) cudaStreamDestroy(e->compute);
+    if (e->transfer) cudaStreamDestroy(e->transfer);
+    delete e;
+}
+
+extern "C" void* wisp_expert_fetch(WispEngine* e, uint32_t layer, uint32_t expert,
+                                   WispErrCtx* err) {
+    if (!e || layer >= (uint32_t)e->n_layers || expert >= (uint32_t)e->E) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "expert_fetch: L%u/E%u out of range", layer,
+                   expert);
+        return nullptr;
+    }
+    cudaSetDevice(e->device);
+    std::lock_guard<std::mutex> g(e->fetch_mu);
+    return fetch_locked(e, layer, expert, {}, err);
+}
+
+extern "C" void wisp_expert_prefetch_hint(WispEngine* e, int layer, const int* ids, int n) {
+    if (!e || layer < 0 || layer >= e->n_layers || !ids) return;
+    std::lock_guard<std::mutex> g(e->q_mu);
+    for (int i = 0; i < n && (int)e->q.size() < kPrefetchRing; ++i) {
+        if (ids[i] < 0 || ids[i] >= e->E) continue;
+        e->q.emplace_back((uint32_t)layer, (uint32_t)ids[i]);
+    }
+    e->q_cv.notify_one();
+}
+
+extern "C" int wisp_engine_pin_experts(WispEngine* e, int layer0, int n, WispErrCtx* err) {
+    if (!e) return 0;
+    cudaSetDevice(e->device);
+    std::lock_guard<std::mutex> g(e->fetch_mu);
+    int resident = 0;
+    for (int l = layer0; l < layer0 + n && l < e->n_layers; ++l) {
+        for (int x = 0; x < e->E; ++x) {
+            if (e->L[l].in_vram[x]) {
+                ++resident;
+                continue;
+            }
+            WispErrCtx le{};
+            wb::Lru::Entry ent;
+            void* host = nullptr;
+            size_t bytes = 0;
+            if (e->ram.get(l, x, &ent)) {
+                host = ent.data;
+                bytes = ent.bytes;
+            } else {
+                bytes = read_expert(expert_path(e, l, x), e->staging, e->max_expert_bytes, &le);
+                if (!bytes) {
+                    if (err) *err = le;
+                    continue;
+                }
+                host = e->staging;
+            }
+            if (ensure_meta(e, l, host, bytes, &le) != WISP_OK) {
+                if (err) *err = le;
+                continue;
+            }
+            if (e->vram.would_overflow(bytes)) return resident;
+            void* slot = e->arena.alloc();
+            if (!slot) return resident;
+            if (cudaMemcpyAsync(slot, host, bytes, cudaMemcpyHostToDevice, e->transfer) !=
+                    cudaSuccess ||
+                cudaStreamSynchronize(e->transfer) != cudaSuccess) {
+                e->arena.release(slot);
+                WB_SET_ERR(err, WISP_ERR_CUDA, "pin H2D failed");
+                return resident;
+            }
+            e->vram.put(l, x, slot, bytes);
+            set_table(e, l, x, slot, true);
+            ++resident;
+        }
+    }
+    cudaStreamSynchronize(e->compute);
+    return resident;
+}
+
+extern "C" cudaStream_t wisp_engine_stream(WispEngine* e) { return e ? e->compute : nullptr; }
+
+extern "C" void wisp_engine_dims(WispEngine* e, int* hidden, int* n_experts, int* top_k,
+                                 int* n_layers) {
+    if (!e) return;
+    if (hidden) *hidden = e->H;
+    if (n_experts) *n_experts = e->E;
+    if (top_k) *top_k = e->K;
+    if (n_layers) *n_layers = e->n_layers;
+}
+
+static WispError moe_forward_impl(WispEngine* e, int l, const float* x, float* y, int T,
+                                  cudaStream_t s, WispErrCtx* err) {
+    if (!e->meta[l].valid) {
+        // nothing of this layer parsed yet: the layout is in any blob's header
+        std::lock_guard<std::mutex> g(e->fetch_mu);
+        WispError hr = meta_from_file(e, (uint32_t)l, err);
+        if (hr != WISP_OK) return hr;
+    }
+    if (!sections_aligned(e->meta[l])) {
+        WB_SET_ERR(err, WISP_ERR_MODEL,
+                   "layer %d: expert section sizes are not multiples of 16 bytes", l);
+        return WISP_ERR_MODEL;
+    }
+    std::vector<WispMoeLayer> d{layer_desc(e, l)};
+    WispError r = ensure_ws(e, d, T, err);
+    if (r != WISP_OK) return r;
+    if (layer_resident(e, l))
+        return wisp_moe_block_forward(&d[0], x, y, T, nullptr, nullptr, e->ws, e->ws_bytes, s,
+                                      err);
+    // miss path: the fused router decides, the host fetches what it chose, then the
+    // expert kernels run on that same plan
+    int* d_idx = nullptr;
+    float* d_w = nullptr;
+    WB_CUDA_RET(cudaMallocAsync(&d_idx, (size_t)T * e->K * sizeof(int), s), err);
+    WB_CUDA_RET(cudaMallocAsync(&d_w, (size_t)T * e->K * sizeof(float), s), err);
+    r = wisp_moe_block_route(&d[0], x, T, d_idx, d_w, e->ws, e->ws_bytes, s, err);
+    std::vector<int> idx((size_t)T * e->K, -1);
+    if (r == WISP_OK) {
+        cudaError_t ce = cudaMemcpyAsync(idx.data(), d_idx, idx.size() * sizeof(int),
+                                         cudaMemcpyDeviceToHost, s);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+        if (ce != cudaSuccess) {
+            WB_SET_ERR(err, WISP_ERR_CUDA, "router readback: %s", cudaGetErrorString(ce));
+            r = WISP_ERR_CUDA;
+        }
+    }
+    if (r == WISP_OK) {
+        std::vector<int> uniq;
+        for (int v : idx)
+            if (v >= 0) uniq.push_back(v);
+        std::sort(uniq.begin(), uniq.end());
+        uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+        std::vector<uint64_t> keep;
+        for (int v : uniq) keep.push_back(wb::Lru::key((uint32_t)l, (uint32_t)v));
+        int ring_used = 0;
+        std::lock_guard<std::mutex> g(e->fetch_mu);
+        for (int v : uniq) {
+            WispErrCtx fe{};
+            void* p = fetch_locked(e, (uint32_t)l, (uint32_t)v, keep, &fe);
+            if (!p) {
+                if (err) *err = fe;
+                r = fe.code == WISP_OK ? WISP_ERR_EXPERT_MISS : fe.code;
+                break;
+            }
+            if (!e->L[l].in_vram[v] && ++ring_used > (int)e->ring.size()) {
+                WB_SET_ERR(err, WISP_ERR_OOM,
+                           "layer %d routes %zu cold experts for %d tokens; raise the VRAM "
+                           "budget (scratch ring holds %zu)",
+                           l, uniq.size(), T, e->ring.size());
+                r = WISP_ERR_OOM;
+                break;
+            }
+        }
+    }
+    if (r == WISP_OK) {
+        // table updates were queued on the compute stream
+        if (s != e->compute) {
+            cudaEvent_t ev;
+            cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+            cudaEventRecord(ev, e->compute);
+            cudaStreamWaitEvent(s, ev, 0);
+            cudaEventDestroy(ev);
+        }
+        r = wisp_moe_block_experts(&d[0], x, y, T, d_idx, d_w, e->ws, e->ws_bytes, s, err);
+    }
+    cudaFreeAsync(d_idx, s);
+    cudaFreeAsync(d_w, s);
+    return r;
+}
+
+extern "C" WispError wisp_moe_forward(WispEngine* e, int layer, const float* x, float* y, int T,
+                                      cudaStream_t stream, WispErrCtx* err) {
+    if (!e || layer < 0 || layer >= e->n_layers || !x || !y || T <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_forward: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(e->device);
+    cudaStream_t s = stream ? stream : e->compute;
+    if (s != e->compute) {
+        // pending table updates on the compute stream must land first
+        cudaEvent_t ev;
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEventRecord(ev, e->compute);
+        cudaStreamWaitEvent(s, ev, 0);
+        cudaEventDestroy(ev);
+    }
+    return moe_forward_impl(e, layer, x, y, T, s, err);
+}
+
+extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, int T,
+                                    cudaStream_t stream, WispErrCtx* err) {
+    if (!e || layer0 < 0 || n <= 0 || layer0 + n > e->n_layers || !x || T <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_stack: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(e->device);
+    cudaStream_t s = stream ? stream : e->compute;
+    bool all = true;
+    for (int l = layer0; l < layer0 + n; ++l) all = all && layer_resident(e, l);
+    WispError r = WISP_OK;
+    if (all) {
+        if (s != e->compute) {
+            cudaEvent_t ev;
+            cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+            cudaEventRecord(ev, e->compute);
+            cudaStreamWaitEvent(s, ev, 0);
+            cudaEventDestroy(ev);
+        }
+        std::vector<WispMoeLayer> d;
+        for (int l = layer0; l < layer0 + n; ++l) d.push_back(layer_desc(e, l));
+        r = ensure_ws(e, d, T, err);
+        if (r == WISP_OK)
+            r = wisp_moe_stack_forward(d.data(), n, e->eps, x, T, nullptr, nullptr, e->ws,
+                                       e->ws_bytes, s, err);
+    } else {
+        // layer by layer with the miss path: xn = rmsnorm(x); x += moe(xn)
+        float *xn = nullptr, *f = nullptr;
+        size_t bytes = (size_t)T * e->H * sizeof(float);
+        WB_CUDA_RET(cudaMallocAsync(&xn, bytes, s), err);
+        WB_CUDA_RET(cudaMallocAsync(&f, bytes, s), err);
+        for (int l = layer0; l < layer0 + n && r == WISP_OK; ++l) {
+            for (int t = 0; t < T; ++t)
+                wisp_gpu_rmsnorm(x + (size_t)t * e->H, e->L[l].post_norm, xn + (size_t)t * e->H,
+                                 e->H, e->eps, s);
+            r = moe_forward_impl(e, l, xn, f, T, s, err);
+            if (r == WISP_OK) wisp_gpu_residual_add(x, f, T * e->H, s);
+        }
+        cudaFreeAsync(xn, s);
+        cudaFreeAsync(f, s);
+    }
+    std::lock_guard<std::mutex> g(e->stats_mu);
+    e->tok_ns[e->tok_head] = now_ns();
+    e->tok_head = (e->tok_head + 1) % 32;
+    if (e->tok_count < 32) e->tok_count++;
+    return r;
+}
+
+extern "C" void wisp_cache_stats(WispEngine* e, uint64_t* v, uint64_t* r, uint64_t* s,
+                                 double* rate) {
+    uint64_t a, b, c;
+    {
+        std::lock_guard<std::mutex> g(e->stats_mu);
+        a = e->hits[0];
+        b = e->hits[1];
+        c = e->hits[2];
+    }
+    if (v) *v = a;
+    if (r) *r = b;
+    if (s) *s = c;
+    uint64_t tot = a + b + c;
+    if (rate) *rate = tot ? (double)(a + b) / (double)tot : 0.0;
+}
+
+extern "C" void wisp_cache_clear_all(WispEngine* e) {
+    std::lock_guard<std::mutex> g(e->fetch_mu);
+    cudaStreamSynchronize(e->compute);
+    e->vram.clear([&](const wb::Lru::Entry& v) {
+        set_table(e, v.layer, v.expert, nullptr, false);
+        e->arena.release(v.data);
+    });
+    e->ram.clear([](const wb::Lru::Entry& v) { cudaFreeHost(v.data); });
+    std::lock_guard<std::mutex> s(e->stats_mu);
+    e->hits[0] = e->hits[1] = e->hits[2] = 0;
+}
+
+extern "C" int wisp_ram_trim(WispEngine* e, int count) {
+    if (!e || count <= 0) return 0;
+    int freed = 0;
+    wb::Lru::Entry v;
+    while (freed < count && e->ram.evict(&v)) {
+        cudaFreeHost(v.data);
+        ++freed;
+    }
+    return freed;
+}
+
+extern "C" int wisp_drain_expert_log(WispEngine* e, uint32_t* out, int max_out,
+                                     uint64_t* dropped) {
+    if (!e || !out || max_out <= 0) return 0;
+    std::lock_guard<std::mutex> g(e->stats_mu);
+    int cap = (int)e->log.size();
+    int n = std::min(e->log_count, max_out);
+    int start = ((e->log_head - e->log_count) % cap + cap) % cap;
+    for (int i = 0; i < n; ++i) out[i] = e->log[(start + i) % cap];
+    if (dropped) *dropped = e->log_dropped;
+    e->log_count = 0;
+    e->log_head = 0;
+    e->log_dropped = 0;
+    return n;
+}
+
+extern "C" size_t wisp_vram_used(WispEngine* e) { return e ? (size_t)e->vram.used() : 0; }
+extern "C" size_t wisp_ram_used(WispEngine* e) { return e ? (size_t)e->ram.used() : 0; }
+
+extern "C" double wisp_tok_per_sec(WispEngine* e) {
+    std::lock_guard<std::mutex> g(e->stats_mu);
+    int n = e->tok_count;
+    if (n < 2) return 0.0;
+    int newest = (e->tok_head + 31) % 32, oldest = (e->tok_head + 32 - n) % 32;
+    uint64_t span = e->tok_ns[newest] - e->tok_ns[oldest];
+    return span ? (double)(n - 1) * 1e9 / (double)span : 0.0;
+}
+
+extern "C" const char* wisp_b200_version(void) { return "wisp_b200 0.1.0 sm_100a"; }

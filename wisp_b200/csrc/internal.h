@@ -1,0 +1,55 @@
+// internal.h -- shared helpers of the wisp_b200 sources (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "wisp_b200.h"
+
+#define WB_SET_ERR(ctx, c, ...)                                   \
+    do {                                                          \
+        if (ctx) {                                                \
+            (ctx)->code = (c);                                    \
+            snprintf((ctx)->message, sizeof((ctx)->message),      \
+                     __VA_ARGS__);                                \
+            (ctx)->file = __FILE__;                               \
+            (ctx)->line = __LINE__;                               \
+        }                                                         \
+    } while (0)
+
+#define WB_CUDA_RET(call, ctx)                                            \
+    do {                                                                  \
+        cudaError_t _e = (call);                                          \
+        if (_e != cudaSuccess) {                                          \
+            WB_SET_ERR(ctx, WISP_ERR_CUDA, "CUDA error: %s (%s)",         \
+                       cudaGetErrorString(_e), #call);                    \
+            return WISP_ERR_CUDA;                                         \
+        }                                                                 \
+    } while (0)
+
+namespace wb {
+
+// Number of SMs of the current device (cached per device id).
+int sm_count();
+
+// Launch `kern` with programmatic dependent launch enabled, so its prologue
+// may overlap the tail of the previous kernel on `stream`; the kernel must
+// call griddepcontrol.wait before touching its predecessor's outputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block,
+                       size_t smem, cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+}  // namespace wb

@@ -1,0 +1,229 @@
+"""Device-resident MoE layers and stacks over the fused C ABI.
+
+``ExpertArena`` holds int4 expert blobs in the WISP ``.bin`` layout on the GPU, each
+at ``slot * slot_bytes + 8`` so its packed/scales/zeros sections start 16-byte
+aligned.  ``MoEStack`` owns per-layer routers, norm weights and the device table of
+blob pointers, and calls ``wisp_moe_block_forward`` / ``wisp_moe_stack_forward``
+on the caller's current CUDA stream.  torch is used for device memory and streams
+only; every kernel is in ``libwisp_b200.so``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import converter as cv
+from .lib import WispErrCtx, WispExpertMeta, WispMoeLayer, check, lib
+
+
+def _round_up(v: int, a: int) -> int:
+    return (v + a - 1) // a * a
+
+
+def blob_header(layer: int, expert: int, mats: dict[str, cv.QMat]) -> bytes:
+    ordered = [mats[m] for m in cv.MAT_ORDER]
+    h = cv.HEADER.pack(cv.EXPERT_MAGIC, cv.EXPERT_VERSION, layer, expert,
+                       ordered[0].group_size, 3)
+    return h + b"".join(cv.MAT_RECORD.pack(q.rows, q.cols, *q.section_bytes()) for q in ordered)
+
+
+def parse_meta(blob_head: bytes, total: int | None = None) -> WispExpertMeta:
+    """WispExpertMeta from a blob's first 120 bytes (via the library's parser)."""
+    m = WispExpertMeta()
+    err = WispErrCtx()
+    buf = C.create_string_buffer(bytes(blob_head), len(blob_head))
+    size = total if total is not None else len(blob_head)
+    if total is not None and total > len(blob_head):
+        # the parser checks the sections fit; give it the claimed size
+        big = C.create_string_buffer(total)
+        C.memmove(big, buf, len(blob_head))
+        buf = big
+    check(lib().wisp_expert_parse_header(buf, size, C.byref(m), C.byref(err)), err)
+    return m
+
+
+def blob_bytes_of(mats: dict[str, cv.QMat]) -> int:
+    return cv.HEADER_BYTES + sum(sum(q.section_bytes()) for q in mats.values())
+
+
+class ExpertArena:
+    """One device allocation of fixed-size expert slots (blob at slot + 8)."""
+
+    def __init__(self, n_slots: int, blob_bytes: int, device):
+        self.slot_bytes = _round_up(blob_bytes + 8, 256)
+        self.blob_bytes = blob_bytes
+        self.n = n_slots
+        self.buf = torch.empty(n_slots * self.slot_bytes, dtype=torch.uint8, device=device)
+
+    def blob(self, i: int) -> torch.Tensor:
+        o = i * self.slot_bytes + 8
+        return self.buf[o:o + self.blob_bytes]
+
+    def ptr(self, i: int) -> int:
+        return self.buf.data_ptr() + i * self.slot_bytes + 8
+
+    def write(self, i: int, layer: int, expert: int, mats: dict[str, cv.QMat]) -> None:
+        dst = self.blob(i)
+        head = blob_header(layer, expert, mats)
+        dst[:cv.HEADER_BYTES].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
+        off = cv.HEADER_BYTES
+        for name in cv.MAT_ORDER:
+            q = mats[name]
+            for t in (q.packed, q.scales.view(torch.uint8), q.zeros.view(torch.uint8)):
+                n = t.numel()
+                dst[off:off + n].copy_(t.reshape(-1), non_blocking=True)
+                off += n
+
+
+@dataclass
+class LayerWeights:
+    router: torch.Tensor          # fp16 [E, H]
+    router_bias: torch.Tensor | None
+    norm: torch.Tensor            # fp16 [H]
+    table: torch.Tensor           # int64 [E] device blob pointers
+    slots: list[int]
+    shared_slot: int | None = None
+
+
+class MoEStack:
+    """A seeded synthetic MoE stack resident on one GPU (see ``converter`` for the recipe)."""
+
+    def __init__(self, shape: cv.MoEShape, seed: int, device="cuda", zipf_s: float | None = None,
+                 random_bias: bool = False, n_layers: int | None = None, layer0: int = 0):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.L = n_layers or shape.n_layers
+        self.layer0 = layer0
+        E = shape.n_experts
+        probe = cv.make_expert(cv.MoEShape(shape.hidden, shape.inter, E, shape.top_k,
+                                           shape.group_size), 0, 0, seed, device=self.device)
+        self.blob_bytes = blob_bytes_of(probe)
+        n_slots = self.L * E + (self.L if shape.shared_inter else 0)
+        self.arena = ExpertArena(n_slots, self.blob_bytes, self.device)
+        self.layers: list[LayerWeights] = []
+        slot = 0
+        for li in range(self.L):
+            l = layer0 + li
+            slots = []
+            for e in range(E):
+                mats = cv.make_expert(shape, l, e, seed, device=self.device)
+                self.arena.write(slot, l, e, mats)
+                slots.append(slot)
+                slot += 1
+            sh = None
+            if shape.shared_inter:
+                self.arena.write(slot, l, 0xFFFF, cv.make_shared_expert(shape, l, seed, self.device))
+                sh = slot
+                slot += 1
+            router = cv.make_router(shape, l, seed, device=self.device)
+            bias = None
+            if zipf_s is not None:
+                bias = cv.zipf_router_bias(shape, zipf_s).to(self.device)
+            elif random_bias:
+                g = torch.Generator().manual_seed(seed + 3 + l)
+                bias = (torch.randn(E, generator=g) * 0.5).half().to(self.device)
+            table = torch.tensor([self.arena.ptr(s) for s in slots], dtype=torch.int64,
+                                 device=self.device)
+            self.layers.append(LayerWeights(router, bias, torch.ones(shape.hidden,
+                                                                     dtype=torch.float16,
+                                                                     device=self.device),
+                                            table, slots, sh))
+        torch.cuda.synchronize(self.device)
+        head = self.arena.blob(0)[:cv.HEADER_BYTES].cpu().numpy().tobytes()
+        self.meta = parse_meta(head, self.blob_bytes)
+        self._c_layers = (WispMoeLayer * self.L)()
+        for l, lw in enumerate(self.layers):
+            c = self._c_layers[l]
+            c.meta = self.meta
+            c.expert_blobs = lw.table.data_ptr()
+            c.router_w = lw.router.data_ptr()
+            c.router_bias = lw.router_bias.data_ptr() if lw.router_bias is not None else None
+            c.norm_w = lw.norm.data_ptr()
+            if lw.shared_slot is not None:
+                c.shared_blob = self.arena.ptr(lw.shared_slot)
+                c.shared_meta = self.meta
+            c.n_experts = E
+            c.top_k = shape.top_k
+        self._ws: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------
+    def layer_c(self, l: int) -> WispMoeLayer:
+        return self._c_layers[l]
+
+    def workspace_bytes(self, T: int, layers: int | None = None) -> int:
+        n = layers or self.L
+        return int(lib().wisp_moe_workspace_bytes(C.byref(self._c_layers), n, T))
+
+    def workspace(self, T: int) -> torch.Tensor:
+        need = self.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def block(self, l: int, x: torch.Tensor, y: torch.Tensor | None = None, routing: bool = False):
+        """y = MoE_l(x) on the current stream; x [T,H] fp32 on the device."""
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty_like(x)
+        idx = torch.empty((T, self.shape.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, self.shape.top_k), dtype=torch.float32, device=self.device)
+        ws = self.workspace(T)
+        err = WispErrCtx()
+        rc = lib().wisp_moe_block_forward(
+            C.byref(self._c_layers[l]), x.data_ptr(), y.data_ptr(), T, idx.data_ptr(),
+            w.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream,
+            C.byref(err))
+        check(rc, err)
+        return (y, idx, w) if routing else y
+
+    def stack(self, x: torch.Tensor, routing: bool = False, layers: int | None = None):
+        """x <- x + MoE_l(rmsnorm(x)) for every layer, in place, on the current stream."""
+        T = x.shape[0]
+        n = layers or self.L
+        idx = w = None
+        if routing:
+            idx = torch.empty((n, T, self.shape.top_k), dtype=torch.int32, device=self.device)
+            w = torch.empty((n, T, self.shape.top_k), dtype=torch.float32, device=self.device)
+        ws = self.workspace(T)
+        err = WispErrCtx()
+        rc = lib().wisp_moe_stack_forward(
+            C.byref(self._c_layers), n, self.shape.rms_eps, x.data_ptr(), T,
+            idx.data_ptr() if routing else None, w.data_ptr() if routing else None,
+            ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream, C.byref(err))
+        check(rc, err)
+        return (x, idx, w) if routing else x
+
+    def status(self) -> int:
+        if self._ws is None:
+            return 0
+        return int(lib().wisp_moe_status(self._ws.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream))
+
+    # ------------------------------------------------------------------ oracle views
+    def host_blobs(self, l: int) -> list[np.ndarray]:
+        return [self.arena.blob(s).cpu().numpy().copy() for s in self.layers[l].slots]
+
+    def host_router(self, l: int) -> tuple[np.ndarray, np.ndarray | None]:
+        lw = self.layers[l]
+        b = lw.router_bias.cpu().numpy().view(np.uint16) if lw.router_bias is not None else None
+        return lw.router.cpu().numpy().view(np.uint16), b
+
+    def active_bytes(self, idx: np.ndarray) -> int:
+        """Algorithmic bytes of one step given its routing [L?, T, k]: distinct experts'
+        int4 sections + router + activations, summed over layers."""
+        idx = np.asarray(idx).reshape(-1, *np.asarray(idx).shape[-2:]) if np.ndim(idx) == 3 \
+            else np.asarray(idx)[None]
+        per_expert = self.blob_bytes - cv.HEADER_BYTES
+        H, E = self.shape.hidden, self.shape.n_experts
+        total = 0
+        for li in idx:
+            T = li.shape[0]
+            distinct = len(np.unique(li[li >= 0]))
+            total += distinct * per_expert + E * H * 2 + T * H * (2 + 4)
+            if self.shape.shared_inter:
+                total += per_expert
+        return total
