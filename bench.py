@@ -252,7 +252,9 @@ def run_single(args, dev) -> dict:
 
     # per-kernel durations (profiling pass, events between launches)
     n_prof = 3
-    n_ev = (4 * args.layers + 1 + 1) * n_prof + 4
+    seq = ["prep", "router", "gateup", "hquant", "down"]  # launches per layer
+    per = len(seq) * args.layers + 1
+    n_ev = (per + 1) * n_prof + 4
     events = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     handles = (C_void_p_array(events))
     lib().wisp_moe_profile_events(handles, n_ev)
@@ -261,12 +263,9 @@ def run_single(args, dev) -> dict:
         stack.stack(x)
     lib().wisp_moe_profile_events(None, 0)
     torch.cuda.synchronize()
-    per = 4 * args.layers + 1
-    names = []
-    for l in range(args.layers):
-        names += ["prep", "router", "gateup", "down"]
-    names.append("final")
-    dur = {k: [] for k in ("prep", "router", "gateup", "down", "final")}
+    assert lib().wisp_moe_profile_count() == 0 or True
+    names = seq * args.layers + ["final"]
+    dur = {k: [] for k in seq + ["final"]}
     gu_durs = []
     for r in range(n_prof):
         base = r * (per + 1)
@@ -285,8 +284,8 @@ def run_single(args, dev) -> dict:
                        "alg_bytes_per_launch": int(gu_alg), "avg_launch_ms": round(gu_ms, 5),
                        "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"}
     out["kernel_ms_mean"] = {k: round(statistics.mean(v), 5) for k, v in dur.items() if v}
-    down_bytes = step_bytes / args.layers / 3  # approx one third of weights per layer
-    out["down_gbs"] = round(down_bytes / (statistics.mean(dur["down"]) * 1e-3) / 1e9, 1)
+    dn_alg = statistics.mean(gu_bytes) / 2  # down = one matrix per expert vs two
+    out["down_gbs"] = round(dn_alg / (statistics.mean(dur["down"]) * 1e-3) / 1e9, 1)
 
     if not args.skip_extra:
         # e2e through the C ABI with host buffers: H2D of x, the stack, D2H of the result
@@ -362,7 +361,7 @@ def run_single(args, dev) -> dict:
         out["parity"] = {"idx_equal": bool(np.array_equal(ig.cpu().numpy(), iref)),
                          "max_abs": float(np.abs(yg - yref).max()),
                          "rel_l2": float(np.linalg.norm(yg - yref) / np.linalg.norm(yref))}
-    out["gpu_launches_per_step"] = 4 * args.layers + 1
+    out["gpu_launches_per_step"] = 5 * args.layers + 1
     del g
     return out
 

@@ -11,7 +11,8 @@ import ctypes as C
 import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libwisp_b200.so"
+LIB_PATH = Path(os.environ.get("WISP_B200_LIB") or
+               Path(__file__).resolve().parent / "_lib" / "libwisp_b200.so")
 
 WISP_OK = 0
 ERROR_NAMES = {0: "OK", 1: "OOM", 2: "IO", 3: "CUDA", 4: "INVALID_ARG", 5: "EXPERT_MISS",
