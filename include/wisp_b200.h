@@ -184,6 +184,21 @@ WispError wisp_moe_block_experts(const WispMoeLayer* layer, const float* x,
                                  size_t workspace_bytes, cudaStream_t stream,
                                  WispErrCtx* err);
 
+/* No counterpart in the reference.  wisp_moe_block_forward without a
+ * workspace argument, for callers that cannot allocate device memory: a host
+ * binding the library through a plain C FFI with no device allocator of its
+ * own, or a serving loop that reserved all device memory up front and must
+ * not allocate per step.  The block runs in a fixed 8 MiB device array inside
+ * the library (enough for a Mixtral-shaped layer up to T = 6); larger requests
+ * fail with WISP_ERR_INVALID_ARG before any GPU work.  Nothing is allocated.
+ * The first call on a device looks up the array's address; make that first
+ * call before any stream capture.  All calls on a device share the array:
+ * calls whose kernels overlap on the GPU race. */
+WispError wisp_moe_block_forward_static(const WispMoeLayer* layer,
+                                        const float* x, float* y, int T,
+                                        int* topk_idx, float* topk_w,
+                                        cudaStream_t stream, WispErrCtx* err);
+
 /* Stack of n_layers blocks: per layer l, x <- x + MoE_l(rmsnorm(x; norm_w_l,
  * eps)).  x [T,H] is updated in place.  topk_idx/topk_w optional, device
  * [n_layers, T, top_k].  Launch-only (capturable into a CUDA graph). */

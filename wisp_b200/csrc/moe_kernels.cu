@@ -1721,3 +1721,76 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
     hook_mark(stream);
     return WISP_OK;
 }
+
+// ------------------------------------------------------------------------
+// Fixed-scratch variant of wisp_moe_block_forward.
+//
+// Some callers cannot hand the library a device workspace: a host that binds
+// this library through a plain C FFI and owns no device allocator, or a
+// serving loop that reserved all device memory before it started and may not
+// allocate per step (a cudaMalloc there can fail under memory pressure in the
+// middle of a decode, and it synchronises the device).  For them the block
+// runs in a file-scope device array instead: no cudaMalloc, cudaFree or
+// allocating library routine is called.
+//
+// Limits: the array holds kStaticScratchBytes (8 MiB), enough for a
+// Mixtral-shaped layer (hidden 4096, intermediate 14336, top-2) up to T = 6;
+// larger requests are rejected with WISP_ERR_INVALID_ARG before any GPU work.
+// Every call on a device shares the one array, so two calls whose kernels
+// overlap on the GPU (different streams, or different host threads without
+// ordering) race and corrupt each other's results.  Each call clears the only
+// word that must start at zero (the status word, by cudaMemsetAsync on the
+// call's stream); the kernels reset their own counters.
+// ------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_block_scratch[kStaticScratchBytes];
+
+// Device address of the array on the current device, looked up once per device
+// (the first call on a device does this look-up).
+static void* block_scratch(WispErrCtx* err) {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess || dev < 0 || dev >= 64) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "moe_block_forward_static: no usable device (%s)",
+                   cudaGetErrorString(ce));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        ce = cudaGetSymbolAddress(&p, g_block_scratch);
+        if (ce != cudaSuccess || !p) {
+            WB_SET_ERR(err, WISP_ERR_CUDA,
+                       "moe_block_forward_static: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(ce));
+            return nullptr;
+        }
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+
+extern "C" WispError wisp_moe_block_forward_static(const WispMoeLayer* layer, const float* x,
+                                                   float* y, int T, int* topk_idx,
+                                                   float* topk_w, cudaStream_t stream,
+                                                   WispErrCtx* err) {
+    if (!layer) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_block_forward_static: NULL layer");
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (!check_layer(layer, T, err)) return WISP_ERR_INVALID_ARG;
+    const size_t need = wisp_moe_workspace_bytes(layer, 1, T);
+    if (need > kStaticScratchBytes) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "moe_block_forward_static: T=%d needs %zu bytes of scratch but the fixed "
+                   "scratch holds %zu; use wisp_moe_block_forward with a workspace",
+                   T, need, kStaticScratchBytes);
+        return WISP_ERR_INVALID_ARG;
+    }
+    void* ws = block_scratch(err);
+    if (!ws) return WISP_ERR_CUDA;
+    return wisp_moe_block_forward(layer, x, y, T, topk_idx, topk_w, ws, kStaticScratchBytes,
+                                  stream, err);
+}
