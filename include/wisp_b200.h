@@ -62,7 +62,8 @@ typedef struct {
 } WispErrCtx;
 
 /* Expert blob layout, parsed from the 120-byte .bin header
- * (reference: csrc/core/wisp_engine.h:241-251). */
+ * (reference: csrc/core/wisp_engine.h:241-251).  `tiled` is set for a blob in
+ * the device layout wisp_expert_tile writes (header version 2). */
 #define WISP_EXPERT_NMATS 3
 typedef struct {
     size_t packed_off[WISP_EXPERT_NMATS];
@@ -73,11 +74,25 @@ typedef struct {
     uint32_t group_size;
     size_t total_bytes;
     int valid;
+    int tiled;
 } WispExpertMeta;
 
-/* Replaces wisp_expert_parse_header (csrc/core/wisp_engine.c:268-303). */
+/* Replaces wisp_expert_parse_header (csrc/core/wisp_engine.c:268-303);
+ * also accepts version 2 (tiled) headers. */
 WispError wisp_expert_parse_header(const void* blob, size_t blob_size,
                                    WispExpertMeta* meta, WispErrCtx* err);
+
+/* New.  Rewrite a .bin expert blob (device memory, `meta` parsed from its
+ * header) into the tiled device layout the fused kernels stream, at dst_blob
+ * (device, not overlapping).  Each matrix keeps its place and size; inside it,
+ * every 8-row block is contiguous: for each quant group g, the g-th gs/2 code
+ * bytes of the block's 8 rows, then for each g the 8 rows' (scale, zero)
+ * fp16 pairs.  The header is copied with version 2.  Both blobs start at an
+ * address = 8 (mod 16); rows must be multiples of 8.  Asynchronous on
+ * `stream`. */
+WispError wisp_expert_tile(const WispExpertMeta* meta, const void* src_blob,
+                           void* dst_blob, cudaStream_t stream,
+                           WispErrCtx* err);
 
 /* ====================================================================== *
  * 1. Reference kernel-launcher ABI (identical signatures)
@@ -134,13 +149,12 @@ cudaError_t async_load_expert(const uint8_t* h_packed,
  * ====================================================================== */
 
 /* One MoE layer as the kernels see it.  All pointers are DEVICE pointers
- * except where noted.  Every expert blob of the layer has the same layout,
- * described by `meta` (host copy, parsed from any blob's header).  The
- * packed, scales and zeros sections of every blob must start 16-byte
- * aligned (true for a .bin blob placed at an address = 8 mod 16 when all
- * section sizes are multiples of 16; the engine's VRAM slots do this).
- * Shape limits: hidden and inter multiples of 32; group_size a multiple of
- * 32 that divides hidden and inter; rows multiples of 8. */
+ * except where noted.  Every expert blob of the layer is in the tiled device
+ * layout (wisp_expert_tile; meta.tiled set) and has the same shape, described
+ * by `meta` (host copy, parsed from any blob's header).  Blobs start at an
+ * address = 8 (mod 16), so every section is 16-byte aligned (the engine's
+ * VRAM slots do this).  Shape limits: hidden a multiple of 32 and at most
+ * 8192, inter a multiple of 32; group_size 32, 64 or 128 dividing both. */
 typedef struct {
     WispExpertMeta meta;               /* host copy                        */
     const void* const* expert_blobs;   /* device array [n_experts]         */
@@ -189,7 +203,7 @@ WispError wisp_moe_block_experts(const WispMoeLayer* layer, const float* x,
  * binding the library through a plain C FFI with no device allocator of its
  * own, or a serving loop that reserved all device memory up front and must
  * not allocate per step.  The block runs in a fixed 8 MiB device array inside
- * the library (enough for a Mixtral-shaped layer up to T = 6); larger requests
+ * the library (enough for a Mixtral-shaped layer up to T = 16); larger requests
  * fail with WISP_ERR_INVALID_ARG before any GPU work.  Nothing is allocated.
  * The first call on a device looks up the array's address; make that first
  * call before any stream capture.  All calls on a device share the array:
@@ -210,7 +224,9 @@ WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_layers,
 
 /* Device-side status word the kernels set instead of faulting (bit 0: a
  * weight section was not 16-byte aligned; bit 1: an expert index was out of
- * range; bit 2: a plan overflowed).  Synchronises `stream`. */
+ * range or its table entry NULL; bit 2: a plan overflowed; bit 3: a bounded
+ * wait timed out; bit 4: a blob was not in the tiled layout).  Synchronises
+ * `stream`. */
 int wisp_moe_status(const void* workspace, cudaStream_t stream);
 
 /* Profiling hook (new): while `events` is set, the calling thread's

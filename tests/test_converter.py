@@ -96,3 +96,28 @@ def test_quantizer_same_bits_on_any_device_layout():
     a = cv.quantize_int4(w.t().contiguous().t(), 64)
     b = cv.quantize_int4(w.clone(), 64)
     assert torch.equal(a.packed, b.packed) and torch.equal(a.scales, b.scales)
+
+
+@pytest.mark.parametrize("H,I,gs", [(128, 256, 64), (192, 96, 32), (512, 256, 128), (4096, 64, 64)])
+def test_tiled_layout_round_trip(H, I, gs):
+    """The tiled device layout is a pure permutation of each matrix region: untile
+    restores the .bin bytes exactly; block b of a matrix holds, for group g, the
+    gs/2 code bytes of rows 8b..8b+7 in order, then their (scale, zero) pairs."""
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=2, top_k=1, group_size=gs)
+    b = cv.expert_blob(0, 1, cv.make_expert(shape, 0, 1, 9))
+    raw = np.frombuffer(b, dtype=np.uint8)
+    t = cv.tile_blob(b)
+    assert len(t) == len(raw) and cv.parse_blob_header(t.tobytes())["tiled"]
+    assert np.array_equal(cv.untile_blob(t), raw)
+    h = cv.parse_blob_header(b)
+    for m in h["mats"]:
+        R, Cc, G = m["rows"], m["cols"], m["cols"] // gs
+        bb = 4 * Cc + 32 * G
+        for (blk, g, j) in [(0, 0, 0), (R // 8 - 1, G - 1, 7), (R // 16, G // 2, 3)]:
+            row = 8 * blk + j
+            src = raw[m["packed_off"] + row * Cc // 2 + g * gs // 2:][:gs // 2]
+            dst = t[m["packed_off"] + blk * bb + (g * 8 + j) * gs // 2:][:gs // 2]
+            assert np.array_equal(src, dst)
+            sz = t[m["packed_off"] + blk * bb + 4 * Cc + (g * 8 + j) * 4:][:4]
+            assert np.array_equal(sz[:2], raw[m["scales_off"] + 2 * (row * G + g):][:2])
+            assert np.array_equal(sz[2:], raw[m["zeros_off"] + 2 * (row * G + g):][:2])

@@ -118,3 +118,49 @@ def test_mixtral_block_matches_oracle(cuda, T):
     nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
     if nd == 0:
         check_outputs(y.cpu().numpy(), yr)
+
+
+@pytest.mark.parametrize("H,I,gs", [(128, 256, 64), (192, 96, 32), (512, 256, 128),
+                                    (4096, 14336, 64)])
+def test_device_tiling_matches_numpy_restatement(cuda, H, I, gs):
+    """wisp_expert_tile on the device is bit-identical to converter.tile_blob."""
+    import ctypes as C
+    from wisp_b200.lib import WispErrCtx, check, lib
+    from wisp_b200.moe import parse_meta
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=2, top_k=1, group_size=gs)
+    b = cv.expert_blob(3, 1, cv.make_expert(shape, 3, 1, 21, device=cuda))
+    n = len(b)
+    src = torch.zeros(n + 264, dtype=torch.uint8, device=cuda)
+    dst = torch.zeros(n + 264, dtype=torch.uint8, device=cuda)
+    src[8:8 + n].copy_(torch.frombuffer(bytearray(b), dtype=torch.uint8))
+    meta = parse_meta(b[:cv.HEADER_BYTES], n)
+    assert not meta.tiled
+    err = WispErrCtx()
+    check(lib().wisp_expert_tile(C.byref(meta), src.data_ptr() + 8, dst.data_ptr() + 8,
+                                 torch.cuda.current_stream().cuda_stream, C.byref(err)), err)
+    torch.cuda.synchronize()
+    got = dst[8:8 + n].cpu().numpy()
+    assert np.array_equal(got, cv.tile_blob(b))
+
+
+def test_untiled_blobs_are_refused_on_the_device(cuda):
+    """A table entry that is a .bin blob (header version 1) while the layer claims
+    the tiled layout: the kernels check each blob's version word before streaming,
+    set status bit 4 and skip the expert instead of reading it."""
+    shape = cv.MoEShape(hidden=256, inter=512, n_experts=4, top_k=2)
+    st = MoEStack(shape, seed=3, device=cuda)
+    blob = cv.expert_blob(0, 0, cv.make_expert(shape, 0, 0, 3))
+    raw = torch.zeros(len(blob) + 264, dtype=torch.uint8, device=cuda)
+    raw[8:8 + len(blob)].copy_(torch.frombuffer(bytearray(blob), dtype=torch.uint8))
+    table = st.layers[0].table.clone()
+    st.layers[0].table[:] = raw.data_ptr() + 8   # every expert now points at the .bin blob
+    try:
+        x = cv.make_input(shape, 2, 1).to(cuda)
+        st.block(0, x)
+        torch.cuda.synchronize()
+        assert st.status() & 16
+    finally:
+        st.layers[0].table.copy_(table)
+    st.block(0, x)
+    torch.cuda.synchronize()
+    assert st.status() == 0

@@ -63,7 +63,7 @@ def test_static_rejects_requests_beyond_the_array(built_lib):
     shape = cv.MoEShape(hidden=4096, inter=14336, n_experts=8, top_k=2)
     from wisp_b200.moe import parse_meta
     dims = [(14336, 4096), (14336, 4096), (4096, 14336)]
-    head = cv.HEADER.pack(cv.EXPERT_MAGIC, cv.EXPERT_VERSION, 0, 0, 64, 3) + b"".join(
+    head = cv.HEADER.pack(cv.EXPERT_MAGIC, cv.TILED_VERSION, 0, 0, 64, 3) + b"".join(
         cv.MAT_RECORD.pack(r, c, r * c // 2, r * c // 32, r * c // 32) for r, c in dims)
     total = cv.HEADER_BYTES + sum(r * c // 2 + r * c // 16 for r, c in dims)
     meta = parse_meta(head, total)

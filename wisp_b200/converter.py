@@ -32,6 +32,7 @@ import struct
 from dataclasses import dataclass
 from pathlib import Path
 
+import numpy as np
 import torch
 
 EXPERT_MAGIC = 0x57455850
@@ -112,7 +113,7 @@ def parse_blob_header(blob: bytes | memoryview) -> dict:
     if len(blob) < HEADER_BYTES:
         raise ValueError(f"expert blob too small: {len(blob)} bytes")
     magic, ver, layer, expert, gs, nm = HEADER.unpack_from(blob, 0)
-    if magic != EXPERT_MAGIC or ver != EXPERT_VERSION or nm != 3:
+    if magic != EXPERT_MAGIC or ver not in (EXPERT_VERSION, TILED_VERSION) or nm != 3:
         raise ValueError(f"expert blob corrupt: magic={magic:08x} version={ver} n_mats={nm}")
     off = HEADER_BYTES
     mats = []
@@ -123,7 +124,61 @@ def parse_blob_header(blob: bytes | memoryview) -> dict:
         off += pb + sb + zb
     if off > len(blob):
         raise ValueError(f"expert blob truncated: needs {off}, have {len(blob)}")
-    return dict(layer=layer, expert=expert, group_size=gs, mats=mats, total_bytes=off)
+    return dict(layer=layer, expert=expert, group_size=gs, mats=mats, total_bytes=off,
+                tiled=ver == TILED_VERSION)
+
+
+# --------------------------------------------------------------------------------------
+# Tiled device layout (version 2): the order the CUDA kernels stream.  Each matrix keeps
+# its region; inside it every 8-row block is contiguous: for each quant group g the
+# gs/2 code bytes of the block's 8 rows, then for each g the 8 rows' (scale, zero) fp16
+# pairs.  These numpy restatements are the test-side checkers of wisp_expert_tile.
+# --------------------------------------------------------------------------------------
+TILED_VERSION = 2
+
+
+def _tile_matrix(region: np.ndarray, rows: int, cols: int, gs: int) -> np.ndarray:
+    G = cols // gs
+    pb, sb = rows * cols // 2, rows * G * 2
+    codes = region[:pb].reshape(rows // 8, 8, G, gs // 2).transpose(0, 2, 1, 3)
+    sc = region[pb:pb + sb].view(np.uint16).reshape(rows // 8, 8, G)
+    ze = region[pb + sb:pb + 2 * sb].view(np.uint16).reshape(rows // 8, 8, G)
+    sz = np.stack([sc, ze], axis=-1).transpose(0, 2, 1, 3)  # [block][g][row][s, z]
+    blocks = np.concatenate([codes.reshape(rows // 8, -1),
+                             np.ascontiguousarray(sz).view(np.uint8).reshape(rows // 8, -1)],
+                            axis=1)
+    return blocks.reshape(-1)
+
+
+def _untile_matrix(region: np.ndarray, rows: int, cols: int, gs: int) -> np.ndarray:
+    G = cols // gs
+    blocks = region.reshape(rows // 8, 4 * cols + 32 * G)
+    codes = blocks[:, :4 * cols].reshape(rows // 8, G, 8, gs // 2).transpose(0, 2, 1, 3)
+    sz = np.ascontiguousarray(blocks[:, 4 * cols:]).view(np.uint16).reshape(rows // 8, G, 8, 2)
+    sc = sz[..., 0].transpose(0, 2, 1)
+    ze = sz[..., 1].transpose(0, 2, 1)
+    return np.concatenate([codes.reshape(-1), np.ascontiguousarray(sc).view(np.uint8).reshape(-1),
+                           np.ascontiguousarray(ze).view(np.uint8).reshape(-1)])
+
+
+def _retile(blob, fn, version: int) -> np.ndarray:
+    b = np.frombuffer(bytes(blob), dtype=np.uint8).copy()
+    h = parse_blob_header(b.tobytes()[:HEADER_BYTES] + b"\0" * (len(b) - HEADER_BYTES))
+    for m in h["mats"]:
+        lo, hi = m["packed_off"], m["zeros_off"] + m["zeros_bytes"]
+        b[lo:hi] = fn(b[lo:hi], m["rows"], m["cols"], h["group_size"])
+    b[4:8] = np.frombuffer(struct.pack("<I", version), dtype=np.uint8)
+    return b
+
+
+def tile_blob(blob) -> np.ndarray:
+    """A ``.bin`` blob rewritten into the tiled device layout (header version 2)."""
+    return _retile(blob, _tile_matrix, TILED_VERSION)
+
+
+def untile_blob(blob) -> np.ndarray:
+    """The ``.bin`` blob a tiled blob was made from."""
+    return _retile(blob, _untile_matrix, EXPERT_VERSION)
 
 
 def expert_filename(layer: int, expert: int) -> str:

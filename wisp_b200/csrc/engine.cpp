@@ -177,6 +177,7 @@ struct WispEngine {
     std::vector<void*> ring;
     int ring_pos = 0;
     void* staging = nullptr;  // pinned SSD staging (one expert)
+    char* d_stage = nullptr;  // device staging slot: .bin blobs are tiled from here
     std::mutex fetch_mu;
     // workspace of the fused kernels
     void* ws = nullptr;
@@ -271,17 +272,34 @@ void ram_put(WispEngine* e, uint32_t layer, uint32_t expert, void* data, size_t 
     e->ram.put(layer, expert, data, n);
 }
 
-// H2D copy into a ring slot (cool experts: no cache insert, no eviction).
+// Host blob -> device slot in the tiled layout the kernels stream, on the
+// transfer stream (synchronised before returning).  A .bin blob is copied to
+// the device staging slot and tiled into `dst`; a blob that is already tiled
+// (a VRAM victim written back to the RAM tier) is copied as is.
+bool put_tiled(WispEngine* e, void* dst, const void* src, size_t n, WispErrCtx* err) {
+    WispExpertMeta m{};
+    if (wisp_expert_parse_header(src, n, &m, err) != WISP_OK) return false;
+    cudaError_t ce;
+    if (m.tiled) {
+        ce = cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, e->transfer);
+    } else {
+        ce = cudaMemcpyAsync(e->d_stage, src, n, cudaMemcpyHostToDevice, e->transfer);
+        if (ce == cudaSuccess && wisp_expert_tile(&m, e->d_stage, dst, e->transfer, err) != WISP_OK)
+            return false;
+    }
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "expert upload failed: %s", cudaGetErrorString(ce));
+        return false;
+    }
+    return true;
+}
+
+// Upload into a ring slot (cool experts: no cache insert, no eviction).
 void* scratch_serve(WispEngine* e, const void* src, size_t n, WispErrCtx* err) {
     void* slot = e->ring[e->ring_pos];
     e->ring_pos = (e->ring_pos + 1) % (int)e->ring.size();
-    cudaError_t ce = cudaMemcpyAsync(slot, src, n, cudaMemcpyHostToDevice, e->transfer);
-    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
-    if (ce != cudaSuccess) {
-        WB_SET_ERR(err, WISP_ERR_CUDA, "scratch H2D failed: %s", cudaGetErrorString(ce));
-        return nullptr;
-    }
-    return slot;
+    return put_tiled(e, slot, src, n, err) ? slot : nullptr;
 }
 
 // A VRAM slot, evicting the VRAM LRU (copied back to the RAM tier) until
@@ -362,13 +380,8 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
             if (p) set_table(e, layer, expert, p, false);
             return p;
         }
-        cudaError_t ce = cudaMemcpyAsync(slot, ent.data, ent.bytes, cudaMemcpyHostToDevice,
-                                         e->transfer);
-        if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
-        if (ce != cudaSuccess) {
+        if (!put_tiled(e, slot, ent.data, ent.bytes, err)) {
             e->arena.release(slot);
-            WB_SET_ERR(err, WISP_ERR_CUDA, "RAM->VRAM promote failed: %s",
-                       cudaGetErrorString(ce));
             return nullptr;
         }
         e->vram.put(layer, expert, slot, ent.bytes);
@@ -392,11 +405,8 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
         if (p) set_table(e, layer, expert, p, false);
         return p;
     }
-    cudaError_t ce = cudaMemcpyAsync(slot, e->staging, n, cudaMemcpyHostToDevice, e->transfer);
-    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
-    if (ce != cudaSuccess) {
+    if (!put_tiled(e, slot, e->staging, n, err)) {
         e->arena.release(slot);
-        WB_SET_ERR(err, WISP_ERR_CUDA, "expert H2D failed: %s", cudaGetErrorString(ce));
         return nullptr;
     }
     e->vram.put(layer, expert, slot, n);
@@ -475,6 +485,7 @@ WispError ensure_ws(WispEngine* e, const std::vector<WispMoeLayer>& layers, int 
 WispMoeLayer layer_desc(WispEngine* e, int l) {
     WispMoeLayer d{};
     d.meta = e->meta[l];
+    d.meta.tiled = 1;  // device copies are tiled (put_tiled)
     d.expert_blobs = const_cast<const void* const*>(e->L[l].d_table);
     d.router_w = e->L[l].router;
     d.router_bias = e->L[l].router_bias;
@@ -502,7 +513,8 @@ WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
     char* base = nullptr;
     WB_CUDA_RET(cudaMalloc(&base, blob.size() + 264), err);
     void* dst = base + 8;
-    WB_CUDA_RET(cudaMemcpy(dst, blob.data(), blob.size(), cudaMemcpyHostToDevice), err);
+    if (!put_tiled(e, dst, blob.data(), blob.size(), err)) return WISP_ERR_CUDA;
+    m.tiled = 1;
     e->L[l].shared_blob = dst;
     e->L[l].shared_meta = m;
     return WISP_OK;
@@ -524,7 +536,7 @@ extern "C" WispError wisp_expert_parse_header(const void* blob, size_t blob_size
     }
     uint32_t h[6];
     memcpy(h, blob, sizeof h);
-    if (h[0] != kMagic || h[1] != 1u || h[5] != 3u) {
+    if (h[0] != kMagic || (h[1] != 1u && h[1] != 2u) || h[5] != 3u) {
         WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob corrupt: magic=%08x version=%u n_mats=%u",
                    h[0], h[1], h[5]);
         return WISP_ERR_MODEL;
@@ -548,6 +560,7 @@ extern "C" WispError wisp_expert_parse_header(const void* blob, size_t blob_size
     meta->group_size = h[4];
     meta->total_bytes = off;
     meta->valid = 1;
+    meta->tiled = h[1] == 2u ? 1 : 0;
     if (off > blob_size) {
         WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob truncated: needs %zu, have %zu", off,
                    blob_size);
@@ -632,6 +645,8 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
     ce = cudaStreamCreateWithFlags(&e->compute, cudaStreamNonBlocking);
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->transfer, cudaStreamNonBlocking);
     if (ce == cudaSuccess) ce = cudaHostAlloc(&e->staging, e->max_expert_bytes, 0);
+    if (ce == cudaSuccess) ce = cudaMalloc(&e->d_stage, e->max_expert_bytes + 264);
+    if (ce == cudaSuccess) e->d_stage += 8;  // blob at 8 (mod 16), like every slot
     if (ce != cudaSuccess) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "stream/staging setup: %s", cudaGetErrorString(ce));
         wisp_engine_destroy(e.release());
@@ -713,6 +728,7 @@ extern "C" void wisp_engine_destroy(WispEngine* e) {
     }
     if (e->ws) cudaFree(e->ws);
     if (e->staging) cudaFreeHost(e->staging);
+    if (e->d_stage) cudaFree(e->d_stage - 8);
     if (e->compute) cudaStreamDestroy(e->compute);
     if (e->transfer) cudaStreamDestroy(e->transfer);
     delete e;
@@ -773,11 +789,9 @@ extern "C" int wisp_engine_pin_experts(WispEngine* e, int layer0, int n, WispErr
             if (e->vram.would_overflow(bytes)) return resident;
             void* slot = e->arena.alloc();
             if (!slot) return resident;
-            if (cudaMemcpyAsync(slot, host, bytes, cudaMemcpyHostToDevice, e->transfer) !=
-                    cudaSuccess ||
-                cudaStreamSynchronize(e->transfer) != cudaSuccess) {
+            if (!put_tiled(e, slot, host, bytes, &le)) {
                 e->arena.release(slot);
-                WB_SET_ERR(err, WISP_ERR_CUDA, "pin H2D failed");
+                if (err) *err = le;
                 return resident;
             }
             e->vram.put(l, x, slot, bytes);

@@ -56,17 +56,18 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaxPlanAssign = 4096;  // T*k limit of the device plan builder
-constexpr int kMaxKp = 32;            // max K parts of the down projection
+constexpr int kMaxKp = 8;             // max K parts of the down projection
 
-enum { C_GU_TASK = 0, C_TOK_DONE = 2, C_NTILES = 3, C_DN_BASE = 8 };
-constexpr int kCounters = C_DN_BASE + kMaxKp;  // gate/up units, tokens, tiles, down units per part
-enum { ST_ALIGN = 1, ST_EXPERT = 2, ST_PLAN = 4, ST_TIMEOUT = 8 };
+enum { C_TOK_DONE = 0, C_NTILES = 1 };
+constexpr int kCounters = 8;          // router CTAs done, tiles of the plan
+enum { ST_ALIGN = 1, ST_EXPERT = 2, ST_PLAN = 4, ST_TIMEOUT = 8, ST_LAYOUT = 16 };
 
 struct Tile {
     int expert;  // 0..E-1, or E for the shared expert
     int m;       // tokens in the tile (1..kMT)
     int tok[kMT];
     int asg[kMT];  // assignment ids: t*K + j, or T*K + t for the shared expert
+    const unsigned char* blob;  // the expert's tiled blob, NULL if unusable (status set)
 };
 
 struct MatOff {
@@ -97,10 +98,10 @@ struct Ws {
     Tile* tiles;
     float* xn;
     uint4* xq;      // [T][H/32][4]  activation digits
-    float2* xqp;    // [T][H/gs]     (k/254, sum of quantised x) per group
+    float4* xqp;    // [T][H/gs]     (k/254, sum of quantised x, 0, 0) per group
     float* h;       // [A][I]
     uint4* hq;      // [A][I/32][4]
-    float2* hqp;    // [A][I/gs]
+    float4* hqp;    // [A][I/gs]
     int* hcnt;      // unused
     float* ypart;   // [kp][A][H]
     int A;          // assignment capacity
@@ -139,7 +140,7 @@ __device__ __forceinline__ bool aligned16(const void* p) {
 // the odd elements, words [8+2w] / [8+2w+1] the same for the b-digits (so one
 // 64-bit load gives an MMA B fragment).
 __device__ __forceinline__ void quantize_block(const float4 v, int lpb, uint32_t* chunk_words,
-                                               float2* block_param, bool block_leader) {
+                                               float4* block_param, bool block_leader) {
     const int lane = threadIdx.x & 31, q = lane & 7;
     float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     for (int o = 1; o < lpb; o <<= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
@@ -174,14 +175,15 @@ __device__ __forceinline__ void quantize_block(const float4 v, int lpb, uint32_t
         reinterpret_cast<uint2*>(chunk_words)[4 + w] =
             make_uint2(be | (be2 << 16), bo | (bo2 << 16));
     }
-    if (block_leader) *block_param = make_float2(k2, fmaf(k, (float)sa, k2 * (float)sb));
+    if (block_leader)
+        *block_param = make_float4(k2, fmaf(k, (float)sa, k2 * (float)sb), 0.f, 0.f);
 }
 
 // Quantise the n-element row `src` (n % gs == 0) with one warp per 128
 // elements; warps and lanes past the end redo the last block (same data).
 // `warp_id`/`n_warps` index the warps taking part.
 __device__ __forceinline__ void quantize_row(const float4* src, int n, int gs, int warp_id,
-                                             int n_warps, uint4* xq, float2* xqp) {
+                                             int n_warps, uint4* xq, float4* xqp) {
     const int lane = threadIdx.x & 31;
     const int lpb = gs / 4;
     const int nblk = n / gs;
@@ -367,6 +369,27 @@ __device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, int ns
     }
 }
 
+// The tiled blob of expert e (E = the shared expert), or NULL with the status
+// flagged: ST_EXPERT for an index out of range or a NULL table entry,
+// ST_LAYOUT for a blob whose header is not the tiled layout's (version 2).
+constexpr uint32_t kTiledVersion = 2;
+__device__ const unsigned char* checked_blob(const LayerArgs& L, const Ws& W, int e) {
+    const void* b = nullptr;
+    if (e == L.E)
+        b = L.shared_blob;
+    else if (e >= 0 && e < L.E)
+        b = L.blobs[e];
+    if (!b) {
+        atomicOr(W.status, ST_EXPERT);
+        return nullptr;
+    }
+    if (__ldg(reinterpret_cast<const uint32_t*>(b) + 1) != kTiledVersion) {
+        atomicOr(W.status, ST_LAYOUT);
+        return nullptr;
+    }
+    return static_cast<const unsigned char*>(b);
+}
+
 __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
                            int* s_idx, int* s_cnt) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -423,6 +446,7 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
         if (e >= E || my_tiles[r] == 0) continue;
         Tile tl;
         tl.expert = e;
+        tl.blob = checked_blob(L, W, e);
         tl.m = 0;
         int ti = base;
         for (int a = 0; a < NA; ++a) {
@@ -440,6 +464,7 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
     for (int s = tid; s < shared_tiles; s += kThreads) {
         Tile tl;
         tl.expert = E;
+        tl.blob = checked_blob(L, W, E);
         tl.m = 0;
         for (int t = s * mt; t < T && tl.m < mt; ++t) {
             tl.tok[tl.m] = t;
@@ -450,8 +475,19 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
     }
     if (tid == 0) {
         W.counters[C_NTILES] = total;
-        W.counters[C_GU_TASK] = 0;
-        for (int p = 0; p < kMaxKp; ++p) W.counters[C_DN_BASE + p] = 0;
+    }
+}
+
+// Re-read every tile's blob pointer from the expert table (for a plan built
+// before the table was filled: the host-driven miss path).
+__global__ void __launch_bounds__(kThreads)
+resolve_kernel(LayerArgs L, Ws W) {
+    pdl_wait();
+    pdl_launch();
+    const int n = __ldcg(W.counters + C_NTILES);
+    for (int t = threadIdx.x; t < n; t += kThreads) {
+        const int e = __ldcg(&W.tiles[t].expert);
+        W.tiles[t].blob = checked_blob(L, W, e);
     }
 }
 
@@ -524,13 +560,17 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
 // ------------------------------------------------------------------------
 // TMA-staged weight streaming (shared by gate/up and down)
 //
-// One CTA = 1 producer warp + the consumer warps.  The producer takes
-// units (tile, block of 8 rows[, K part]) from an atomic counter and issues
-// cp.async.bulk global->shared copies of the unit's packed rows and fp16
-// scales/zeros into a ring of shared-memory stages, each guarded by a "full"
+// Experts are in the tiled device layout (expert_layout.cu): every 8-row
+// block of a matrix is contiguous, codes ordered [group][row] and then the
+// (scale, zero) pairs [group][row].  A unit is two 8-row blocks (MMA rows 0-7
+// and 8-15) over a K range of ng quant groups: gate/up = gate block b + up
+// block b over all of H; down = blocks 2j, 2j+1 over one K part.  One CTA per
+// SM = 1 producer warp + kNcw consumer warps.  The producer walks the CTA's
+// units (static round robin: unit = CTA + k * CTAs, so no atomics) and issues
+// four cp.async.bulk copies per unit (codes and scale/zero pairs of each
+// block) into a ring of shared-memory stages, each guarded by a "full"
 // mbarrier (transaction bytes) and an "empty" mbarrier (one arrival per
-// consumer warp).  Consumer warp w computes row 8*rb + w of the unit from
-// shared memory.  Every wait is bounded by %globaltimer: on timeout the warp
+// consumer warp).  Every wait is bounded by %globaltimer: on timeout the warp
 // sets ST_TIMEOUT in the status word and leaves, and the producer drains the
 // copies it issued (bounded too) before the CTA exits.
 // ------------------------------------------------------------------------
@@ -578,8 +618,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         if (gtimer() - t0 > kWaitNs) return false;
     return true;
 }
+// Weights are read exactly once per kernel: their copies carry an L2
+// evict-first policy so that streaming them does not push the small
+// activation and partial-sum buffers the kernels share out of L2.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
+                                         uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Plain bulk copy (activations: small, re-read by every CTA, left to the
+// default L2 policy).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes,
+                                               uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
             "r"(smem_addr(dst)),
@@ -587,36 +646,110 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-// One bulk copy request of a unit: up to 48 per unit (gate/up: 6; down with a
-// K split: 3 per row).
-struct Copy {
-    const void* src;
-    uint32_t dst_off, bytes;
-};
+// A streaming CTA: warp 0 = producer (lane 0), warp 1 = reducer, warps
+// 2 .. kNcw+1 = tensor-core consumers.
+constexpr int kNcw = 8;                           // consumer warps per CTA
+constexpr int kStreamCta = 32 * (kNcw + 2);
+constexpr int kMaxWarpK = 1024;                   // K elements per consumer warp
+constexpr int kMaxPartK = kNcw * kMaxWarpK;       // K elements per unit
+constexpr int kSkip = 0x40000000;                 // unit flag: weights unusable, contribute 0
 
-__host__ __device__ constexpr size_t ring_extra_bytes(int stages) {
-    return (size_t)stages * 20 + 64;  // full + empty barriers, unit ids, slack
+// Geometry of a unit's stage: block A (MMA rows 0-7) at 0, block B (rows
+// 8-15) at bbytes; each block = codes [ng][8][gs/2] then pairs [ng][8].
+struct Geo {
+    int ng;           // quant groups in the K range
+    uint32_t pbytes;  // code bytes of one block's range = ng * 4 * gs
+    uint32_t bbytes;  // pbytes + ng * 32
+};
+__host__ __device__ inline Geo make_geo(int ng, int gs) {
+    Geo g;
+    g.ng = ng;
+    g.pbytes = (uint32_t)ng * 4u * (uint32_t)gs;
+    g.bbytes = g.pbytes + (uint32_t)ng * 32u;
+    return g;
+}
+__host__ __device__ inline uint32_t stage_bytes_of(const Geo& g) {
+    return (2 * g.bbytes + 127) / 128 * 128;
+}
+// Bytes of one 8-row block of a [rows, cols] matrix in the tiled layout.
+__host__ __device__ inline size_t block_bytes_of(int cols, int gs) {
+    return 4 * (size_t)cols + 32 * (size_t)(cols / gs);
+}
+// Activation tile of a K range of ng groups (NPG chunks each) for kMT token
+// slots: the quantised words [slot][chunk][64 B], then (k/254, S) per group
+// [slot][group][16 B].
+__host__ __device__ inline uint32_t act_row_bytes(int ng, int npg) { return (uint32_t)ng * npg * 64u; }
+__host__ __device__ inline uint32_t act_bytes_of(int ng, int npg) {
+    return kMT * (act_row_bytes(ng, npg) + (uint32_t)ng * 16u);
 }
 
-struct StreamSmem {
-    uint8_t* stages;
-    uint64_t* full;
-    uint64_t* empty;
-    int* unit;
-    uint32_t stage_bytes;
-    int n_stages;
+// Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
+// the end; the tile's token count and assignment ids (for the reducer).
+struct UnitInfo {
+    int u, m;
+    int asg[kMT];
 };
 
+// Shared memory of a streaming CTA.
+struct StreamSmem {
+    uint8_t* stages;   // [n_stages][stage_bytes]
+    float2* red;       // [n_stages][kNcw][32] consumer partials
+    uint8_t* act;      // activation tile (act_bytes_of)
+    float2* kp;        // [kNcw][NGmax][kMT] (k/254, S) of each warp's groups
+    UnitInfo* info;    // [n_stages]
+    uint64_t* full;    // [n_stages] weights landed (tx)
+    uint64_t* red_bar; // [n_stages] consumer partials written (kNcw arrivals)
+    uint64_t* empty;   // [n_stages] stage reusable (reducer)
+    uint64_t* act_full;
+    uint64_t* act_empty;
+    uint32_t stage_bytes, act_row, act_bytes;
+    int n_stages;
+};
+__host__ __device__ constexpr size_t red_bytes_per_stage() { return (size_t)kNcw * 32 * 8; }
+constexpr size_t kKpBytes = (size_t)(kMaxPartK / 32) * 4 * 8;  // all groups x 4 slots
+__host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage_bytes,
+                                                     uint32_t act_bytes) {
+    return (size_t)n_stages * (stage_bytes + red_bytes_per_stage() + sizeof(UnitInfo) + 24) +
+           act_bytes + kKpBytes + 16 + 128;
+}
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
-                                                  uint32_t stage_bytes) {
+                                                  uint32_t stage_bytes, const Geo& geo, int npg) {
     StreamSmem s;
-    s.stages = base;
-    s.full = reinterpret_cast<uint64_t*>(base + (size_t)n_stages * stage_bytes);
-    s.empty = s.full + n_stages;
-    s.unit = reinterpret_cast<int*>(s.empty + n_stages);
     s.stage_bytes = stage_bytes;
     s.n_stages = n_stages;
+    s.act_row = act_row_bytes(geo.ng, npg);
+    s.act_bytes = act_bytes_of(geo.ng, npg);
+    size_t o = 0;
+    s.stages = base;
+    o += (size_t)n_stages * stage_bytes;
+    s.act = base + o;
+    o += (s.act_bytes + 127) / 128 * 128;
+    s.red = reinterpret_cast<float2*>(base + o);
+    o += (size_t)n_stages * red_bytes_per_stage();
+    s.kp = reinterpret_cast<float2*>(base + o);
+    o += kKpBytes;
+    s.info = reinterpret_cast<UnitInfo*>(base + o);
+    o += (size_t)n_stages * sizeof(UnitInfo);
+    o = (o + 7) & ~size_t(7);
+    s.full = reinterpret_cast<uint64_t*>(base + o);
+    s.red_bar = s.full + n_stages;
+    s.empty = s.red_bar + n_stages;
+    s.act_full = s.empty + n_stages;
+    s.act_empty = s.act_full + 1;
     return s;
+}
+__device__ __forceinline__ void stream_init(const StreamSmem& S) {
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S.n_stages; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.red_bar[s], kNcw);
+            mbar_init(&S.empty[s], 1);
+        }
+        mbar_init(S.act_full, 1);
+        mbar_init(S.act_empty, kNcw);
+        mbar_fence_init();
+    }
+    __syncthreads();
 }
 
 __device__ __forceinline__ void load_tile(const Tile* src, Tile& tl) {
@@ -626,142 +759,172 @@ __device__ __forceinline__ void load_tile(const Tile* src, Tile& tl) {
     for (int i = 0; i < (int)(sizeof(Tile) / 4); ++i) d[i] = __ldcg(s + i);
 }
 
-__device__ __forceinline__ const void* tile_blob(const LayerArgs& L, int expert,
-                                                 const MatOff*& off) {
-    if (expert == L.E) {
-        off = L.smat;
-        return L.shared_blob;
-    }
-    off = L.mat;
-    return (expert >= 0 && expert < L.E) ? L.blobs[expert] : nullptr;
-}
-
-// Stage layout of a unit of 16 rows x K range (see UnitGeom); `padded`
-// when every row can be its own 16-byte-multiple copy.
-struct StageLayout {
-    uint32_t rb, sb;    // row bytes of the range: packed, scales
-    uint32_t rbp, sbp;  // strides in the stage
-    bool padded;
-    uint32_t bytes;
+// Where the producer finds a tile's activations: quantised rows `xq`
+// ([row][chunk][64 B], nchk chunks per row) and their per-group parameters
+// `xqp` ([row][group] float4, ngrp groups per row), K range starting at
+// group kg0; rows are token ids (gate/up) or assignment ids (down).
+struct ActSrc {
+    const uint8_t* xq;
+    const float4* xqp;
+    int nchk, ngrp, kg0, npg;
+    bool by_asg;
 };
-__host__ __device__ inline StageLayout stage_layout(int k_range, int gs) {
-    StageLayout s;
-    s.rb = (uint32_t)k_range / 2;
-    s.sb = (uint32_t)(k_range / gs) * 2;
-    s.padded = (s.rb % 16 == 0) && (s.sb % 16 == 0);
-    s.rbp = s.padded ? s.rb + 16 : s.rb;
-    s.sbp = s.padded ? s.sb + 16 : s.sb;
-    s.bytes = 16 * s.rbp + 32 * s.sbp;
-    return s;
-}
 
-// Producer warp: fill stages until the units run out, then post a sentinel.
-// The next unit id is fetched from the counter one unit ahead, so the atomic's
-// latency overlaps the current unit's copies.  Lane r < 16 owns MMA row r of
-// the unit: `rowsrc(u, r, p, sc, ze)` gives the global addresses of its packed
-// bytes, scales and zeros (false = unusable unit, status already flagged).
-// Padded layout: every lane < 16 copies its own row's three sections;
-// otherwise lanes 0 and 8 copy 8 contiguous rows each.
-template <typename RowSrc>
-__device__ void produce(const StreamSmem& S, const Ws& W, int* counter, long long total,
-                        const StageLayout& sl, RowSrc rowsrc) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t soff = 16 * sl.rbp, zoff = soff + 16 * sl.sbp;
-    const uint32_t tx = 16 * (sl.rb + 2 * sl.sb);
-    int u_next = 0;
-    if (lane == 0) u_next = atomicAdd(counter, 1);
-    u_next = __shfl_sync(kFull, u_next, 0);
-    int it = 0;
-    bool ok = true;
-    for (;; ++it) {
+// Producer (lane 0 of warp 0): for the units [u_begin, u_end) in order, fill
+// the weight stages and, for each tile, the activation tile; then post a
+// sentinel.  Unit u is unit r = u % upt of tile u / upt; blk(blob, r, c) gives
+// the global address of its copy c (0: codes of block A, 1: pairs of block A,
+// 2/3: block B).  The next tile's record is loaded one tile ahead.  With
+// `act_after_pdl` the activations come from the previous kernel in the
+// stream: the first tile's activation copies wait for it (griddepcontrol)
+// but only after the weight stages have been filled.
+template <typename Blk>
+__device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
+                        int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
+                        Blk blk) {
+    const uint32_t tx = 2 * geo.bbytes, zb = (uint32_t)geo.ng * 32u;
+    const uint32_t rowb = act_row_bytes(geo.ng, as.npg), pb = (uint32_t)geo.ng * 16u;
+    const uint64_t pol = evict_first_policy();
+    int ti = u_begin / upt, r = u_begin - ti * upt;
+    Tile cur, nxt;
+    if (u_begin < u_end) load_tile(W.tiles + ti, cur);
+    if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
+    int it = 0, tiles_done = 0;
+    bool ok = true, act_due = true, waited_pdl = !act_after_pdl;
+    // activation tile of `cur`, once the consumers copied the previous one
+    auto issue_act = [&]() -> bool {
+        if (!waited_pdl) {
+            pdl_wait();
+            waited_pdl = true;
+        }
+        if (tiles_done > 0 && !mbar_wait(S.act_empty, (tiles_done - 1) & 1)) return false;
+        mbar_expect_tx(S.act_full, (uint32_t)cur.m * (rowb + pb));
+        for (int t = 0; t < cur.m; ++t) {
+            const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
+            bulk_g2s_plain(S.act + t * rowb,
+                           as.xq + ((size_t)row * as.nchk + (size_t)as.kg0 * as.npg) * 64, rowb,
+                           S.act_full);
+            bulk_g2s_plain(S.act + kMT * rowb + t * pb, as.xqp + (size_t)row * as.ngrp + as.kg0,
+                           pb, S.act_full);
+        }
+        ++tiles_done;
+        act_due = false;
+        return true;
+    };
+    for (int u = u_begin;; ++u, ++it) {
         const int s = it % S.n_stages;
-        int waited = 1;
-        if (lane == 0) waited = mbar_wait(&S.empty[s], ((it / S.n_stages) & 1) ^ 1) ? 1 : 0;
-        if (!__shfl_sync(kFull, waited, 0)) {
-            if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+        if (!mbar_wait(&S.empty[s], ((it / S.n_stages) & 1) ^ 1)) {
             ok = false;
             break;
         }
-        const int u = u_next;
-        if (u >= total) {
-            if (lane == 0) {
-                S.unit[s] = -1;
-                mbar_arrive(&S.full[s]);
-            }
+        if (u >= u_end) {
+            S.info[s].u = -1;
+            mbar_arrive(&S.full[s]);
             break;
         }
-        if (lane == 0) u_next = atomicAdd(counter, 1);
-        const uint8_t *p = nullptr, *sc = nullptr, *ze = nullptr;
-        bool good = true;
-        if (lane < 16) good = rowsrc(u, lane, p, sc, ze);
-        int n = 0;
-        Copy c[3];
-        if (sl.padded) {
-            if (lane < 16) {
-                c[0] = Copy{p, lane * sl.rbp, sl.rb};
-                c[1] = Copy{sc, soff + lane * sl.sbp, sl.sb};
-                c[2] = Copy{ze, zoff + lane * sl.sbp, sl.sb};
-                n = 3;
-            }
-        } else if (lane == 0 || lane == 8) {
-            const uint32_t h = lane / 8;
-            c[0] = Copy{p, 8 * h * sl.rb, 8 * sl.rb};
-            c[1] = Copy{sc, soff + 8 * h * sl.sb, 8 * sl.sb};
-            c[2] = Copy{ze, zoff + 8 * h * sl.sb, 8 * sl.sb};
-            n = 3;
+        if (r == upt) {
+            r = 0;
+            ++ti;
+            cur = nxt;
+            if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
+            act_due = true;
         }
-        for (int i = 0; i < n; ++i)
-            good = good && aligned16(c[i].src) && !(c[i].bytes & 15u) && !(c[i].dst_off & 15u);
-        const bool all = __all_sync(kFull, good);
-        if (lane == 0) {
-            S.unit[s] = all ? u : -2;
-            if (all) {
-                mbar_expect_tx(&S.full[s], tx);
-            } else {
-                atomicOr(W.status, ST_ALIGN);
-                mbar_arrive(&S.full[s]);
+        if (act_due && waited_pdl && !issue_act()) {
+            ok = false;
+            break;
+        }
+        UnitInfo& inf = S.info[s];
+        inf.m = cur.m;
+#pragma unroll
+        for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
+        const unsigned char* p[4] = {nullptr, nullptr, nullptr, nullptr};
+        bool good = cur.blob != nullptr;
+        if (good) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                p[c] = blk(cur.blob, r, c);
+                if (!aligned16(p[c])) {
+                    good = false;
+                    atomicOr(W.status, ST_ALIGN);
+                }
             }
         }
-        __syncwarp();
-        if (all) {
+        inf.u = good ? u : (u | kSkip);
+        if (good) {
+            mbar_expect_tx(&S.full[s], tx);
             uint8_t* dst = S.stages + (size_t)s * S.stage_bytes;
-            for (int i = 0; i < n; ++i) bulk_g2s(dst + c[i].dst_off, c[i].src, c[i].bytes, &S.full[s]);
+            bulk_g2s(dst, p[0], geo.pbytes, &S.full[s], pol);
+            bulk_g2s(dst + geo.pbytes, p[1], zb, &S.full[s], pol);
+            bulk_g2s(dst + geo.bbytes, p[2], geo.pbytes, &S.full[s], pol);
+            bulk_g2s(dst + geo.bbytes + geo.pbytes, p[3], zb, &S.full[s], pol);
+        } else {
+            mbar_arrive(&S.full[s]);
         }
-        u_next = __shfl_sync(kFull, u_next, 0);
+        ++r;
+        // a deferred first activation tile: once the stages are full, or before
+        // the tile or the range ends
+        if (act_due && !waited_pdl &&
+            (it + 1 >= S.n_stages || r == upt || u + 1 >= u_end) && !issue_act()) {
+            ok = false;
+            break;
+        }
     }
-    __syncwarp();
-    if (!ok && lane == 0) {
+    if (!ok) {
+        atomicOr(W.status, ST_TIMEOUT);
         // a consumer stopped early: let every issued copy land before exiting
         for (int k = 0; k < S.n_stages && k < it; ++k) {
             const int j = it - 1 - k;
             mbar_wait(&S.full[j % S.n_stages], (j / S.n_stages) & 1);
         }
+        if (tiles_done > 0) mbar_wait(S.act_full, (tiles_done - 1) & 1);
+    }
+}
+
+// Reducer (warp 1): per unit, once the consumers' partials are in, sum them in
+// warp order (deterministic) and store the result; then release the stage.
+// out(u, asg, g, sum) is called by lane (g, q) for token slot q < m.
+template <typename Out>
+__device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    for (int it = 0;; ++it) {
+        const int s = it % S.n_stages;
+        const uint32_t ph = (it / S.n_stages) & 1;
+        if (!mbar_wait(&S.full[s], ph)) {
+            if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+            break;
+        }
+        const UnitInfo& inf = S.info[s];
+        const int u = *reinterpret_cast<const volatile int*>(&inf.u);
+        if (u == -1) break;
+        if (!mbar_wait(&S.red_bar[s], ph)) {
+            if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+            break;
+        }
+        if (!(u & kSkip) && q < inf.m) {
+            const float2* red = S.red + (size_t)s * kNcw * 32;
+            float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kNcw; ++w) {
+                const float2 v = red[w * 32 + lane];
+                sum.x += v.x;
+                sum.y += v.y;
+            }
+            out(u, inf.asg[q], g, sum);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);
     }
 }
 
 // ------------------------------------------------------------------------
-// Tensor-core consumers.  A unit is 16 MMA rows over a K range of ng quant
-// groups (gate/up: rows 0-7 = gate rows, 8-15 = up rows of 8 output rows;
-// down: 16 output rows of one K part).  kNcw consumer warps split the K range
-// into contiguous runs of group pairs; thread (g = lane/4, q = lane%4)
-// accumulates rows g and g+8 for token q in fp32.
-//
-// Shared memory of a streaming CTA: the stage ring, then the activation tile
-// (the B fragments of every MMA of the K range in per-lane order, and the
-// per-group (k/254, S) of each token slot) -- written once per tile (and
-// part) by the consumers, so the steady state reads only shared memory --
-// then the cross-warp reduction scratch.
+// Tensor-core consumers.  Consumer warp w owns the groups [g0, g0 + n) of the
+// unit's K range (g0 = w*ng/kNcw) for every unit of the CTA, so the B
+// fragments of its range (the quantised activations) are loaded into
+// registers once per tile, from the activation tile the producer staged.
+// Thread (g = lane/4, q = lane%4) accumulates MMA rows g (block A) and g+8
+// (block B) for token slot q in fp32, and per unit writes its partial to the
+// stage's reduction slot.
 // ------------------------------------------------------------------------
-constexpr int kNcw = 16;                          // consumer warps per CTA
-constexpr int kStreamCta = 32 * (kNcw + 1);       // + 1 producer warp
-
-struct UnitGeom {
-    int ng;         // quant groups in the unit's K range
-    uint32_t rbp;   // packed row stride in the stage
-    uint32_t sbp;   // scale/zero row stride in the stage
-    uint32_t zoff;  // offset of the zero rows from the scale rows
-};
-
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                        uint32_t b1) {
     asm volatile(
@@ -774,11 +937,6 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     uint32_t v;
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    unsigned short v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
     return v;
 }
 __device__ __forceinline__ uint2 lds64(uint32_t a) {
@@ -817,264 +975,177 @@ __device__ __forceinline__ Words<NPG> lds_w(uint32_t a) {
     return r;
 }
 
-// Stage the activation tile of a K range: for each group G and MMA i, the
-// (b0, b1) of every lane, and (k/254, S) of each token slot.  xw/xp point at
-// the range's first chunk/group of token row 0; rows are nchk chunks / ngrp
-// groups apart.  Executed by all consumer threads.
-template <int NPG>
-__device__ __forceinline__ void stage_xtile(uint2* xt, float2* xtp, int ng, const uint4* xw,
-                                            const float2* xp, int nchk, int ngrp,
-                                            const int* xrow, int m_tok) {
-    const int ct = threadIdx.x - 32, nct = kNcw * 32;
-    const uint2* xw2 = reinterpret_cast<const uint2*>(xw);
-    const int nent = ng * NPG * 32;
-    for (int e = ct; e < nent; e += nct) {
-        const int l = e & 31, gi = e >> 5;  // gi = G*NPG + i
-        const int G = gi / NPG, i = gi - G * NPG;
-        const int g = l >> 2, q = l & 3;
-        const int bt = g >> 1, bd = g & 1;
-        uint2 v = make_uint2(0u, 0u);
-        if (bt < m_tok) {
-            const int wi = q * NPG + i;
-            const int chunk = G * NPG + (wi >> 2);
-            v = __ldg(xw2 + (size_t)xrow[bt] * nchk * 8 + (size_t)chunk * 8 + bd * 4 + (wi & 3));
-        }
-        xt[e] = v;
-    }
-    for (int e = ct; e < ng * kMT; e += nct) {
-        const int G = e / kMT, t = e - G * kMT;
-        xtp[e] = t < m_tok ? __ldg(xp + (size_t)xrow[t] * ngrp + G) : make_float2(0.f, 0.f);
-    }
-}
-
-// Operands of a pair of groups (2P, 2P+1), loaded one pair ahead of use.
-template <int NPG>
-struct PairFrag {
-    Words<NPG> wl[2], wh[2];  // packed words of rows g, g+8
-    uint2 b[2][NPG];          // B fragments
-    float2 kp[2];             // (k/254, S) of token q
-    uint32_t s_lo, z_lo, s_hi, z_hi;  // half2 scales/zeros of rows g, g+8
-    bool two;                         // the pair's second group exists
+// B fragments of NG groups (registers).  A warp owns n <= NG groups of the
+// unit's K range; the kernels are built for a few NG per NPG (ng_bucket) and
+// the groups past n are masked (zero B fragments and (k/254, S) = 0, so they
+// add exactly 0).  The (k/254, S) pairs of the warp's groups live in shared
+// memory, NG x kMT per warp, written and read by the owning warp only.
+template <int NPG, int NG>
+struct WarpAct {
+    uint2 b[NG][NPG];
 };
 
-// Partial dot products of one unit for this thread: acc[0] = row g, acc[1] =
-// row g+8, token q.  `xt`/`xtp`: the staged activation tile (shared memory).
-template <int NPG>
-__device__ __forceinline__ void mma_unit(const uint8_t* st, const UnitGeom& geo, uint32_t xt,
-                                         uint32_t xtp, float (&acc)[2]) {
+// Copy the warp's B fragments and (k/254, S) pairs of the current tile from
+// the staged activation tile (slots t < m; the rest are zero).
+template <int NPG, int NG>
+__device__ __forceinline__ void load_act(WarpAct<NPG, NG>& A, float2* kp_w, const StreamSmem& S,
+                                         int g0, int n, int m) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    const int cw = (threadIdx.x >> 5) - 1;  // consumer warp
-    const int npair = (geo.ng + 1) >> 1;
-    const int p0 = (cw * npair) / kNcw, p1 = ((cw + 1) * npair) / kNcw;
-    if (p0 >= p1) return;
-    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(st);
-    const uint32_t a_lo = sbase + g * geo.rbp + q * (NPG * 4);
-    const uint32_t a_hi = a_lo + 8 * geo.rbp;
-    const uint32_t s_lo = sbase + 16 * geo.rbp + g * geo.sbp;
-    const uint32_t s_hi = s_lo + 8 * geo.sbp;
-    const bool s_al = (geo.sbp & 3) == 0;  // scale rows allow half2 loads
-    const uint32_t xtl = xt + lane * 8, xtq = xtp + q * 8;
-    const int ng = geo.ng;
-    auto ld2 = [&](uint32_t a) -> uint32_t {
-        return s_al ? lds32(a) : (lds16(a) | (lds16(a + 2) << 16));
-    };
-    auto load = [&](int P, PairFrag<NPG>& f) {
-        const int G = 2 * P;
+    const int bt = g >> 1, bd = g & 1;
+    const uint32_t base = smem_addr(S.act) + bt * S.act_row + bd * 32;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int Gh = min(G + h, ng - 1);  // a missing odd group reads group ng-1 with kp = 0
-            f.wl[h] = lds_w<NPG>(a_lo + Gh * (NPG * 16));
-            f.wh[h] = lds_w<NPG>(a_hi + Gh * (NPG * 16));
+    for (int G = 0; G < NG; ++G) {
 #pragma unroll
-            for (int i = 0; i < NPG; ++i) f.b[h][i] = lds64(xtl + (Gh * NPG + i) * 256);
-            const uint2 kv = lds64(xtq + Gh * (kMT * 8));
-            f.kp[h] = G + h < ng ? make_float2(__uint_as_float(kv.x), __uint_as_float(kv.y))
-                                 : make_float2(0.f, 0.f);
+        for (int i = 0; i < NPG; ++i) {
+            const int wi = q * NPG + i;
+            const int chunk = (g0 + G) * NPG + (wi >> 2);
+            A.b[G][i] = (G < n && bt < m) ? lds64(base + chunk * 64 + (wi & 3) * 8)
+                                          : make_uint2(0u, 0u);
         }
-        f.two = G + 1 < ng;
-        f.s_lo = ld2(s_lo + 2 * G);
-        f.z_lo = ld2(s_lo + geo.zoff + 2 * G);
-        f.s_hi = ld2(s_hi + 2 * G);
-        f.z_hi = ld2(s_hi + geo.zoff + 2 * G);
-    };
-    auto compute = [&](const PairFrag<NPG>& f) {
-        const float2 slo = __half22float2(*reinterpret_cast<const __half2*>(&f.s_lo));
-        const float2 zlo = __half22float2(*reinterpret_cast<const __half2*>(&f.z_lo));
-        const float2 shi = __half22float2(*reinterpret_cast<const __half2*>(&f.s_hi));
-        const float2 zhi = __half22float2(*reinterpret_cast<const __half2*>(&f.z_hi));
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            int d[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < NPG; ++i) {
-                uint32_t a[4];
-                a[0] = f.wl[h].w[i] & 0x0F0F0F0Fu;
-                a[1] = f.wh[h].w[i] & 0x0F0F0F0Fu;
-                a[2] = (f.wl[h].w[i] >> 4) & 0x0F0F0F0Fu;
-                a[3] = (f.wh[h].w[i] >> 4) & 0x0F0F0F0Fu;
-                mma_s8(d, a, f.b[h][i].x, f.b[h][i].y);
-            }
-            // kp = 0 (absent group or token) makes the contribution 0
-            const float m8 = -8.0f * f.kp[h].y;
-            const float c_lo = (float)(d[0] * 254 + d[1]);
-            const float c_hi = (float)(d[2] * 254 + d[3]);
-            // an absent second group (odd count) has kp = 0 and may have read
-            // scale bytes past the row end: use 0 so they cannot make a NaN
-            const bool live = h == 0 || f.two;
-            const float sl = live ? (h ? slo.y : slo.x) : 0.f, zl = live ? (h ? zlo.y : zlo.x) : 0.f;
-            const float sh = live ? (h ? shi.y : shi.x) : 0.f, zh = live ? (h ? zhi.y : zhi.x) : 0.f;
-            acc[0] = fmaf(sl, fmaf(f.kp[h].x, c_lo, m8), fmaf(zl, f.kp[h].y, acc[0]));
-            acc[1] = fmaf(sh, fmaf(f.kp[h].x, c_hi, m8), fmaf(zh, f.kp[h].y, acc[1]));
+    }
+    const float4* par = reinterpret_cast<const float4*>(S.act + kMT * S.act_row);
+    const int ngr = (int)(S.act_row / (64u * NPG));  // groups in the range
+    for (int e = lane; e < NG * kMT; e += 32) {
+        const int G = e / kMT, t = e - G * kMT;
+        float2 v = make_float2(0.f, 0.f);
+        if (G < n && t < m) {
+            const float4 p = par[t * ngr + g0 + G];
+            v = make_float2(p.x, p.y);
         }
-    };
-    PairFrag<NPG> fa, fb;
-    load(p0, fa);
-    for (int P = p0; P < p1; P += 2) {
-        if (P + 1 < p1) load(P + 1, fb);
-        compute(fa);
-        if (P + 1 >= p1) break;
-        if (P + 2 < p1) load(P + 2, fa);
-        compute(fb);
+        kp_w[e] = v;
     }
+    __syncwarp();
 }
 
-// Sum the consumer warps' partials (fixed order).  Returns, for the threads
-// of consumer warp 0, the unit sums of rows g and g+8 for token q.
-__device__ __forceinline__ bool unit_reduce(const float (&acc)[2], float2* part,
-                                            float (&out)[2]) {
-    const int lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
-    part[cw * 32 + lane] = make_float2(acc[0], acc[1]);
-    asm volatile("bar.sync 1, %0;" ::"r"(kNcw * 32) : "memory");
-    if (cw != 0) return false;
-    float a = 0.f, b = 0.f;
+// This warp's partial dot products of a unit: acc.x = MMA row g (block A),
+// acc.y = row g+8 (block B), for token slot q.  `st`: the stage (shared
+// address); groups g0 .. g0+NG-1 of the unit's range (those past the range
+// are read at the range's last group and contribute 0); kp: shared address of
+// this warp's (k/254, S) pairs.
+template <int NPG, int NG>
+__device__ __forceinline__ float2 mma_unit(uint32_t st, const Geo& geo, int g0,
+                                           const WarpAct<NPG, NG>& A, uint32_t kp) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    constexpr uint32_t kGroupCode = 4u * 32u * NPG;  // 8 rows x gs/2 bytes
+    const uint32_t a_lo = st + g * (16 * NPG) + q * (4 * NPG);
+    const uint32_t z_lo = st + geo.pbytes + g * 4;
+    const uint32_t kq = kp + q * 8;
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < kNcw; ++w) {
-        const float2 v = part[w * 32 + lane];
-        a += v.x;
-        b += v.y;
-    }
-    out[0] = a;
-    out[1] = b;
-    return true;
-}
-
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"r"(kNcw * 32) : "memory");
-}
-
-// Dynamic shared memory of a streaming CTA (see the section comment).
-struct StreamLayout {
-    uint8_t* ring;
-    uint2* xt;
-    float2* xtp;
-    float2* red;  // [2][kNcw*32]
-};
-__device__ __forceinline__ StreamLayout stream_layout(uint8_t* base, int n_stages,
-                                                      uint32_t stage_bytes, int ng, int npg) {
-    StreamLayout s;
-    s.ring = base;
-    size_t o = (size_t)n_stages * stage_bytes + ring_extra_bytes(n_stages);
-    o = (o + 127) & ~size_t(127);
-    s.xt = reinterpret_cast<uint2*>(base + o);
-    o += (size_t)ng * npg * 32 * sizeof(uint2);
-    s.xtp = reinterpret_cast<float2*>(base + o);
-    o += (size_t)ng * kMT * sizeof(float2);
-    o = (o + 15) & ~size_t(15);
-    s.red = reinterpret_cast<float2*>(base + o);
-    return s;
-}
-
-// ------------------------------------------------------------------------
-// gate/up + SwiGLU: unit = 8 output rows (gate rows + up rows) x all of H
-// ------------------------------------------------------------------------
-template <int NPG>
-__global__ void __launch_bounds__(kStreamCta, 1)
-gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int H = L.H, I = L.I, gs = L.gs;
-    const StreamLayout X = stream_layout(smem_raw, n_stages, stage_bytes, H / gs, NPG);
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < n_stages; ++s) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kNcw);
+    for (int G = 0; G < NG; ++G) {
+        const uint32_t gg = (uint32_t)min(g0 + G, geo.ng - 1);
+        const Words<NPG> wl = lds_w<NPG>(a_lo + gg * kGroupCode);
+        const Words<NPG> wh = lds_w<NPG>(a_lo + geo.bbytes + gg * kGroupCode);
+        const uint32_t pl = lds32(z_lo + gg * 32), ph = lds32(z_lo + geo.bbytes + gg * 32);
+        const uint2 kv = lds64(kq + G * (kMT * 8));
+        // one accumulator per MMA (independent, so they overlap), summed in int
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < NPG; ++i) {
+            uint32_t a[4];
+            a[0] = wl.w[i] & 0x0F0F0F0Fu;
+            a[1] = wh.w[i] & 0x0F0F0F0Fu;
+            a[2] = (wl.w[i] >> 4) & 0x0F0F0F0Fu;
+            a[3] = (wh.w[i] >> 4) & 0x0F0F0F0Fu;
+            int di[4] = {0, 0, 0, 0};
+            mma_s8(di, a, A.b[G][i].x, A.b[G][i].y);
+            d[0] += di[0];
+            d[1] += di[1];
+            d[2] += di[2];
+            d[3] += di[3];
         }
-        mbar_fence_init();
+        // row += s * (k/254 * (254*A + B) - 8*S) + z * S
+        const float k2 = __uint_as_float(kv.x), S = __uint_as_float(kv.y);
+        const float m8 = -8.0f * S;
+        const float2 sl = __half22float2(*reinterpret_cast<const __half2*>(&pl));
+        const float2 sh = __half22float2(*reinterpret_cast<const __half2*>(&ph));
+        acc.x = fmaf(sl.x, fmaf(k2, (float)(d[0] * 254 + d[1]), m8), fmaf(sl.y, S, acc.x));
+        acc.y = fmaf(sh.x, fmaf(k2, (float)(d[2] * 254 + d[3]), m8), fmaf(sh.y, S, acc.y));
     }
-    __syncthreads();
-    pdl_wait();
-    pdl_launch();
-    const int rbs = I / 8;  // 8-row blocks per tile
-    const long long total = (long long)__ldcg(W.counters + C_NTILES) * rbs;
-    const StageLayout sl = stage_layout(H, gs);
+    return acc;
+}
 
-    if (warp == 0) {
-        int ctile = -1;
-        const uint8_t* cblob = nullptr;
-        const MatOff* coff = nullptr;
-        produce(S, W, W.counters + C_GU_TASK, total, sl,
-                [&](int u, int r, const uint8_t*& p, const uint8_t*& sc,
-                    const uint8_t*& ze) -> bool {
-                    const int ti = u / rbs;
-                    if (ti != ctile) {
-                        Tile tl;
-                        load_tile(W.tiles + ti, tl);
-                        cblob = static_cast<const uint8_t*>(tile_blob(L, tl.expert, coff));
-                        ctile = ti;
-                    }
-                    if (!cblob) {
-                        atomicOr(W.status, ST_EXPERT);
-                        return false;
-                    }
-                    const MatOff& o = coff[r < 8 ? 0 : 1];
-                    const size_t row = (size_t)(u % rbs) * 8 + (r & 7);
-                    p = cblob + o.packed + row * sl.rb;
-                    sc = cblob + o.scales + row * sl.sb;
-                    ze = cblob + o.zeros + row * sl.sb;
-                    return true;
-                });
-        return;
-    }
-    const UnitGeom geo{H / gs, sl.rbp, sl.sbp, 16 * sl.sbp};
-    const uint32_t xt = (uint32_t)__cvta_generic_to_shared(X.xt);
-    const uint32_t xtp = (uint32_t)__cvta_generic_to_shared(X.xtp);
-    int cur = -1;
-    Tile tl;
+// Consumer loop: `upt` units per tile.
+template <int NPG, int NG>
+__device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int upt) {
+    const int lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 2;
+    const int g0 = cw * geo.ng / kNcw, n = (cw + 1) * geo.ng / kNcw - g0;
+    float2* kp_w = S.kp + cw * NG * kMT;
+    const uint32_t st0 = smem_addr(S.stages), kp = smem_addr(kp_w);
+    WarpAct<NPG, NG> A;
+    int cur = -1, tiles = 0;
     for (int it = 0;; ++it) {
-        const int s = it % n_stages;
-        if (!mbar_wait(&S.full[s], (it / n_stages) & 1)) {
+        const int s = it % S.n_stages;
+        const uint32_t ph = (it / S.n_stages) & 1;
+        if (!mbar_wait(&S.full[s], ph)) {
             if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
             break;
         }
-        const int u = *reinterpret_cast<volatile int*>(&S.unit[s]);
-        if (u == -1) break;
-        if (u < 0) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[s]);
-            continue;
-        }
-        const int ti = u / rbs;
+        const UnitInfo& inf = S.info[s];
+        const int uf = *reinterpret_cast<const volatile int*>(&inf.u);
+        if (uf == -1) break;
+        const int u = uf & ~kSkip;
+        const int ti = u / upt;
         if (ti != cur) {
-            // every consumer is past the previous unit's reduction barrier
-            load_tile(W.tiles + ti, tl);
-            stage_xtile<NPG>(X.xt, X.xtp, H / gs, W.xq, W.xqp, H / kChunk, H / gs, tl.tok, tl.m);
-            consumers_sync();
+            if (!mbar_wait(S.act_full, tiles & 1)) {
+                if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+                break;
+            }
+            load_act<NPG, NG>(A, kp_w, S, g0, n, inf.m);
+            if (lane == 0) mbar_arrive(S.act_empty);
+            ++tiles;
             cur = ti;
         }
-        float acc[2] = {0.f, 0.f};
-        mma_unit<NPG>(S.stages + (size_t)s * stage_bytes, geo, xt, xtp, acc);
+        float2 part = make_float2(0.f, 0.f);
+        if (!(uf & kSkip)) part = mma_unit<NPG, NG>(st0 + s * S.stage_bytes, geo, g0, A, kp);
+        S.red[((size_t)s * kNcw + cw) * 32 + lane] = part;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[s]);  // the stage is no longer read
-        float out[2];
-        if (unit_reduce(acc, X.red + (it & 1) * kNcw * 32, out)) {
-            const int g = lane >> 2, q = lane & 3;
-            if (q < tl.m) {
-                const int row = (u % rbs) * 8 + g;
-                W.h[(size_t)tl.asg[q] * I + row] = out[0] / (1.0f + expf(-out[0])) * out[1];
-            }
-        }
+        if (lane == 0) mbar_arrive(&S.red_bar[s]);
     }
+}
+
+// ------------------------------------------------------------------------
+// gate/up + SwiGLU: unit = gate block b + up block b (8 output rows) x all of H
+// ------------------------------------------------------------------------
+template <int NPG, int NG>
+__global__ void __launch_bounds__(kStreamCta, 1)
+gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const int H = L.H, I = L.I, gs = L.gs;
+    const Geo geo = make_geo(H / gs, gs);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG);
+    stream_init(S);
+    pdl_wait();
+    pdl_launch();
+    const int warp = threadIdx.x >> 5;
+    const int rbs = I / 8;  // 8-row blocks per matrix
+    const int ntiles = __ldcg(W.counters + C_NTILES);
+    const long long total = (long long)ntiles * rbs;
+
+    if (warp == 0) {
+        if ((threadIdx.x & 31) == 0) {
+            const int b = (int)(total * blockIdx.x / gridDim.x);
+            const int e = (int)(total * (blockIdx.x + 1) / gridDim.x);
+            const size_t bb = block_bytes_of(H, gs);
+            const size_t off_g = L.mat[0].packed, off_u = L.mat[1].packed;
+            const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, H / kChunk, H / gs, 0,
+                            NPG, false};
+            produce(S, W, b, e, rbs, ntiles, geo, as, false,
+                    [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
+                        const unsigned char* blk = blob + (c < 2 ? off_g : off_u) + (size_t)r * bb;
+                        return (c & 1) ? blk + 4 * (size_t)H : blk;
+                    });
+        }
+        return;
+    }
+    if (warp == 1) {
+        reduce_units(S, W, [&](int u, int asg, int g, float2 v) {
+            const size_t row = (size_t)(u % rbs) * 8 + g;
+            W.h[(size_t)asg * I + row] = v.x / (1.0f + expf(-v.x)) * v.y;
+        });
+        return;
+    }
+    consume<NPG, NG>(S, W, geo, rbs);
 }
 
 // ------------------------------------------------------------------------
@@ -1097,111 +1168,61 @@ hquant_kernel(LayerArgs L, Ws W) {
 }
 
 // ------------------------------------------------------------------------
-// down projection: unit = 16 output rows x one of kp K parts.  A CTA serves
-// one part (blockIdx.x % kp), so its activation tile changes only with the
-// expert tile; units of a part come from that part's counter.  Each part is
-// written to its own ypart buffer and the combine adds them in fixed order
-// (deterministic, no float atomics).
+// down projection: unit = blocks 2j, 2j+1 (16 output rows) x one of kp K
+// parts.  CTA c serves part c % kp, with a contiguous range of the part's
+// units.  Each part is written to its own ypart buffer and the combine adds
+// them in fixed order (deterministic, no float atomics).
 // ------------------------------------------------------------------------
-template <int NPG>
+template <int NPG, int NG>
 __global__ void __launch_bounds__(kStreamCta, 1)
 down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
-    const int kp = L.kp;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kp = L.kp;
     const int H = L.H, I = L.I, gs = L.gs;
-    const int kr = I / kp;  // K range of a part
-    const StreamLayout X = stream_layout(smem_raw, n_stages, stage_bytes, kr / gs, NPG);
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < n_stages; ++s) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kNcw);
-        }
-        mbar_fence_init();
-    }
-    __syncthreads();
-    // The producer streams weights before the previous kernel (the h
-    // quantiser) has finished: weights, the expert table and the tile plan
-    // (written by the router, which completed before the gate/up kernel that
-    // precedes the quantiser could start) do not depend on it.  Consumers wait
-    // for it before reading the quantised h.
+    const int ngp = I / gs / kp;  // groups per part
+    const Geo geo = make_geo(ngp, gs);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG);
+    stream_init(S);
+    // Weights, the expert table and the tile plan (written by the router,
+    // which completed before the gate/up kernel preceding the quantiser could
+    // start) do not depend on the previous kernel (the h quantiser): the
+    // producer waits for it only before the first activation copy.
     pdl_launch();
+    const int warp = threadIdx.x >> 5;
     const int pi = blockIdx.x % kp;
-    const int rbs = H / 16;
-    const long long total = (long long)__ldcg(W.counters + C_NTILES) * rbs;
-    const StageLayout sl = stage_layout(kr, gs);
+    const int cpp = (gridDim.x - pi + kp - 1) / kp;  // CTAs serving this part
+    const int upt = H / 16;
+    const int ntiles = __ldcg(W.counters + C_NTILES);
+    const long long total = (long long)ntiles * upt;
 
     if (warp == 0) {
-        int ctile = -1;
-        const uint8_t* cblob = nullptr;
-        const MatOff* coff = nullptr;
-        const size_t rowb = I / 2, rows = (size_t)(I / gs) * 2;
-        produce(S, W, W.counters + C_DN_BASE + pi, total, sl,
-                [&](int u, int r, const uint8_t*& p, const uint8_t*& sc,
-                    const uint8_t*& ze) -> bool {
-                    const int ti = u / rbs;
-                    if (ti != ctile) {
-                        Tile tl;
-                        load_tile(W.tiles + ti, tl);
-                        cblob = static_cast<const uint8_t*>(tile_blob(L, tl.expert, coff));
-                        ctile = ti;
-                    }
-                    if (!cblob) {
-                        atomicOr(W.status, ST_EXPERT);
-                        return false;
-                    }
-                    const size_t row = (size_t)(u % rbs) * 16 + r;
-                    p = cblob + coff[2].packed + row * rowb + pi * sl.rb;
-                    sc = cblob + coff[2].scales + row * rows + pi * sl.sb;
-                    ze = cblob + coff[2].zeros + row * rows + pi * sl.sb;
-                    return true;
-                });
+        if ((threadIdx.x & 31) == 0) {
+            const int j = blockIdx.x / kp;
+            const int b = (int)(total * j / cpp), e = (int)(total * (j + 1) / cpp);
+            const size_t bb = block_bytes_of(I, gs);
+            const size_t off_d = L.mat[2].packed;
+            const size_t z_off = 4 * (size_t)I + (size_t)pi * geo.ng * 32;
+            const size_t p_off = (size_t)pi * geo.pbytes;
+            const ActSrc as{reinterpret_cast<const uint8_t*>(W.hq), W.hqp, I / kChunk, I / gs,
+                            pi * ngp, NPG, true};
+            produce(S, W, b, e, upt, ntiles, geo, as, true,
+                    [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
+                        const unsigned char* blk = blob + off_d + (size_t)(2 * r + (c >> 1)) * bb;
+                        return blk + ((c & 1) ? z_off : p_off);
+                    });
+        }
         return;
     }
-    pdl_wait();
-    const UnitGeom geo{kr / gs, sl.rbp, sl.sbp, 16 * sl.sbp};
-    const uint32_t xt = (uint32_t)__cvta_generic_to_shared(X.xt);
-    const uint32_t xtp = (uint32_t)__cvta_generic_to_shared(X.xtp);
-    int cur = -1;
-    Tile tl;
-    for (int it = 0;; ++it) {
-        const int s = it % n_stages;
-        if (!mbar_wait(&S.full[s], (it / n_stages) & 1)) {
-            if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
-            break;
-        }
-        const int u = *reinterpret_cast<volatile int*>(&S.unit[s]);
-        if (u == -1) break;
-        if (u < 0) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[s]);
-            continue;
-        }
-        const int ti = u / rbs;
-        if (ti != cur) {
-            load_tile(W.tiles + ti, tl);
-            // activations of this part: chunks [pi*kr/32, ...), groups [pi*kr/gs, ...)
-            stage_xtile<NPG>(X.xt, X.xtp, kr / gs, W.hq + (size_t)pi * (kr / kChunk) * 4,
-                             W.hqp + (size_t)pi * (kr / gs), I / kChunk, I / gs, tl.asg, tl.m);
-            consumers_sync();
-            cur = ti;
-        }
-        float acc[2] = {0.f, 0.f};
-        mma_unit<NPG>(S.stages + (size_t)s * stage_bytes, geo, xt, xtp, acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[s]);
-        float out[2];
-        if (unit_reduce(acc, X.red + (it & 1) * kNcw * 32, out)) {
-            const int g = lane >> 2, q = lane & 3;
-            if (q < tl.m) {
-                const int row = (u % rbs) * 16 + g;
-                float* dst = W.ypart + ((size_t)pi * W.A + tl.asg[q]) * H + row;
-                dst[0] = out[0];
-                dst[8] = out[1];
-            }
-        }
+    if (warp == 1) {
+        reduce_units(S, W, [&](int u, int asg, int g, float2 v) {
+            const size_t row = (size_t)(u % upt) * 16 + g;
+            float* dst = W.ypart + ((size_t)pi * W.A + asg) * H + row;
+            dst[0] = v.x;
+            dst[8] = v.y;
+        });
+        return;
     }
+    consume<NPG, NG>(S, W, geo, upt);
 }
 
 // ------------------------------------------------------------------------
@@ -1236,10 +1257,10 @@ Layout make_layout(int T, int H, int I, int E, int K, bool shared) {
     l.tiles = take((size_t)l.max_tiles * sizeof(Tile));
     l.xn = take((size_t)T * H * sizeof(float));
     l.xq = take((size_t)T * (H / kChunk) * 64);
-    l.xqp = take((size_t)T * (H / kChunk) * sizeof(float2));  // >= per-group params
+    l.xqp = take((size_t)T * (H / kChunk) * sizeof(float4));  // >= per-group params
     l.h = take((size_t)l.A * I * sizeof(float));
     l.hq = take((size_t)l.A * (I / kChunk) * 64);
-    l.hqp = take((size_t)l.A * (I / kChunk) * sizeof(float2));
+    l.hqp = take((size_t)l.A * (I / kChunk) * sizeof(float4));
     l.hcnt = take((size_t)l.A * (I / kChunk) * sizeof(int));
     l.ypart = take((size_t)kMaxKp * l.A * H * sizeof(float));
     l.total = o;
@@ -1260,10 +1281,10 @@ Ws make_ws(void* base, const Layout& l) {
     w.tiles = reinterpret_cast<Tile*>(b + l.tiles);
     w.xn = reinterpret_cast<float*>(b + l.xn);
     w.xq = reinterpret_cast<uint4*>(b + l.xq);
-    w.xqp = reinterpret_cast<float2*>(b + l.xqp);
+    w.xqp = reinterpret_cast<float4*>(b + l.xqp);
     w.h = reinterpret_cast<float*>(b + l.h);
     w.hq = reinterpret_cast<uint4*>(b + l.hq);
-    w.hqp = reinterpret_cast<float2*>(b + l.hqp);
+    w.hqp = reinterpret_cast<float4*>(b + l.hqp);
     w.hcnt = reinterpret_cast<int*>(b + l.hcnt);
     w.ypart = reinterpret_cast<float*>(b + l.ypart);
     w.A = l.A;
@@ -1274,6 +1295,33 @@ Ws make_ws(void* base, const Layout& l) {
 MatOff mat_off(const WispExpertMeta& m, int i) {
     return {(unsigned long long)m.packed_off[i], (unsigned long long)m.scales_off[i],
             (unsigned long long)m.zeros_off[i]};
+}
+
+// Group counts per consumer warp the streaming kernels are built for (per
+// NPG = gs / 32); a warp's actual count is rounded up to the next one and the
+// rest masked.
+constexpr int kNgSet1[] = {1, 2, 4, 8, 16};
+constexpr int kNgSet2[] = {1, 2, 4, 8, 14, 16};
+constexpr int kNgSet4[] = {1, 2, 4, 8};
+template <size_t N>
+int bucket_in(const int (&set)[N], int need) {
+    for (size_t i = 0; i < N; ++i)
+        if (set[i] >= need) return set[i];
+    return 0;
+}
+int ng_bucket(int npg, int ng) {
+    const int need = std::max(1, (ng + kNcw - 1) / kNcw);
+    return npg == 1 ? bucket_in(kNgSet1, need) : npg == 2 ? bucket_in(kNgSet2, need)
+                                                          : bucket_in(kNgSet4, need);
+}
+
+// Smallest split of the down projection's K (= I) into parts of whole quant
+// groups, each at most kMaxPartK wide; 0 when none exists.
+int min_down_parts(int I, int gs) {
+    const int G = I / gs;
+    for (int kp = 1; kp <= kMaxKp; ++kp)
+        if (G % kp == 0 && (I / kp) <= kMaxPartK) return kp;
+    return 0;
 }
 
 bool check_layer(const WispMoeLayer* ly, int T, WispErrCtx* err) {
@@ -1311,30 +1359,37 @@ bool check_layer(const WispMoeLayer* ly, int T, WispErrCtx* err) {
     if (ly->shared_blob) {
         const WispExpertMeta& s = ly->shared_meta;
         if (!s.valid || s.cols[0] != (uint32_t)H || s.rows[0] != (uint32_t)I ||
-            s.group_size != (uint32_t)gs) {
+            s.group_size != (uint32_t)gs || !s.tiled) {
             WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
-                       "moe layer: shared expert must match the routed experts' shape "
-                       "and group size");
+                       "moe layer: shared expert must match the routed experts' shape, group "
+                       "size and tiled layout");
             return false;
         }
+    }
+    if (!m.tiled) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "moe layer: expert blobs must be in the tiled device layout (see "
+                   "wisp_expert_tile); meta describes a .bin blob");
+        return false;
+    }
+    if (H > kMaxPartK || !ng_bucket(gs / kChunk, H / gs)) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe layer: hidden %d above the supported %d", H,
+                   kMaxPartK);
+        return false;
+    }
+    if (min_down_parts(I, gs) == 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "moe layer: intermediate %d cannot be split into at most %d parts of whole "
+                   "quant groups of at most %d elements",
+                   I, kMaxKp, kMaxPartK);
+        return false;
     }
     return true;
 }
 
-// K parts of the down projection: the smallest split whose part is at most
-// 2048 wide and still splits into whole quant groups with padded stage rows.
-int down_parts(int I, int gs) {
-    for (int kp = 1; kp <= kMaxKp; ++kp) {
-        if (I % kp) continue;
-        const int kr = I / kp;
-        if (kr % kChunk || kr % gs) continue;
-        if (kp > 1 && (kr / gs) % 8) continue;
-        if (kr <= 2048) return kp;
-    }
-    return 1;
-}
+int down_parts(int I, int gs, long long units, int ctas);
 
-LayerArgs layer_args(const WispMoeLayer* ly) {
+LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     LayerArgs a{};
     a.blobs = ly->expert_blobs;
     a.shared_blob = ly->shared_blob;
@@ -1351,12 +1406,14 @@ LayerArgs layer_args(const WispMoeLayer* ly) {
     a.K = ly->top_k;
     a.gs = (int)ly->meta.group_size;
     a.has_shared = ly->shared_blob != nullptr;
-    a.kp = down_parts(a.I, a.gs);
+    const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
+                            (a.has_shared ? (T + kMT - 1) / kMT : 0);
+    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas);
     return a;
 }
 
-// Shared memory of a streaming CTA (one per SM): the activation tile of its
-// K range and the reduction scratch, and as many ring stages as fit (up to 8).
+// Shared memory of a streaming CTA (one per SM): as many ring stages (each
+// with its reduction slot) as fit, up to 8.
 struct StreamCfg {
     int stages = 0, blocks = 0;
     uint32_t stage_bytes = 0;
@@ -1365,29 +1422,62 @@ struct StreamCfg {
 
 constexpr size_t kSmemPerCta = 227 * 1024;
 
-StreamCfg plan_stream(uint32_t unit_bytes, int ng, int npg) {
+// Stages: enough to keep about kInFlight bytes of weights in flight per SM
+// (more only lengthens the DRAM queues every other load waits in), at least
+// 2, at most 8, within the shared memory left after the activation tile.
+constexpr size_t kInFlight = 160 * 1024;
+
+StreamCfg plan_stream(const Geo& geo, int npg) {
     StreamCfg c;
-    c.stage_bytes = (unit_bytes + 127) / 128 * 128;
-    const size_t xtile = (size_t)ng * npg * 32 * 8 + (size_t)ng * kMT * 8 + 256;
-    const size_t red = (size_t)2 * kNcw * 32 * 8;
-    const size_t fixed = xtile + red + 1024;
+    c.stage_bytes = stage_bytes_of(geo);
+    const uint32_t act = act_bytes_of(geo.ng, npg);
+    int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
+    want = std::max(2, std::min(8, want));
     c.stages = 0;
-    for (int st = 8; st >= 2; --st)
-        if ((size_t)st * c.stage_bytes + ring_extra_bytes(st) + fixed <= kSmemPerCta) {
+    for (int st = want; st >= 2; --st)
+        if (stream_smem_bytes(st, c.stage_bytes, act) <= kSmemPerCta) {
             c.stages = st;
             break;
         }
-    c.smem = (size_t)c.stages * c.stage_bytes + ring_extra_bytes(c.stages) + fixed;
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act);
     return c;
 }
 
 StreamCfg gateup_cfg(const LayerArgs& a) {
-    return plan_stream(stage_layout(a.H, a.gs).bytes, a.H / a.gs, a.gs / kChunk);
+    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk);
 }
 
 StreamCfg down_cfg(const LayerArgs& a) {
-    const int kr = a.I / a.kp;
-    return plan_stream(stage_layout(kr, a.gs).bytes, kr / a.gs, a.gs / kChunk);
+    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk);
+}
+
+// K parts of the down projection.  A part is a whole number of quant groups
+// and at most kMaxPartK wide (the consumer warps hold its activations in
+// registers).  Among the valid splits, pick the one that wastes least: masked
+// groups (the per-warp group count rounded up to a built bucket), uneven
+// units per CTA (`units` = down units of one part, tiles x H/16), and a small
+// cost per extra part (the combine reads every part).
+int down_parts(int I, int gs, long long units, int ctas) {
+    const int G = I / gs, npg = gs / kChunk;
+    int best = 0;
+    double best_score = -1.0;
+    for (int kp = 1; kp <= kMaxKp; ++kp) {
+        if (G % kp || I / kp > kMaxPartK) continue;
+        const int ngp = G / kp, ng = ng_bucket(npg, ngp);
+        if (!ng) continue;
+        const double eff = std::min(1.0, (double)ngp / (double)(ng * kNcw));
+        const double per = (double)units * kp / (double)ctas;
+        const double bal = per > 0 ? per / std::ceil(per) : 1.0;
+        // a shallow ring (big stages) starves the consumers while a stage turns over
+        const int st = plan_stream(make_geo(ngp, gs), npg).stages;
+        const double depth = std::min(1.0, st / 4.0);
+        const double score = eff * bal * depth * (1.0 - 0.01 * kp);
+        if (score > best_score + 1e-9) {
+            best_score = score;
+            best = kp;
+        }
+    }
+    return best ? best : 1;
 }
 
 template <typename K>
@@ -1470,27 +1560,75 @@ cudaError_t launch_hquant(const LayerArgs& a, const Ws& W, cudaStream_t s) {
     return launch(hquant_kernel, dim3((warps + wpc - 1) / wpc), dim3(kPrepThreads), 0, s, a, W);
 }
 
-template <int NPG>
-cudaError_t launch_streams_npg(const LayerArgs& a, const Ws& W, cudaStream_t s) {
-    StreamCfg gu = gateup_cfg(a), dn = down_cfg(a);
-    cudaError_t e = finish_cfg(gateup_kernel<NPG>, gu);
+template <int NPG, int NG>
+cudaError_t launch_gateup(const LayerArgs& a, const Ws& W, cudaStream_t s) {
+    StreamCfg c = gateup_cfg(a);
+    cudaError_t e = finish_cfg(gateup_kernel<NPG, NG>, c);
     if (e != cudaSuccess) return e;
-    if ((e = finish_cfg(down_kernel<NPG>, dn)) != cudaSuccess) return e;
-    e = launch(gateup_kernel<NPG>, dim3(gu.blocks), dim3(kStreamCta), gu.smem, s, a, W,
-               gu.stages, gu.stage_bytes);
-    if (e == cudaSuccess) e = launch_hquant(a, W, s);
+    return launch(gateup_kernel<NPG, NG>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a, W,
+                  c.stages, c.stage_bytes);
+}
+
+template <int NPG, int NG>
+cudaError_t launch_down(const LayerArgs& a, const Ws& W, cudaStream_t s) {
+    StreamCfg c = down_cfg(a);
+    cudaError_t e = finish_cfg(down_kernel<NPG, NG>, c);
     if (e != cudaSuccess) return e;
-    return launch(down_kernel<NPG>, dim3(dn.blocks), dim3(kStreamCta), dn.smem, s, a, W,
-                  dn.stages, dn.stage_bytes);
+    return launch(down_kernel<NPG, NG>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a, W,
+                  c.stages, c.stage_bytes);
+}
+
+cudaError_t launch_gateup_any(int npg, int ng, const LayerArgs& a, const Ws& W,
+                          cudaStream_t s) {
+    switch (npg * 100 + ng) {
+        case 101: return launch_gateup<1, 1>(a, W, s);
+        case 102: return launch_gateup<1, 2>(a, W, s);
+        case 104: return launch_gateup<1, 4>(a, W, s);
+        case 108: return launch_gateup<1, 8>(a, W, s);
+        case 116: return launch_gateup<1, 16>(a, W, s);
+        case 201: return launch_gateup<2, 1>(a, W, s);
+        case 202: return launch_gateup<2, 2>(a, W, s);
+        case 204: return launch_gateup<2, 4>(a, W, s);
+        case 208: return launch_gateup<2, 8>(a, W, s);
+        case 214: return launch_gateup<2, 14>(a, W, s);
+        case 216: return launch_gateup<2, 16>(a, W, s);
+        case 401: return launch_gateup<4, 1>(a, W, s);
+        case 402: return launch_gateup<4, 2>(a, W, s);
+        case 404: return launch_gateup<4, 4>(a, W, s);
+        case 408: return launch_gateup<4, 8>(a, W, s);
+        default: return cudaErrorInvalidConfiguration;
+    }
+}
+
+cudaError_t launch_down_any(int npg, int ng, const LayerArgs& a, const Ws& W,
+                          cudaStream_t s) {
+    switch (npg * 100 + ng) {
+        case 101: return launch_down<1, 1>(a, W, s);
+        case 102: return launch_down<1, 2>(a, W, s);
+        case 104: return launch_down<1, 4>(a, W, s);
+        case 108: return launch_down<1, 8>(a, W, s);
+        case 116: return launch_down<1, 16>(a, W, s);
+        case 201: return launch_down<2, 1>(a, W, s);
+        case 202: return launch_down<2, 2>(a, W, s);
+        case 204: return launch_down<2, 4>(a, W, s);
+        case 208: return launch_down<2, 8>(a, W, s);
+        case 214: return launch_down<2, 14>(a, W, s);
+        case 216: return launch_down<2, 16>(a, W, s);
+        case 401: return launch_down<4, 1>(a, W, s);
+        case 402: return launch_down<4, 2>(a, W, s);
+        case 404: return launch_down<4, 4>(a, W, s);
+        case 408: return launch_down<4, 8>(a, W, s);
+        default: return cudaErrorInvalidConfiguration;
+    }
 }
 
 cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t s) {
     (void)T;
-    switch (a.gs / kChunk) {
-        case 1: return launch_streams_npg<1>(a, W, s);
-        case 2: return launch_streams_npg<2>(a, W, s);
-        default: return launch_streams_npg<4>(a, W, s);
-    }
+    const int npg = a.gs / kChunk;
+    cudaError_t e = launch_gateup_any(npg, ng_bucket(npg, a.H / a.gs), a, W, s);
+    if (e == cudaSuccess) e = launch_hquant(a, W, s);
+    if (e != cudaSuccess) return e;
+    return launch_down_any(npg, ng_bucket(npg, a.I / a.gs / a.kp), a, W, s);
 }
 
 cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* xin,
@@ -1580,7 +1718,7 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe block: x NULL or not 16-byte aligned");
         return WISP_ERR_INVALID_ARG;
     }
-    LayerArgs a = layer_args(layer);
+    LayerArgs a = layer_args(layer, T, dev_info().sms);
     Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
     Ws W = make_ws(workspace, lo);
     if (topk_idx) W.topk_idx = topk_idx;
@@ -1598,7 +1736,9 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
 
 // gate/up + down + combine, on the plan the preceding route left in the workspace.
 static WispError block_experts(const LayerArgs& a, const Ws& W, int T, const float* x, float* y,
-                               cudaStream_t stream, WispErrCtx* err) {
+                               cudaStream_t stream, WispErrCtx* err, bool resolve = false) {
+    if (resolve)
+        WB_CUDA_RET(launch(resolve_kernel, dim3(1), dim3(kThreads), 0, stream, a, W), err);
     WB_CUDA_RET(launch_streams(a, W, T, stream), err);
     Ws Wc = W;
     Wc.prev_idx = W.topk_idx;
@@ -1649,13 +1789,13 @@ extern "C" WispError wisp_moe_block_experts(const WispMoeLayer* layer, const flo
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_block_experts: bad x/y");
         return WISP_ERR_INVALID_ARG;
     }
-    LayerArgs a = layer_args(layer);
+    LayerArgs a = layer_args(layer, T, dev_info().sms);
     Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
     Ws W = make_ws(workspace, lo);
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    return block_experts(a, W, T, x, y, stream, err);
+    return block_experts(a, W, T, x, y, stream, err, /*resolve=*/true);
 }
 
 extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_layers, float eps,
@@ -1688,7 +1828,7 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
     WB_CUDA_RET(cudaMemsetAsync(workspace, 0, sizeof(int), stream), err);
     int prevK = 0, prev_sh = 0, prev_kp = 1;
     for (int l = 0; l < n_layers; ++l) {
-        LayerArgs a = layer_args(&layers[l]);
+        LayerArgs a = layer_args(&layers[l], T, dev_info().sms);
         Layout lo = make_layout(T, H, maxI, maxE, maxK, anysh);
         Ws W = make_ws(workspace, lo);
         // previous layer's routing lives in the "current" slots until this
@@ -1734,7 +1874,7 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
 // allocating library routine is called.
 //
 // Limits: the array holds kStaticScratchBytes (8 MiB), enough for a
-// Mixtral-shaped layer (hidden 4096, intermediate 14336, top-2) up to T = 6;
+// Mixtral-shaped layer (hidden 4096, intermediate 14336, top-2) up to T = 16;
 // larger requests are rejected with WISP_ERR_INVALID_ARG before any GPU work.
 // Every call on a device shares the one array, so two calls whose kernels
 // overlap on the GPU (different streams, or different host threads without

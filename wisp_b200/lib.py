@@ -28,7 +28,7 @@ class WispExpertMeta(C.Structure):
     _fields_ = [("packed_off", C.c_size_t * 3), ("scales_off", C.c_size_t * 3),
                 ("zeros_off", C.c_size_t * 3), ("rows", C.c_uint32 * 3),
                 ("cols", C.c_uint32 * 3), ("group_size", C.c_uint32),
-                ("total_bytes", C.c_size_t), ("valid", C.c_int)]
+                ("total_bytes", C.c_size_t), ("valid", C.c_int), ("tiled", C.c_int)]
 
 
 class WispMoeLayer(C.Structure):
@@ -57,6 +57,8 @@ _SIGS = {
     "wisp_moe_block_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
                                          C.POINTER(WispErrCtx)]),
+    "wisp_expert_tile": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.POINTER(WispErrCtx)]),
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),

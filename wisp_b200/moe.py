@@ -51,13 +51,15 @@ def blob_bytes_of(mats: dict[str, cv.QMat]) -> int:
 
 
 class ExpertArena:
-    """One device allocation of fixed-size expert slots (blob at slot + 8)."""
+    """One device allocation of fixed-size expert slots (blob at slot + 8), holding
+    blobs in the tiled device layout (``wisp_expert_tile``)."""
 
     def __init__(self, n_slots: int, blob_bytes: int, device):
         self.slot_bytes = _round_up(blob_bytes + 8, 256)
         self.blob_bytes = blob_bytes
         self.n = n_slots
         self.buf = torch.empty(n_slots * self.slot_bytes, dtype=torch.uint8, device=device)
+        self._tmp = torch.empty(self.slot_bytes, dtype=torch.uint8, device=device)
 
     def blob(self, i: int) -> torch.Tensor:
         o = i * self.slot_bytes + 8
@@ -67,7 +69,8 @@ class ExpertArena:
         return self.buf.data_ptr() + i * self.slot_bytes + 8
 
     def write(self, i: int, layer: int, expert: int, mats: dict[str, cv.QMat]) -> None:
-        dst = self.blob(i)
+        """Assemble the .bin blob in a staging slot, then tile it into slot i."""
+        dst = self._tmp[8:8 + self.blob_bytes]
         head = blob_header(layer, expert, mats)
         dst[:cv.HEADER_BYTES].copy_(torch.frombuffer(bytearray(head), dtype=torch.uint8))
         off = cv.HEADER_BYTES
@@ -77,6 +80,11 @@ class ExpertArena:
                 n = t.numel()
                 dst[off:off + n].copy_(t.reshape(-1), non_blocking=True)
                 off += n
+        meta = parse_meta(head, self.blob_bytes)
+        err = WispErrCtx()
+        check(lib().wisp_expert_tile(C.byref(meta), dst.data_ptr(), self.ptr(i),
+                                     torch.cuda.current_stream(self.buf.device).cuda_stream,
+                                     C.byref(err)), err)
 
 
 @dataclass
@@ -205,7 +213,9 @@ class MoEStack:
 
     # ------------------------------------------------------------------ oracle views
     def host_blobs(self, l: int) -> list[np.ndarray]:
-        return [self.arena.blob(s).cpu().numpy().copy() for s in self.layers[l].slots]
+        """The layer's expert blobs as .bin bytes (read back from the device and
+        untiled), for the CPU oracle."""
+        return [cv.untile_blob(self.arena.blob(s).cpu().numpy()) for s in self.layers[l].slots]
 
     def host_router(self, l: int) -> tuple[np.ndarray, np.ndarray | None]:
         lw = self.layers[l]
