@@ -252,7 +252,7 @@ def run_single(args, dev) -> dict:
 
     # per-kernel durations (profiling pass, events between launches)
     n_prof = 3
-    seq = ["prep", "router", "gateup", "hquant", "down"]  # launches per layer
+    seq = ["prep", "router", "gateup", "down"]  # launches per layer
     per = len(seq) * args.layers + 1
     n_ev = (per + 1) * n_prof + 4
     events = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -361,7 +361,7 @@ def run_single(args, dev) -> dict:
         out["parity"] = {"idx_equal": bool(np.array_equal(ig.cpu().numpy(), iref)),
                          "max_abs": float(np.abs(yg - yref).max()),
                          "rel_l2": float(np.linalg.norm(yg - yref) / np.linalg.norm(yref))}
-    out["gpu_launches_per_step"] = 5 * args.layers + 1
+    out["gpu_launches_per_step"] = 4 * args.layers + 1
     del g
     return out
 

@@ -18,13 +18,16 @@
 //   router_kernel  partial logits per (expert, 1024-slice); the last CTA does
 //                  softmax + top-k per token and builds the expert-tile plan
 //   gateup_kernel  h = silu(G.x) * (U.x) per routed (expert, token tile)
-//   hquant_kernel  quantise h
-//   down_kernel    ypart[part][assignment][row] = D.h over one K part
+//   down_kernel    ypart[part][assignment][row] = D.h over one K part (h is
+//                  quantised by the consuming warps)
 //   prep_kernel    (next layer, or the final combine) sum_j w_j * sum_parts
 //
-// Weight streaming (gate/up, down): a producer warp hands (tile, row block)
-// units from an atomic counter to a ring of shared-memory stages filled by
-// cp.async.bulk (TMA) copies; eight consumer warps split the unit's K range.
+// Weight streaming (gate/up, down): experts are in the tiled device layout
+// (expert_layout.cu).  Each CTA owns a contiguous range of units (two 8-row
+// blocks over a K range); its producer thread fills a ring of shared-memory
+// stages with four cp.async.bulk (TMA) copies per unit and stages each tile's
+// activations, eight consumer warps split the unit's K range on the tensor
+// cores, and a reducer warp sums their partials.
 //
 // Int4 arithmetic on the tensor cores.  Activations are split per quant
 // group into two int8 digits, x ~= k*a + (k/254)*b (|a|,|b| <= 127,
@@ -100,9 +103,6 @@ struct Ws {
     uint4* xq;      // [T][H/32][4]  activation digits
     float4* xqp;    // [T][H/gs]     (k/254, sum of quantised x, 0, 0) per group
     float* h;       // [A][I]
-    uint4* hq;      // [A][I/32][4]
-    float4* hqp;    // [A][I/gs]
-    int* hcnt;      // unused
     float* ypart;   // [kp][A][H]
     int A;          // assignment capacity
     int max_tiles;
@@ -648,9 +648,9 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint3
 
 // A streaming CTA: warp 0 = producer (lane 0), warp 1 = reducer, warps
 // 2 .. kNcw+1 = tensor-core consumers.
-constexpr int kNcw = 8;                           // consumer warps per CTA
+constexpr int kNcw = 16;                          // consumer warps per CTA
 constexpr int kStreamCta = 32 * (kNcw + 2);
-constexpr int kMaxWarpK = 1024;                   // K elements per consumer warp
+constexpr int kMaxWarpK = 512;                    // K elements per consumer warp
 constexpr int kMaxPartK = kNcw * kMaxWarpK;       // K elements per unit
 constexpr int kSkip = 0x40000000;                 // unit flag: weights unusable, contribute 0
 
@@ -675,13 +675,19 @@ __host__ __device__ inline uint32_t stage_bytes_of(const Geo& g) {
 __host__ __device__ inline size_t block_bytes_of(int cols, int gs) {
     return 4 * (size_t)cols + 32 * (size_t)(cols / gs);
 }
-// Activation tile of a K range of ng groups (NPG chunks each) for kMT token
-// slots: the quantised words [slot][chunk][64 B], then (k/254, S) per group
-// [slot][group][16 B].
-__host__ __device__ inline uint32_t act_row_bytes(int ng, int npg) { return (uint32_t)ng * npg * 64u; }
-__host__ __device__ inline uint32_t act_bytes_of(int ng, int npg) {
-    return kMT * (act_row_bytes(ng, npg) + (uint32_t)ng * 16u);
+// Activation tile of a K range of ng groups (NPG 32-element chunks each) for
+// kMT token slots.  Quantised (gate/up): the words [slot][chunk][64 B], then
+// (k/254, S) per group [slot][group][16 B].  Float (down): the fp32 rows
+// [slot][ng * gs], quantised by the consumer warps themselves.
+__host__ __device__ inline uint32_t act_row_bytes(int ng, int npg, bool f32) {
+    return (uint32_t)ng * npg * (f32 ? 128u : 64u);
 }
+__host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32) {
+    return kMT * (act_row_bytes(ng, npg, f32) + (f32 ? 0u : (uint32_t)ng * 16u));
+}
+// Per consumer warp scratch of the float path: one group of every slot in
+// the quantised word layout, and its (k/254, S).
+__host__ __device__ inline uint32_t qs_warp_bytes(int npg) { return kMT * (npg * 64u + 16u); }
 
 // Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
 // the end; the tile's token count and assignment ids (for the reducer).
@@ -695,6 +701,7 @@ struct StreamSmem {
     uint8_t* stages;   // [n_stages][stage_bytes]
     float2* red;       // [n_stages][kNcw][32] consumer partials
     uint8_t* act;      // activation tile (act_bytes_of)
+    uint8_t* qs;       // [kNcw][qs_warp_bytes] (float path)
     float2* kp;        // [kNcw][NGmax][kMT] (k/254, S) of each warp's groups
     UnitInfo* info;    // [n_stages]
     uint64_t* full;    // [n_stages] weights landed (tx)
@@ -702,28 +709,32 @@ struct StreamSmem {
     uint64_t* empty;   // [n_stages] stage reusable (reducer)
     uint64_t* act_full;
     uint64_t* act_empty;
-    uint32_t stage_bytes, act_row, act_bytes;
+    uint32_t stage_bytes, act_row, act_bytes, qs_warp;
     int n_stages;
 };
 __host__ __device__ constexpr size_t red_bytes_per_stage() { return (size_t)kNcw * 32 * 8; }
 constexpr size_t kKpBytes = (size_t)(kMaxPartK / 32) * 4 * 8;  // all groups x 4 slots
 __host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage_bytes,
-                                                     uint32_t act_bytes) {
+                                                     uint32_t act_bytes, uint32_t qs_bytes) {
     return (size_t)n_stages * (stage_bytes + red_bytes_per_stage() + sizeof(UnitInfo) + 24) +
-           act_bytes + kKpBytes + 16 + 128;
+           (act_bytes + 127) / 128 * 128 + qs_bytes + kKpBytes + 16 + 128;
 }
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
-                                                  uint32_t stage_bytes, const Geo& geo, int npg) {
+                                                  uint32_t stage_bytes, const Geo& geo, int npg,
+                                                  bool f32) {
     StreamSmem s;
     s.stage_bytes = stage_bytes;
     s.n_stages = n_stages;
-    s.act_row = act_row_bytes(geo.ng, npg);
-    s.act_bytes = act_bytes_of(geo.ng, npg);
+    s.act_row = act_row_bytes(geo.ng, npg, f32);
+    s.act_bytes = act_bytes_of(geo.ng, npg, f32);
+    s.qs_warp = f32 ? qs_warp_bytes(npg) : 0u;
     size_t o = 0;
     s.stages = base;
     o += (size_t)n_stages * stage_bytes;
     s.act = base + o;
     o += (s.act_bytes + 127) / 128 * 128;
+    s.qs = base + o;
+    o += (size_t)kNcw * s.qs_warp;
     s.red = reinterpret_cast<float2*>(base + o);
     o += (size_t)n_stages * red_bytes_per_stage();
     s.kp = reinterpret_cast<float2*>(base + o);
@@ -766,7 +777,8 @@ __device__ __forceinline__ void load_tile(const Tile* src, Tile& tl) {
 struct ActSrc {
     const uint8_t* xq;
     const float4* xqp;
-    int nchk, ngrp, kg0, npg;
+    const float* xf;   // fp32 rows instead (float path), row_elems per row
+    int nchk, ngrp, kg0, npg, gs, row_elems;
     bool by_asg;
 };
 
@@ -782,8 +794,11 @@ template <typename Blk>
 __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
                         int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
                         Blk blk) {
+    const int lane = threadIdx.x & 31;
     const uint32_t tx = 2 * geo.bbytes, zb = (uint32_t)geo.ng * 32u;
-    const uint32_t rowb = act_row_bytes(geo.ng, as.npg), pb = (uint32_t)geo.ng * 16u;
+    const bool f32 = as.xf != nullptr;
+    const uint32_t rowb = act_row_bytes(geo.ng, as.npg, f32);
+    const uint32_t pb = f32 ? 0u : (uint32_t)geo.ng * 16u;
     const uint64_t pol = evict_first_policy();
     int ti = u_begin / upt, r = u_begin - ti * upt;
     Tile cur, nxt;
@@ -791,21 +806,37 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
     if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
     int it = 0, tiles_done = 0;
     bool ok = true, act_due = true, waited_pdl = !act_after_pdl;
-    // activation tile of `cur`, once the consumers copied the previous one
+    // barrier waits by lane 0, result shared with the warp
+    auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
+        int v = 1;
+        if (lane == 0) v = mbar_wait(bar, parity) ? 1 : 0;
+        return __shfl_sync(kFull, v, 0) != 0;
+    };
+    // activation tile of `cur`, once the consumers copied the previous one;
+    // one copy per lane
     auto issue_act = [&]() -> bool {
         if (!waited_pdl) {
             pdl_wait();
             waited_pdl = true;
         }
-        if (tiles_done > 0 && !mbar_wait(S.act_empty, (tiles_done - 1) & 1)) return false;
-        mbar_expect_tx(S.act_full, (uint32_t)cur.m * (rowb + pb));
-        for (int t = 0; t < cur.m; ++t) {
+        if (tiles_done > 0 && !wait0(S.act_empty, (tiles_done - 1) & 1)) return false;
+        if (lane == 0) mbar_expect_tx(S.act_full, (uint32_t)cur.m * (rowb + pb));
+        __syncwarp();
+        const int per = f32 ? 1 : 2, t = lane / per;
+        if (t < cur.m) {
             const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
-            bulk_g2s_plain(S.act + t * rowb,
-                           as.xq + ((size_t)row * as.nchk + (size_t)as.kg0 * as.npg) * 64, rowb,
-                           S.act_full);
-            bulk_g2s_plain(S.act + kMT * rowb + t * pb, as.xqp + (size_t)row * as.ngrp + as.kg0,
-                           pb, S.act_full);
+            if (f32) {
+                bulk_g2s_plain(S.act + t * rowb,
+                               as.xf + (size_t)row * as.row_elems + (size_t)as.kg0 * as.gs, rowb,
+                               S.act_full);
+            } else if ((lane & 1) == 0) {
+                bulk_g2s_plain(S.act + t * rowb,
+                               as.xq + ((size_t)row * as.nchk + (size_t)as.kg0 * as.npg) * 64,
+                               rowb, S.act_full);
+            } else {
+                bulk_g2s_plain(S.act + kMT * rowb + t * pb,
+                               as.xqp + (size_t)row * as.ngrp + as.kg0, pb, S.act_full);
+            }
         }
         ++tiles_done;
         act_due = false;
@@ -813,13 +844,15 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
     };
     for (int u = u_begin;; ++u, ++it) {
         const int s = it % S.n_stages;
-        if (!mbar_wait(&S.empty[s], ((it / S.n_stages) & 1) ^ 1)) {
+        if (!wait0(&S.empty[s], ((it / S.n_stages) & 1) ^ 1)) {
             ok = false;
             break;
         }
         if (u >= u_end) {
-            S.info[s].u = -1;
-            mbar_arrive(&S.full[s]);
+            if (lane == 0) {
+                S.info[s].u = -1;
+                mbar_arrive(&S.full[s]);
+            }
             break;
         }
         if (r == upt) {
@@ -833,32 +866,27 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             ok = false;
             break;
         }
-        UnitInfo& inf = S.info[s];
-        inf.m = cur.m;
+        // lanes 0-3 each issue one of the unit's four copies
+        const unsigned char* p = (lane < 4 && cur.blob) ? blk(cur.blob, r, lane) : nullptr;
+        const bool misaligned = __any_sync(kFull, p && !aligned16(p));
+        const bool good = cur.blob != nullptr && !misaligned;
+        if (lane == 0) {
+            UnitInfo& inf = S.info[s];
+            inf.m = cur.m;
 #pragma unroll
-        for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
-        const unsigned char* p[4] = {nullptr, nullptr, nullptr, nullptr};
-        bool good = cur.blob != nullptr;
-        if (good) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                p[c] = blk(cur.blob, r, c);
-                if (!aligned16(p[c])) {
-                    good = false;
-                    atomicOr(W.status, ST_ALIGN);
-                }
-            }
+            for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
+            inf.u = good ? u : (u | kSkip);
+            if (misaligned) atomicOr(W.status, ST_ALIGN);
+            if (good)
+                mbar_expect_tx(&S.full[s], tx);
+            else
+                mbar_arrive(&S.full[s]);
         }
-        inf.u = good ? u : (u | kSkip);
-        if (good) {
-            mbar_expect_tx(&S.full[s], tx);
-            uint8_t* dst = S.stages + (size_t)s * S.stage_bytes;
-            bulk_g2s(dst, p[0], geo.pbytes, &S.full[s], pol);
-            bulk_g2s(dst + geo.pbytes, p[1], zb, &S.full[s], pol);
-            bulk_g2s(dst + geo.bbytes, p[2], geo.pbytes, &S.full[s], pol);
-            bulk_g2s(dst + geo.bbytes + geo.pbytes, p[3], zb, &S.full[s], pol);
-        } else {
-            mbar_arrive(&S.full[s]);
+        __syncwarp();
+        if (good && lane < 4) {
+            uint8_t* dst = S.stages + (size_t)s * S.stage_bytes + (lane >> 1) * geo.bbytes +
+                           (lane & 1) * geo.pbytes;
+            bulk_g2s(dst, p, (lane & 1) ? zb : geo.pbytes, &S.full[s], pol);
         }
         ++r;
         // a deferred first activation tile: once the stages are full, or before
@@ -869,7 +897,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             break;
         }
     }
-    if (!ok) {
+    if (!ok && lane == 0) {
         atomicOr(W.status, ST_TIMEOUT);
         // a consumer stopped early: let every issued copy land before exiting
         for (int k = 0; k < S.n_stages && k < it; ++k) {
@@ -1017,6 +1045,55 @@ __device__ __forceinline__ void load_act(WarpAct<NPG, NG>& A, float2* kp_w, cons
     __syncwarp();
 }
 
+// Float path: quantise the warp's groups of the staged fp32 rows (slots
+// t < m) with the activation quantiser (quantize_block, one group of a slot
+// per gs/4 lanes), one group at a time through the warp's scratch, and take
+// the B fragments and (k/254, S) pairs from there.
+template <int NPG, int NG>
+__device__ __forceinline__ void load_act_quant(WarpAct<NPG, NG>& A, float2* kp_w,
+                                               const StreamSmem& S, int g0, int n, int m,
+                                               int cw) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    const int bt = g >> 1, bd = g & 1;
+    constexpr int kGs = 32 * NPG, kLpb = kGs / 4, kPer = 32 / kLpb;  // lanes / group, groups / pass
+    uint8_t* qs = S.qs + cw * S.qs_warp;
+    float4* qpar = reinterpret_cast<float4*>(qs + kMT * NPG * 64);
+    const uint32_t qbase = smem_addr(qs) + bt * (NPG * 64) + bd * 32;
+    const float* rows = reinterpret_cast<const float*>(S.act);
+    const int row_elems = (int)(S.act_row / 4);
+#pragma unroll
+    for (int G = 0; G < NG; ++G) {
+#pragma unroll
+        for (int p0 = 0; p0 < kMT; p0 += kPer) {
+            if (p0 < m) {
+                const int t = p0 + lane / kLpb, pos = (lane % kLpb) * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (G < n && t < m)
+                    v = *reinterpret_cast<const float4*>(rows + t * row_elems + (g0 + G) * kGs + pos);
+                quantize_block(v, kLpb,
+                               reinterpret_cast<uint32_t*>(qs + t * (NPG * 64) + (pos / kChunk) * 64),
+                               qpar + t, pos == 0);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < NPG; ++i) {
+            const int wi = q * NPG + i;
+            A.b[G][i] = (G < n && bt < m) ? lds64(qbase + (wi >> 2) * 64 + (wi & 3) * 8)
+                                          : make_uint2(0u, 0u);
+        }
+        if (lane < kMT) {
+            float2 v = make_float2(0.f, 0.f);
+            if (G < n && lane < m) {
+                const float4 pr = qpar[lane];
+                v = make_float2(pr.x, pr.y);
+            }
+            kp_w[G * kMT + lane] = v;
+        }
+        __syncwarp();
+    }
+}
+
 // This warp's partial dot products of a unit: acc.x = MMA row g (block A),
 // acc.y = row g+8 (block B), for token slot q.  `st`: the stage (shared
 // address); groups g0 .. g0+NG-1 of the unit's range (those past the range
@@ -1065,8 +1142,8 @@ __device__ __forceinline__ float2 mma_unit(uint32_t st, const Geo& geo, int g0,
     return acc;
 }
 
-// Consumer loop: `upt` units per tile.
-template <int NPG, int NG>
+// Consumer loop: `upt` units per tile; F32: the activation tile is fp32.
+template <int NPG, int NG, bool F32>
 __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int upt) {
     const int lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 2;
     const int g0 = cw * geo.ng / kNcw, n = (cw + 1) * geo.ng / kNcw - g0;
@@ -1091,7 +1168,10 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
                 if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
                 break;
             }
-            load_act<NPG, NG>(A, kp_w, S, g0, n, inf.m);
+            if constexpr (F32)
+                load_act_quant<NPG, NG>(A, kp_w, S, g0, n, inf.m, cw);
+            else
+                load_act<NPG, NG>(A, kp_w, S, g0, n, inf.m);
             if (lane == 0) mbar_arrive(S.act_empty);
             ++tiles;
             cur = ti;
@@ -1113,7 +1193,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int H = L.H, I = L.I, gs = L.gs;
     const Geo geo = make_geo(H / gs, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false);
     stream_init(S);
     pdl_wait();
     pdl_launch();
@@ -1123,13 +1203,13 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const long long total = (long long)ntiles * rbs;
 
     if (warp == 0) {
-        if ((threadIdx.x & 31) == 0) {
+        {
             const int b = (int)(total * blockIdx.x / gridDim.x);
             const int e = (int)(total * (blockIdx.x + 1) / gridDim.x);
             const size_t bb = block_bytes_of(H, gs);
             const size_t off_g = L.mat[0].packed, off_u = L.mat[1].packed;
-            const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, H / kChunk, H / gs, 0,
-                            NPG, false};
+            const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, nullptr, H / kChunk,
+                            H / gs, 0, NPG, gs, H, false};
             produce(S, W, b, e, rbs, ntiles, geo, as, false,
                     [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
                         const unsigned char* blk = blob + (c < 2 ? off_g : off_u) + (size_t)r * bb;
@@ -1145,26 +1225,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         });
         return;
     }
-    consume<NPG, NG>(S, W, geo, rbs);
-}
-
-// ------------------------------------------------------------------------
-// h quantiser: every quant group of h (all assignments), 128 elements per
-// warp.
-// ------------------------------------------------------------------------
-__global__ void __launch_bounds__(kPrepThreads)
-hquant_kernel(LayerArgs L, Ws W) {
-    pdl_wait();
-    pdl_launch();
-    const int I = L.I;
-    const int warps = kPrepThreads / 32;
-    const int per_a = (I + 127) / 128;  // warps per assignment row
-    const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
-    const int a = gw / per_a;
-    if (a >= W.A) return;
-    const int wi = gw % per_a;
-    quantize_row(reinterpret_cast<const float4*>(W.h + (size_t)a * I), I, L.gs, wi, per_a,
-                 W.hq + (size_t)a * (I / kChunk) * 4, W.hqp + (size_t)a * (I / L.gs));
+    consume<NPG, NG, false>(S, W, geo, rbs);
 }
 
 // ------------------------------------------------------------------------
@@ -1181,12 +1242,13 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int H = L.H, I = L.I, gs = L.gs;
     const int ngp = I / gs / kp;  // groups per part
     const Geo geo = make_geo(ngp, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true);
     stream_init(S);
     // Weights, the expert table and the tile plan (written by the router,
-    // which completed before the gate/up kernel preceding the quantiser could
-    // start) do not depend on the previous kernel (the h quantiser): the
-    // producer waits for it only before the first activation copy.
+    // which completed before the gate/up kernel could start) do not depend on
+    // the previous kernel (gate/up, which writes h): the producer waits for it
+    // only before the first activation copy, so these CTAs start streaming
+    // weights on SMs that gate/up's CTAs have already left.
     pdl_launch();
     const int warp = threadIdx.x >> 5;
     const int pi = blockIdx.x % kp;
@@ -1196,15 +1258,14 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const long long total = (long long)ntiles * upt;
 
     if (warp == 0) {
-        if ((threadIdx.x & 31) == 0) {
+        {
             const int j = blockIdx.x / kp;
             const int b = (int)(total * j / cpp), e = (int)(total * (j + 1) / cpp);
             const size_t bb = block_bytes_of(I, gs);
             const size_t off_d = L.mat[2].packed;
             const size_t z_off = 4 * (size_t)I + (size_t)pi * geo.ng * 32;
             const size_t p_off = (size_t)pi * geo.pbytes;
-            const ActSrc as{reinterpret_cast<const uint8_t*>(W.hq), W.hqp, I / kChunk, I / gs,
-                            pi * ngp, NPG, true};
+            const ActSrc as{nullptr, nullptr, W.h, I / kChunk, I / gs, pi * ngp, NPG, gs, I, true};
             produce(S, W, b, e, upt, ntiles, geo, as, true,
                     [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
                         const unsigned char* blk = blob + off_d + (size_t)(2 * r + (c >> 1)) * bb;
@@ -1222,7 +1283,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         });
         return;
     }
-    consume<NPG, NG>(S, W, geo, upt);
+    consume<NPG, NG, true>(S, W, geo, upt);
 }
 
 // ------------------------------------------------------------------------
@@ -1230,7 +1291,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
 // ------------------------------------------------------------------------
 struct Layout {
     size_t status, counters, tok_cnt, logits, topk_idx, topk_w, pidx, pw, tiles,
-        xn, xq, xqp, h, hq, hqp, hcnt, ypart, total;
+        xn, xq, xqp, h, ypart, total;
     int A, max_tiles;
 };
 
@@ -1259,9 +1320,6 @@ Layout make_layout(int T, int H, int I, int E, int K, bool shared) {
     l.xq = take((size_t)T * (H / kChunk) * 64);
     l.xqp = take((size_t)T * (H / kChunk) * sizeof(float4));  // >= per-group params
     l.h = take((size_t)l.A * I * sizeof(float));
-    l.hq = take((size_t)l.A * (I / kChunk) * 64);
-    l.hqp = take((size_t)l.A * (I / kChunk) * sizeof(float4));
-    l.hcnt = take((size_t)l.A * (I / kChunk) * sizeof(int));
     l.ypart = take((size_t)kMaxKp * l.A * H * sizeof(float));
     l.total = o;
     return l;
@@ -1283,9 +1341,6 @@ Ws make_ws(void* base, const Layout& l) {
     w.xq = reinterpret_cast<uint4*>(b + l.xq);
     w.xqp = reinterpret_cast<float4*>(b + l.xqp);
     w.h = reinterpret_cast<float*>(b + l.h);
-    w.hq = reinterpret_cast<uint4*>(b + l.hq);
-    w.hqp = reinterpret_cast<float4*>(b + l.hqp);
-    w.hcnt = reinterpret_cast<int*>(b + l.hcnt);
     w.ypart = reinterpret_cast<float*>(b + l.ypart);
     w.A = l.A;
     w.max_tiles = l.max_tiles;
@@ -1301,8 +1356,8 @@ MatOff mat_off(const WispExpertMeta& m, int i) {
 // NPG = gs / 32); a warp's actual count is rounded up to the next one and the
 // rest masked.
 constexpr int kNgSet1[] = {1, 2, 4, 8, 16};
-constexpr int kNgSet2[] = {1, 2, 4, 8, 14, 16};
-constexpr int kNgSet4[] = {1, 2, 4, 8};
+constexpr int kNgSet2[] = {1, 2, 4, 7, 8};
+constexpr int kNgSet4[] = {1, 2};
 template <size_t N>
 int bucket_in(const int (&set)[N], int need) {
     for (size_t i = 0; i < N; ++i)
@@ -1427,28 +1482,29 @@ constexpr size_t kSmemPerCta = 227 * 1024;
 // 2, at most 8, within the shared memory left after the activation tile.
 constexpr size_t kInFlight = 160 * 1024;
 
-StreamCfg plan_stream(const Geo& geo, int npg) {
+StreamCfg plan_stream(const Geo& geo, int npg, bool f32) {
     StreamCfg c;
     c.stage_bytes = stage_bytes_of(geo);
-    const uint32_t act = act_bytes_of(geo.ng, npg);
+    const uint32_t act = act_bytes_of(geo.ng, npg, f32);
+    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg) : 0u;
     int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
     want = std::max(2, std::min(8, want));
     c.stages = 0;
     for (int st = want; st >= 2; --st)
-        if (stream_smem_bytes(st, c.stage_bytes, act) <= kSmemPerCta) {
+        if (stream_smem_bytes(st, c.stage_bytes, act, qs) <= kSmemPerCta) {
             c.stages = st;
             break;
         }
-    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act);
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs);
     return c;
 }
 
 StreamCfg gateup_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk);
+    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk, false);
 }
 
 StreamCfg down_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk);
+    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk, true);
 }
 
 // K parts of the down projection.  A part is a whole number of quant groups
@@ -1469,7 +1525,7 @@ int down_parts(int I, int gs, long long units, int ctas) {
         const double per = (double)units * kp / (double)ctas;
         const double bal = per > 0 ? per / std::ceil(per) : 1.0;
         // a shallow ring (big stages) starves the consumers while a stage turns over
-        const int st = plan_stream(make_geo(ngp, gs), npg).stages;
+        const int st = plan_stream(make_geo(ngp, gs), npg, true).stages;
         const double depth = std::min(1.0, st / 4.0);
         const double score = eff * bal * depth * (1.0 - 0.01 * kp);
         if (score > best_score + 1e-9) {
@@ -1553,12 +1609,6 @@ cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, c
 }
 
 
-cudaError_t launch_hquant(const LayerArgs& a, const Ws& W, cudaStream_t s) {
-    const int per_a = (a.I + 127) / 128;
-    const int warps = W.A * per_a;
-    const int wpc = kPrepThreads / 32;
-    return launch(hquant_kernel, dim3((warps + wpc - 1) / wpc), dim3(kPrepThreads), 0, s, a, W);
-}
 
 template <int NPG, int NG>
 cudaError_t launch_gateup(const LayerArgs& a, const Ws& W, cudaStream_t s) {
@@ -1589,13 +1639,10 @@ cudaError_t launch_gateup_any(int npg, int ng, const LayerArgs& a, const Ws& W,
         case 201: return launch_gateup<2, 1>(a, W, s);
         case 202: return launch_gateup<2, 2>(a, W, s);
         case 204: return launch_gateup<2, 4>(a, W, s);
+        case 207: return launch_gateup<2, 7>(a, W, s);
         case 208: return launch_gateup<2, 8>(a, W, s);
-        case 214: return launch_gateup<2, 14>(a, W, s);
-        case 216: return launch_gateup<2, 16>(a, W, s);
         case 401: return launch_gateup<4, 1>(a, W, s);
         case 402: return launch_gateup<4, 2>(a, W, s);
-        case 404: return launch_gateup<4, 4>(a, W, s);
-        case 408: return launch_gateup<4, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
@@ -1611,13 +1658,10 @@ cudaError_t launch_down_any(int npg, int ng, const LayerArgs& a, const Ws& W,
         case 201: return launch_down<2, 1>(a, W, s);
         case 202: return launch_down<2, 2>(a, W, s);
         case 204: return launch_down<2, 4>(a, W, s);
+        case 207: return launch_down<2, 7>(a, W, s);
         case 208: return launch_down<2, 8>(a, W, s);
-        case 214: return launch_down<2, 14>(a, W, s);
-        case 216: return launch_down<2, 16>(a, W, s);
         case 401: return launch_down<4, 1>(a, W, s);
         case 402: return launch_down<4, 2>(a, W, s);
-        case 404: return launch_down<4, 4>(a, W, s);
-        case 408: return launch_down<4, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
@@ -1626,7 +1670,6 @@ cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t 
     (void)T;
     const int npg = a.gs / kChunk;
     cudaError_t e = launch_gateup_any(npg, ng_bucket(npg, a.H / a.gs), a, W, s);
-    if (e == cudaSuccess) e = launch_hquant(a, W, s);
     if (e != cudaSuccess) return e;
     return launch_down_any(npg, ng_bucket(npg, a.I / a.gs / a.kp), a, W, s);
 }

@@ -141,5 +141,5 @@ def bench_main(args) -> None:
                        "global_batch": global_batch, "parallelism": f"pp{world}",
                        "micro_batches": M, "layers_per_rank": per,
                        "l2": "weights per step exceed L2"},
-            "gpu_launches": (5 * per + 1) * M * args.steps,
+            "gpu_launches": (4 * per + 1) * M * args.steps,
             "wall_s_timed": round(t_wall, 3)}), flush=True)
