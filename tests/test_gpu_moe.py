@@ -164,3 +164,30 @@ def test_untiled_blobs_are_refused_on_the_device(cuda):
     st.block(0, x)
     torch.cuda.synchronize()
     assert st.status() == 0
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_separate_router_kernel_path(cuda, T, monkeypatch):
+    """Layers whose router would be re-read too often inside prep use the
+    separate router kernel: force it and check block and stack against the
+    oracle."""
+    monkeypatch.setenv("WISP_B200_PREP_ROUTER_BYTES", "0")
+    shape = cv.MoEShape(hidden=256, inter=512, n_experts=16, top_k=4, n_layers=2)
+    st = MoEStack(shape, seed=19, device=cuda, random_bias=True)
+    x = (torch.randn(T, 256, generator=torch.Generator().manual_seed(T))).half().float()
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 4, x.numpy())
+    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
+        check_outputs(y.cpu().numpy(), yr)
+    xs = x.clone().to(cuda)
+    xs2 = x.clone().to(cuda)
+    st.stack(xs)
+    monkeypatch.delenv("WISP_B200_PREP_ROUTER_BYTES")
+    st.stack(xs2)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    # the two router placements sum the logits in different orders
+    np.testing.assert_allclose(xs.cpu().numpy(), xs2.cpu().numpy(), rtol=1e-4, atol=1e-5)

@@ -5,6 +5,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <utility>
+
 #include "wisp_b200.h"
 
 #define WB_SET_ERR(ctx, c, ...)                                   \
@@ -36,20 +38,35 @@ int sm_count();
 // Launch `kern` with programmatic dependent launch enabled, so its prologue
 // may overlap the tail of the previous kernel on `stream`; the kernel must
 // call griddepcontrol.wait before touching its predecessor's outputs.
+// `cluster` > 1 launches thread-block clusters of that many CTAs along x.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block,
-                       size_t smem, cudaStream_t stream, Args&&... args) {
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, int cluster, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int n = 1;
+    if (cluster > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)cluster;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        n = 2;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block,
+                       size_t smem, cudaStream_t stream, Args&&... args) {
+    return launch_pdl_cluster(kern, grid, block, smem, stream, 1, std::forward<Args>(args)...);
 }
 
 }  // namespace wb

@@ -46,9 +46,12 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "internal.h"
+
+#include <cooperative_groups.h>
 
 namespace wb {
 namespace {
@@ -87,6 +90,7 @@ struct LayerArgs {
     MatOff smat[3];
     int H, I, E, K, gs, has_shared;
     int kp;   // K parts of the down projection
+    int act_slots;  // token slots of the staged activation tile (min(T, kMT))
 };
 
 struct Ws {
@@ -199,121 +203,21 @@ __device__ __forceinline__ void quantize_row(const float4* src, int n, int gs, i
 }
 
 // ------------------------------------------------------------------------
-// prep: combine + residual + RMSNorm + activation quantisation (per token)
-// ------------------------------------------------------------------------
-enum { P_COMBINE = 1, P_RESID = 2, P_NORM = 4, P_QUANT = 8 };
-constexpr int kPrepThreads = 1024;
-
-// One CTA per token, 1024 threads, float4 granules.
-__global__ void __launch_bounds__(kPrepThreads)
-prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, int prevK,
-            int prev_shared, int prev_kp) {
-    pdl_wait();
-    pdl_launch();
-    const int t = blockIdx.x;
-    const int H = L.H, n4 = H / 4;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float red[32];
-    __shared__ float s_scale;
-    __shared__ float s_w[64];
-    __shared__ int s_i[64];
-    extern __shared__ float4 sx4[];  // [H/4]
-    float4* xt = reinterpret_cast<float4*>(x + (size_t)t * H);
-
-    if (t == 0 && tid == 0) W.counters[C_TOK_DONE] = 0;
-    if (flags & P_COMBINE) {
-        if (tid < prevK) {
-            s_i[tid] = W.prev_idx[t * prevK + tid];
-            s_w[tid] = W.prev_w[t * prevK + tid];
-        }
-        __syncthreads();
-    }
-    const size_t part_stride = (size_t)W.A * H;
-    float ss = 0.f;
-    for (int i = tid; i < n4; i += kPrepThreads) {
-        float4 v = xt[i];
-        if (flags & P_COMBINE) {
-            // reference order: shared expert first (weight 1), then top-k order
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (prev_shared) {
-                const size_t a = (size_t)T * prevK + t;
-                for (int p = 0; p < prev_kp; ++p) {
-                    const float4 yv =
-                        reinterpret_cast<const float4*>(W.ypart + p * part_stride + a * H)[i];
-                    acc.x += yv.x; acc.y += yv.y; acc.z += yv.z; acc.w += yv.w;
-                }
-            }
-            for (int j = 0; j < prevK; ++j) {
-                if (s_i[j] < 0) continue;
-                const size_t a = (size_t)t * prevK + j;
-                float4 yj = reinterpret_cast<const float4*>(W.ypart + a * H)[i];
-                for (int p = 1; p < prev_kp; ++p) {
-                    const float4 yv =
-                        reinterpret_cast<const float4*>(W.ypart + p * part_stride + a * H)[i];
-                    yj.x += yv.x; yj.y += yv.y; yj.z += yv.z; yj.w += yv.w;
-                }
-                const float wj = s_w[j];
-                acc.x += wj * yj.x; acc.y += wj * yj.y; acc.z += wj * yj.z; acc.w += wj * yj.w;
-            }
-            if (flags & P_RESID) {
-                v.x += acc.x; v.y += acc.y; v.z += acc.z; v.w += acc.w;
-                xt[i] = v;
-            } else {
-                v = acc;
-            }
-            if (y) reinterpret_cast<float4*>(y + (size_t)t * H)[i] = v;
-        }
-        sx4[i] = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    }
-    if (!(flags & (P_NORM | P_QUANT))) return;
-    if (flags & P_NORM) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        if (warp == 0) {
-            float v = red[lane];
-            v = warp_sum(v);
-            if (lane == 0) s_scale = 1.0f / sqrtf(v / (float)H + eps);
-        }
-        __syncthreads();
-        const float sc = s_scale;
-        float4* xn = reinterpret_cast<float4*>(W.xn + (size_t)t * H);
-        const __half2* nw = reinterpret_cast<const __half2*>(L.norm_w);
-        for (int i = tid; i < n4; i += kPrepThreads) {
-            float4 v = sx4[i];
-            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
-            if (nw) {
-                const float2 a = __half22float2(nw[2 * i]), b = __half22float2(nw[2 * i + 1]);
-                v.x *= a.x; v.y *= a.y; v.z *= b.x; v.w *= b.y;
-            }
-            sx4[i] = v;
-            xn[i] = v;
-        }
-    }
-    __syncthreads();
-    if (flags & P_QUANT)
-        quantize_row(sx4, H, L.gs, warp, kPrepThreads / 32, W.xq + (size_t)t * (H / kChunk) * 4,
-                     W.xqp + (size_t)t * (H / L.gs));
-}
-
-// ------------------------------------------------------------------------
 // router: per-(expert, 1024-element slice) partial logits for every token,
 // then the last CTA to finish sums the slices (fixed order), adds the bias,
 // does softmax + top-k per token and builds the expert-tile plan.
 // ------------------------------------------------------------------------
 constexpr int kSlice = 1024;
 
-__device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, int nsl, float* sp,
-                           int* staken) {
-    // one warp; sp/staken: [E] shared scratch of this warp
+// Softmax + top-k of token t from its logits lg[E] (without the bias), by one
+// warp; sp/staken: [E] shared scratch of this warp.
+__device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, const float* lg,
+                           float* sp, int* staken) {
     const int lane = threadIdx.x & 31;
     const int E = L.E;
     float mx = -1e30f;
     for (int e = lane; e < E; e += 32) {
-        const float* pp = W.logits + ((size_t)t * E + e) * nsl;
-        float v = 0.f;
-        for (int s = 0; s < nsl; ++s) v += __ldcg(pp + s);
+        float v = lg[e];
         if (L.router_bias) v += __half2float(L.router_bias[e]);
         sp[e] = v;
         staken[e] = 0;
@@ -478,6 +382,167 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
     }
 }
 
+// ------------------------------------------------------------------------
+// prep: [combine the previous block's expert outputs + residual] [+ RMSNorm]
+// + quantise the activations [+ router logits, softmax + top-k and the tile
+// plan].  One thread-block cluster of cs CTAs per token; CTA r of a cluster
+// owns the slice [r*H/cs, (r+1)*H/cs) of the token (a whole number of quant
+// groups).  The RMSNorm sum of squares and the router logits are reduced
+// across the cluster through distributed shared memory in rank order
+// (deterministic).  With P_ROUTE, rank 0 of each cluster does the token's
+// softmax + top-k and the last token to finish builds the expert-tile plan.
+// ------------------------------------------------------------------------
+enum { P_COMBINE = 1, P_RESID = 2, P_NORM = 4, P_QUANT = 8, P_ROUTE = 16 };
+constexpr int kPrepThreads = 256;
+
+__host__ __device__ inline size_t prep_smem_bytes(int H, int cs, int E) {
+    return (size_t)(H / cs) * sizeof(float) + (size_t)E * sizeof(float) +
+           (size_t)(kMaxPlanAssign + 64 > 3 * E ? kMaxPlanAssign + 64 : 3 * E) * sizeof(int);
+}
+
+__global__ void __launch_bounds__(kPrepThreads)
+prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, int prevK,
+            int prev_shared, int prev_kp, int mt) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+    pdl_wait();
+    pdl_launch();
+    const int t = blockIdx.x / cs;
+    const int H = L.H, E = L.E;
+    const int n4 = H / 4 / cs, i0 = rank * n4;  // this CTA's float4 range of the row
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int nw = kPrepThreads / 32;
+    extern __shared__ float4 smem4[];
+    float4* sx4 = smem4;                                // [n4] the slice
+    float* s_lg = reinterpret_cast<float*>(sx4 + n4);  // [E] partial router logits
+    int* s_scr = reinterpret_cast<int*>(s_lg + E);      // top-k / plan scratch (rank 0)
+    __shared__ float red[nw];
+    __shared__ float s_ss;
+    __shared__ int s_last;
+    float4* xt = reinterpret_cast<float4*>(x + (size_t)t * H) + i0;
+
+    const size_t part_stride = (size_t)W.A * H;
+    float ss = 0.f;
+    for (int i = tid; i < n4; i += kPrepThreads) {
+        float4 v = xt[i];
+        if (flags & P_COMBINE) {
+            // reference order: shared expert first (weight 1), then top-k order
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (prev_shared) {
+                const size_t a = (size_t)T * prevK + t;
+                for (int p = 0; p < prev_kp; ++p) {
+                    const float4 yv = reinterpret_cast<const float4*>(
+                        W.ypart + p * part_stride + a * H)[i0 + i];
+                    acc.x += yv.x; acc.y += yv.y; acc.z += yv.z; acc.w += yv.w;
+                }
+            }
+            for (int j = 0; j < prevK; ++j) {
+                // loads do not wait for the routing; an unrouted slot is skipped by a select
+                const bool live = __ldg(W.prev_idx + t * prevK + j) >= 0;
+                const float wj = __ldg(W.prev_w + t * prevK + j);
+                const size_t a = (size_t)t * prevK + j;
+                float4 yj = reinterpret_cast<const float4*>(W.ypart + a * H)[i0 + i];
+                for (int p = 1; p < prev_kp; ++p) {
+                    const float4 yv = reinterpret_cast<const float4*>(
+                        W.ypart + p * part_stride + a * H)[i0 + i];
+                    yj.x += yv.x; yj.y += yv.y; yj.z += yv.z; yj.w += yv.w;
+                }
+                if (live) {
+                    acc.x += wj * yj.x; acc.y += wj * yj.y; acc.z += wj * yj.z; acc.w += wj * yj.w;
+                }
+            }
+            if (flags & P_RESID) {
+                v.x += acc.x; v.y += acc.y; v.z += acc.z; v.w += acc.w;
+                xt[i] = v;
+            } else {
+                v = acc;
+            }
+            if (y) reinterpret_cast<float4*>(y + (size_t)t * H)[i0 + i] = v;
+        }
+        sx4[i] = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    if (!(flags & (P_NORM | P_QUANT | P_ROUTE))) return;
+    if (flags & P_NORM) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float v = 0.f;
+            for (int w = 0; w < nw; ++w) v += red[w];
+            s_ss = v;
+        }
+        cl.sync();  // every CTA's partial sum of squares is in place
+        float tot = 0.f;
+        for (int r = 0; r < cs; ++r) tot += *cl.map_shared_rank(&s_ss, r);
+        const float sc = 1.0f / sqrtf(tot / (float)H + eps);
+        float4* xn = reinterpret_cast<float4*>(W.xn + (size_t)t * H) + i0;
+        const __half2* nw2 = reinterpret_cast<const __half2*>(L.norm_w) + 2 * i0;
+        for (int i = tid; i < n4; i += kPrepThreads) {
+            float4 v = sx4[i];
+            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+            if (L.norm_w) {
+                const float2 a = __half22float2(nw2[2 * i]), b = __half22float2(nw2[2 * i + 1]);
+                v.x *= a.x; v.y *= a.y; v.z *= b.x; v.w *= b.y;
+            }
+            sx4[i] = v;
+            xn[i] = v;
+        }
+    }
+    __syncthreads();
+    if (flags & P_QUANT)
+        quantize_row(sx4, n4 * 4, L.gs, warp, nw,
+                     W.xq + ((size_t)t * (H / kChunk) + (size_t)i0 * 4 / kChunk) * 4,
+                     W.xqp + (size_t)t * (H / L.gs) + (size_t)i0 * 4 / L.gs);
+    if (flags & P_ROUTE) {
+        // partial logits of this slice: warp per expert
+        const uint4* wr = reinterpret_cast<const uint4*>(L.router_w);
+        for (int e = warp; e < E; e += nw) {
+            const uint4* row = wr + ((size_t)e * H + (size_t)i0 * 4) / 8;
+            float acc = 0.f;
+            for (int c = lane; c < n4 / 2; c += 32) {
+                const uint4 wv = __ldg(row + c);
+                const float4 a = sx4[2 * c], b = sx4[2 * c + 1];
+                const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+                float2 f = __half22float2(w2[0]);
+                acc = fmaf(f.x, a.x, acc); acc = fmaf(f.y, a.y, acc);
+                f = __half22float2(w2[1]);
+                acc = fmaf(f.x, a.z, acc); acc = fmaf(f.y, a.w, acc);
+                f = __half22float2(w2[2]);
+                acc = fmaf(f.x, b.x, acc); acc = fmaf(f.y, b.y, acc);
+                f = __half22float2(w2[3]);
+                acc = fmaf(f.x, b.z, acc); acc = fmaf(f.y, b.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) s_lg[e] = acc;
+        }
+        cl.sync();  // every CTA's partial logits are in place
+        if (rank == 0)
+            for (int e = tid; e < E; e += kPrepThreads) {
+                float v = 0.f;
+                for (int r = 0; r < cs; ++r) v += cl.map_shared_rank(s_lg, r)[e];
+                s_scr[2 * E + e] = __float_as_int(v);
+            }
+    }
+    if (cs > 1 && (flags & (P_NORM | P_ROUTE))) cl.sync();  // peers read; CTAs may leave
+    if (!(flags & P_ROUTE) || rank != 0) return;
+    __syncthreads();
+    if (warp == 0)
+        topk_token(L, W, t, L.K, reinterpret_cast<const float*>(s_scr + 2 * E),
+                   reinterpret_cast<float*>(s_scr), s_scr + E);
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = T == 1 || atomicAdd(W.counters + C_TOK_DONE, 1) == T - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    build_plan(L, W, T, mt, s_scr, s_scr + kMaxPlanAssign);
+    if (tid == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
+}
+
 // Re-read every tile's blob pointer from the expert table (for a plan built
 // before the table was filled: the host-driven miss path).
 __global__ void __launch_bounds__(kThreads)
@@ -548,13 +613,25 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
     if (!s_last) return;
     __threadfence();
     {
-        float* sp = reinterpret_cast<float*>(smem) + (size_t)warp * 2 * E;
-        int* staken = smem + (size_t)warp * 2 * E + E;
-        for (int t = warp; t < T; t += kWarps) topk_token(L, W, t, L.K, nsl, sp, staken);
+        float* sp = reinterpret_cast<float*>(smem) + (size_t)warp * 3 * E;
+        int* staken = smem + (size_t)warp * 3 * E + E;
+        float* lg = sp + 2 * E;
+        for (int t = warp; t < T; t += kWarps) {
+            for (int e = lane; e < E; e += 32) {
+                const float* pp = W.logits + ((size_t)t * E + e) * nsl;
+                float v = 0.f;
+                for (int q = 0; q < nsl; ++q) v += __ldcg(pp + q);
+                lg[e] = v;
+            }
+            __syncwarp();
+            topk_token(L, W, t, L.K, lg, sp, staken);
+            __syncwarp();
+        }
     }
     __syncthreads();
     __threadfence();
     build_plan(L, W, T, mt, smem, smem + kMaxPlanAssign);
+    if (threadIdx.x == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
 }
 
 // ------------------------------------------------------------------------
@@ -682,8 +759,8 @@ __host__ __device__ inline size_t block_bytes_of(int cols, int gs) {
 __host__ __device__ inline uint32_t act_row_bytes(int ng, int npg, bool f32) {
     return (uint32_t)ng * npg * (f32 ? 128u : 64u);
 }
-__host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32) {
-    return kMT * (act_row_bytes(ng, npg, f32) + (f32 ? 0u : (uint32_t)ng * 16u));
+__host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32, int slots) {
+    return (uint32_t)slots * (act_row_bytes(ng, npg, f32) + (f32 ? 0u : (uint32_t)ng * 16u));
 }
 // Per consumer warp scratch of the float path: one group of every slot in
 // the quantised word layout, and its (k/254, S).
@@ -692,7 +769,7 @@ __host__ __device__ inline uint32_t qs_warp_bytes(int npg) { return kMT * (npg *
 // Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
 // the end; the tile's token count and assignment ids (for the reducer).
 struct UnitInfo {
-    int u, m;
+    int u, m, tile;  // tile: the tile whose m/asg the record holds
     int asg[kMT];
 };
 
@@ -710,6 +787,7 @@ struct StreamSmem {
     uint64_t* act_full;
     uint64_t* act_empty;
     uint32_t stage_bytes, act_row, act_bytes, qs_warp;
+    int act_slots;
     int n_stages;
 };
 __host__ __device__ constexpr size_t red_bytes_per_stage() { return (size_t)kNcw * 32 * 8; }
@@ -721,12 +799,13 @@ __host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage
 }
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
                                                   uint32_t stage_bytes, const Geo& geo, int npg,
-                                                  bool f32) {
+                                                  bool f32, int slots) {
     StreamSmem s;
     s.stage_bytes = stage_bytes;
     s.n_stages = n_stages;
     s.act_row = act_row_bytes(geo.ng, npg, f32);
-    s.act_bytes = act_bytes_of(geo.ng, npg, f32);
+    s.act_bytes = act_bytes_of(geo.ng, npg, f32, slots);
+    s.act_slots = slots;
     s.qs_warp = f32 ? qs_warp_bytes(npg) : 0u;
     size_t o = 0;
     s.stages = base;
@@ -758,6 +837,7 @@ __device__ __forceinline__ void stream_init(const StreamSmem& S) {
         }
         mbar_init(S.act_full, 1);
         mbar_init(S.act_empty, kNcw);
+        for (int s = 0; s < S.n_stages; ++s) S.info[s].tile = -1;
         mbar_fence_init();
     }
     __syncthreads();
@@ -790,21 +870,44 @@ struct ActSrc {
 // `act_after_pdl` the activations come from the previous kernel in the
 // stream: the first tile's activation copies wait for it (griddepcontrol)
 // but only after the weight stages have been filled.
-template <typename Blk>
+// Global addresses of a unit's four copies (0: codes of block A, 1: pairs of
+// block A, 2/3: block B): blob + off0 + r * ustride + coff[c] for unit r of a
+// tile whose expert blob is `blob`.
+struct UnitAddr {
+    size_t off0, ustride;
+    size_t coff[4];
+};
+
+template <typename Dummy = void>
 __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
                         int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
-                        Blk blk) {
+                        const UnitAddr& ua) {
     const int lane = threadIdx.x & 31;
     const uint32_t tx = 2 * geo.bbytes, zb = (uint32_t)geo.ng * 32u;
     const bool f32 = as.xf != nullptr;
     const uint32_t rowb = act_row_bytes(geo.ng, as.npg, f32);
     const uint32_t pb = f32 ? 0u : (uint32_t)geo.ng * 16u;
     const uint64_t pol = evict_first_policy();
+    // this lane's copy: destination offset in a stage and size
+    const uint32_t dst_off = (lane >> 1) * geo.bbytes + (lane & 1) * geo.pbytes;
+    const uint32_t csize = (lane & 1) ? zb : geo.pbytes;
+    const size_t coff = lane < 4 ? ua.coff[lane] : 0;
     int ti = u_begin / upt, r = u_begin - ti * upt;
     Tile cur, nxt;
     if (u_begin < u_end) load_tile(W.tiles + ti, cur);
     if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
-    int it = 0, tiles_done = 0;
+    const unsigned char* p = nullptr;
+    bool tile_ok = false;
+    // per tile: the lane's source pointer and whether the tile's copies are usable
+    auto start_tile = [&]() {
+        p = cur.blob ? cur.blob + ua.off0 + (size_t)r * ua.ustride + coff : nullptr;
+        const bool mis = __any_sync(kFull, lane < 4 && p && !aligned16(p));
+        tile_ok = cur.blob != nullptr && !mis;
+        if (mis && lane == 0) atomicOr(W.status, ST_ALIGN);
+    };
+    if (u_begin < u_end) start_tile();
+    int it = 0, tiles_done = 0, s = 0;
+    uint32_t ph = 0;
     bool ok = true, act_due = true, waited_pdl = !act_after_pdl;
     // barrier waits by lane 0, result shared with the warp
     auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -834,7 +937,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
                                as.xq + ((size_t)row * as.nchk + (size_t)as.kg0 * as.npg) * 64,
                                rowb, S.act_full);
             } else {
-                bulk_g2s_plain(S.act + kMT * rowb + t * pb,
+                bulk_g2s_plain(S.act + S.act_slots * rowb + t * pb,
                                as.xqp + (size_t)row * as.ngrp + as.kg0, pb, S.act_full);
             }
         }
@@ -843,8 +946,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
         return true;
     };
     for (int u = u_begin;; ++u, ++it) {
-        const int s = it % S.n_stages;
-        if (!wait0(&S.empty[s], ((it / S.n_stages) & 1) ^ 1)) {
+        if (!wait0(&S.empty[s], ph ^ 1)) {
             ok = false;
             break;
         }
@@ -861,33 +963,30 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             cur = nxt;
             if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
             act_due = true;
+            start_tile();
         }
         if (act_due && waited_pdl && !issue_act()) {
             ok = false;
             break;
         }
-        // lanes 0-3 each issue one of the unit's four copies
-        const unsigned char* p = (lane < 4 && cur.blob) ? blk(cur.blob, r, lane) : nullptr;
-        const bool misaligned = __any_sync(kFull, p && !aligned16(p));
-        const bool good = cur.blob != nullptr && !misaligned;
         if (lane == 0) {
             UnitInfo& inf = S.info[s];
-            inf.m = cur.m;
+            if (inf.tile != ti) {
+                inf.tile = ti;
+                inf.m = cur.m;
 #pragma unroll
-            for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
-            inf.u = good ? u : (u | kSkip);
-            if (misaligned) atomicOr(W.status, ST_ALIGN);
-            if (good)
+                for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
+            }
+            inf.u = tile_ok ? u : (u | kSkip);
+            if (tile_ok)
                 mbar_expect_tx(&S.full[s], tx);
             else
                 mbar_arrive(&S.full[s]);
         }
         __syncwarp();
-        if (good && lane < 4) {
-            uint8_t* dst = S.stages + (size_t)s * S.stage_bytes + (lane >> 1) * geo.bbytes +
-                           (lane & 1) * geo.pbytes;
-            bulk_g2s(dst, p, (lane & 1) ? zb : geo.pbytes, &S.full[s], pol);
-        }
+        if (tile_ok && lane < 4)
+            bulk_g2s(S.stages + (size_t)s * S.stage_bytes + dst_off, p, csize, &S.full[s], pol);
+        p += ua.ustride;
         ++r;
         // a deferred first activation tile: once the stages are full, or before
         // the tile or the range ends
@@ -895,6 +994,10 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             (it + 1 >= S.n_stages || r == upt || u + 1 >= u_end) && !issue_act()) {
             ok = false;
             break;
+        }
+        if (++s == S.n_stages) {
+            s = 0;
+            ph ^= 1;
         }
     }
     if (!ok && lane == 0) {
@@ -914,9 +1017,9 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
 template <typename Out>
 __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    for (int it = 0;; ++it) {
-        const int s = it % S.n_stages;
-        const uint32_t ph = (it / S.n_stages) & 1;
+    int s = 0;
+    uint32_t ph = 0;
+    for (;;) {
         if (!mbar_wait(&S.full[s], ph)) {
             if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
             break;
@@ -941,6 +1044,10 @@ __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.empty[s]);
+        if (++s == S.n_stages) {
+            s = 0;
+            ph ^= 1;
+        }
     }
 }
 
@@ -1031,7 +1138,7 @@ __device__ __forceinline__ void load_act(WarpAct<NPG, NG>& A, float2* kp_w, cons
                                           : make_uint2(0u, 0u);
         }
     }
-    const float4* par = reinterpret_cast<const float4*>(S.act + kMT * S.act_row);
+    const float4* par = reinterpret_cast<const float4*>(S.act + S.act_slots * S.act_row);
     const int ngr = (int)(S.act_row / (64u * NPG));  // groups in the range
     for (int e = lane; e < NG * kMT; e += 32) {
         const int G = e / kMT, t = e - G * kMT;
@@ -1150,10 +1257,9 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
     float2* kp_w = S.kp + cw * NG * kMT;
     const uint32_t st0 = smem_addr(S.stages), kp = smem_addr(kp_w);
     WarpAct<NPG, NG> A;
-    int cur = -1, tiles = 0;
-    for (int it = 0;; ++it) {
-        const int s = it % S.n_stages;
-        const uint32_t ph = (it / S.n_stages) & 1;
+    int tile_end = -1, tiles = 0, s = 0;
+    uint32_t ph = 0;
+    for (;;) {
         if (!mbar_wait(&S.full[s], ph)) {
             if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
             break;
@@ -1162,8 +1268,8 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
         const int uf = *reinterpret_cast<const volatile int*>(&inf.u);
         if (uf == -1) break;
         const int u = uf & ~kSkip;
-        const int ti = u / upt;
-        if (ti != cur) {
+        if (u >= tile_end) {  // first unit of a tile (units arrive in increasing order)
+            tile_end = (u / upt + 1) * upt;
             if (!mbar_wait(S.act_full, tiles & 1)) {
                 if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
                 break;
@@ -1174,13 +1280,16 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
                 load_act<NPG, NG>(A, kp_w, S, g0, n, inf.m);
             if (lane == 0) mbar_arrive(S.act_empty);
             ++tiles;
-            cur = ti;
         }
         float2 part = make_float2(0.f, 0.f);
         if (!(uf & kSkip)) part = mma_unit<NPG, NG>(st0 + s * S.stage_bytes, geo, g0, A, kp);
         S.red[((size_t)s * kNcw + cw) * 32 + lane] = part;
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.red_bar[s]);
+        if (++s == S.n_stages) {
+            s = 0;
+            ph ^= 1;
+        }
     }
 }
 
@@ -1193,7 +1302,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int H = L.H, I = L.I, gs = L.gs;
     const Geo geo = make_geo(H / gs, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots);
     stream_init(S);
     pdl_wait();
     pdl_launch();
@@ -1210,11 +1319,8 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const size_t off_g = L.mat[0].packed, off_u = L.mat[1].packed;
             const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, nullptr, H / kChunk,
                             H / gs, 0, NPG, gs, H, false};
-            produce(S, W, b, e, rbs, ntiles, geo, as, false,
-                    [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
-                        const unsigned char* blk = blob + (c < 2 ? off_g : off_u) + (size_t)r * bb;
-                        return (c & 1) ? blk + 4 * (size_t)H : blk;
-                    });
+            const UnitAddr ua{off_g, bb, {0, 4 * (size_t)H, off_u - off_g, off_u - off_g + 4 * (size_t)H}};
+            produce(S, W, b, e, rbs, ntiles, geo, as, false, ua);
         }
         return;
     }
@@ -1242,7 +1348,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int H = L.H, I = L.I, gs = L.gs;
     const int ngp = I / gs / kp;  // groups per part
     const Geo geo = make_geo(ngp, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots);
     stream_init(S);
     // Weights, the expert table and the tile plan (written by the router,
     // which completed before the gate/up kernel could start) do not depend on
@@ -1262,15 +1368,11 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const int j = blockIdx.x / kp;
             const int b = (int)(total * j / cpp), e = (int)(total * (j + 1) / cpp);
             const size_t bb = block_bytes_of(I, gs);
-            const size_t off_d = L.mat[2].packed;
             const size_t z_off = 4 * (size_t)I + (size_t)pi * geo.ng * 32;
             const size_t p_off = (size_t)pi * geo.pbytes;
             const ActSrc as{nullptr, nullptr, W.h, I / kChunk, I / gs, pi * ngp, NPG, gs, I, true};
-            produce(S, W, b, e, upt, ntiles, geo, as, true,
-                    [&](const unsigned char* blob, int r, int c) -> const unsigned char* {
-                        const unsigned char* blk = blob + off_d + (size_t)(2 * r + (c >> 1)) * bb;
-                        return blk + ((c & 1) ? z_off : p_off);
-                    });
+            const UnitAddr ua{L.mat[2].packed, 2 * bb, {p_off, z_off, bb + p_off, bb + z_off}};
+            produce(S, W, b, e, upt, ntiles, geo, as, true, ua);
         }
         return;
     }
@@ -1442,7 +1544,40 @@ bool check_layer(const WispMoeLayer* ly, int T, WispErrCtx* err) {
     return true;
 }
 
-int down_parts(int I, int gs, long long units, int ctas);
+// Shared memory of a streaming CTA (one per SM): as many ring stages (each
+// with its reduction slot) as fit, up to 8.
+struct StreamCfg {
+    int stages = 0, blocks = 0;
+    uint32_t stage_bytes = 0;
+    size_t smem = 0;
+};
+
+constexpr size_t kSmemPerCta = 227 * 1024;
+
+// Stages: enough to keep about kInFlight bytes of weights in flight per SM
+// (more only lengthens the DRAM queues every other load waits in), at least
+// 2, at most 8, within the shared memory left after the activation tile.
+constexpr size_t kInFlight = 192 * 1024;
+constexpr int kMaxStages = 12;
+
+StreamCfg plan_stream(const Geo& geo, int npg, bool f32, int slots) {
+    StreamCfg c;
+    c.stage_bytes = stage_bytes_of(geo);
+    const uint32_t act = act_bytes_of(geo.ng, npg, f32, slots);
+    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg) : 0u;
+    int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
+    want = std::max(2, std::min(kMaxStages, want));
+    c.stages = 0;
+    for (int st = want; st >= 2; --st)
+        if (stream_smem_bytes(st, c.stage_bytes, act, qs) <= kSmemPerCta) {
+            c.stages = st;
+            break;
+        }
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs);
+    return c;
+}
+
+int down_parts(int I, int gs, long long units, int ctas, int slots);
 
 LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     LayerArgs a{};
@@ -1463,48 +1598,25 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.has_shared = ly->shared_blob != nullptr;
     const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
                             (a.has_shared ? (T + kMT - 1) / kMT : 0);
-    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas);
+    a.act_slots = std::min(T, kMT);
+    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots);
+    // tuning override: WISP_B200_DOWN_PARTS=<kp>, used when it is a valid split
+    if (const char* v = getenv("WISP_B200_DOWN_PARTS")) {
+        const int kp = atoi(v), G = a.I / a.gs;
+        if (kp >= 1 && kp <= kMaxKp && G % kp == 0 && a.I / kp <= kMaxPartK &&
+            ng_bucket(a.gs / kChunk, G / kp) &&
+            plan_stream(make_geo(G / kp, a.gs), a.gs / kChunk, true, a.act_slots).stages >= 2)
+            a.kp = kp;
+    }
     return a;
 }
 
-// Shared memory of a streaming CTA (one per SM): as many ring stages (each
-// with its reduction slot) as fit, up to 8.
-struct StreamCfg {
-    int stages = 0, blocks = 0;
-    uint32_t stage_bytes = 0;
-    size_t smem = 0;
-};
-
-constexpr size_t kSmemPerCta = 227 * 1024;
-
-// Stages: enough to keep about kInFlight bytes of weights in flight per SM
-// (more only lengthens the DRAM queues every other load waits in), at least
-// 2, at most 8, within the shared memory left after the activation tile.
-constexpr size_t kInFlight = 160 * 1024;
-
-StreamCfg plan_stream(const Geo& geo, int npg, bool f32) {
-    StreamCfg c;
-    c.stage_bytes = stage_bytes_of(geo);
-    const uint32_t act = act_bytes_of(geo.ng, npg, f32);
-    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg) : 0u;
-    int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
-    want = std::max(2, std::min(8, want));
-    c.stages = 0;
-    for (int st = want; st >= 2; --st)
-        if (stream_smem_bytes(st, c.stage_bytes, act, qs) <= kSmemPerCta) {
-            c.stages = st;
-            break;
-        }
-    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs);
-    return c;
-}
-
 StreamCfg gateup_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk, false);
+    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk, false, a.act_slots);
 }
 
 StreamCfg down_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk, true);
+    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk, true, a.act_slots);
 }
 
 // K parts of the down projection.  A part is a whole number of quant groups
@@ -1513,7 +1625,7 @@ StreamCfg down_cfg(const LayerArgs& a) {
 // groups (the per-warp group count rounded up to a built bucket), uneven
 // units per CTA (`units` = down units of one part, tiles x H/16), and a small
 // cost per extra part (the combine reads every part).
-int down_parts(int I, int gs, long long units, int ctas) {
+int down_parts(int I, int gs, long long units, int ctas, int slots) {
     const int G = I / gs, npg = gs / kChunk;
     int best = 0;
     double best_score = -1.0;
@@ -1524,10 +1636,13 @@ int down_parts(int I, int gs, long long units, int ctas) {
         const double eff = std::min(1.0, (double)ngp / (double)(ng * kNcw));
         const double per = (double)units * kp / (double)ctas;
         const double bal = per > 0 ? per / std::ceil(per) : 1.0;
-        // a shallow ring (big stages) starves the consumers while a stage turns over
-        const int st = plan_stream(make_geo(ngp, gs), npg, true).stages;
+        // a shallow ring (big stages) starves the consumers while a stage turns
+        // over; small units pay the fixed per-unit cost (barriers, reduction)
+        const Geo geo = make_geo(ngp, gs);
+        const int st = plan_stream(geo, npg, true, slots).stages;
         const double depth = std::min(1.0, st / 4.0);
-        const double score = eff * bal * depth * (1.0 - 0.01 * kp);
+        const double size = std::min(1.0, 2.0 * geo.bbytes / 32768.0);
+        const double score = eff * bal * depth * size * (1.0 - 0.01 * kp);
         if (score > best_score + 1e-9) {
             best_score = score;
             best = kp;
@@ -1566,10 +1681,10 @@ DevInfo dev_info() {
     return d;
 }
 
-size_t prep_smem(int H) { return (size_t)H * sizeof(float); }
 size_t router_smem(int E) {
-    return std::max((size_t)(kMaxPlanAssign + 64), (size_t)kWarps * 2 * E) * sizeof(int);
+    return std::max((size_t)(kMaxPlanAssign + 64), (size_t)kWarps * 3 * E) * sizeof(int);
 }
+constexpr int kMaxHidden = 8192;
 
 cudaError_t ensure_attrs(int H) {
     static std::mutex mu;
@@ -1577,9 +1692,10 @@ cudaError_t ensure_attrs(int H) {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> g(mu);
-    if (done[dev & 63] && H <= 16384) return cudaSuccess;
+    if (done[dev & 63]) return cudaSuccess;
+    (void)H;
     cudaError_t e = cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)prep_smem(std::max(H, 16384)));
+                                         (int)prep_smem_bytes(kMaxHidden, 1, 1024));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)router_smem(1024));
@@ -1587,6 +1703,26 @@ cudaError_t ensure_attrs(int H) {
     done[dev & 63] = true;
     return cudaSuccess;
 }
+
+// CTAs per token in prep: the largest of 8/4/2/1 that splits the row into
+// whole quant groups.
+int prep_cluster(int H, int gs) {
+    for (int cs = 8; cs > 1; cs >>= 1)
+        if (H % (cs * gs) == 0) return cs;
+    return 1;
+}
+
+// Router inside prep (every token's cluster reads the whole router matrix)
+// unless that re-reads more than 32 MB (the environment variable
+// WISP_B200_PREP_ROUTER_BYTES overrides the limit); then the separate router
+// kernel, which reads it once for all tokens.
+bool route_in_prep(const LayerArgs& a, int T) {
+    size_t limit = (size_t)32 << 20;
+    if (const char* v = getenv("WISP_B200_PREP_ROUTER_BYTES")) limit = strtoull(v, nullptr, 10);
+    return (size_t)T * a.E * a.H * 2 <= limit;
+}
+
+int plan_tokens(int T) { return T == 1 ? 1 : kMT; }
 
 // Optional profiling hook: when set, an event is recorded on the launch stream
 // before every kernel of the fused path and once after the last, so a caller
@@ -1676,7 +1812,7 @@ cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t 
 
 cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* xin,
                           cudaStream_t s) {
-    const int mt = T == 1 ? 1 : kMT;
+    const int mt = plan_tokens(T);
     const int nsl = (a.H + kSlice - 1) / kSlice;
     const int blocks = (a.E * nsl + kWarps - 1) / kWarps;
     return launch(router_kernel, dim3(blocks), dim3(kThreads), router_smem(a.E), s, a, W, T, mt,
@@ -1685,11 +1821,27 @@ cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* x
 
 // Run one layer's router + expert kernels.  The layer's input is already
 // quantised in W.xq (and xin holds the router input).
-cudaError_t run_layer_experts(const LayerArgs& a, const Ws& W, int T, const float* xin,
+// prep over T tokens (one cluster per token).  P_ROUTE is added when the
+// router runs inside prep; otherwise the separate router kernel follows.
+cudaError_t launch_prep(const LayerArgs& a, const Ws& W, int T, int flags, float* x, float* y,
+                        float eps, int prevK, int prev_sh, int prev_kp, cudaStream_t s) {
+    const int cs = prep_cluster(a.H, a.gs);
+    hook_mark(s);
+    return launch_pdl_cluster(prep_kernel, dim3(T * cs), dim3(kPrepThreads),
+                              prep_smem_bytes(a.H, cs, a.E), s, cs, a, W, T, flags, x, y, eps,
+                              prevK, prev_sh, prev_kp, plan_tokens(T));
+}
+
+// Routing of a layer whose input prep is about to quantise: the router in
+// prep, or prep then the router kernel on `xin`.
+cudaError_t launch_prep_route(const LayerArgs& a, const Ws& W, int T, int flags, float* x,
+                              float eps, int prevK, int prev_sh, int prev_kp, const float* xin,
                               cudaStream_t s) {
-    cudaError_t e = launch_router(a, W, T, xin, s);
-    if (e != cudaSuccess) return e;
-    return launch_streams(a, W, T, s);
+    const bool fused = route_in_prep(a, T);
+    cudaError_t e = launch_prep(a, W, T, flags | (fused ? (int)P_ROUTE : 0), x, nullptr, eps,
+                                prevK, prev_sh, prev_kp, s);
+    if (e != cudaSuccess || fused) return e;
+    return launch_router(a, W, T, xin, s);
 }
 
 }  // namespace
@@ -1767,11 +1919,10 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    WB_CUDA_RET(cudaMemsetAsync(W.status, 0, sizeof(int), stream), err);
-    WB_CUDA_RET(launch(prep_kernel, dim3(T), dim3(kPrepThreads), prep_smem(a.H), stream, a, W, T,
-                       (int)P_QUANT, const_cast<float*>(x), (float*)nullptr, 0.f, 0, 0, 1),
+    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    WB_CUDA_RET(launch_prep_route(a, W, T, (int)P_QUANT, const_cast<float*>(x), 0.f, 0, 0, 1, x,
+                                  stream),
                 err);
-    WB_CUDA_RET(launch_router(a, W, T, x, stream), err);
     *a_out = a;
     *w_out = W;
     return WISP_OK;
@@ -1786,8 +1937,8 @@ static WispError block_experts(const LayerArgs& a, const Ws& W, int T, const flo
     Ws Wc = W;
     Wc.prev_idx = W.topk_idx;
     Wc.prev_w = W.topk_w;
-    WB_CUDA_RET(launch(prep_kernel, dim3(T), dim3(kPrepThreads), prep_smem(a.H), stream, a, Wc,
-                       T, (int)P_COMBINE, const_cast<float*>(x), y, 0.f, a.K, a.has_shared, a.kp),
+    WB_CUDA_RET(launch_prep(a, Wc, T, (int)P_COMBINE, const_cast<float*>(x), y, 0.f, a.K,
+                            a.has_shared, a.kp, stream),
                 err);
     hook_mark(stream);
     return WISP_OK;
@@ -1868,26 +2019,30 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
     }
     const int H = (int)layers[0].meta.cols[0];
     WB_CUDA_RET(ensure_attrs(H), err);
-    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, sizeof(int), stream), err);
+    {
+        const Layout lo0 = make_layout(T, H, maxI, maxE, maxK, anysh);
+        WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo0.counters + kCounters * sizeof(int), stream),
+                    err);
+    }
     int prevK = 0, prev_sh = 0, prev_kp = 1;
     for (int l = 0; l < n_layers; ++l) {
         LayerArgs a = layer_args(&layers[l], T, dev_info().sms);
         Layout lo = make_layout(T, H, maxI, maxE, maxK, anysh);
         Ws W = make_ws(workspace, lo);
-        // previous layer's routing lives in the "current" slots until this
-        // layer's router overwrites them; prep reads it first (stream order)
+        // the previous layer's routing is read (per token, before this
+        // layer's routing of the same token is written) by prep's combine
         Ws Wp = W;
         if (l > 0) {
             Wp.prev_idx = topk_idx ? topk_idx + (size_t)(l - 1) * T * prevK : W.topk_idx;
             Wp.prev_w = topk_w ? topk_w + (size_t)(l - 1) * T * prevK : W.topk_w;
         }
+        if (topk_idx) W.topk_idx = Wp.topk_idx = topk_idx + (size_t)l * T * a.K;
+        if (topk_w) W.topk_w = Wp.topk_w = topk_w + (size_t)l * T * a.K;
         const int flags = (l > 0 ? (P_COMBINE | P_RESID) : 0) | P_NORM | P_QUANT;
-        WB_CUDA_RET(launch(prep_kernel, dim3(T), dim3(kPrepThreads), prep_smem(H), stream, a, Wp,
-                           T, flags, x, (float*)nullptr, eps, prevK, prev_sh, prev_kp),
+        WB_CUDA_RET(launch_prep_route(a, Wp, T, flags, x, eps, prevK, prev_sh, prev_kp, W.xn,
+                                      stream),
                     err);
-        if (topk_idx) W.topk_idx = topk_idx + (size_t)l * T * a.K;
-        if (topk_w) W.topk_w = topk_w + (size_t)l * T * a.K;
-        WB_CUDA_RET(run_layer_experts(a, W, T, W.xn, stream), err);
+        WB_CUDA_RET(launch_streams(a, W, T, stream), err);
         prevK = a.K;
         prev_sh = a.has_shared;
         prev_kp = a.kp;
@@ -1895,9 +2050,8 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
             Ws Wf = W;
             Wf.prev_idx = W.topk_idx;
             Wf.prev_w = W.topk_w;
-            WB_CUDA_RET(launch(prep_kernel, dim3(T), dim3(kPrepThreads), prep_smem(H), stream, a,
-                               Wf, T, (int)(P_COMBINE | P_RESID), x, (float*)nullptr, eps, prevK,
-                               prev_sh, prev_kp),
+            WB_CUDA_RET(launch_prep(a, Wf, T, (int)(P_COMBINE | P_RESID), x, nullptr, eps, prevK,
+                                    prev_sh, prev_kp, stream),
                         err);
         }
     }
@@ -1921,9 +2075,9 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
 // larger requests are rejected with WISP_ERR_INVALID_ARG before any GPU work.
 // Every call on a device shares the one array, so two calls whose kernels
 // overlap on the GPU (different streams, or different host threads without
-// ordering) race and corrupt each other's results.  Each call clears the only
-// word that must start at zero (the status word, by cudaMemsetAsync on the
-// call's stream); the kernels reset their own counters.
+// ordering) race and corrupt each other's results.  Each call clears what
+// must start at zero (the status word and the kernels' counters, by
+// cudaMemsetAsync on the call's stream).
 // ------------------------------------------------------------------------
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_block_scratch[kStaticScratchBytes];
