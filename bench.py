@@ -7,11 +7,12 @@ weights (N(0, 0.02), quantised by the reference quantiser's rule) and inputs (fp
 N(0,1) upcast to fp32), generated on the GPU.
 
 N = 1: the whole stack on one GPU, one CUDA graph per step.
-N > 1 (torchrun): layer pipeline -- rank r owns layers [32r/N, 32(r+1)/N); the batch
-is split into micro-batches of 4 tokens that flow rank to rank with NCCL send/recv
-(torch.distributed) and the last rank hands each micro-batch back to rank 0 for the
-next decode step.  Per-GPU work is fixed (16 tokens x 32/N layers per rank per
-micro-batch round), so scaling is weak: global batch = 16 * N.
+N > 1 (torchrun): layer pipeline -- rank r owns layers [32r/N, 32(r+1)/N); the global
+batch (16 tokens per GPU) is split into N micro-batches of 16 tokens that flow rank to
+rank with NCCL send/recv (torch.distributed), and the last rank hands each micro-batch
+back to rank 0 for the next decode step.  Decode streams the routed experts' weights
+once per micro-batch, so micro-batches are as large as keeping every stage busy allows
+(M = N).  Per-GPU work is fixed, so scaling is weak: global batch = 16 * N.
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference engine's own
 CPU run_moe (oracle/_ref, built from the reference sources) on a bounded sample of the
@@ -33,6 +34,8 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from wisp_b200.benchutil import ClockSampler, alg_bytes, peaks  # noqa: E402
+
 METRIC = "MoE-block decode tokens/s (Mixtral-8x7B-shaped 32-block stack)"
 UNIT = "tokens/s"
 SEED = 20251201
@@ -46,84 +49,12 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--batch", type=int, default=16, help="tokens per decode step per GPU")
     p.add_argument("--layers", type=int, default=32)
-    p.add_argument("--micro", type=int, default=4, help="tokens per pipeline micro-batch")
+    p.add_argument("--micro", type=int, default=0,
+                   help="tokens per pipeline micro-batch (default: the per-GPU batch)")
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--skip-extra", action="store_true", help="no per-batch / e2e / profile legs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     return p.parse_args()
-
-
-# --------------------------------------------------------------------------- clocks
-class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
-
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, device_index: int):
-        import torch
-        self.sel = None
-        try:
-            self.sel = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
-        except Exception:
-            pass
-        self.proc = None
-
-    def __enter__(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"]
-        if self.sel:
-            cmd += ["-i", self.sel]
-        try:
-            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
-        except OSError:
-            self.proc = None
-        time.sleep(0.15)
-        return self
-
-    def __exit__(self, *a):
-        self.out = ""
-        if self.proc:
-            time.sleep(0.15)
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
-
-    def summary(self) -> dict:
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                rows.append(dict(sm=float(f[1]), smax=float(f[2]), power=float(f[3]),
-                                 hw=f[5], hwt=f[6], swt=f[7], swp=f[8]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        reasons = set()
-        for r in rows:
-            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
-                              ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
-                if r[key].lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": rows[0]["smax"],
-                "power_w_max": max(r["power"] for r in rows), "reasons": sorted(reasons),
-                "samples": len(rows)}
-
-
-# --------------------------------------------------------------------------- peaks
-def peaks() -> dict:
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
 # --------------------------------------------------------------------------- CPU side
@@ -182,20 +113,6 @@ def time_reference_cpu(model_dir: Path, x, seconds: float, threads: int):
 
 
 # --------------------------------------------------------------------------- GPU side
-def alg_bytes(stack, idx_layers, T) -> tuple[int, list[int]]:
-    """Algorithmic bytes of one step and of each gate/up launch: distinct routed experts'
-    int4 sections (gate+up for gate/up; all three for the step) + router + activations."""
-    import numpy as np
-    s = stack.shape
-    mat = (s.inter * s.hidden) // 2 + 2 * 2 * (s.inter * s.hidden) // s.group_size
-    total, gu = 0, []
-    for li in idx_layers:
-        d = len(np.unique(li[li >= 0]))
-        total += d * 3 * mat + s.n_experts * s.hidden * 2 + T * s.hidden * (2 + 4)
-        gu.append(d * 2 * mat + T * s.hidden * 2)
-    return total, gu
-
-
 def run_single(args, dev) -> dict:
     import numpy as np
     import torch

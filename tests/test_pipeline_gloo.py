@@ -1,0 +1,65 @@
+"""The layer pipeline's ring protocol on CPU: world_size-2 gloo ranks, a stand-in
+for each rank's layers (an affine map per rank), and the same LayerPipeline the GPU
+bench drives.  After K decode steps every micro-batch must equal the composition of
+all ranks' maps applied K times, in rank order -- which checks the send/receive
+pairing, the wrap-around from the last rank to rank 0, the first/last-step rules and
+the two-group send/receive split."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, steps, M, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from wisp_b200.pipeline import LayerPipeline
+    groups = [dist.new_group(list(range(world))), dist.new_group(list(range(world)))]
+    bufs = [torch.full((3, 4), float(m + 1)) for m in range(M)]
+
+    def run(m):  # this rank's "layers"
+        bufs[m].mul_(2.0).add_(rank + 1)
+
+    pipe = LayerPipeline(run, bufs, rank, world, groups)
+    for s in range(steps):
+        pipe.step(first=(s == 0), last=(s == steps - 1))
+    pipe.close()
+    if rank == world - 1:
+        out.put([b[0, 0].item() for b in bufs])
+    for g in groups:
+        dist.destroy_process_group(g)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,M,steps", [(2, 2, 3), (2, 3, 2)])
+def test_ring_applies_every_rank_in_order(world, M, steps):
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, steps, M, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = []
+    for m in range(M):
+        v = float(m + 1)
+        for _ in range(steps):
+            for r in range(world):
+                v = v * 2.0 + (r + 1)
+        want.append(v)
+    assert got == want

@@ -6,14 +6,18 @@ Here each rank owns a contiguous layer range and runs it with the fused stack
 kernels (one CUDA graph per micro-batch); micro-batches of hidden states
 ``[mb, H]`` fp32 move between neighbouring ranks with NCCL send/recv, and the last
 rank hands every micro-batch back to rank 0, which is where the next decode step of
-that micro-batch starts (the autoregressive dependency).  With M micro-batches and
-S ranks the steady-state utilisation bound is min(1, M/S); the benchmark keeps
-M = 4S.
+that micro-batch starts (the autoregressive dependency).
+
+Decode is bound by streaming the routed experts' weights, and every micro-batch
+re-streams its layers' experts, so micro-batches are as large as the ring allows:
+the default is one micro-batch per stage (M = S, the per-GPU batch each), which keeps
+every stage busy in the steady state (utilisation bound min(1, M/S) = 1).
 
 Ordering: a micro-batch buffer is re-filled by a receive only after its previous
 send completed (the send's work handle is waited on the compute stream first), and
-compute waits on the receive; the sends/receives of different peers run on
-torch's per-peer NCCL streams, overlapping the next micro-batch's compute.
+compute waits on the receive.  Sends and receives use two process groups (a rank
+sends on group rank % 2 and receives on group (rank - 1) % 2), so a rank's send and
+its next receive are not serialised behind each other.
 """
 
 from __future__ import annotations
@@ -26,28 +30,44 @@ import time
 
 
 class LayerPipeline:
-    def __init__(self, stack, micro_inputs, rank: int, world: int):
-        import torch
-        self.stack, self.rank, self.world = stack, rank, world
-        self.bufs = [x.clone() for x in micro_inputs]
-        self.M = len(self.bufs)
+    """The ring of one rank: `bufs` are its micro-batch buffers, `run(m)` applies this
+    rank's layers to bufs[m] in place on the current stream."""
+
+    def __init__(self, run, bufs, rank: int, world: int, groups=None):
+        self.run, self.bufs, self.rank, self.world = run, bufs, rank, world
+        self.M = len(bufs)
         self.send_work = [None] * self.M
-        self.graphs = []
-        stack.workspace(self.bufs[0].shape[0])
+        # (send group, receive group); None = the default group for both
+        self.send_pg = groups[rank % 2] if groups else None
+        self.recv_pg = groups[(rank - 1) % 2] if groups else None
+
+    @classmethod
+    def for_stack(cls, stack, micro_inputs, rank: int, world: int, groups=None):
+        """One CUDA graph per micro-batch of `stack` (a MoEStack) over its layers."""
+        import torch
+        bufs = [x.clone() for x in micro_inputs]
+        stack.workspace(bufs[0].shape[0])
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            tmp = self.bufs[0].clone()
+            tmp = bufs[0].clone()
             stack.stack(tmp)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
-        for b in self.bufs:
+        graphs = []
+        for b in bufs:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 stack.stack(b)
-            self.graphs.append(g)
+            graphs.append(g)
+        pipe = cls(lambda m: graphs[m].replay(), bufs, rank, world, groups)
+        pipe.graphs = graphs
+        return pipe
 
-    def step(self, first: bool, last: bool) -> None:
+    def step(self, first: bool, last: bool, on_input=None, on_output=None) -> None:
+        """One decode step of every micro-batch.  `first`: rank 0 has nothing to
+        receive yet; `last`: the last rank keeps its outputs.  on_input(m) runs after
+        micro-batch m's receive and before its compute, on_output(m) after it."""
         import torch.distributed as dist
         r, w = self.rank, self.world
         src, dst = (r - 1) % w, (r + 1) % w
@@ -56,10 +76,14 @@ class LayerPipeline:
                 if self.send_work[m] is not None:
                     self.send_work[m].wait()
                     self.send_work[m] = None
-                dist.irecv(self.bufs[m], src).wait()
-            self.graphs[m].replay()
+                dist.irecv(self.bufs[m], src, group=self.recv_pg).wait()
+            if on_input is not None:
+                on_input(m)
+            self.run(m)
+            if on_output is not None:
+                on_output(m)
             if r < w - 1 or not last:
-                self.send_work[m] = dist.isend(self.bufs[m], dst)
+                self.send_work[m] = dist.isend(self.bufs[m], dst, group=self.send_pg)
 
     def drain(self) -> None:
         for m in range(self.M):
@@ -69,15 +93,25 @@ class LayerPipeline:
 
     def close(self) -> None:
         self.drain()
-        self.graphs.clear()
+        getattr(self, "graphs", []).clear()
+
+
+def launches_per_layer(shape, T: int) -> int:
+    """Kernels the stack launches per layer: prep (+ the router kernel when the router
+    does not run inside prep, i.e. T*E*H*2 bytes > WISP_B200_PREP_ROUTER_BYTES, 32 MB
+    by default) + gate/up + down."""
+    limit = int(os.environ.get("WISP_B200_PREP_ROUTER_BYTES", 32 << 20))
+    return 3 if T * shape.n_experts * shape.hidden * 2 <= limit else 4
 
 
 def bench_main(args) -> None:
+    import numpy as np
     import torch
     import torch.distributed as dist
 
     from . import build
     from . import converter as cv
+    from .benchutil import ClockSampler, alg_bytes, peaks
     from .moe import MoEStack
 
     rank = int(os.environ["RANK"])
@@ -98,48 +132,92 @@ def bench_main(args) -> None:
     per = L // world
     shape = cv.MoEShape(hidden=4096, inter=14336, n_experts=8, top_k=2, n_layers=L)
     stack = MoEStack(shape, seed, device=dev, n_layers=per, layer0=rank * per)
-    mb = args.micro
     global_batch = args.batch * world
+    mb = args.micro or args.batch  # default: one micro-batch per stage
+    if global_batch % mb:
+        raise SystemExit(f"micro-batch {mb} does not divide the global batch {global_batch}")
     M = global_batch // mb
     micro = [cv.make_input(shape, mb, seed + 1000 + m).to(dev) for m in range(M)]
-    pipe = LayerPipeline(stack, micro, rank, world)
+    groups = [dist.new_group(list(range(world))), dist.new_group(list(range(world)))]
+    pipe = LayerPipeline.for_stack(stack, micro, rank, world, groups)
 
-    total = args.warmup + args.steps
-    for s in range(args.warmup):
-        pipe.step(first=(s == 0), last=False)
-    pipe.drain()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_wall = time.time()
-    e0.record()
-    for s in range(args.warmup, total):
-        pipe.step(first=False, last=(s == total - 1))
-    pipe.drain()
-    e1.record()
-    torch.cuda.synchronize()
-    t_wall = time.time() - t_wall
-    ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    dist.barrier()
-    ms_step = ms.item() / args.steps
+    def run(steps, first, last, host_in=None, host_out=None):
+        # the ring stays primed between runs (last=False) except for the final one
+        on_in = on_out = None
+        if host_in is not None and rank == 0:
+            # fresh hidden states enter at rank 0 from pinned host memory
+            def on_in(m):
+                pipe.bufs[m].copy_(host_in[m], non_blocking=True)
+        if host_out is not None and rank == world - 1:
+            def on_out(m):
+                host_out[m].copy_(pipe.bufs[m], non_blocking=True)
+        for s in range(steps):
+            pipe.step(first=first and s == 0, last=last and s == steps - 1, on_input=on_in,
+                      on_output=on_out)
+        pipe.drain()
+
+    def timed(steps, last, host_in=None, host_out=None):
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run(steps, False, last, host_in, host_out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item() / steps
+
+    run(args.warmup, True, False)
+    with ClockSampler(local) as clk:
+        ms_step = timed(args.steps, False)
     value = global_batch * 1000.0 / ms_step
+    # end to end: inputs from pinned host memory at rank 0, outputs to pinned host
+    # memory at the last rank, every step
+    host_in = [x.cpu().pin_memory() for x in micro]
+    host_out = [torch.empty_like(h).pin_memory() for h in host_in]
+    e2e_ms = timed(args.steps, True, host_in, host_out)
+    # algorithmic bytes of this rank's layers per step (routing of the last step's
+    # activations), summed over ranks
+    step_bytes = 0
+    for m in range(M):
+        xb = pipe.bufs[m].clone()
+        _, idx, _ = stack.stack(xb, routing=True)
+        torch.cuda.synchronize()
+        step_bytes += alg_bytes(stack, idx.cpu().numpy(), mb)[0]
+    tb = torch.tensor([float(step_bytes)], device=dev)
+    dist.all_reduce(tb)
     pipe.close()
     del pipe
     torch.cuda.synchronize()
     dist.barrier()
+    for g in groups:
+        dist.destroy_process_group(g)
     dist.destroy_process_group()
     if rank == 0:
+        pk = peaks()
+        achieved = tb.item() / world / (ms_step * 1e-3) / 1e9  # per GPU
         print(json.dumps({
             "metric": "MoE-block decode tokens/s (Mixtral-8x7B-shaped 32-block stack)",
             "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised int4 gs64; fp16 N(0,1) "
+                    "inputs)",
             "config": {"workload": f"config1: Mixtral-8x7B-shaped {L}-block stack decode, layer "
                                    f"pipeline over {world} GPUs, {M} micro-batches of {mb}",
                        "global_batch": global_batch, "parallelism": f"pp{world}",
                        "micro_batches": M, "layers_per_rank": per,
                        "l2": "weights per step exceed L2"},
-            "gpu_launches": (4 * per + 1) * M * args.steps,
-            "wall_s_timed": round(t_wall, 3)}), flush=True)
+            "roofline": {"bound": "hbm", "kernel": "whole step per GPU (all kernels)",
+                         "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "peak_source": pk["source"]},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(global_batch * 1000.0 / e2e_ms, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(sum(h.numel() for h in host_in) * 4),
+                    "d2h_bytes_per_step": int(sum(h.numel() for h in host_out) * 4),
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": (launches_per_layer(shape, mb) * per + 1) * M * args.steps * world,
+        }), flush=True)
