@@ -262,6 +262,38 @@ def run_single(args, dev) -> dict:
                                  "hbm_gbs": round(sb / bm / 1e6, 1)}
             del gb
         out["per_batch"] = per_batch
+        # config 0: one Mixtral block (no norm/residual), 1 token, graph of the block
+        x1 = cv.make_input(shape, 1, SEED + 7).to(dev)
+        y1 = torch.empty_like(x1)
+        stack.workspace(max(B, 1))
+        with torch.cuda.stream(s):
+            stack.block(0, x1, y1)
+        torch.cuda.synchronize()
+        g0 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g0):
+            stack.block(0, x1, y1)
+        for _ in range(5):
+            g0.replay()
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nb = 200
+        b0.record()
+        for _ in range(nb):
+            g0.replay()
+        b1.record()
+        torch.cuda.synchronize()
+        blk_ms = b0.elapsed_time(b1) / nb
+        _, i0, _ = stack.block(0, x1, y1, routing=True)
+        torch.cuda.synchronize()
+        blk_bytes, _ = alg_bytes(stack, i0.cpu().numpy()[None], 1)
+        gbs = blk_bytes / blk_ms / 1e6
+        out["config0"] = {"workload": "one Mixtral-shaped MoE block, decode batch 1 (graph of "
+                                      "back-to-back blocks)",
+                          "us_per_block": round(blk_ms * 1e3, 2),
+                          "blocks_per_s": round(1000.0 / blk_ms, 1),
+                          "alg_bytes_per_block": int(blk_bytes), "hbm_gbs": round(gbs, 1),
+                          "frac_of_measured_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
+        del g0
 
     # CPU baseline + parity on the same bytes: layer 0, token 0
     if not args.skip_cpu:
@@ -326,7 +358,7 @@ def main_ours(args):
         "gpu_launches": r["gpu_launches_per_step"] * args.steps,
         "step_hbm_gbs": round(r["step_gbs"], 1), "kernel_ms_mean": r["kernel_ms_mean"],
     }
-    for k in ("e2e", "per_batch", "cpu_baseline", "parity"):
+    for k in ("e2e", "per_batch", "config0", "cpu_baseline", "parity"):
         if k in r:
             line[k] = r[k]
     print(json.dumps(line), flush=True)

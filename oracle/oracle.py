@@ -120,8 +120,9 @@ def port_moe_block(m: Model, layer: int, x: np.ndarray, threads: int | None = No
 
 
 def port_moe_block_arrays(router_w: np.ndarray, router_bias: np.ndarray | None, blobs: list,
-                          k: int, x: np.ndarray, threads: int | None = None):
-    """Same as ``port_moe_block`` on explicit arrays (fp16 bits as uint16, blob bytes)."""
+                          k: int, x: np.ndarray, threads: int | None = None, shared=None):
+    """Same as ``port_moe_block`` on explicit arrays (fp16 bits as uint16, blob bytes);
+    `shared` = (gate [I,H], up [I,H], down [H,I]) fp16 bits of a dense shared expert."""
     lib = port_lib()
     E, H = router_w.shape
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -130,8 +131,13 @@ def port_moe_block_arrays(router_w: np.ndarray, router_bias: np.ndarray | None, 
     idx = np.zeros((T, k), np.int32)
     w = np.zeros((T, k), np.float32)
     bp = _ptr_array(blobs)
-    rc = lib.oracle_moe_block(_ptr(router_w), _ptr(router_bias), E, H, k, _ptr(bp), None, None,
-                              None, 0, _ptr(x), T, _ptr(y), _ptr(idx), _ptr(w),
+    sg = su = sd = None
+    si = 0
+    if shared is not None:
+        sg, su, sd = (np.ascontiguousarray(a) for a in shared)
+        si = sg.shape[0]
+    rc = lib.oracle_moe_block(_ptr(router_w), _ptr(router_bias), E, H, k, _ptr(bp), _ptr(sg),
+                              _ptr(su), _ptr(sd), si, _ptr(x), T, _ptr(y), _ptr(idx), _ptr(w),
                               threads or host_threads())
     if rc:
         raise RuntimeError(f"oracle_moe_block failed: {rc}")

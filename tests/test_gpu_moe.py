@@ -191,3 +191,41 @@ def test_separate_router_kernel_path(cuda, T, monkeypatch):
     assert st.status() == 0
     # the two router placements sum the logits in different orders
     np.testing.assert_allclose(xs.cpu().numpy(), xs2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("T", [6, 16])
+def test_eight_token_tiles(cuda, T, monkeypatch):
+    """The 8-token tile kernels (two MMA column quads; WISP_B200_TILE_TOKENS=8)
+    against the oracle, with tiles of more and of fewer than 4 tokens."""
+    monkeypatch.setenv("WISP_B200_TILE_TOKENS", "8")
+    shape = cv.MoEShape(hidden=512, inter=1024, n_experts=4, top_k=2)
+    st = MoEStack(shape, seed=23 + T, device=cuda, random_bias=True)
+    x = (torch.randn(T, 512, generator=torch.Generator().manual_seed(T))).half().float()
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 2, x.numpy())
+    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
+        check_outputs(y.cpu().numpy(), yr)
+
+
+@pytest.mark.parametrize("H,I,E,T", [(1024, 512, 64, 8),
+                                     pytest.param(7168, 2048, 256, 4, marks=pytest.mark.slow)])
+def test_deepseek_shaped_block_with_shared_expert(cuda, H, I, E, T):
+    """DeepSeek-V3-shaped routing (top-8 of many experts, Zipf-skewed bias) plus the
+    always-on shared expert (int4 here, fp16-dense in the oracle, as the reference
+    computes it); the last case is one full DeepSeek-V3 layer."""
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=E, top_k=8, shared_inter=I)
+    st = MoEStack(shape, seed=E + T, device=cuda, zipf_s=1.1)
+    x = cv.make_input(shape, T, 3)
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.numpy(),
+                                           shared=st.host_shared(0))
+    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
+        np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-6)
+        # the shared expert's weights are fp16-rounded dequantised int4 in the oracle
+        check_outputs(y.cpu().numpy(), yr, tight=False)

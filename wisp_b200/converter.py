@@ -181,6 +181,23 @@ def untile_blob(blob) -> np.ndarray:
     return _retile(blob, _untile_matrix, EXPERT_VERSION)
 
 
+def qmats_from_blob(blob) -> dict[str, QMat]:
+    """The three matrices of a ``.bin`` blob (bytes or uint8 array) as QMats."""
+    b = bytes(blob)
+    h = parse_blob_header(b)
+    if h["tiled"]:
+        raise ValueError("qmats_from_blob wants a .bin blob (untile it first)")
+    out = {}
+    for name, m in zip(MAT_ORDER, h["mats"]):
+        def sect(off, n, dt):
+            return torch.frombuffer(bytearray(b[off:off + n]), dtype=dt)
+        out[name] = QMat(sect(m["packed_off"], m["packed_bytes"], torch.uint8),
+                         sect(m["scales_off"], m["scales_bytes"], torch.float16),
+                         sect(m["zeros_off"], m["zeros_bytes"], torch.float16),
+                         m["rows"], m["cols"], h["group_size"])
+    return out
+
+
 def expert_filename(layer: int, expert: int) -> str:
     return f"L{layer:03d}_E{expert:05d}.bin"
 

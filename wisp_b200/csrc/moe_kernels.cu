@@ -57,7 +57,7 @@ namespace wb {
 namespace {
 
 constexpr int kChunk = 32;      // elements per MMA k-slice (16 packed bytes)
-constexpr int kMT = 4;          // max tokens per expert tile (= MMA N / 2)
+constexpr int kMT = 8;          // max tokens per expert tile (two MMA column quads)
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
@@ -90,7 +90,8 @@ struct LayerArgs {
     MatOff smat[3];
     int H, I, E, K, gs, has_shared;
     int kp;   // K parts of the down projection
-    int act_slots;  // token slots of the staged activation tile (min(T, kMT))
+    int act_slots;  // token slots of the staged activation tile (min(T, mt))
+    int mt;         // tokens per expert tile of the plan (1, 4 or 8)
 };
 
 struct Ws {
@@ -687,13 +688,15 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.
+// Bounded wait for the phase with the given parity to complete (the timer is
+// read every 64 polls; each poll may itself suspend the thread briefly).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = gtimer();
-    while (!mbar_try(bar, parity))
-        if (gtimer() - t0 > kWaitNs) return false;
-    return true;
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try(bar, parity)) return true;
+        if ((n & 63u) == 0 && gtimer() - t0 > kWaitNs) return false;
+    }
 }
 // Weights are read exactly once per kernel: their copies carry an L2
 // evict-first policy so that streaming them does not push the small
@@ -764,7 +767,9 @@ __host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32, int 
 }
 // Per consumer warp scratch of the float path: one group of every slot in
 // the quantised word layout, and its (k/254, S).
-__host__ __device__ inline uint32_t qs_warp_bytes(int npg) { return kMT * (npg * 64u + 16u); }
+__host__ __device__ inline uint32_t qs_warp_bytes(int npg, int mt) {
+    return (uint32_t)mt * (npg * 64u + 16u);
+}
 
 // Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
 // the end; the tile's token count and assignment ids (for the reducer).
@@ -790,23 +795,28 @@ struct StreamSmem {
     int act_slots;
     int n_stages;
 };
-__host__ __device__ constexpr size_t red_bytes_per_stage() { return (size_t)kNcw * 32 * 8; }
-constexpr size_t kKpBytes = (size_t)(kMaxPartK / 32) * 4 * 8;  // all groups x 4 slots
+// Per stage: consumer partials for the tile width's token quads.
+__host__ __device__ constexpr size_t red_bytes_per_stage(int mt) {
+    return (size_t)kNcw * 32 * 8 * (mt / 4);
+}
+// (k/254, S) pairs: every group of a unit's K range x the tile width.
+__host__ __device__ constexpr size_t kp_bytes(int mt) { return (size_t)(kMaxPartK / 32) * mt * 8; }
 __host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage_bytes,
-                                                     uint32_t act_bytes, uint32_t qs_bytes) {
-    return (size_t)n_stages * (stage_bytes + red_bytes_per_stage() + sizeof(UnitInfo) + 24) +
-           (act_bytes + 127) / 128 * 128 + qs_bytes + kKpBytes + 16 + 128;
+                                                     uint32_t act_bytes, uint32_t qs_bytes,
+                                                     int mt) {
+    return (size_t)n_stages * (stage_bytes + red_bytes_per_stage(mt) + sizeof(UnitInfo) + 24) +
+           (act_bytes + 127) / 128 * 128 + qs_bytes + kp_bytes(mt) + 16 + 128;
 }
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
                                                   uint32_t stage_bytes, const Geo& geo, int npg,
-                                                  bool f32, int slots) {
+                                                  bool f32, int slots, int mt) {
     StreamSmem s;
     s.stage_bytes = stage_bytes;
     s.n_stages = n_stages;
     s.act_row = act_row_bytes(geo.ng, npg, f32);
     s.act_bytes = act_bytes_of(geo.ng, npg, f32, slots);
     s.act_slots = slots;
-    s.qs_warp = f32 ? qs_warp_bytes(npg) : 0u;
+    s.qs_warp = f32 ? qs_warp_bytes(npg, mt) : 0u;
     size_t o = 0;
     s.stages = base;
     o += (size_t)n_stages * stage_bytes;
@@ -815,9 +825,9 @@ __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
     s.qs = base + o;
     o += (size_t)kNcw * s.qs_warp;
     s.red = reinterpret_cast<float2*>(base + o);
-    o += (size_t)n_stages * red_bytes_per_stage();
+    o += (size_t)n_stages * red_bytes_per_stage(mt);
     s.kp = reinterpret_cast<float2*>(base + o);
-    o += kKpBytes;
+    o += kp_bytes(mt);
     s.info = reinterpret_cast<UnitInfo*>(base + o);
     o += (size_t)n_stages * sizeof(UnitInfo);
     o = (o + 7) & ~size_t(7);
@@ -1014,7 +1024,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
 // Reducer (warp 1): per unit, once the consumers' partials are in, sum them in
 // warp order (deterministic) and store the result; then release the stage.
 // out(u, asg, g, sum) is called by lane (g, q) for token slot q < m.
-template <typename Out>
+template <int MT, typename Out>
 __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     int s = 0;
@@ -1031,16 +1041,21 @@ __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
             if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
             break;
         }
-        if (!(u & kSkip) && q < inf.m) {
-            const float2* red = S.red + (size_t)s * kNcw * 32;
-            float2 sum = make_float2(0.f, 0.f);
+        if (!(u & kSkip)) {
+            const float2* red = S.red + (size_t)s * kNcw * 32 * (MT / 4);
 #pragma unroll
-            for (int w = 0; w < kNcw; ++w) {
-                const float2 v = red[w * 32 + lane];
-                sum.x += v.x;
-                sum.y += v.y;
+            for (int h = 0; h < MT / 4; ++h) {
+                if (4 * h + q < inf.m) {
+                    float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int w = 0; w < kNcw; ++w) {
+                        const float2 v = red[(w * (MT / 4) + h) * 32 + lane];
+                        sum.x += v.x;
+                        sum.y += v.y;
+                    }
+                    out(u, inf.asg[4 * h + q], g, sum);
+                }
             }
-            out(u, inf.asg[q], g, sum);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.empty[s]);
@@ -1115,33 +1130,37 @@ __device__ __forceinline__ Words<NPG> lds_w(uint32_t a) {
 // the groups past n are masked (zero B fragments and (k/254, S) = 0, so they
 // add exactly 0).  The (k/254, S) pairs of the warp's groups live in shared
 // memory, NG x kMT per warp, written and read by the owning warp only.
-template <int NPG, int NG>
+template <int NPG, int NG, int MT>
 struct WarpAct {
-    uint2 b[NG][NPG];
+    uint2 b[NG][NPG][MT / 4];  // per token quad: slots 4h .. 4h+3
 };
 
 // Copy the warp's B fragments and (k/254, S) pairs of the current tile from
 // the staged activation tile (slots t < m; the rest are zero).
-template <int NPG, int NG>
-__device__ __forceinline__ void load_act(WarpAct<NPG, NG>& A, float2* kp_w, const StreamSmem& S,
-                                         int g0, int n, int m) {
+template <int NPG, int NG, int MT>
+__device__ __forceinline__ void load_act(WarpAct<NPG, NG, MT>& A, float2* kp_w,
+                                         const StreamSmem& S, int g0, int n, int m) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    const int bt = g >> 1, bd = g & 1;
-    const uint32_t base = smem_addr(S.act) + bt * S.act_row + bd * 32;
+    const int bd = g & 1;
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
+    for (int h = 0; h < MT / 4; ++h) {
+        const int bt = 4 * h + (g >> 1);
+        const uint32_t base = smem_addr(S.act) + bt * S.act_row + bd * 32;
 #pragma unroll
-        for (int i = 0; i < NPG; ++i) {
-            const int wi = q * NPG + i;
-            const int chunk = (g0 + G) * NPG + (wi >> 2);
-            A.b[G][i] = (G < n && bt < m) ? lds64(base + chunk * 64 + (wi & 3) * 8)
-                                          : make_uint2(0u, 0u);
+        for (int G = 0; G < NG; ++G) {
+#pragma unroll
+            for (int i = 0; i < NPG; ++i) {
+                const int wi = q * NPG + i;
+                const int chunk = (g0 + G) * NPG + (wi >> 2);
+                A.b[G][i][h] = (G < n && bt < m) ? lds64(base + chunk * 64 + (wi & 3) * 8)
+                                                 : make_uint2(0u, 0u);
+            }
         }
     }
     const float4* par = reinterpret_cast<const float4*>(S.act + S.act_slots * S.act_row);
     const int ngr = (int)(S.act_row / (64u * NPG));  // groups in the range
-    for (int e = lane; e < NG * kMT; e += 32) {
-        const int G = e / kMT, t = e - G * kMT;
+    for (int e = lane; e < NG * MT; e += 32) {
+        const int G = e / MT, t = e - G * MT;
         float2 v = make_float2(0.f, 0.f);
         if (G < n && t < m) {
             const float4 p = par[t * ngr + g0 + G];
@@ -1156,22 +1175,21 @@ __device__ __forceinline__ void load_act(WarpAct<NPG, NG>& A, float2* kp_w, cons
 // t < m) with the activation quantiser (quantize_block, one group of a slot
 // per gs/4 lanes), one group at a time through the warp's scratch, and take
 // the B fragments and (k/254, S) pairs from there.
-template <int NPG, int NG>
-__device__ __forceinline__ void load_act_quant(WarpAct<NPG, NG>& A, float2* kp_w,
+template <int NPG, int NG, int MT>
+__device__ __forceinline__ void load_act_quant(WarpAct<NPG, NG, MT>& A, float2* kp_w,
                                                const StreamSmem& S, int g0, int n, int m,
                                                int cw) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    const int bt = g >> 1, bd = g & 1;
+    const int bd = g & 1;
     constexpr int kGs = 32 * NPG, kLpb = kGs / 4, kPer = 32 / kLpb;  // lanes / group, groups / pass
     uint8_t* qs = S.qs + cw * S.qs_warp;
-    float4* qpar = reinterpret_cast<float4*>(qs + kMT * NPG * 64);
-    const uint32_t qbase = smem_addr(qs) + bt * (NPG * 64) + bd * 32;
+    float4* qpar = reinterpret_cast<float4*>(qs + MT * NPG * 64);
     const float* rows = reinterpret_cast<const float*>(S.act);
     const int row_elems = (int)(S.act_row / 4);
 #pragma unroll
     for (int G = 0; G < NG; ++G) {
 #pragma unroll
-        for (int p0 = 0; p0 < kMT; p0 += kPer) {
+        for (int p0 = 0; p0 < MT; p0 += kPer) {
             if (p0 < m) {
                 const int t = p0 + lane / kLpb, pos = (lane % kLpb) * 4;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1184,46 +1202,56 @@ __device__ __forceinline__ void load_act_quant(WarpAct<NPG, NG>& A, float2* kp_w
         }
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < NPG; ++i) {
-            const int wi = q * NPG + i;
-            A.b[G][i] = (G < n && bt < m) ? lds64(qbase + (wi >> 2) * 64 + (wi & 3) * 8)
-                                          : make_uint2(0u, 0u);
+        for (int h = 0; h < MT / 4; ++h) {
+            const int bt = 4 * h + (g >> 1);
+            const uint32_t qbase = smem_addr(qs) + bt * (NPG * 64) + bd * 32;
+#pragma unroll
+            for (int i = 0; i < NPG; ++i) {
+                const int wi = q * NPG + i;
+                A.b[G][i][h] = (G < n && bt < m) ? lds64(qbase + (wi >> 2) * 64 + (wi & 3) * 8)
+                                                 : make_uint2(0u, 0u);
+            }
         }
-        if (lane < kMT) {
+        if (lane < MT) {
             float2 v = make_float2(0.f, 0.f);
             if (G < n && lane < m) {
                 const float4 pr = qpar[lane];
                 v = make_float2(pr.x, pr.y);
             }
-            kp_w[G * kMT + lane] = v;
+            kp_w[G * MT + lane] = v;
         }
         __syncwarp();
     }
 }
 
-// This warp's partial dot products of a unit: acc.x = MMA row g (block A),
-// acc.y = row g+8 (block B), for token slot q.  `st`: the stage (shared
-// address); groups g0 .. g0+NG-1 of the unit's range (those past the range
-// are read at the range's last group and contribute 0); kp: shared address of
-// this warp's (k/254, S) pairs.
-template <int NPG, int NG>
-__device__ __forceinline__ float2 mma_unit(uint32_t st, const Geo& geo, int g0,
-                                           const WarpAct<NPG, NG>& A, uint32_t kp) {
+// This warp's partial dot products of a unit: acc[h].x = MMA row g (block A),
+// acc[h].y = row g+8 (block B), for token slot 4h + q.  `st`: the stage
+// (shared address); groups g0 .. g0+NG-1 of the unit's range (those past the
+// range are read at the range's last group and contribute 0); kp: shared
+// address of this warp's (k/254, S) pairs.
+template <int NPG, int NG, int MT, int NQ>
+__device__ __forceinline__ void mma_unit(uint32_t st, const Geo& geo, int g0,
+                                         const WarpAct<NPG, NG, MT>& A, uint32_t kp,
+                                         float2 (&acc)[MT / 4]) {
+    static_assert(NQ >= 1 && NQ <= MT / 4, "active token quads");
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     constexpr uint32_t kGroupCode = 4u * 32u * NPG;  // 8 rows x gs/2 bytes
     const uint32_t a_lo = st + g * (16 * NPG) + q * (4 * NPG);
     const uint32_t z_lo = st + geo.pbytes + g * 4;
     const uint32_t kq = kp + q * 8;
-    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int h = 0; h < MT / 4; ++h) acc[h] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int G = 0; G < NG; ++G) {
         const uint32_t gg = (uint32_t)min(g0 + G, geo.ng - 1);
         const Words<NPG> wl = lds_w<NPG>(a_lo + gg * kGroupCode);
         const Words<NPG> wh = lds_w<NPG>(a_lo + geo.bbytes + gg * kGroupCode);
         const uint32_t pl = lds32(z_lo + gg * 32), ph = lds32(z_lo + geo.bbytes + gg * 32);
-        const uint2 kv = lds64(kq + G * (kMT * 8));
-        // one accumulator per MMA (independent, so they overlap), summed in int
-        int d[4] = {0, 0, 0, 0};
+        const float2 sl = __half22float2(*reinterpret_cast<const __half2*>(&pl));
+        const float2 sh = __half22float2(*reinterpret_cast<const __half2*>(&ph));
+        int d[NQ][4];
+#pragma unroll
+        for (int h = 0; h < NQ; ++h) d[h][0] = d[h][1] = d[h][2] = d[h][3] = 0;
 #pragma unroll
         for (int i = 0; i < NPG; ++i) {
             uint32_t a[4];
@@ -1231,32 +1259,39 @@ __device__ __forceinline__ float2 mma_unit(uint32_t st, const Geo& geo, int g0,
             a[1] = wh.w[i] & 0x0F0F0F0Fu;
             a[2] = (wl.w[i] >> 4) & 0x0F0F0F0Fu;
             a[3] = (wh.w[i] >> 4) & 0x0F0F0F0Fu;
-            int di[4] = {0, 0, 0, 0};
-            mma_s8(di, a, A.b[G][i].x, A.b[G][i].y);
-            d[0] += di[0];
-            d[1] += di[1];
-            d[2] += di[2];
-            d[3] += di[3];
+            // one accumulator per MMA (independent, so they overlap), summed in int
+#pragma unroll
+            for (int h = 0; h < NQ; ++h) {
+                int di[4] = {0, 0, 0, 0};
+                mma_s8(di, a, A.b[G][i][h].x, A.b[G][i][h].y);
+                d[h][0] += di[0];
+                d[h][1] += di[1];
+                d[h][2] += di[2];
+                d[h][3] += di[3];
+            }
         }
         // row += s * (k/254 * (254*A + B) - 8*S) + z * S
-        const float k2 = __uint_as_float(kv.x), S = __uint_as_float(kv.y);
-        const float m8 = -8.0f * S;
-        const float2 sl = __half22float2(*reinterpret_cast<const __half2*>(&pl));
-        const float2 sh = __half22float2(*reinterpret_cast<const __half2*>(&ph));
-        acc.x = fmaf(sl.x, fmaf(k2, (float)(d[0] * 254 + d[1]), m8), fmaf(sl.y, S, acc.x));
-        acc.y = fmaf(sh.x, fmaf(k2, (float)(d[2] * 254 + d[3]), m8), fmaf(sh.y, S, acc.y));
+#pragma unroll
+        for (int h = 0; h < NQ; ++h) {
+            const uint2 kv = lds64(kq + (G * MT + 4 * h) * 8);
+            const float k2 = __uint_as_float(kv.x), S = __uint_as_float(kv.y);
+            const float m8 = -8.0f * S;
+            acc[h].x = fmaf(sl.x, fmaf(k2, (float)(d[h][0] * 254 + d[h][1]), m8),
+                            fmaf(sl.y, S, acc[h].x));
+            acc[h].y = fmaf(sh.x, fmaf(k2, (float)(d[h][2] * 254 + d[h][3]), m8),
+                            fmaf(sh.y, S, acc[h].y));
+        }
     }
-    return acc;
 }
 
 // Consumer loop: `upt` units per tile; F32: the activation tile is fp32.
-template <int NPG, int NG, bool F32>
+template <int NPG, int NG, int MT, bool F32>
 __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int upt) {
     const int lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 2;
     const int g0 = cw * geo.ng / kNcw, n = (cw + 1) * geo.ng / kNcw - g0;
-    float2* kp_w = S.kp + cw * NG * kMT;
+    float2* kp_w = S.kp + cw * NG * MT;
     const uint32_t st0 = smem_addr(S.stages), kp = smem_addr(kp_w);
-    WarpAct<NPG, NG> A;
+    WarpAct<NPG, NG, MT> A;
     int tile_end = -1, tiles = 0, s = 0;
     uint32_t ph = 0;
     for (;;) {
@@ -1275,15 +1310,25 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
                 break;
             }
             if constexpr (F32)
-                load_act_quant<NPG, NG>(A, kp_w, S, g0, n, inf.m, cw);
+                load_act_quant<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m, cw);
             else
-                load_act<NPG, NG>(A, kp_w, S, g0, n, inf.m);
+                load_act<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m);
             if (lane == 0) mbar_arrive(S.act_empty);
             ++tiles;
         }
-        float2 part = make_float2(0.f, 0.f);
-        if (!(uf & kSkip)) part = mma_unit<NPG, NG>(st0 + s * S.stage_bytes, geo, g0, A, kp);
-        S.red[((size_t)s * kNcw + cw) * 32 + lane] = part;
+        float2 part[MT / 4];
+#pragma unroll
+        for (int h = 0; h < MT / 4; ++h) part[h] = make_float2(0.f, 0.f);
+        if (!(uf & kSkip)) {
+            // the second token quad only for tiles of more than 4 tokens (uniform)
+            if (MT == 8 && inf.m > 4)
+                mma_unit<NPG, NG, MT, MT / 4>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+            else
+                mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+        }
+        float2* red = S.red + ((size_t)s * kNcw + cw) * 32 * (MT / 4);
+#pragma unroll
+        for (int h = 0; h < MT / 4; ++h) red[h * 32 + lane] = part[h];
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.red_bar[s]);
         if (++s == S.n_stages) {
@@ -1296,13 +1341,13 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
 // ------------------------------------------------------------------------
 // gate/up + SwiGLU: unit = gate block b + up block b (8 output rows) x all of H
 // ------------------------------------------------------------------------
-template <int NPG, int NG>
+template <int NPG, int NG, int MT>
 __global__ void __launch_bounds__(kStreamCta, 1)
 gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int H = L.H, I = L.I, gs = L.gs;
     const Geo geo = make_geo(H / gs, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots, MT);
     stream_init(S);
     pdl_wait();
     pdl_launch();
@@ -1325,13 +1370,13 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         return;
     }
     if (warp == 1) {
-        reduce_units(S, W, [&](int u, int asg, int g, float2 v) {
+        reduce_units<MT>(S, W, [&](int u, int asg, int g, float2 v) {
             const size_t row = (size_t)(u % rbs) * 8 + g;
             W.h[(size_t)asg * I + row] = v.x / (1.0f + expf(-v.x)) * v.y;
         });
         return;
     }
-    consume<NPG, NG, false>(S, W, geo, rbs);
+    consume<NPG, NG, MT, false>(S, W, geo, rbs);
 }
 
 // ------------------------------------------------------------------------
@@ -1340,7 +1385,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
 // units.  Each part is written to its own ypart buffer and the combine adds
 // them in fixed order (deterministic, no float atomics).
 // ------------------------------------------------------------------------
-template <int NPG, int NG>
+template <int NPG, int NG, int MT>
 __global__ void __launch_bounds__(kStreamCta, 1)
 down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1348,7 +1393,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int H = L.H, I = L.I, gs = L.gs;
     const int ngp = I / gs / kp;  // groups per part
     const Geo geo = make_geo(ngp, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots);
+    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots, MT);
     stream_init(S);
     // Weights, the expert table and the tile plan (written by the router,
     // which completed before the gate/up kernel could start) do not depend on
@@ -1377,7 +1422,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         return;
     }
     if (warp == 1) {
-        reduce_units(S, W, [&](int u, int asg, int g, float2 v) {
+        reduce_units<MT>(S, W, [&](int u, int asg, int g, float2 v) {
             const size_t row = (size_t)(u % upt) * 16 + g;
             float* dst = W.ypart + ((size_t)pi * W.A + asg) * H + row;
             dst[0] = v.x;
@@ -1385,7 +1430,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         });
         return;
     }
-    consume<NPG, NG, true>(S, W, geo, upt);
+    consume<NPG, NG, MT, true>(S, W, geo, upt);
 }
 
 // ------------------------------------------------------------------------
@@ -1560,24 +1605,24 @@ constexpr size_t kSmemPerCta = 227 * 1024;
 constexpr size_t kInFlight = 192 * 1024;
 constexpr int kMaxStages = 12;
 
-StreamCfg plan_stream(const Geo& geo, int npg, bool f32, int slots) {
+StreamCfg plan_stream(const Geo& geo, int npg, bool f32, int slots, int mt) {
     StreamCfg c;
     c.stage_bytes = stage_bytes_of(geo);
     const uint32_t act = act_bytes_of(geo.ng, npg, f32, slots);
-    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg) : 0u;
+    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg, mt) : 0u;
     int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
     want = std::max(2, std::min(kMaxStages, want));
     c.stages = 0;
     for (int st = want; st >= 2; --st)
-        if (stream_smem_bytes(st, c.stage_bytes, act, qs) <= kSmemPerCta) {
+        if (stream_smem_bytes(st, c.stage_bytes, act, qs, mt) <= kSmemPerCta) {
             c.stages = st;
             break;
         }
-    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs);
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs, mt);
     return c;
 }
 
-int down_parts(int I, int gs, long long units, int ctas, int slots);
+int down_parts(int I, int gs, long long units, int ctas, int slots, int mt);
 
 LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     LayerArgs a{};
@@ -1596,27 +1641,42 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.K = ly->top_k;
     a.gs = (int)ly->meta.group_size;
     a.has_shared = ly->shared_blob != nullptr;
-    const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
-                            (a.has_shared ? (T + kMT - 1) / kMT : 0);
-    a.act_slots = std::min(T, kMT);
-    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots);
+    // Tokens per expert tile: 4 (one MMA column quad).  8-token tiles (two quads,
+    // WISP_B200_TILE_TOKENS=8) stream fewer duplicate tiles at larger batches but
+    // measured slower on Mixtral shapes at 16 tokens (the consumers become
+    // issue-bound); they need groups x NPG <= 8 per warp.
+    const int npg = a.gs / kChunk;
+    auto choose = [&](int mtk) {
+        a.mt = mtk;
+        a.act_slots = std::min(T, mtk);
+        const long long tiles =
+            std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
+            (a.has_shared ? (T + mtk - 1) / mtk : 0);
+        a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, mtk);
+    };
+    int want = 4;
+    if (const char* v = getenv("WISP_B200_TILE_TOKENS")) want = (atoi(v) == 8 && T > 4) ? 8 : 4;
+    choose(want);
+    if (a.mt == 8 && (ng_bucket(npg, a.H / a.gs) * npg > 8 ||
+                      ng_bucket(npg, a.I / a.gs / a.kp) * npg > 8))
+        choose(4);
     // tuning override: WISP_B200_DOWN_PARTS=<kp>, used when it is a valid split
     if (const char* v = getenv("WISP_B200_DOWN_PARTS")) {
         const int kp = atoi(v), G = a.I / a.gs;
         if (kp >= 1 && kp <= kMaxKp && G % kp == 0 && a.I / kp <= kMaxPartK &&
             ng_bucket(a.gs / kChunk, G / kp) &&
-            plan_stream(make_geo(G / kp, a.gs), a.gs / kChunk, true, a.act_slots).stages >= 2)
+            plan_stream(make_geo(G / kp, a.gs), a.gs / kChunk, true, a.act_slots, a.mt).stages >= 2)
             a.kp = kp;
     }
     return a;
 }
 
 StreamCfg gateup_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk, false, a.act_slots);
+    return plan_stream(make_geo(a.H / a.gs, a.gs), a.gs / kChunk, false, a.act_slots, a.mt);
 }
 
 StreamCfg down_cfg(const LayerArgs& a) {
-    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk, true, a.act_slots);
+    return plan_stream(make_geo(a.I / a.gs / a.kp, a.gs), a.gs / kChunk, true, a.act_slots, a.mt);
 }
 
 // K parts of the down projection.  A part is a whole number of quant groups
@@ -1625,7 +1685,7 @@ StreamCfg down_cfg(const LayerArgs& a) {
 // groups (the per-warp group count rounded up to a built bucket), uneven
 // units per CTA (`units` = down units of one part, tiles x H/16), and a small
 // cost per extra part (the combine reads every part).
-int down_parts(int I, int gs, long long units, int ctas, int slots) {
+int down_parts(int I, int gs, long long units, int ctas, int slots, int mt) {
     const int G = I / gs, npg = gs / kChunk;
     int best = 0;
     double best_score = -1.0;
@@ -1639,7 +1699,7 @@ int down_parts(int I, int gs, long long units, int ctas, int slots) {
         // a shallow ring (big stages) starves the consumers while a stage turns
         // over; small units pay the fixed per-unit cost (barriers, reduction)
         const Geo geo = make_geo(ngp, gs);
-        const int st = plan_stream(geo, npg, true, slots).stages;
+        const int st = plan_stream(geo, npg, true, slots, mt).stages;
         const double depth = std::min(1.0, st / 4.0);
         const double size = std::min(1.0, 2.0 * geo.bbytes / 32768.0);
         const double score = eff * bal * depth * size * (1.0 - 0.01 * kp);
@@ -1722,7 +1782,7 @@ bool route_in_prep(const LayerArgs& a, int T) {
     return (size_t)T * a.E * a.H * 2 <= limit;
 }
 
-int plan_tokens(int T) { return T == 1 ? 1 : kMT; }
+int plan_tokens(const LayerArgs& a, int T) { return T == 1 ? 1 : a.mt; }
 
 // Optional profiling hook: when set, an event is recorded on the launch stream
 // before every kernel of the fused path and once after the last, so a caller
@@ -1746,58 +1806,76 @@ cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, c
 
 
 
-template <int NPG, int NG>
+template <int NPG, int NG, int MT>
 cudaError_t launch_gateup(const LayerArgs& a, const Ws& W, cudaStream_t s) {
     StreamCfg c = gateup_cfg(a);
-    cudaError_t e = finish_cfg(gateup_kernel<NPG, NG>, c);
+    cudaError_t e = finish_cfg(gateup_kernel<NPG, NG, MT>, c);
     if (e != cudaSuccess) return e;
-    return launch(gateup_kernel<NPG, NG>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a, W,
-                  c.stages, c.stage_bytes);
+    return launch(gateup_kernel<NPG, NG, MT>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a,
+                  W, c.stages, c.stage_bytes);
 }
 
-template <int NPG, int NG>
+template <int NPG, int NG, int MT>
 cudaError_t launch_down(const LayerArgs& a, const Ws& W, cudaStream_t s) {
     StreamCfg c = down_cfg(a);
-    cudaError_t e = finish_cfg(down_kernel<NPG, NG>, c);
+    cudaError_t e = finish_cfg(down_kernel<NPG, NG, MT>, c);
     if (e != cudaSuccess) return e;
-    return launch(down_kernel<NPG, NG>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a, W,
+    return launch(down_kernel<NPG, NG, MT>, dim3(c.blocks), dim3(kStreamCta), c.smem, s, a, W,
                   c.stages, c.stage_bytes);
 }
 
-cudaError_t launch_gateup_any(int npg, int ng, const LayerArgs& a, const Ws& W,
+cudaError_t launch_gateup_any(int npg, int ng, int mt, const LayerArgs& a, const Ws& W,
                           cudaStream_t s) {
-    switch (npg * 100 + ng) {
-        case 101: return launch_gateup<1, 1>(a, W, s);
-        case 102: return launch_gateup<1, 2>(a, W, s);
-        case 104: return launch_gateup<1, 4>(a, W, s);
-        case 108: return launch_gateup<1, 8>(a, W, s);
-        case 116: return launch_gateup<1, 16>(a, W, s);
-        case 201: return launch_gateup<2, 1>(a, W, s);
-        case 202: return launch_gateup<2, 2>(a, W, s);
-        case 204: return launch_gateup<2, 4>(a, W, s);
-        case 207: return launch_gateup<2, 7>(a, W, s);
-        case 208: return launch_gateup<2, 8>(a, W, s);
-        case 401: return launch_gateup<4, 1>(a, W, s);
-        case 402: return launch_gateup<4, 2>(a, W, s);
+    switch (mt * 1000 + npg * 100 + ng) {
+        case 4101: return launch_gateup<1, 1, 4>(a, W, s);
+        case 8101: return launch_gateup<1, 1, 8>(a, W, s);
+        case 4102: return launch_gateup<1, 2, 4>(a, W, s);
+        case 8102: return launch_gateup<1, 2, 8>(a, W, s);
+        case 4104: return launch_gateup<1, 4, 4>(a, W, s);
+        case 8104: return launch_gateup<1, 4, 8>(a, W, s);
+        case 4108: return launch_gateup<1, 8, 4>(a, W, s);
+        case 8108: return launch_gateup<1, 8, 8>(a, W, s);
+        case 4116: return launch_gateup<1, 16, 4>(a, W, s);
+        case 4201: return launch_gateup<2, 1, 4>(a, W, s);
+        case 8201: return launch_gateup<2, 1, 8>(a, W, s);
+        case 4202: return launch_gateup<2, 2, 4>(a, W, s);
+        case 8202: return launch_gateup<2, 2, 8>(a, W, s);
+        case 4204: return launch_gateup<2, 4, 4>(a, W, s);
+        case 8204: return launch_gateup<2, 4, 8>(a, W, s);
+        case 4207: return launch_gateup<2, 7, 4>(a, W, s);
+        case 4208: return launch_gateup<2, 8, 4>(a, W, s);
+        case 4401: return launch_gateup<4, 1, 4>(a, W, s);
+        case 8401: return launch_gateup<4, 1, 8>(a, W, s);
+        case 4402: return launch_gateup<4, 2, 4>(a, W, s);
+        case 8402: return launch_gateup<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
 
-cudaError_t launch_down_any(int npg, int ng, const LayerArgs& a, const Ws& W,
+cudaError_t launch_down_any(int npg, int ng, int mt, const LayerArgs& a, const Ws& W,
                           cudaStream_t s) {
-    switch (npg * 100 + ng) {
-        case 101: return launch_down<1, 1>(a, W, s);
-        case 102: return launch_down<1, 2>(a, W, s);
-        case 104: return launch_down<1, 4>(a, W, s);
-        case 108: return launch_down<1, 8>(a, W, s);
-        case 116: return launch_down<1, 16>(a, W, s);
-        case 201: return launch_down<2, 1>(a, W, s);
-        case 202: return launch_down<2, 2>(a, W, s);
-        case 204: return launch_down<2, 4>(a, W, s);
-        case 207: return launch_down<2, 7>(a, W, s);
-        case 208: return launch_down<2, 8>(a, W, s);
-        case 401: return launch_down<4, 1>(a, W, s);
-        case 402: return launch_down<4, 2>(a, W, s);
+    switch (mt * 1000 + npg * 100 + ng) {
+        case 4101: return launch_down<1, 1, 4>(a, W, s);
+        case 8101: return launch_down<1, 1, 8>(a, W, s);
+        case 4102: return launch_down<1, 2, 4>(a, W, s);
+        case 8102: return launch_down<1, 2, 8>(a, W, s);
+        case 4104: return launch_down<1, 4, 4>(a, W, s);
+        case 8104: return launch_down<1, 4, 8>(a, W, s);
+        case 4108: return launch_down<1, 8, 4>(a, W, s);
+        case 8108: return launch_down<1, 8, 8>(a, W, s);
+        case 4116: return launch_down<1, 16, 4>(a, W, s);
+        case 4201: return launch_down<2, 1, 4>(a, W, s);
+        case 8201: return launch_down<2, 1, 8>(a, W, s);
+        case 4202: return launch_down<2, 2, 4>(a, W, s);
+        case 8202: return launch_down<2, 2, 8>(a, W, s);
+        case 4204: return launch_down<2, 4, 4>(a, W, s);
+        case 8204: return launch_down<2, 4, 8>(a, W, s);
+        case 4207: return launch_down<2, 7, 4>(a, W, s);
+        case 4208: return launch_down<2, 8, 4>(a, W, s);
+        case 4401: return launch_down<4, 1, 4>(a, W, s);
+        case 8401: return launch_down<4, 1, 8>(a, W, s);
+        case 4402: return launch_down<4, 2, 4>(a, W, s);
+        case 8402: return launch_down<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
@@ -1805,14 +1883,14 @@ cudaError_t launch_down_any(int npg, int ng, const LayerArgs& a, const Ws& W,
 cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t s) {
     (void)T;
     const int npg = a.gs / kChunk;
-    cudaError_t e = launch_gateup_any(npg, ng_bucket(npg, a.H / a.gs), a, W, s);
+    cudaError_t e = launch_gateup_any(npg, ng_bucket(npg, a.H / a.gs), a.mt, a, W, s);
     if (e != cudaSuccess) return e;
-    return launch_down_any(npg, ng_bucket(npg, a.I / a.gs / a.kp), a, W, s);
+    return launch_down_any(npg, ng_bucket(npg, a.I / a.gs / a.kp), a.mt, a, W, s);
 }
 
 cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* xin,
                           cudaStream_t s) {
-    const int mt = plan_tokens(T);
+    const int mt = plan_tokens(a, T);
     const int nsl = (a.H + kSlice - 1) / kSlice;
     const int blocks = (a.E * nsl + kWarps - 1) / kWarps;
     return launch(router_kernel, dim3(blocks), dim3(kThreads), router_smem(a.E), s, a, W, T, mt,
@@ -1829,7 +1907,7 @@ cudaError_t launch_prep(const LayerArgs& a, const Ws& W, int T, int flags, float
     hook_mark(s);
     return launch_pdl_cluster(prep_kernel, dim3(T * cs), dim3(kPrepThreads),
                               prep_smem_bytes(a.H, cs, a.E), s, cs, a, W, T, flags, x, y, eps,
-                              prevK, prev_sh, prev_kp, plan_tokens(T));
+                              prevK, prev_sh, prev_kp, plan_tokens(a, T));
 }
 
 // Routing of a layer whose input prep is about to quantise: the router in

@@ -217,6 +217,16 @@ class MoEStack:
         untiled), for the CPU oracle."""
         return [cv.untile_blob(self.arena.blob(s).cpu().numpy()) for s in self.layers[l].slots]
 
+    def host_shared(self, l: int):
+        """The shared expert of layer l as fp16 dense gate/up/down (raw bits, the
+        form the reference computes it in), or None."""
+        lw = self.layers[l]
+        if lw.shared_slot is None:
+            return None
+        q = cv.qmats_from_blob(cv.untile_blob(self.arena.blob(lw.shared_slot).cpu().numpy()))
+        return tuple(cv.dequantize_int4(q[n]).half().numpy().view(np.uint16)
+                     for n in cv.MAT_ORDER)
+
     def host_router(self, l: int) -> tuple[np.ndarray, np.ndarray | None]:
         lw = self.layers[l]
         b = lw.router_bias.cpu().numpy().view(np.uint16) if lw.router_bias is not None else None
