@@ -199,9 +199,15 @@ def run_single(args, dev) -> dict:
     gu_alg = statistics.mean(gu_bytes)
     pk = peaks()
     achieved = gu_alg / (gu_ms * 1e-3) / 1e9
+    # DRAM bytes per gate/up launch from the committed ncu capture of the same
+    # workload (Mixtral-shaped layer, decode batch 16), when the batch matches
+    traffic = None
+    tf = ROOT / "profiles" / "roofline_traffic.json"
+    if tf.exists() and B == 16:
+        traffic = json.loads(tf.read_text())["gateup_kernel"]["dram_bytes_per_launch"]
     out["roofline"] = {"bound": "hbm", "kernel": "gateup_kernel (int4 gate/up + SwiGLU stream)",
                        "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                       "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                       "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
                        "alg_bytes_per_launch": int(gu_alg), "avg_launch_ms": round(gu_ms, 5),
                        "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"}
     out["kernel_ms_mean"] = {k: round(statistics.mean(v), 5) for k, v in dur.items() if v}
