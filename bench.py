@@ -54,6 +54,9 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--skip-extra", action="store_true", help="no per-batch / e2e / profile legs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--workload", default="stack", choices=["stack", "ep"],
+                   help="stack: config 1 (default); ep: config 2, one DeepSeek-V3-shaped layer "
+                        "expert-sharded over the GPUs, 64 tokens per GPU")
     return p.parse_args()
 
 
@@ -370,6 +373,87 @@ def main_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def main_ep(args):
+    """Config 2: one DeepSeek-V3-shaped MoE layer (256 routed experts, top-8, shared
+    expert, Zipf(1.1) router bias) expert-sharded over N GPUs (256/N experts each),
+    decode batch 64 per GPU, NCCL all-to-all dispatch and combine (wisp_b200.ep)."""
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from wisp_b200 import build
+    from wisp_b200 import converter as cv
+    from wisp_b200.ep import EPLayer
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if rank == 0:
+        build.build()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        dist.barrier()
+    B = 64
+    shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=256, top_k=8, shared_inter=2048)
+    ep = EPLayer(shape, SEED, rank, world, dev, zipf_s=1.1)
+    x = cv.make_input(shape, B, SEED + 100 * rank).to(dev)
+
+    def timed(steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            ep.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item()
+
+    for _ in range(max(3, args.warmup)):
+        ep.forward(x)
+    with ClockSampler(local) as clk:
+        ms = timed(args.steps)
+    # algorithmic bytes on this GPU per step: distinct local experts routed to it by any
+    # rank + the shared expert + the router
+    _, idx, _ = ep.forward(x)
+    ids = torch.as_tensor(idx.cpu().numpy().reshape(-1))
+    if world > 1:
+        allidx = [torch.empty_like(ids.to(dev)) for _ in range(world)]
+        dist.all_gather(allidx, ids.to(dev))
+        ids = torch.cat([a.cpu() for a in allidx])
+    ids = ids.numpy()
+    mine = np.unique(ids[(ids >= rank * ep.per) & (ids < (rank + 1) * ep.per)])
+    blob = ep.local.blob_bytes - cv.HEADER_BYTES
+    step_bytes = (len(mine) + 1) * blob + shape.n_experts * shape.hidden * 2
+    tb = torch.tensor([float(step_bytes)], device=dev)
+    if world > 1:
+        dist.all_reduce(tb, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        pk = peaks()
+        gbs = tb.item() / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "MoE-block decode tokens/s (DeepSeek-V3-shaped layer, expert parallel)",
+            "value": round(B * world * 1000.0 / ms, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4xf32", "data": "synthetic (seeded; Zipf(1.1) router bias)",
+            "config": {"workload": f"config2: DeepSeek-V3-shaped MoE layer (H 7168, 256 experts "
+                                   f"top-8 + shared, inter 2048), decode batch {B} per GPU, "
+                                   f"experts sharded over {world} GPU(s), NCCL all-to-all",
+                       "global_batch": B * world, "parallelism": f"ep{world}"},
+            "roofline": {"bound": "hbm", "kernel": "whole step, most loaded GPU",
+                         "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None},
+            "clocks": clk.summary()}), flush=True)
+
+
 def main_reference(args):
     """The reference's own CPU implementation (run_moe, built from its sources), all host
     threads, bounded sample: each step = 1 token through one Mixtral-shaped block, the
@@ -428,5 +512,7 @@ if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         main_reference(a)
+    elif a.workload == "ep":
+        main_ep(a)
     else:
         main_ours(a)

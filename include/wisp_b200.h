@@ -198,6 +198,31 @@ WispError wisp_moe_block_experts(const WispMoeLayer* layer, const float* x,
                                  size_t workspace_bytes, cudaStream_t stream,
                                  WispErrCtx* err);
 
+/* New: the experts of one layer on a routing the caller supplies (device
+ * topk_idx [T, top_k] of expert indices of THIS layer descriptor, or -1, and
+ * topk_w [T, top_k]): y[t] = [shared(x[t])] + sum_j w[t,j] * E_idx[t,j](x[t]).
+ * router_w may be NULL.  The expert-parallel path runs each GPU's experts on the
+ * token rows dispatched to it (layer->top_k = 1, weights 1). */
+WispError wisp_moe_experts_routed(const WispMoeLayer* layer, const float* x,
+                                  float* y, int T, const int* topk_idx,
+                                  const float* topk_w, void* workspace,
+                                  size_t workspace_bytes, cudaStream_t stream,
+                                  WispErrCtx* err);
+/* New: routing only -- router logits (+bias), softmax and the k strict-argmax
+ * passes for T tokens into device topk_idx / topk_w [T, top_k]; the layer's
+ * expert table may be NULL.  The expert-parallel path routes on the tokens'
+ * home GPU with the full router. */
+WispError wisp_moe_route(const WispMoeLayer* layer, const float* x, int T,
+                         int* topk_idx, float* topk_w, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream,
+                         WispErrCtx* err);
+/* New: y[t] += sum_j weights[t,j] * rows[row_idx[t,j]] for j in order
+ * (row_idx < 0: skipped) -- the expert-parallel combine on the tokens' home GPU.
+ * y [T,H], rows [*,H] fp32 device buffers, row_idx/weights [T,K] device. */
+WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
+                              const float* weights, int T, int K, int H,
+                              cudaStream_t stream, WispErrCtx* err);
+
 /* No counterpart in the reference.  wisp_moe_block_forward without a
  * workspace argument, for callers that cannot allocate device memory: a host
  * binding the library through a plain C FFI with no device allocator of its

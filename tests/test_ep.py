@@ -1,0 +1,106 @@
+"""Expert parallelism (config 2).  On CPU: the dispatch bookkeeping and a 2-rank gloo
+round trip of dispatch -> per-owner expert compute -> return -> top-k-ordered combine,
+with stand-in experts.  On one GPU: the expert-parallel layer (world size 1, every
+expert local) against the fused block and against the oracle."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from wisp_b200.ep import dispatch_plan, exchange, exchange_back
+
+
+def test_dispatch_plan_orders_by_owner_then_token_then_slot():
+    idx = np.array([[5, 0, -1], [1, 7, 4], [6, 2, 3]], dtype=np.int32)
+    order, counts, tokens, eid, row_idx = dispatch_plan(idx, per=4, world=2)
+    assert counts.tolist() == [4, 4]
+    # owner 0: (0,1)=0 (1,0)=1 (2,1)=2 (2,2)=3 ; owner 1: (0,0)=5 (1,1)=7 (1,2)=4 (2,0)=6
+    assert order.tolist() == [1, 3, 7, 8, 0, 4, 5, 6]
+    assert tokens.tolist() == [0, 1, 2, 2, 0, 1, 1, 2]
+    assert eid.tolist() == [0, 1, 2, 3, 1, 3, 0, 2]
+    assert row_idx.tolist() == [[4, 0, -1], [1, 5, 6], [7, 2, 3]]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ep_rank(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    per, E, K, B, H = 3, 6, 2, 5, 4
+    g = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn(B, H, generator=g)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(B)]).int()
+    idx[1, 1] = -1  # an unrouted slot
+    w = torch.rand(B, K, generator=g)
+    order, counts, tokens, eid, row_idx = dispatch_plan(idx.numpy(), per, world)
+    send = x[torch.as_tensor(tokens)]
+    recv, rcl = exchange(send, counts, H)
+    eids, _ = exchange(torch.as_tensor(eid).view(-1, 1).float(), counts, 1)
+    # stand-in expert e (global id rank*per + local): y = (e + 1) * x + e
+    ge = eids.view(-1) + rank * per
+    rows = recv * (ge + 1).view(-1, 1) + ge.view(-1, 1)
+    back = exchange_back(rows, counts, rcl)
+    y = torch.zeros(B, H)
+    for t in range(B):
+        for j in range(K):
+            r = int(row_idx[t, j])
+            if r >= 0:
+                y[t] += w[t, j] * back[r]
+    # what the experts compute directly on this rank's tokens
+    want = torch.zeros(B, H)
+    for t in range(B):
+        for j in range(K):
+            e = int(idx[t, j])
+            if e >= 0:
+                want[t] += w[t, j] * ((e + 1) * x[t] + e)
+    out.put((rank, float((y - want).abs().max())))
+    dist.destroy_process_group()
+
+
+def test_two_rank_dispatch_compute_return_combine():
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [out.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(err < 1e-5 for _, err in res), res
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 12])
+def test_ep_layer_matches_block_and_oracle(cuda, B):
+    from oracle import oracle as orc
+    from wisp_b200 import converter as cv
+    from wisp_b200.ep import EPLayer
+    from wisp_b200.moe import MoEStack
+    from parity import check_outputs, check_routing
+    shape = cv.MoEShape(hidden=1024, inter=512, n_experts=32, top_k=8, shared_inter=512)
+    ep = EPLayer(shape, 41, 0, 1, cuda, zipf_s=1.1)
+    st = MoEStack(shape, 41, device=cuda, zipf_s=1.1)
+    x = cv.make_input(shape, B, 9).to(cuda)
+    y, idx, w = ep.forward(x)
+    yb, ib, wb = st.block(0, x, routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    assert np.array_equal(idx.cpu().numpy(), ib.cpu().numpy())
+    np.testing.assert_allclose(y.cpu().numpy(), yb.cpu().numpy(), rtol=1e-5, atol=1e-6)
+    Wb, bb = st.host_router(0)
+    yr, ir, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
+                                          shared=st.host_shared(0))
+    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.cpu().numpy()) == 0:
+        check_outputs(y.cpu().numpy(), yr, tight=False)

@@ -532,6 +532,7 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     if (warp == 0)
         topk_token(L, W, t, L.K, reinterpret_cast<const float*>(s_scr + 2 * E),
                    reinterpret_cast<float*>(s_scr), s_scr + E);
+    if (mt == 0) return;  // routing only, no plan
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -542,6 +543,38 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     __threadfence();
     build_plan(L, W, T, mt, s_scr, s_scr + kMaxPlanAssign);
     if (tid == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
+}
+
+// Expert-tile plan from a routing the caller supplies (W.topk_idx / W.topk_w,
+// [T, K]) instead of the router: the expert-parallel path routes on the tokens'
+// home GPU and runs the experts where they live.
+__global__ void __launch_bounds__(kThreads)
+plan_kernel(LayerArgs L, Ws W, int T, int mt) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ int smem[];
+    build_plan(L, W, T, mt, smem, smem + kMaxPlanAssign);
+}
+
+// y[t] += sum_j w[t,j] * rows[ridx[t,j]] in j order (ridx < 0: skipped); the
+// combine of the expert-parallel path on the tokens' home GPU.
+__global__ void __launch_bounds__(kPrepThreads)
+ep_combine_kernel(float* y, const float* rows, const int* ridx, const float* w, int T, int K,
+                  int H) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    float4* yt = reinterpret_cast<float4*>(y + (size_t)t * H);
+    for (int i = threadIdx.x; i < H / 4; i += kPrepThreads) {
+        float4 acc = yt[i];
+        for (int j = 0; j < K; ++j) {
+            const int r = ridx[t * K + j];
+            if (r < 0) continue;
+            const float wj = w[t * K + j];
+            const float4 v = reinterpret_cast<const float4*>(rows + (size_t)r * H)[i];
+            acc.x += wj * v.x; acc.y += wj * v.y; acc.z += wj * v.z; acc.w += wj * v.w;
+        }
+        yt[i] = acc;
+    }
 }
 
 // Re-read every tile's blob pointer from the expert table (for a plan built
@@ -631,6 +664,7 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
     }
     __syncthreads();
     __threadfence();
+    if (mt == 0) return;  // routing only, no plan
     build_plan(L, W, T, mt, smem, smem + kMaxPlanAssign);
     if (threadIdx.x == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
 }
@@ -1760,6 +1794,9 @@ cudaError_t ensure_attrs(int H) {
     e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)router_smem(1024));
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)router_smem(1024));
+    if (e != cudaSuccess) return e;
     done[dev & 63] = true;
     return cudaSuccess;
 }
@@ -2134,6 +2171,93 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
         }
     }
     hook_mark(stream);
+    return WISP_OK;
+}
+
+// ------------------------------------------------------------------------
+// Expert-parallel building blocks: experts on a supplied routing, and the
+// weighted combine of rows returned by the expert owners.
+// ------------------------------------------------------------------------
+extern "C" WispError wisp_moe_experts_routed(const WispMoeLayer* layer, const float* x,
+                                             float* y, int T, const int* topk_idx,
+                                             const float* topk_w, void* workspace,
+                                             size_t workspace_bytes, cudaStream_t stream,
+                                             WispErrCtx* err) {
+    if (!layer || !x || !y || x == y || !topk_idx || !topk_w || !aligned_io(x) ||
+        !aligned_io(y)) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_experts_routed: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    // the router is not used: check the layer with a stand-in router pointer
+    WispMoeLayer chk = *layer;
+    if (!chk.router_w) chk.router_w = reinterpret_cast<const wisp_half*>(x);
+    WispError ce = common_checks(&chk, 1, T, workspace, workspace_bytes, err);
+    if (ce != WISP_OK) return ce;
+    LayerArgs a = layer_args(layer, T, dev_info().sms);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Ws W = make_ws(workspace, lo);
+    W.topk_idx = const_cast<int*>(topk_idx);
+    W.topk_w = const_cast<float*>(topk_w);
+    WB_CUDA_RET(ensure_attrs(a.H), err);
+    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    WB_CUDA_RET(launch_prep(a, W, T, (int)P_QUANT, const_cast<float*>(x), nullptr, 0.f, 0, 0, 1,
+                            stream),
+                err);
+    WB_CUDA_RET(launch(plan_kernel, dim3(1), dim3(kThreads), router_smem(a.E), stream, a, W, T,
+                       plan_tokens(a, T)),
+                err);
+    return block_experts(a, W, T, x, y, stream, err);
+}
+
+extern "C" WispError wisp_moe_route(const WispMoeLayer* layer, const float* x, int T,
+                                    int* topk_idx, float* topk_w, void* workspace,
+                                    size_t workspace_bytes, cudaStream_t stream,
+                                    WispErrCtx* err) {
+    if (!layer || !x || !topk_idx || !topk_w || !aligned_io(x)) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_route: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    // the experts are not used: check the layer with a stand-in table pointer
+    WispMoeLayer chk = *layer;
+    if (!chk.expert_blobs) chk.expert_blobs = reinterpret_cast<const void* const*>(x);
+    WispError ce = common_checks(&chk, 1, T, workspace, workspace_bytes, err);
+    if (ce != WISP_OK) return ce;
+    LayerArgs a = layer_args(&chk, T, dev_info().sms);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Ws W = make_ws(workspace, lo);
+    W.topk_idx = topk_idx;
+    W.topk_w = topk_w;
+    WB_CUDA_RET(ensure_attrs(a.H), err);
+    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    const int cs = prep_cluster(a.H, a.gs);
+    const bool fused = route_in_prep(a, T);
+    hook_mark(stream);
+    WB_CUDA_RET(launch_pdl_cluster(prep_kernel, dim3(T * cs), dim3(kPrepThreads),
+                                   prep_smem_bytes(a.H, cs, a.E), stream, cs, a, W, T,
+                                   (int)(P_QUANT | (fused ? P_ROUTE : 0)),
+                                   const_cast<float*>(x), (float*)nullptr, 0.f, 0, 0, 1, 0),
+                err);
+    if (!fused) {
+        const int nsl = (a.H + kSlice - 1) / kSlice;
+        const int blocks = (a.E * nsl + kWarps - 1) / kWarps;
+        WB_CUDA_RET(launch(router_kernel, dim3(blocks), dim3(kThreads), router_smem(a.E), stream,
+                           a, W, T, 0, x, nsl),
+                    err);
+    }
+    return WISP_OK;
+}
+
+extern "C" WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
+                                         const float* weights, int T, int K, int H,
+                                         cudaStream_t stream, WispErrCtx* err) {
+    if (!y || !row_idx || !weights || T <= 0 || K <= 0 || H <= 0 || H % 4 || !aligned_io(y) ||
+        (rows && !aligned_io(rows))) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_ep_combine: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    WB_CUDA_RET(launch(ep_combine_kernel, dim3(T), dim3(kPrepThreads), 0, stream, y, rows,
+                       row_idx, weights, T, K, H),
+                err);
     return WISP_OK;
 }
 

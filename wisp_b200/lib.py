@@ -59,6 +59,13 @@ _SIGS = {
                                          C.POINTER(WispErrCtx)]),
     "wisp_expert_tile": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.POINTER(WispErrCtx)]),
+    "wisp_moe_experts_routed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                          C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_moe_route": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_size_t, C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_moe_ep_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                      C.c_int, C.c_int, C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),

@@ -101,29 +101,35 @@ class MoEStack:
     """A seeded synthetic MoE stack resident on one GPU (see ``converter`` for the recipe)."""
 
     def __init__(self, shape: cv.MoEShape, seed: int, device="cuda", zipf_s: float | None = None,
-                 random_bias: bool = False, n_layers: int | None = None, layer0: int = 0):
+                 random_bias: bool = False, n_layers: int | None = None, layer0: int = 0,
+                 expert_ids=None, with_shared: bool = True):
+        """`expert_ids`: the experts this stack holds (default all; the expert-parallel
+        path holds a slice, table entry i = expert expert_ids[i]); `with_shared`: build
+        the shape's shared expert (if any)."""
         self.shape = shape
         self.device = torch.device(device)
         self.L = n_layers or shape.n_layers
         self.layer0 = layer0
-        E = shape.n_experts
+        self.expert_ids = list(range(shape.n_experts)) if expert_ids is None else list(expert_ids)
+        has_shared = bool(shape.shared_inter) and with_shared
+        E = len(self.expert_ids)
         probe = cv.make_expert(cv.MoEShape(shape.hidden, shape.inter, E, shape.top_k,
                                            shape.group_size), 0, 0, seed, device=self.device)
         self.blob_bytes = blob_bytes_of(probe)
-        n_slots = self.L * E + (self.L if shape.shared_inter else 0)
+        n_slots = self.L * E + (self.L if has_shared else 0)
         self.arena = ExpertArena(n_slots, self.blob_bytes, self.device)
         self.layers: list[LayerWeights] = []
         slot = 0
         for li in range(self.L):
             l = layer0 + li
             slots = []
-            for e in range(E):
+            for e in self.expert_ids:
                 mats = cv.make_expert(shape, l, e, seed, device=self.device)
                 self.arena.write(slot, l, e, mats)
                 slots.append(slot)
                 slot += 1
             sh = None
-            if shape.shared_inter:
+            if has_shared:
                 self.arena.write(slot, l, 0xFFFF, cv.make_shared_expert(shape, l, seed, self.device))
                 sh = slot
                 slot += 1
@@ -135,7 +141,7 @@ class MoEStack:
                 g = torch.Generator().manual_seed(seed + 3 + l)
                 bias = (torch.randn(E, generator=g) * 0.5).half().to(self.device)
             table = torch.tensor([self.arena.ptr(s) for s in slots], dtype=torch.int64,
-                                 device=self.device)
+                                 device=self.device) if slots else None
             self.layers.append(LayerWeights(router, bias, torch.ones(shape.hidden,
                                                                      dtype=torch.float16,
                                                                      device=self.device),
@@ -147,7 +153,7 @@ class MoEStack:
         for l, lw in enumerate(self.layers):
             c = self._c_layers[l]
             c.meta = self.meta
-            c.expert_blobs = lw.table.data_ptr()
+            c.expert_blobs = lw.table.data_ptr() if lw.table is not None else None
             c.router_w = lw.router.data_ptr()
             c.router_bias = lw.router_bias.data_ptr() if lw.router_bias is not None else None
             c.norm_w = lw.norm.data_ptr()
