@@ -223,6 +223,24 @@ WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
                               const float* weights, int T, int K, int H,
                               cudaStream_t stream, WispErrCtx* err);
 
+/* New: the block for batched / prefill tokens on the tensor cores (tcgen05).
+ * Same contract as wisp_moe_block_forward -- x [T,H] fp32 MoE input (already
+ * normalised), y [T,H] fp32 output (overwritten), optional device
+ * topk_idx/topk_w [T, top_k] -- for T independent tokens of run_moe
+ * (csrc/core/wisp_engine.c:1411-1522): the tokens are grouped by expert and
+ * every expert runs as one GEMM over its tokens, int4 dequantised to fp16 in
+ * shared memory, fp32 accumulation.  Needs tiled experts with group_size 64,
+ * hidden and intermediate sizes multiples of 128, and a shared expert (if any)
+ * of the routed experts' layout.  Launch-only; the status word (offset 0 of
+ * the workspace, wisp_moe_status) reports missing or misaligned experts and
+ * timeouts.  workspace: wisp_moe_prefill_workspace_bytes(layer, T) bytes,
+ * 1024-byte aligned. */
+size_t wisp_moe_prefill_workspace_bytes(const WispMoeLayer* layer, int T);
+WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x,
+                                   float* y, int T, int* topk_idx, float* topk_w,
+                                   void* workspace, size_t workspace_bytes,
+                                   cudaStream_t stream, WispErrCtx* err);
+
 /* No counterpart in the reference.  wisp_moe_block_forward without a
  * workspace argument, for callers that cannot allocate device memory: a host
  * binding the library through a plain C FFI with no device allocator of its

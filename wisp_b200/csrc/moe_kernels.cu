@@ -50,6 +50,7 @@
 #include <mutex>
 
 #include "internal.h"
+#include "route_common.cuh"
 
 #include <cooperative_groups.h>
 
@@ -211,67 +212,11 @@ __device__ __forceinline__ void quantize_row(const float4* src, int n, int gs, i
 constexpr int kSlice = 1024;
 
 // Softmax + top-k of token t from its logits lg[E] (without the bias), by one
-// warp; sp/staken: [E] shared scratch of this warp.
+// warp; sp/staken: [E] shared scratch of this warp (rule: route_common.cuh).
 __device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, const float* lg,
                            float* sp, int* staken) {
-    const int lane = threadIdx.x & 31;
-    const int E = L.E;
-    float mx = -1e30f;
-    for (int e = lane; e < E; e += 32) {
-        float v = lg[e];
-        if (L.router_bias) v += __half2float(L.router_bias[e]);
-        sp[e] = v;
-        staken[e] = 0;
-        mx = fmaxf(mx, v);
-    }
-    mx = warp_max(mx);
-    float den = 0.f;
-    for (int e = lane; e < E; e += 32) {
-        const float v = expf(sp[e] - mx);
-        sp[e] = v;
-        den += v;
-    }
-    den = warp_sum(den);
-    for (int e = lane; e < E; e += 32) sp[e] = sp[e] / den;
-    __syncwarp();
-    float wsum = 0.f;
-    float wsel[64];
-    int isel[64];
-    for (int j = 0; j < K; ++j) {
-        float bv = -1.f;
-        int be = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            const float v = sp[e];
-            if (!staken[e] && v > bv) {
-                bv = v;
-                be = e;
-            }
-        }
-        // warp argmax: larger value wins, equal values -> lower index
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(kFull, bv, o);
-            const int oe = __shfl_xor_sync(kFull, be, o);
-            if (ov > bv || (ov == bv && oe < be)) {
-                bv = ov;
-                be = oe;
-            }
-        }
-        if (bv < 0.f) be = -1;
-        if (lane == 0 && be >= 0) staken[be] = 1;
-        __syncwarp();
-        wsel[j] = bv;
-        isel[j] = be;
-        if (be >= 0) wsum += bv;
-    }
-    if (lane == 0) {
-        for (int j = 0; j < K; ++j) {
-            float wj = isel[j] >= 0 ? wsel[j] : 0.f;
-            if (wsum > 0.f) wj = wj / wsum;
-            W.topk_idx[t * K + j] = isel[j];
-            W.topk_w[t * K + j] = wj;
-        }
-    }
+    wisp_route::warp_topk(lg, L.router_bias, L.E, K, sp, staken, W.topk_idx + t * K,
+                          W.topk_w + t * K);
 }
 
 // The tiled blob of expert e (E = the shared expert), or NULL with the status

@@ -1,0 +1,1090 @@
+// prefill.cu -- the MoE block for batched and prefill tokens on the 5th-generation
+// tensor cores (tcgen05 + TMA).
+//
+// Semantics are the reference's run_moe (csrc/core/wisp_engine.c:1411-1522) per
+// token -- the reference has no batch, a batch of T tokens is T independent
+// calls -- with the router rule of router.cu:60-120 / wisp_engine.c:520-556
+// (route_common.cuh), the int4 rule of quantizer.py:89-105 (weight =
+// (q - 8) * scale + zero, scale and zero fp16), SwiGLU h = silu(g) * u
+// (matmul.cu:169-205) and the combine y = shared(x) + sum_j w_j * down_j(h_j)
+// (wisp_engine.c:1443-1522).  Like the reference's GPU dequant
+// (expert_loader.cu:23-43) the weights are rounded to fp16 before the matmul;
+// the activations are rounded to fp16 too, and every product is accumulated in
+// fp32 (TMEM).
+//
+// One block, all on one stream, no host synchronisation:
+//   router_logits_kernel  logits [T, E] in fp32 on the CUDA cores
+//   route_topk_kernel     softmax(+bias) top-k, one warp per token
+//   prefill_plan_kernel   one CTA: the (token, slot) assignments grouped by
+//                         expert into rows, the tile lists, and the per-expert
+//                         TMA descriptors (a host-encoded template whose global
+//                         address is replaced on the device, so experts may sit
+//                         anywhere: resident arena, cache slots, scratch ring)
+//   prefill_scatter_kernel xs[row] = fp16(x[token(row)]) for every row; y = 0
+//   grouped_gemm<2>       gate/up: hs[row] = silu(Wg xs[row]) * (Wu xs[row])
+//   grouped_gemm<1>       down:    y[token(row)] += w(row) * (Wd hs[row])
+//
+// The grouped GEMM puts the weights on the MMA's M side (128 weight rows per
+// tile) and the tokens of one expert on N (16..256 per tile), so an expert with
+// few tokens wastes little of the tensor core.  A persistent CTA per SM walks
+// the tile list (static round robin) with warp-specialised roles:
+//   warps 0-3   epilogue: tcgen05.ld of the fp32 accumulators (warp q reads
+//               TMEM lanes 32q..32q+31), SwiGLU / gate-weighted combine
+//   warp 4      weight producer: two 3-D TMA loads per matrix and K block
+//               (the codes and the scale/zero pairs of 16 tiled 8-row blocks)
+//   warp 5      MMA issuer (one thread): tcgen05.mma kind::f16, M=128, K=16
+//   warp 6      activation producer: 2-D TMA loads, 128-byte swizzle
+//   warps 7-14  dequantisers: int4 codes -> fp16 in the 128-byte swizzled
+//               K-major layout tcgen05 reads (one quant group of 64 = one row
+//               of a swizzle atom)
+// Shared-memory rings with mbarriers connect the roles; every wait is bounded
+// (2 s of %globaltimer) and a timeout sets ST_TIMEOUT in the status word, makes
+// every role leave, drains the copies and MMAs in flight and frees TMEM.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "internal.h"
+#include "route_common.cuh"
+
+namespace {
+
+enum { ST_ALIGN = 1, ST_EXPERT = 2, ST_PLAN = 4, ST_TIMEOUT = 8, ST_LAYOUT = 16 };
+constexpr uint32_t kTiledVersion = 2;
+constexpr unsigned kFull = 0xffffffffu;
+
+constexpr int kBM = 128;        // weight rows per tile (MMA M)
+constexpr int kBK = 64;         // K per stage: one quant group
+constexpr int kNT = 256;        // max tokens per tile (MMA N)
+constexpr int kGemmThreads = 480;
+constexpr int kWProdWarp = 4, kMmaWarp = 5, kBProdWarp = 6, kDqWarp0 = 7, kDqWarps = 8;
+constexpr int kMaps = 6;        // per expert: (gate, up, down) x (codes, scale/zero)
+constexpr int kBoxes = 5;       // activation boxes of 16, 32, 64, 128, 256 rows
+constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr int kPlanThreads = 1024;
+constexpr int kRouteTile = 64;
+
+constexpr int kATile = kBM * 128;          // 128 rows x 64 fp16 (16 KB)
+constexpr int kBTile = kNT * 128;          // 256 rows x 64 fp16 (32 KB)
+constexpr int kWCodes = 16 * 8 * 32;       // 16 blocks x 8 rows x 32 code bytes
+constexpr int kWStage = kWCodes + 16 * 32;  // + 16 blocks x 8 (scale, zero) pairs
+
+struct PTile {
+    int e, mt, row0, n;  // expert (E = shared), weight-row tile, first row, tokens
+};
+
+struct BMaps {
+    CUtensorMap box[kBoxes];  // box i: 64 columns x (16 << i) rows
+};
+struct WTemplates {
+    CUtensorMap m[kMaps];  // global address replaced per expert on the device
+};
+
+struct PArgs {
+    const void* const* blobs;
+    const void* shared_blob;
+    const __half* router_w;
+    const __half* router_bias;
+    unsigned long long mat_off[3];  // packed_off of gate, up, down in a blob
+    int H, I, E, K, has_shared;
+};
+
+struct PWs {
+    int* status;
+    int* counters;    // [0] gate/up tiles, [1] down tiles
+    float* logits;    // [T, E]
+    int* idx;         // [T, K]
+    float* w;         // [T, K]
+    int* cnt;         // [E + 1] rows per expert (E = shared)
+    int* seg;         // [E + 2] first row per expert
+    int* row_tok;     // [R]
+    float* row_w;     // [R]
+    int* row_of;      // [T * K]
+    PTile* tiles_gu;  // [max_gu]
+    PTile* tiles_dn;  // [max_dn]
+    CUtensorMap* wmaps;  // [(E + 1) * kMaps]
+    __half* xs;       // [R, H]
+    __half* hs;       // [R, I]
+    int R, max_gu, max_dn;
+};
+
+template <int NMAT>
+struct GCfg;
+template <>
+struct GCfg<2> {  // gate + up
+    static constexpr int WS = 6, AS = 2, BS = 3, NACC = 1;
+};
+template <>
+struct GCfg<1> {  // down
+    static constexpr int WS = 8, AS = 3, BS = 4, NACC = 2;
+};
+
+template <int NMAT>
+constexpr size_t gemm_smem_bytes() {
+    using C = GCfg<NMAT>;
+    return 1024 + (size_t)C::AS * NMAT * kATile + (size_t)C::BS * kBTile +
+           (size_t)C::WS * NMAT * kWStage + 256;
+}
+
+// ------------------------------------------------------------------------
+// device helpers
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait of one thread; false on timeout (sets the abort flag and
+// ST_TIMEOUT) or when another role aborted.
+__device__ __forceinline__ bool wait1(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                      int* status) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63) == 63) {
+            if (*abort_flag) return false;
+            const uint64_t t = gtimer();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > kWaitNs) {
+                *abort_flag = 1;
+                atomicOr(status, ST_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+// The same for a whole warp, with a warp-uniform result.
+__device__ __forceinline__ bool wait_warp(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                          int* status) {
+    const int lane = threadIdx.x & 31;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (__all_sync(kFull, mbar_try(b, parity))) return true;
+        if ((it & 63) == 63) {
+            int stop = 0;
+            if (lane == 0) {
+                if (*abort_flag) {
+                    stop = 1;
+                } else {
+                    const uint64_t t = gtimer();
+                    if (t0 == 0) {
+                        t0 = t;
+                    } else if (t - t0 > kWaitNs) {
+                        *abort_flag = 1;
+                        atomicOr(status, ST_TIMEOUT);
+                        stop = 1;
+                    }
+                }
+            }
+            if (__shfl_sync(kFull, stop, 0)) return false;
+        }
+    }
+}
+// Drain wait: ignores the abort flag, bounded by time only.
+__device__ __forceinline__ void wait_drain(uint64_t* b, uint32_t parity) {
+    const uint64_t t0 = gtimer();
+    while (!mbar_try(b, parity))
+        if (gtimer() - t0 > kWaitNs) return;
+}
+
+__device__ __forceinline__ void tma3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                      uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(saddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(saddr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                      uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(saddr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmap_acquire(const CUtensorMap* map) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
+                     reinterpret_cast<uint64_t>(map))
+                 : "memory");
+}
+
+// tcgen05 ------------------------------------------------------------------
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 B (stride byte offset 1024, leading byte offset unused = 16 B),
+// descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, both
+// K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t id,
+                                        uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            saddr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(addr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Eight int4 codes (one 32-bit word, low nibble = even element) with their
+// group's fp16 scale and zero -> eight fp16 weights (q - 8) * s + z, rounded
+// once (fused multiply-add on the exact q - 8).  1024 + q is built in the
+// fp16 bit pattern (0x6400 | q) and 1032 subtracted exactly.
+__device__ __forceinline__ uint4 dequant8(uint32_t v, uint32_t sz) {
+    const uint32_t t0 = (v & 0x000F000Fu) | 0x64006400u;          // (e0, e4)
+    const uint32_t t1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;   // (e1, e5)
+    const uint32_t t2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;   // (e2, e6)
+    const uint32_t t3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;  // (e3, e7)
+    uint32_t p[4];
+    p[0] = __byte_perm(t0, t1, 0x5410);  // (e0, e1)
+    p[1] = __byte_perm(t2, t3, 0x5410);  // (e2, e3)
+    p[2] = __byte_perm(t0, t1, 0x7632);  // (e4, e5)
+    p[3] = __byte_perm(t2, t3, 0x7632);  // (e6, e7)
+    const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
+    const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(sz >> 16)));
+    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6408u));  // 1032
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&p[i]), off);
+        const __half2 w = __hfma2(q, s2, z2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&w);
+    }
+    return out;
+}
+
+// ------------------------------------------------------------------------
+// routing
+// ------------------------------------------------------------------------
+
+// logits[t][e] = sum_h x[t][h] * W[e][h] in fp32.  CTA tile 64 tokens x 64
+// experts, 256 threads of 4 x 4 outputs, K in chunks of 32.
+__global__ void __launch_bounds__(256)
+router_logits_kernel(const float* __restrict__ x, const __half* __restrict__ Wr,
+                     float* __restrict__ lg, int T, int E, int H) {
+    pdl_wait();
+    pdl_launch();
+    __shared__ float xs[32][kRouteTile + 4];
+    __shared__ float ws[32][kRouteTile + 4];
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int t0 = blockIdx.x * kRouteTile, e0 = blockIdx.y * kRouteTile;
+    float acc[4][4] = {};
+    for (int h0 = 0; h0 < H; h0 += 32) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int id = tid + 256 * i, r = id >> 5, k = id & 31;
+            const int t = t0 + r, e = e0 + r;
+            xs[k][r] = t < T ? x[(size_t)t * H + h0 + k] : 0.f;
+            ws[k][r] = e < E ? __half2float(Wr[(size_t)e * H + h0 + k]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty * 4 + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + tx * 4 + j;
+            if (e < E) lg[(size_t)t * E + e] = acc[i][j];
+        }
+    }
+}
+
+// softmax(+bias) top-k per token, one warp per token.
+__global__ void __launch_bounds__(256)
+route_topk_kernel(const float* __restrict__ lg, const __half* bias, int T, int E, int K,
+                  int* idx, float* w) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ float rs[];
+    const int warp = threadIdx.x >> 5;
+    float* sp = rs + (size_t)warp * 2 * E;
+    int* staken = reinterpret_cast<int*>(sp + E);
+    for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+        wisp_route::warp_topk(lg + (size_t)t * E, bias, E, K, sp, staken, idx + (size_t)t * K,
+                              w + (size_t)t * K);
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------------
+// plan: rows grouped by expert, tiles, TMA descriptors
+// ------------------------------------------------------------------------
+__device__ const void* blob_of(const PArgs& P, int e) {
+    return e == P.E ? P.shared_blob : P.blobs[e];
+}
+
+__global__ void __launch_bounds__(kPlanThreads)
+prefill_plan_kernel(PArgs P, PWs W, int T, const __grid_constant__ WTemplates tmpl) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ int ps[];
+    __shared__ alignas(128) CUtensorMap s_map[kPlanThreads / 32];
+    const int E = P.E, K = P.K, NE = E + 1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int* s_cnt = ps;               // [E + 1]
+    int* s_fill = s_cnt + NE;      // [E + 1]
+    int* s_seg = s_fill + NE;      // [E + 2]
+    int* s_tgu = s_seg + NE + 1;   // [E + 2]
+    int* s_tdn = s_tgu + NE + 1;   // [E + 2]
+    const int mt_gu = P.I / kBM, mt_dn = P.H / kBM;
+    for (int e = tid; e < NE; e += kPlanThreads) {
+        s_cnt[e] = 0;
+        s_fill[e] = 0;
+    }
+    __syncthreads();
+    for (int a = tid; a < T * K; a += kPlanThreads) {
+        const int e = W.idx[a];
+        if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+    }
+    if (tid == 0) s_cnt[E] = P.has_shared ? T : 0;
+    __syncthreads();
+    // the experts that have rows must be present, tiled and 16-byte aligned
+    for (int e = tid; e < NE; e += kPlanThreads) {
+        if (s_cnt[e] == 0) continue;
+        const void* b = blob_of(P, e);
+        int bad = 0;
+        if (!b)
+            bad = ST_EXPERT;
+        else if ((reinterpret_cast<uintptr_t>(b) & 15) != 8)
+            bad = ST_ALIGN;
+        else if (__ldg(reinterpret_cast<const uint32_t*>(b) + 1) != kTiledVersion)
+            bad = ST_LAYOUT;
+        if (bad) {
+            atomicOr(W.status, bad);
+            s_cnt[e] = 0;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0, tg = 0, td = 0;
+        for (int e = 0; e < NE; ++e) {
+            s_seg[e] = run;
+            s_tgu[e] = tg;
+            s_tdn[e] = td;
+            const int nt = (s_cnt[e] + kNT - 1) / kNT;
+            run += s_cnt[e];
+            tg += nt * mt_gu;
+            td += nt * mt_dn;
+        }
+        s_seg[NE] = run;
+        s_tgu[NE] = tg;
+        s_tdn[NE] = td;
+        if (run > W.R || tg > W.max_gu || td > W.max_dn) {
+            atomicOr(W.status, ST_PLAN);
+            tg = td = 0;
+        }
+        W.counters[0] = tg;
+        W.counters[1] = td;
+    }
+    __syncthreads();
+    for (int e = tid; e < NE; e += kPlanThreads) {
+        W.cnt[e] = s_cnt[e];
+        W.seg[e] = s_seg[e];
+    }
+    if (tid == 0) W.seg[NE] = s_seg[NE];
+    for (int a = tid; a < T * K; a += kPlanThreads) {
+        const int e = W.idx[a];
+        int r = -1;
+        if (e >= 0 && e < E && s_cnt[e] > 0 && s_seg[e] + s_cnt[e] <= W.R) {
+            r = s_seg[e] + atomicAdd(&s_fill[e], 1);
+            W.row_tok[r] = a / K;
+            W.row_w[r] = W.w[a];
+        }
+        W.row_of[a] = r;
+    }
+    if (s_cnt[E] > 0 && s_seg[E] + T <= W.R)
+        for (int t = tid; t < T; t += kPlanThreads) {
+            W.row_tok[s_seg[E] + t] = t;
+            W.row_w[s_seg[E] + t] = 1.f;
+        }
+    // tile lists, ordered (expert, token tile, weight-row tile)
+    const int ntg = W.counters[0] ? s_tgu[NE] : 0, ntd = W.counters[1] ? s_tdn[NE] : 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        const int* base = pass ? s_tdn : s_tgu;
+        const int n = pass ? ntd : ntg, mt_per = pass ? mt_dn : mt_gu;
+        PTile* out = pass ? W.tiles_dn : W.tiles_gu;
+        for (int i = tid; i < n; i += kPlanThreads) {
+            int lo = 0, hi = NE;  // last e with base[e] <= i
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (base[mid] <= i) lo = mid; else hi = mid;
+            }
+            // experts with no tiles share a base: take the one that has tiles
+            int e = lo;
+            while (e + 1 < NE && base[e + 1] <= i) ++e;
+            const int local = i - base[e], nt = local / mt_per;
+            PTile tl;
+            tl.e = e;
+            tl.mt = local - nt * mt_per;
+            tl.row0 = s_seg[e] + nt * kNT;
+            tl.n = min(kNT, s_cnt[e] - nt * kNT);
+            out[i] = tl;
+        }
+    }
+    // TMA descriptors of the experts with rows: one warp per descriptor
+    for (int j = warp; j < NE * kMaps; j += kPlanThreads / 32) {
+        const int e = j / kMaps, m = j - e * kMaps;
+        if (s_cnt[e] == 0) continue;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&tmpl.m[m]);
+        reinterpret_cast<uint32_t*>(&s_map[warp])[lane] = src[lane];
+        __syncwarp();
+        if (lane == 0) {
+            const int mat = m >> 1;
+            const unsigned long long cols = mat == 2 ? (unsigned long long)P.I : P.H;
+            const unsigned long long addr = reinterpret_cast<unsigned long long>(blob_of(P, e)) +
+                                            P.mat_off[mat] + ((m & 1) ? 4ull * cols : 0ull);
+            asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;"
+                         ::"r"(saddr(&s_map[warp])), "l"(addr)
+                         : "memory");
+        }
+        __syncwarp();
+        asm volatile(
+            "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync."
+            "aligned [%0], [%1], 128;" ::"l"(reinterpret_cast<uint64_t>(W.wmaps + j)),
+            "r"(saddr(&s_map[warp]))
+            : "memory");
+        __syncwarp();
+    }
+}
+
+// xs[row] = fp16(x[token]) for each row of token t (routed slots + shared);
+// y[t] = 0 (the down GEMM accumulates into it).
+__global__ void __launch_bounds__(256)
+prefill_scatter_kernel(PArgs P, PWs W, int T, const float* __restrict__ x, float* __restrict__ y) {
+    pdl_wait();
+    pdl_launch();
+    const int t = blockIdx.x, K = P.K, H = P.H;
+    __shared__ int rows[65];
+    if (threadIdx.x < K) rows[threadIdx.x] = W.row_of[t * K + threadIdx.x];
+    if (threadIdx.x == 0) rows[K] = W.cnt[P.E] > 0 ? W.seg[P.E] + t : -1;
+    __syncthreads();
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
+    float4* yr = reinterpret_cast<float4*>(y + (size_t)t * H);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+        const float4 a = xr[2 * c], b = xr[2 * c + 1];
+        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+        const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+        uint4 v;
+        v.x = *reinterpret_cast<const uint32_t*>(&h0);
+        v.y = *reinterpret_cast<const uint32_t*>(&h1);
+        v.z = *reinterpret_cast<const uint32_t*>(&h2);
+        v.w = *reinterpret_cast<const uint32_t*>(&h3);
+        for (int j = 0; j <= K; ++j) {
+            const int r = rows[j];
+            if (r >= 0) reinterpret_cast<uint4*>(W.xs + (size_t)r * H)[c] = v;
+        }
+        yr[2 * c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        yr[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// ------------------------------------------------------------------------
+// the grouped GEMM
+// ------------------------------------------------------------------------
+template <int NMAT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __restrict__ y) {
+    using C = GCfg<NMAT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~(uintptr_t)1023);
+    uint8_t* sA = base;
+    uint8_t* sB = sA + C::AS * NMAT * kATile;
+    uint8_t* sW = sB + C::BS * kBTile;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * kWStage);
+    uint64_t* w_empty = w_full + C::WS;
+    uint64_t* a_full = w_empty + C::WS;
+    uint64_t* a_empty = a_full + C::AS;
+    uint64_t* b_full = a_empty + C::AS;
+    uint64_t* b_empty = b_full + C::BS;
+    uint64_t* acc_full = b_empty + C::BS;
+    uint64_t* acc_empty = acc_full + C::NACC;
+    uint64_t* drain = acc_empty + C::NACC;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < C::WS; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], kDqWarps);
+        }
+        for (int i = 0; i < C::AS; ++i) {
+            mbar_init(&a_full[i], kDqWarps);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < C::BS; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < C::NACC; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        mbar_init(drain, 1);
+        *s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                         saddr(s_tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    pdl_wait();
+    pdl_launch();
+    const int ntiles = __ldcg(W.counters + (NMAT == 2 ? 0 : 1));
+    const PTile* tiles = NMAT == 2 ? W.tiles_gu : W.tiles_dn;
+    const int KB = (NMAT == 2 ? P.H : P.I) / kBK;
+    int* status = W.status;
+
+    if (warp == kWProdWarp) {
+        if (lane == 0) {
+            uint32_t wi = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+                const PTile tl = tiles[t];
+                const CUtensorMap* maps[NMAT][2];
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    const int mat = NMAT == 2 ? m : 2;
+                    maps[m][0] = W.wmaps + tl.e * kMaps + mat * 2;
+                    maps[m][1] = maps[m][0] + 1;
+                    tmap_acquire(maps[m][0]);
+                    tmap_acquire(maps[m][1]);
+                }
+                for (int kb = 0; kb < KB; ++kb, ++wi) {
+                    const int s = wi % C::WS;
+                    if (!wait1(&w_empty[s], ((wi / C::WS) & 1) ^ 1, s_abort, status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&w_full[s], NMAT * kWStage);
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        uint8_t* dst = sW + (s * NMAT + m) * kWStage;
+                        tma3d(dst, maps[m][0], 0, kb, tl.mt * 16, &w_full[s]);
+                        tma3d(dst + kWCodes, maps[m][1], 0, kb, tl.mt * 16, &w_full[s]);
+                    }
+                }
+            }
+            const uint32_t first = wi > (uint32_t)C::WS ? wi - C::WS : 0;
+            for (uint32_t i = first; i < wi; ++i) wait_drain(&w_full[i % C::WS], (i / C::WS) & 1);
+        }
+    } else if (warp == kBProdWarp) {
+        if (lane == 0) {
+            uint32_t bi = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+                const PTile tl = tiles[t];
+                const int nmma = (tl.n + 15) & ~15;
+                for (int kb = 0; kb < KB; ++kb, ++bi) {
+                    const int s = bi % C::BS;
+                    if (!wait1(&b_empty[s], ((bi / C::BS) & 1) ^ 1, s_abort, status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&b_full[s], (uint32_t)nmma * 128);
+                    int off = 0;
+#pragma unroll
+                    for (int i = kBoxes - 1; i >= 0; --i) {
+                        const int h = 16 << i;
+                        if ((nmma - off) >= h) {
+                            tma2d(sB + s * kBTile + off * 128, &bm.box[i], kb * kBK, tl.row0 + off,
+                                  &b_full[s]);
+                            off += h;
+                        }
+                    }
+                }
+            }
+            const uint32_t first = bi > (uint32_t)C::BS ? bi - C::BS : 0;
+            for (uint32_t i = first; i < bi; ++i) wait_drain(&b_full[i % C::BS], (i / C::BS) & 1);
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            uint32_t ai = 0, bi = 0, ci = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++ci) {
+                const PTile tl = tiles[t];
+                const int nmma = (tl.n + 15) & ~15;
+                const uint32_t id = idesc_f16(nmma);
+                const int buf = ci % C::NACC;
+                if (!wait1(&acc_empty[buf], ((ci / C::NACC) & 1) ^ 1, s_abort, status)) break;
+                tc_fence_after();
+                for (int kb = 0; kb < KB; ++kb, ++ai, ++bi) {
+                    const int sa = ai % C::AS, sb = bi % C::BS;
+                    if (!wait1(&a_full[sa], (ai / C::AS) & 1, s_abort, status) ||
+                        !wait1(&b_full[sb], (bi / C::BS) & 1, s_abort, status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t bad = saddr(sB + sb * kBTile);
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        const uint32_t aad = saddr(sA + (sa * NMAT + m) * kATile);
+                        const uint32_t d = tmem + (uint32_t)((NMAT == 2 ? m : buf) * 256);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mma_f16(d, sdesc(aad + k * 32), sdesc(bad + k * 32), id,
+                                    (kb | k) ? 1u : 0u);
+                    }
+                    mma_commit(&a_empty[sa]);
+                    mma_commit(&b_empty[sb]);
+                }
+                if (ok) mma_commit(&acc_full[buf]);
+            }
+            mma_commit(drain);
+            wait_drain(drain, 0);
+        }
+    } else if (warp < 4) {
+        // epilogue: warp q owns TMEM lanes (weight rows) 32q .. 32q+31
+        const int q = warp;
+        uint32_t ci = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ci) {
+            const PTile tl = tiles[t];
+            const int nmma = (tl.n + 15) & ~15;
+            const int buf = ci % C::NACC;
+            if (!wait_warp(&acc_full[buf], (ci / C::NACC) & 1, s_abort, status)) break;
+            tc_fence_after();
+            const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+            const int f = tl.mt * kBM + q * 32 + lane;  // output feature of this thread
+            for (int c = 0; c < nmma; c += 16) {
+                if (NMAT == 2) {
+                    float g[16], u[16];
+                    tmem_ld16(lane_base + c, g);
+                    tmem_ld16(lane_base + 256 + c, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (c + j < tl.n) {
+                            const float h = g[j] / (1.0f + expf(-g[j])) * u[j];
+                            W.hs[(size_t)(tl.row0 + c + j) * P.I + f] = __float2half_rn(h);
+                        }
+                    }
+                } else {
+                    float v[16];
+                    tmem_ld16(lane_base + buf * 256 + c, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (c + j < tl.n) {
+                            const int r = tl.row0 + c + j;
+                            const int tok = __ldg(W.row_tok + r);
+                            const float wr = __ldg(W.row_w + r);
+                            atomicAdd(y + (size_t)tok * P.H + f, wr * v[j]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+    } else {
+        // dequantisers: item = (row r, 16-byte chunk c) of a 128 x 64 tile
+        const int dt = tid - kDqWarp0 * 32;
+        uint32_t wi = 0, ai = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+            for (int kb = 0; kb < KB; ++kb, ++wi, ++ai) {
+                const int ws = wi % C::WS, as = ai % C::AS;
+                if (!wait_warp(&w_full[ws], (wi / C::WS) & 1, s_abort, status) ||
+                    !wait_warp(&a_empty[as], ((ai / C::AS) & 1) ^ 1, s_abort, status)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    const uint32_t* codes =
+                        reinterpret_cast<const uint32_t*>(sW + (ws * NMAT + m) * kWStage);
+                    const uint32_t* sz = codes + kWCodes / 4;
+                    uint8_t* dst = sA + (as * NMAT + m) * kATile;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int item = dt + 256 * i, r = item >> 3, c = item & 7;
+                        const uint4 v = dequant8(codes[r * 8 + c], sz[r]);
+                        *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[as]);
+                    mbar_arrive(&w_empty[ws]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+size_t al(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct PLayout {
+    size_t status, counters, logits, idx, w, cnt, seg, row_tok, row_w, row_of, tiles_gu, tiles_dn,
+        wmaps, xs, hs, total;
+    int R, max_gu, max_dn;
+};
+
+PLayout make_playout(int T, int H, int I, int E, int K) {
+    PLayout L{};
+    const int R = T * K + T;
+    const int nt_max = (R + kNT - 1) / kNT + E + 2;  // token tiles over all experts
+    L.R = R;
+    L.max_gu = nt_max * (I / kBM);
+    L.max_dn = nt_max * (H / kBM);
+    size_t o = 0;
+    L.status = o; o += 256;
+    L.counters = o; o += 256;
+    L.logits = o; o = al(o + (size_t)T * E * 4, 256);
+    L.idx = o; o = al(o + (size_t)T * K * 4, 256);
+    L.w = o; o = al(o + (size_t)T * K * 4, 256);
+    L.cnt = o; o = al(o + (size_t)(E + 1) * 4, 256);
+    L.seg = o; o = al(o + (size_t)(E + 2) * 4, 256);
+    L.row_tok = o; o = al(o + (size_t)R * 4, 256);
+    L.row_w = o; o = al(o + (size_t)R * 4, 256);
+    L.row_of = o; o = al(o + (size_t)T * K * 4, 256);
+    L.tiles_gu = o; o = al(o + (size_t)L.max_gu * sizeof(PTile), 256);
+    L.tiles_dn = o; o = al(o + (size_t)L.max_dn * sizeof(PTile), 256);
+    L.wmaps = o; o = al(o + (size_t)(E + 1) * kMaps * sizeof(CUtensorMap), 1024);
+    L.xs = o; o = al(o + (size_t)R * H * 2, 1024);
+    L.hs = o; o = al(o + (size_t)R * I * 2, 1024);
+    L.total = o;
+    return L;
+}
+
+PWs make_pws(void* ws, const PLayout& L) {
+    char* b = static_cast<char*>(ws);
+    PWs W;
+    W.status = reinterpret_cast<int*>(b + L.status);
+    W.counters = reinterpret_cast<int*>(b + L.counters);
+    W.logits = reinterpret_cast<float*>(b + L.logits);
+    W.idx = reinterpret_cast<int*>(b + L.idx);
+    W.w = reinterpret_cast<float*>(b + L.w);
+    W.cnt = reinterpret_cast<int*>(b + L.cnt);
+    W.seg = reinterpret_cast<int*>(b + L.seg);
+    W.row_tok = reinterpret_cast<int*>(b + L.row_tok);
+    W.row_w = reinterpret_cast<float*>(b + L.row_w);
+    W.row_of = reinterpret_cast<int*>(b + L.row_of);
+    W.tiles_gu = reinterpret_cast<PTile*>(b + L.tiles_gu);
+    W.tiles_dn = reinterpret_cast<PTile*>(b + L.tiles_dn);
+    W.wmaps = reinterpret_cast<CUtensorMap*>(b + L.wmaps);
+    W.xs = reinterpret_cast<__half*>(b + L.xs);
+    W.hs = reinterpret_cast<__half*>(b + L.hs);
+    W.R = L.R;
+    W.max_gu = L.max_gu;
+    W.max_dn = L.max_dn;
+    return W;
+}
+
+// The layer's geometry must suit the tensor-core tiles: tiled int4 experts with
+// 64-element groups, 128-row tiles of every matrix, a shared expert (if any) of
+// the routed experts' shape.
+WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err) {
+    const WispExpertMeta& m = l->meta;
+    const int H = (int)m.cols[0], I = (int)m.rows[0];
+    if (!l->expert_blobs || !l->router_w || !m.valid || T <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: missing layer pointers or T <= 0");
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (!m.tiled || m.group_size != 64 || H % kBM || I % kBM || m.rows[1] != (uint32_t)I ||
+        m.cols[1] != (uint32_t)H || m.rows[2] != (uint32_t)H || m.cols[2] != (uint32_t)I) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "prefill: needs tiled experts with group_size 64 and hidden/intermediate "
+                   "multiples of 128 (got tiled=%d gs=%u H=%d I=%d)",
+                   m.tiled, m.group_size, H, I);
+        return WISP_ERR_INVALID_ARG;
+    }
+    for (int i = 0; i < 3; ++i)
+        if ((m.packed_off[i] - 120) % 16) {
+            WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: matrix %d not 16-byte aligned", i);
+            return WISP_ERR_INVALID_ARG;
+        }
+    if (l->n_experts <= 0 || l->n_experts > 1024 || l->top_k <= 0 || l->top_k > 64 ||
+        l->top_k > l->n_experts) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: n_experts %d / top_k %d out of range",
+                   l->n_experts, l->top_k);
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (l->shared_blob) {
+        const WispExpertMeta& s = l->shared_meta;
+        for (int i = 0; i < 3; ++i)
+            if (s.rows[i] != m.rows[i] || s.cols[i] != m.cols[i] ||
+                s.packed_off[i] != m.packed_off[i] || !s.tiled || s.group_size != m.group_size) {
+                WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                           "prefill: the shared expert must have the routed experts' layout");
+                return WISP_ERR_INVALID_ARG;
+            }
+    }
+    return WISP_OK;
+}
+
+PArgs make_pargs(const WispMoeLayer* l) {
+    PArgs P;
+    P.blobs = l->expert_blobs;
+    P.shared_blob = l->shared_blob;
+    P.router_w = static_cast<const __half*>(l->router_w);
+    P.router_bias = static_cast<const __half*>(l->router_bias);
+    for (int i = 0; i < 3; ++i) P.mat_off[i] = l->meta.packed_off[i];
+    P.H = (int)l->meta.cols[0];
+    P.I = (int)l->meta.rows[0];
+    P.E = l->n_experts;
+    P.K = l->top_k;
+    P.has_shared = l->shared_blob ? 1 : 0;
+    return P;
+}
+
+bool encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* addr, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(map, dt, (cuuint32_t)rank, addr, dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Templates of the weight descriptors: codes [16 blocks][8 rows x 32 B] and
+// (scale, zero) pairs [16 blocks][8 x 4 B] of one quant group, as 32-bit words
+// over (word, group, 8-row block).  `anchor`: any 16-byte aligned device address
+// (replaced per expert on the device).
+bool weight_templates(const PArgs& P, const WispExpertMeta& m, void* anchor, WTemplates* t) {
+    for (int mat = 0; mat < 3; ++mat) {
+        const cuuint64_t rows = m.rows[mat], cols = m.cols[mat];
+        const cuuint64_t G = cols / 64, nblk = rows / 8, block_bytes = 4 * cols + 32 * G;
+        const cuuint64_t dc[3] = {64, G, nblk}, sc[2] = {256, block_bytes};
+        const cuuint32_t bc[3] = {64, 1, 16};
+        const cuuint64_t ds[3] = {8, G, nblk}, ss[2] = {32, block_bytes};
+        const cuuint32_t bs[3] = {8, 1, 16};
+        if (!encode(&t->m[mat * 2], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, dc, sc, bc,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+            !encode(&t->m[mat * 2 + 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, ds, ss, bs,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    (void)P;
+    return true;
+}
+
+// Activation rows [R][cols] fp16, boxes of 64 columns x (16 << i) rows, with the
+// 128-byte swizzle tcgen05 reads.
+bool row_maps(__half* rows_base, int R, int cols, BMaps* b) {
+    const cuuint64_t d[2] = {(cuuint64_t)cols, (cuuint64_t)R}, s[1] = {(cuuint64_t)cols * 2};
+    for (int i = 0; i < kBoxes; ++i) {
+        const cuuint32_t box[2] = {64, (cuuint32_t)(16 << i)};
+        if (!encode(&b->box[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows_base, d, s, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+            return false;
+    }
+    return true;
+}
+
+cudaError_t ensure_gemm_attrs() {
+    static cudaError_t e = [] {
+        cudaError_t r = cudaFuncSetAttribute(grouped_gemm_kernel<2>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)gemm_smem_bytes<2>());
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(grouped_gemm_kernel<1>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)gemm_smem_bytes<1>());
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(prefill_plan_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 5 * 1026 * 4);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(route_topk_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 1024 * 4);
+        return r;
+    }();
+    return e;
+}
+
+// Route x, then run the experts; x [T, H] fp32 is the MoE input (normalised).
+WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int T,
+                        int* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream, WispErrCtx* err) {
+    WispError ce = check_prefill_layer(layer, T, err);
+    if (ce != WISP_OK) return ce;
+    const PArgs P = make_pargs(layer);
+    const PLayout L = make_playout(T, P.H, P.I, P.E, P.K);
+    if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 1023)) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "prefill: workspace %zu bytes (need %zu, 1024-byte aligned)", workspace_bytes,
+                   L.total);
+        return WISP_ERR_INVALID_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: x and y must be 16-byte aligned");
+        return WISP_ERR_INVALID_ARG;
+    }
+    PWs W = make_pws(workspace, L);
+    if (topk_idx) W.idx = topk_idx;
+    if (topk_w) W.w = topk_w;
+    WTemplates wt;
+    BMaps bx, bh;
+    if (!weight_templates(P, layer->meta, W.xs, &wt) || !row_maps(W.xs, L.R, P.H, &bx) ||
+        !row_maps(W.hs, L.R, P.I, &bh)) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed or unavailable");
+        return WISP_ERR_CUDA;
+    }
+    WB_CUDA_RET(ensure_gemm_attrs(), err);
+    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, L.counters + 256, stream), err);
+    const int sms = wb::sm_count();
+    const dim3 rg((T + kRouteTile - 1) / kRouteTile, (P.E + kRouteTile - 1) / kRouteTile);
+    WB_CUDA_RET(wb::launch_pdl(router_logits_kernel, rg, dim3(256), 0, stream, x, P.router_w,
+                               W.logits, T, P.E, P.H),
+                err);
+    WB_CUDA_RET(wb::launch_pdl(route_topk_kernel, dim3(std::min((T + 7) / 8, 4 * sms)), dim3(256),
+                               (size_t)8 * 2 * P.E * 4, stream, (const float*)W.logits,
+                               P.router_bias, T, P.E, P.K, W.idx, W.w),
+                err);
+    WB_CUDA_RET(wb::launch_pdl(prefill_plan_kernel, dim3(1), dim3(kPlanThreads),
+                               (size_t)5 * (P.E + 2) * 4, stream, P, W, T, wt),
+                err);
+    WB_CUDA_RET(wb::launch_pdl(prefill_scatter_kernel, dim3(T), dim3(256), 0, stream, P, W, T, x,
+                               y),
+                err);
+    WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<2>, dim3(sms), dim3(kGemmThreads),
+                               gemm_smem_bytes<2>(), stream, P, W, bx, y),
+                err);
+    WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1>, dim3(sms), dim3(kGemmThreads),
+                               gemm_smem_bytes<1>(), stream, P, W, bh, y),
+                err);
+    return WISP_OK;
+}
+
+}  // namespace
+
+extern "C" size_t wisp_moe_prefill_workspace_bytes(const WispMoeLayer* layer, int T) {
+    if (!layer || T <= 0) return 0;
+    const WispExpertMeta& m = layer->meta;
+    return make_playout(T, (int)m.cols[0], (int)m.rows[0], layer->n_experts, layer->top_k).total;
+}
+
+extern "C" WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x, float* y,
+                                              int T, int* topk_idx, float* topk_w,
+                                              void* workspace, size_t workspace_bytes,
+                                              cudaStream_t stream, WispErrCtx* err) {
+    if (!layer || !x || !y) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: NULL layer, x or y");
+        return WISP_ERR_INVALID_ARG;
+    }
+    return prefill_block(layer, x, y, T, topk_idx, topk_w, workspace, workspace_bytes, stream,
+                         err);
+}

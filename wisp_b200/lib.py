@@ -66,6 +66,10 @@ _SIGS = {
                                  C.c_void_p, C.c_size_t, C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_moe_ep_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                       C.c_int, C.c_int, C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_moe_prefill_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
+    "wisp_moe_prefill_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                           C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),

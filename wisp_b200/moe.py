@@ -194,6 +194,39 @@ class MoEStack:
         check(rc, err)
         return (y, idx, w) if routing else y
 
+    def prefill_workspace(self, T: int) -> torch.Tensor:
+        need = int(lib().wisp_moe_prefill_workspace_bytes(C.byref(self._c_layers[0]), T)) + 1024
+        if getattr(self, "_pws", None) is None or self._pws.numel() < need:
+            self._pws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._pws
+
+    def prefill(self, l: int, x: torch.Tensor, y: torch.Tensor | None = None,
+                routing: bool = False):
+        """y = MoE_l(x) for a batch of tokens on the tensor-core path
+        (``wisp_moe_prefill_forward``); x [T,H] fp32 on the device."""
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty_like(x)
+        idx = torch.empty((T, self.shape.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, self.shape.top_k), dtype=torch.float32, device=self.device)
+        ws = self.prefill_workspace(T)
+        off = (-ws.data_ptr()) % 1024
+        err = WispErrCtx()
+        rc = lib().wisp_moe_prefill_forward(
+            C.byref(self._c_layers[l]), x.data_ptr(), y.data_ptr(), T, idx.data_ptr(),
+            w.data_ptr(), ws.data_ptr() + off, ws.numel() - off,
+            torch.cuda.current_stream().cuda_stream, C.byref(err))
+        check(rc, err)
+        return (y, idx, w) if routing else y
+
+    def prefill_status(self) -> int:
+        ws = getattr(self, "_pws", None)
+        if ws is None:
+            return 0
+        off = (-ws.data_ptr()) % 1024
+        return int(lib().wisp_moe_status(ws.data_ptr() + off,
+                                         torch.cuda.current_stream().cuda_stream))
+
     def stack(self, x: torch.Tensor, routing: bool = False, layers: int | None = None):
         """x <- x + MoE_l(rmsnorm(x)) for every layer, in place, on the current stream."""
         T = x.shape[0]
