@@ -25,18 +25,20 @@
 //   grouped_gemm<1>       down:    y[token(row)] += w(row) * (Wd hs[row])
 //
 // The grouped GEMM puts the weights on the MMA's M side (128 weight rows per
-// tile) and the tokens of one expert on N (16..256 per tile), so an expert with
+// tile) and the tokens of one expert on N (16..128 per tile), so an expert with
 // few tokens wastes little of the tensor core.  A persistent CTA per SM walks
 // the tile list (static round robin) with warp-specialised roles:
 //   warps 0-3   epilogue: tcgen05.ld of the fp32 accumulators (warp q reads
 //               TMEM lanes 32q..32q+31), SwiGLU / gate-weighted combine
 //   warp 4      weight producer: two 3-D TMA loads per matrix and K block
 //               (the codes and the scale/zero pairs of 16 tiled 8-row blocks)
-//   warp 5      MMA issuer (one thread): tcgen05.mma kind::f16, M=128, K=16
+//   warp 5      MMA issuer (one thread): tcgen05.mma kind::f16, M=128, K=16,
+//               A from tensor memory, B from shared memory
 //   warp 6      activation producer: 2-D TMA loads, 128-byte swizzle
-//   warps 7-14  dequantisers: int4 codes -> fp16 in the 128-byte swizzled
-//               K-major layout tcgen05 reads (one quant group of 64 = one row
-//               of a swizzle atom)
+//   warps 7-22  dequantisers: int4 codes -> fp16, written straight into
+//               tensor memory with tcgen05.st (TMEM lane = weight row), so the
+//               dequantised weights never round-trip through shared memory
+// TMEM (512 columns): accumulators in [0, 256), dequantised A stages above.
 // Shared-memory rings with mbarriers connect the roles; every wait is bounded
 // (2 s of %globaltimer) and a timeout sets ST_TIMEOUT in the status word, makes
 // every role leave, drains the copies and MMAs in flight and frees TMEM.
@@ -60,17 +62,18 @@ constexpr unsigned kFull = 0xffffffffu;
 
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // K per stage: one quant group
-constexpr int kNT = 256;        // max tokens per tile (MMA N)
-constexpr int kGemmThreads = 480;
-constexpr int kWProdWarp = 4, kMmaWarp = 5, kBProdWarp = 6, kDqWarp0 = 7, kDqWarps = 8;
+constexpr int kNT = 128;        // max tokens per tile (MMA N)
+constexpr int kWProdWarp = 4, kMmaWarp = 5, kBProdWarp = 6, kDqWarp0 = 7, kDqWarps = 16;
+constexpr int kGemmThreads = (kDqWarp0 + kDqWarps) * 32;  // 736
 constexpr int kMaps = 6;        // per expert: (gate, up, down) x (codes, scale/zero)
-constexpr int kBoxes = 5;       // activation boxes of 16, 32, 64, 128, 256 rows
+constexpr int kBoxes = 4;       // activation boxes of 16, 32, 64, 128 rows
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr int kPlanThreads = 1024;
 constexpr int kRouteTile = 64;
+constexpr int kRouterTcMinT = 64;  // tokens from which the router runs on the tensor cores
+constexpr uint32_t kAcol0 = 256;  // TMEM: accumulators in columns [0, 256), A stages above
 
-constexpr int kATile = kBM * 128;          // 128 rows x 64 fp16 (16 KB)
-constexpr int kBTile = kNT * 128;          // 256 rows x 64 fp16 (32 KB)
+constexpr int kBTile = kNT * 128;          // 128 rows x 64 fp16 (16 KB)
 constexpr int kWCodes = 16 * 8 * 32;       // 16 blocks x 8 rows x 32 code bytes
 constexpr int kWStage = kWCodes + 16 * 32;  // + 16 blocks x 8 (scale, zero) pairs
 
@@ -113,22 +116,25 @@ struct PWs {
     int R, max_gu, max_dn;
 };
 
+// Ring depths.  WS: weight staging (smem); BS: activation tiles (smem, deep:
+// their loads are the longest-latency step); S: dequantised weight tiles in
+// TMEM (NMAT x 32 columns each); NACC: accumulator buffers (TMEM, 128 columns
+// per matrix).  TMEM: 256 accumulator columns + S * NMAT * 32 = 256 A columns.
 template <int NMAT>
 struct GCfg;
 template <>
 struct GCfg<2> {  // gate + up
-    static constexpr int WS = 6, AS = 2, BS = 3, NACC = 1;
+    static constexpr int WS = 8, BS = 8, S = 4, NACC = 1;
 };
 template <>
 struct GCfg<1> {  // down
-    static constexpr int WS = 8, AS = 3, BS = 4, NACC = 2;
+    static constexpr int WS = 16, BS = 8, S = 8, NACC = 2;
 };
 
 template <int NMAT>
 constexpr size_t gemm_smem_bytes() {
     using C = GCfg<NMAT>;
-    return 1024 + (size_t)C::AS * NMAT * kATile + (size_t)C::BS * kBTile +
-           (size_t)C::WS * NMAT * kWStage + 256;
+    return 1024 + (size_t)C::BS * kBTile + (size_t)C::WS * NMAT * kWStage + 1024;
 }
 
 // ------------------------------------------------------------------------
@@ -216,6 +222,55 @@ __device__ __forceinline__ bool wait_warp(uint64_t* b, uint32_t parity, volatile
         }
     }
 }
+// Waits of the roles that are not latency-critical (producers refilling deep
+// rings, the epilogue waiting for a whole tile): after a few polls they back
+// off with __nanosleep so they do not take issue slots from the MMA thread
+// and the dequantisers.
+__device__ __forceinline__ bool wait1_lazy(uint64_t* b, uint32_t parity,
+                                           volatile int* abort_flag, int* status) {
+    for (int i = 0; i < 8; ++i)
+        if (mbar_try(b, parity)) return true;
+    uint64_t t0 = gtimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try(b, parity)) return true;
+        __nanosleep(64);
+        if ((it & 15) == 15) {
+            if (*abort_flag) return false;
+            if (gtimer() - t0 > kWaitNs) {
+                *abort_flag = 1;
+                atomicOr(status, ST_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ bool wait_warp_lazy(uint64_t* b, uint32_t parity,
+                                               volatile int* abort_flag, int* status) {
+    const int lane = threadIdx.x & 31;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (__all_sync(kFull, mbar_try(b, parity))) return true;
+        __nanosleep(256);
+        if ((it & 15) == 15) {
+            int stop = 0;
+            if (lane == 0) {
+                if (*abort_flag) {
+                    stop = 1;
+                } else {
+                    const uint64_t t = gtimer();
+                    if (t0 == 0) {
+                        t0 = t;
+                    } else if (t - t0 > kWaitNs) {
+                        *abort_flag = 1;
+                        atomicOr(status, ST_TIMEOUT);
+                        stop = 1;
+                    }
+                }
+            }
+            if (__shfl_sync(kFull, stop, 0)) return false;
+        }
+    }
+}
 // Drain wait: ignores the abort flag, bounded by time only.
 __device__ __forceinline__ void wait_drain(uint64_t* b, uint32_t parity) {
     const uint64_t t0 = gtimer();
@@ -258,12 +313,13 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
 __device__ __forceinline__ uint32_t idesc_f16(int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
-__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t id,
-                                        uint32_t acc) {
+// D (TMEM) += A (TMEM, 128 lanes x 8 columns of fp16 pairs) * B (smem descriptor)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id,
+                                       uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(id), "r"(acc)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(id), "r"(acc), "r"(0u)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -293,33 +349,45 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16};" ::"r"(addr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t addr, const uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(addr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// K order inside every 8-element chunk of the MMA operands: position 2i holds
+// element i and position 2i+1 element i+4 (i < 4), the order in which one
+// 32-bit word of int4 codes unpacks into fp16 pairs without byte permutes.
+// The activation rows (xs, hs) are written in the same order.
+__device__ __forceinline__ int kperm(int f) { return (f & ~7) | ((f & 3) << 1) | ((f >> 2) & 1); }
 
 // Eight int4 codes (one 32-bit word, low nibble = even element) with their
-// group's fp16 scale and zero -> eight fp16 weights (q - 8) * s + z, rounded
-// once (fused multiply-add on the exact q - 8).  1024 + q is built in the
-// fp16 bit pattern (0x6400 | q) and 1032 subtracted exactly.
-__device__ __forceinline__ uint4 dequant8(uint32_t v, uint32_t sz) {
-    const uint32_t t0 = (v & 0x000F000Fu) | 0x64006400u;          // (e0, e4)
-    const uint32_t t1 = ((v >> 4) & 0x000F000Fu) | 0x64006400u;   // (e1, e5)
-    const uint32_t t2 = ((v >> 8) & 0x000F000Fu) | 0x64006400u;   // (e2, e6)
-    const uint32_t t3 = ((v >> 12) & 0x000F000Fu) | 0x64006400u;  // (e3, e7)
-    uint32_t p[4];
-    p[0] = __byte_perm(t0, t1, 0x5410);  // (e0, e1)
-    p[1] = __byte_perm(t2, t3, 0x5410);  // (e2, e3)
-    p[2] = __byte_perm(t0, t1, 0x7632);  // (e4, e5)
-    p[3] = __byte_perm(t2, t3, 0x7632);  // (e6, e7)
-    const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
-    const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(sz >> 16)));
+// group's fp16 scale and zero -> four TMEM columns of fp16 weight pairs
+// (e0,e4) (e1,e5) (e2,e6) (e3,e7), each weight (q - 8) * s + z rounded once
+// (fused multiply-add on the exact q - 8): 1024 + q is built in the fp16 bit
+// pattern (0x6400 | q) and 1032 subtracted exactly.
+__device__ __forceinline__ void dequant_cols(uint32_t v, __half2 s2, __half2 z2, uint32_t* o) {
     const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6408u));  // 1032
-    uint4 out;
-    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&p[i]), off);
+        const uint32_t t = ((v >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&t), off);
         const __half2 w = __hfma2(q, s2, z2);
         o[i] = *reinterpret_cast<const uint32_t*>(&w);
     }
-    return out;
 }
 
 // ------------------------------------------------------------------------
@@ -368,6 +436,152 @@ router_logits_kernel(const float* __restrict__ x, const __half* __restrict__ Wr,
             const int e = e0 + tx * 4 + j;
             if (e < E) lg[(size_t)t * E + e] = acc[i][j];
         }
+    }
+}
+
+// x [T, H] fp32 -> hi = fp16(x), lo = fp16(x - hi): the router GEMM on the
+// tensor cores sums W*hi + W*lo, which carries x to ~2^-22 relative precision
+// (fp16 x fp16 products are exact in the fp32 accumulator).
+__global__ void __launch_bounds__(256)
+split_hilo_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo,
+                  long long n4) {
+    pdl_wait();
+    pdl_launch();
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n4; i += (long long)gridDim.x * 256) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const __half2 l0 = __floats2half2_rn(v.x - f0.x, v.y - f0.y);
+        const __half2 l1 = __floats2half2_rn(v.z - f1.x, v.w - f1.y);
+        uint2 a, b;
+        a.x = *reinterpret_cast<const uint32_t*>(&h0);
+        a.y = *reinterpret_cast<const uint32_t*>(&h1);
+        b.x = *reinterpret_cast<const uint32_t*>(&l0);
+        b.y = *reinterpret_cast<const uint32_t*>(&l1);
+        reinterpret_cast<uint2*>(hi)[i] = a;
+        reinterpret_cast<uint2*>(lo)[i] = b;
+    }
+}
+
+// Router logits on the tensor cores: logits[t][e] = W[e] . (hi[t] + lo[t]).
+// One CTA per (128 experts x 128 tokens) tile; warp 4 loads W, hi and lo tiles
+// (64-wide K blocks, 128-byte swizzle) into a 4-stage ring, warp 5 issues
+// eight kind::f16 MMAs per K block into one fp32 accumulator (128 TMEM
+// columns), warps 0-3 write the logits.  Rows past E and tokens past T are
+// zero-filled by TMA and not stored.
+struct RouterMaps {
+    CUtensorMap w, hi, lo;
+};
+constexpr int kRtStages = 4;
+constexpr int kRtTile = 128 * 128;  // bytes of one 128 x 64 fp16 tile
+constexpr size_t kRouterSmem = 1024 + (size_t)kRtStages * 3 * kRtTile + 256;
+
+__global__ void __launch_bounds__(192, 1)
+router_tc_kernel(const __grid_constant__ RouterMaps rm, float* __restrict__ lg, int T, int E,
+                 int H, int* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + kRtStages * 3 * kRtTile);
+    uint64_t* empty = full + kRtStages;
+    uint64_t* done = empty + kRtStages;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e0 = blockIdx.x * 128, t0 = blockIdx.y * 128;
+    const int KB = H / kBK;
+    if (tid == 0) {
+        for (int i = 0; i < kRtStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        *s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+                         saddr(s_tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    pdl_wait();
+    pdl_launch();
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t i = 0;
+            for (int kb = 0; kb < KB; ++kb, ++i) {
+                const int s = i % kRtStages;
+                if (!wait1_lazy(&empty[s], ((i / kRtStages) & 1) ^ 1, s_abort, status)) break;
+                mbar_expect_tx(&full[s], 3 * kRtTile);
+                uint8_t* st = base + s * 3 * kRtTile;
+                tma2d(st, &rm.w, kb * kBK, e0, &full[s]);
+                tma2d(st + kRtTile, &rm.hi, kb * kBK, t0, &full[s]);
+                tma2d(st + 2 * kRtTile, &rm.lo, kb * kBK, t0, &full[s]);
+            }
+            const uint32_t first = i > (uint32_t)kRtStages ? i - kRtStages : 0;
+            for (uint32_t j = first; j < i; ++j) wait_drain(&full[j % kRtStages], (j / kRtStages) & 1);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t id = idesc_f16(128);
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % kRtStages;
+                if (!wait1(&full[s], (kb / kRtStages) & 1, s_abort, status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = saddr(base + s * 3 * kRtTile);
+                const uint64_t wd = sdesc(st), hd = sdesc(st + kRtTile), ld = sdesc(st + 2 * kRtTile);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                        "l"(wd + 2 * k), "l"(hd + 2 * k), "r"(id), "r"((kb | k) ? 1u : 0u)
+                        : "memory");
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                        "l"(wd + 2 * k), "l"(ld + 2 * k), "r"(id), "r"(1u)
+                        : "memory");
+                }
+                mma_commit(&empty[s]);
+            }
+            (void)ok;
+            mma_commit(done);  // also the drain: every MMA of this CTA has completed
+            wait_drain(done, 0);
+        }
+    } else {
+        // warps 0-3: TMEM lane = expert row of the tile, column = token
+        if (wait_warp_lazy(done, 0, s_abort, status)) {
+            tc_fence_after();
+            const int e = e0 + warp * 32 + lane;
+            const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+            for (int c = 0; c < 128; c += 16) {
+                float v[16];
+                tmem_ld16(lb + c, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + c + j;
+                    if (e < E && t < T) lg[(size_t)t * E + e] = v[j];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem)
+                     : "memory");
     }
 }
 
@@ -544,8 +758,9 @@ prefill_scatter_kernel(PArgs P, PWs W, int T, const float* __restrict__ x, float
     float4* yr = reinterpret_cast<float4*>(y + (size_t)t * H);
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
         const float4 a = xr[2 * c], b = xr[2 * c + 1];
-        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-        const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+        // the operands' K order inside a chunk: x0 x4 x1 x5 x2 x6 x3 x7 (kperm)
+        const __half2 h0 = __floats2half2_rn(a.x, b.x), h1 = __floats2half2_rn(a.y, b.y);
+        const __half2 h2 = __floats2half2_rn(a.z, b.z), h3 = __floats2half2_rn(a.w, b.w);
         uint4 v;
         v.x = *reinterpret_cast<const uint32_t*>(&h0);
         v.y = *reinterpret_cast<const uint32_t*>(&h1);
@@ -570,14 +785,13 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~(uintptr_t)1023);
-    uint8_t* sA = base;
-    uint8_t* sB = sA + C::AS * NMAT * kATile;
+    uint8_t* sB = base;
     uint8_t* sW = sB + C::BS * kBTile;
     uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * kWStage);
     uint64_t* w_empty = w_full + C::WS;
-    uint64_t* a_full = w_empty + C::WS;
-    uint64_t* a_empty = a_full + C::AS;
-    uint64_t* b_full = a_empty + C::AS;
+    uint64_t* a_full = w_empty + C::WS;   // dequantised tile in TMEM
+    uint64_t* a_empty = a_full + C::S;
+    uint64_t* b_full = a_empty + C::S;    // activation tile in smem
     uint64_t* b_empty = b_full + C::BS;
     uint64_t* acc_full = b_empty + C::BS;
     uint64_t* acc_empty = acc_full + C::NACC;
@@ -591,7 +805,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
             mbar_init(&w_full[i], 1);
             mbar_init(&w_empty[i], kDqWarps);
         }
-        for (int i = 0; i < C::AS; ++i) {
+        for (int i = 0; i < C::S; ++i) {
             mbar_init(&a_full[i], kDqWarps);
             mbar_init(&a_empty[i], 1);
         }
@@ -641,7 +855,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 }
                 for (int kb = 0; kb < KB; ++kb, ++wi) {
                     const int s = wi % C::WS;
-                    if (!wait1(&w_empty[s], ((wi / C::WS) & 1) ^ 1, s_abort, status)) {
+                    if (!wait1_lazy(&w_empty[s], ((wi / C::WS) & 1) ^ 1, s_abort, status)) {
                         ok = false;
                         break;
                     }
@@ -666,7 +880,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 const int nmma = (tl.n + 15) & ~15;
                 for (int kb = 0; kb < KB; ++kb, ++bi) {
                     const int s = bi % C::BS;
-                    if (!wait1(&b_empty[s], ((bi / C::BS) & 1) ^ 1, s_abort, status)) {
+                    if (!wait1_lazy(&b_empty[s], ((bi / C::BS) & 1) ^ 1, s_abort, status)) {
                         ok = false;
                         break;
                     }
@@ -688,8 +902,9 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            uint32_t ai = 0, bi = 0, ci = 0;
+            uint32_t si = 0, ci = 0;
             bool ok = true;
+            const uint64_t bdesc0 = sdesc(saddr(sB));
             for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++ci) {
                 const PTile tl = tiles[t];
                 const int nmma = (tl.n + 15) & ~15;
@@ -697,25 +912,24 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 const int buf = ci % C::NACC;
                 if (!wait1(&acc_empty[buf], ((ci / C::NACC) & 1) ^ 1, s_abort, status)) break;
                 tc_fence_after();
-                for (int kb = 0; kb < KB; ++kb, ++ai, ++bi) {
-                    const int sa = ai % C::AS, sb = bi % C::BS;
-                    if (!wait1(&a_full[sa], (ai / C::AS) & 1, s_abort, status) ||
-                        !wait1(&b_full[sb], (bi / C::BS) & 1, s_abort, status)) {
+                const uint32_t d0 = tmem + (uint32_t)((NMAT == 2 ? 0 : buf) * kNT);
+                for (int kb = 0; kb < KB; ++kb, ++si) {
+                    const int s = si % C::S, sb = si % C::BS;
+                    if (!wait1(&a_full[s], (si / C::S) & 1, s_abort, status) ||
+                        !wait1(&b_full[sb], (si / C::BS) & 1, s_abort, status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t bad = saddr(sB + sb * kBTile);
+                    const uint64_t bd = bdesc0 + (uint64_t)(sb * (kBTile >> 4));
+                    const uint32_t at = tmem + kAcol0 + (uint32_t)(s * NMAT * 32);
 #pragma unroll
-                    for (int m = 0; m < NMAT; ++m) {
-                        const uint32_t aad = saddr(sA + (sa * NMAT + m) * kATile);
-                        const uint32_t d = tmem + (uint32_t)((NMAT == 2 ? m : buf) * 256);
+                    for (int k = 0; k < 4; ++k)
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            mma_f16(d, sdesc(aad + k * 32), sdesc(bad + k * 32), id,
-                                    (kb | k) ? 1u : 0u);
-                    }
-                    mma_commit(&a_empty[sa]);
+                        for (int m = 0; m < NMAT; ++m)
+                            mma_ts(d0 + (uint32_t)(m * kNT), at + (uint32_t)(m * 32 + k * 8),
+                                   bd + (uint64_t)(2 * k), id, (kb | k) ? 1u : 0u);
+                    mma_commit(&a_empty[s]);
                     mma_commit(&b_empty[sb]);
                 }
                 if (ok) mma_commit(&acc_full[buf]);
@@ -731,7 +945,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
             const PTile tl = tiles[t];
             const int nmma = (tl.n + 15) & ~15;
             const int buf = ci % C::NACC;
-            if (!wait_warp(&acc_full[buf], (ci / C::NACC) & 1, s_abort, status)) break;
+            if (!wait_warp_lazy(&acc_full[buf], (ci / C::NACC) & 1, s_abort, status)) break;
             tc_fence_after();
             const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
             const int f = tl.mt * kBM + q * 32 + lane;  // output feature of this thread
@@ -739,18 +953,19 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 if (NMAT == 2) {
                     float g[16], u[16];
                     tmem_ld16(lane_base + c, g);
-                    tmem_ld16(lane_base + 256 + c, u);
+                    tmem_ld16(lane_base + kNT + c, u);
                     tmem_ld_wait();
+                    const int fp = kperm(f);  // hs is the down GEMM's operand: K order
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         if (c + j < tl.n) {
                             const float h = g[j] / (1.0f + expf(-g[j])) * u[j];
-                            W.hs[(size_t)(tl.row0 + c + j) * P.I + f] = __float2half_rn(h);
+                            W.hs[(size_t)(tl.row0 + c + j) * P.I + fp] = __float2half_rn(h);
                         }
                     }
                 } else {
                     float v[16];
-                    tmem_ld16(lane_base + buf * 256 + c, v);
+                    tmem_ld16(lane_base + buf * kNT + c, v);
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
@@ -768,32 +983,54 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     } else {
-        // dequantisers: item = (row r, 16-byte chunk c) of a 128 x 64 tile
-        const int dt = tid - kDqWarp0 * 32;
+        // dequantisers: warp (g, q) writes TMEM lanes 32q..32q+31 (weight rows) of
+        // part g of each stage: gate/up -> matrix g/2, half g%2 of the 64-wide
+        // group (16 columns); down -> quarter g (8 columns)
+        const int dw = warp - kDqWarp0, q = warp & 3, g = dw >> 2;
+        const int r = q * 32 + lane;
+        const int mat = NMAT == 2 ? (g >> 1) : 0;
+        constexpr int PW = NMAT == 2 ? 4 : 2;  // code words per thread and stage
+        const int part = NMAT == 2 ? (g & 1) : g;
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + kAcol0 +
+                                   (uint32_t)(mat * 32 + part * PW * 4);
         uint32_t wi = 0, ai = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
             for (int kb = 0; kb < KB; ++kb, ++wi, ++ai) {
-                const int ws = wi % C::WS, as = ai % C::AS;
+                const int ws = wi % C::WS, as = ai % C::S;
                 if (!wait_warp(&w_full[ws], (wi / C::WS) & 1, s_abort, status) ||
-                    !wait_warp(&a_empty[as], ((ai / C::AS) & 1) ^ 1, s_abort, status)) {
+                    !wait_warp(&a_empty[as], ((ai / C::S) & 1) ^ 1, s_abort, status)) {
                     ok = false;
                     break;
                 }
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m) {
-                    const uint32_t* codes =
-                        reinterpret_cast<const uint32_t*>(sW + (ws * NMAT + m) * kWStage);
-                    const uint32_t* sz = codes + kWCodes / 4;
-                    uint8_t* dst = sA + (as * NMAT + m) * kATile;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int item = dt + 256 * i, r = item >> 3, c = item & 7;
-                        const uint4 v = dequant8(codes[r * 8 + c], sz[r]);
-                        *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
-                    }
+                tc_fence_after();
+                const uint32_t* st =
+                    reinterpret_cast<const uint32_t*>(sW + (ws * NMAT + mat) * kWStage);
+                const uint32_t szw = st[kWCodes / 4 + r];
+                const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFFu)));
+                const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
+                uint32_t v[PW];
+                if (PW == 4) {
+                    const uint4 c4 = *reinterpret_cast<const uint4*>(st + r * 8 + part * 4);
+                    v[0] = c4.x; v[1] = c4.y; v[2] = c4.z; v[3] = c4.w;
+                } else {
+                    const uint2 c2 = *reinterpret_cast<const uint2*>(st + r * 8 + part * 2);
+                    v[0] = c2.x; v[1] = c2.y;
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                const uint32_t ta = lane_addr + (uint32_t)(as * NMAT * 32);
+                if (PW == 4) {
+                    uint32_t o[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dequant_cols(v[i], s2, z2, o + 4 * i);
+                    tmem_st16(ta, o);
+                } else {
+                    uint32_t o[8];
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) dequant_cols(v[i], s2, z2, o + 4 * i);
+                    tmem_st8(ta, o);
+                }
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&a_full[as]);
@@ -1008,6 +1245,9 @@ cudaError_t ensure_gemm_attrs() {
             r = cudaFuncSetAttribute(prefill_plan_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 5 * 1026 * 4);
         if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kRouterSmem);
+        if (r == cudaSuccess)
             r = cudaFuncSetAttribute(route_topk_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 1024 * 4);
         return r;
@@ -1046,10 +1286,38 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     WB_CUDA_RET(ensure_gemm_attrs(), err);
     WB_CUDA_RET(cudaMemsetAsync(workspace, 0, L.counters + 256, stream), err);
     const int sms = wb::sm_count();
-    const dim3 rg((T + kRouteTile - 1) / kRouteTile, (P.E + kRouteTile - 1) / kRouteTile);
-    WB_CUDA_RET(wb::launch_pdl(router_logits_kernel, rg, dim3(256), 0, stream, x, P.router_w,
-                               W.logits, T, P.E, P.H),
-                err);
+    if (T >= kRouterTcMinT) {
+        // hi/lo halves of x live in the (not yet used) activation-row buffer
+        __half* hi = W.xs;
+        __half* lo = W.xs + (size_t)T * P.H;
+        RouterMaps rm;
+        const cuuint64_t dw[2] = {(cuuint64_t)P.H, (cuuint64_t)P.E}, sw[1] = {(cuuint64_t)P.H * 2};
+        const cuuint64_t dx[2] = {(cuuint64_t)P.H, (cuuint64_t)T};
+        const cuuint32_t box[2] = {64, 128};
+        if (!encode(&rm.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(P.router_w), dw,
+                    sw, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode(&rm.hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, dx, sw, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode(&rm.lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, dx, sw, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B)) {
+            WB_SET_ERR(err, WISP_ERR_CUDA, "prefill: router tensor maps could not be encoded");
+            return WISP_ERR_CUDA;
+        }
+        const long long n4 = (long long)T * P.H / 4;
+        WB_CUDA_RET(wb::launch_pdl(split_hilo_kernel,
+                                   dim3((unsigned)std::min<long long>((n4 + 255) / 256, 8 * sms)),
+                                   dim3(256), 0, stream, x, hi, lo, n4),
+                    err);
+        WB_CUDA_RET(wb::launch_pdl(router_tc_kernel, dim3((P.E + 127) / 128, (T + 127) / 128),
+                                   dim3(192), kRouterSmem, stream, rm, W.logits, T, P.E, P.H,
+                                   W.status),
+                    err);
+    } else {
+        const dim3 rg((T + kRouteTile - 1) / kRouteTile, (P.E + kRouteTile - 1) / kRouteTile);
+        WB_CUDA_RET(wb::launch_pdl(router_logits_kernel, rg, dim3(256), 0, stream, x, P.router_w,
+                                   W.logits, T, P.E, P.H),
+                    err);
+    }
     WB_CUDA_RET(wb::launch_pdl(route_topk_kernel, dim3(std::min((T + 7) / 8, 4 * sms)), dim3(256),
                                (size_t)8 * 2 * P.E * 4, stream, (const float*)W.logits,
                                P.router_bias, T, P.E, P.K, W.idx, W.w),
