@@ -54,7 +54,9 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--skip-extra", action="store_true", help="no per-batch / e2e / profile legs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
-    p.add_argument("--workload", default="stack", choices=["stack", "ep"],
+    p.add_argument("--config3-layers", type=int, default=4,
+                   help="resident DeepSeek-shaped layers of the config-3 leg (0 = skip)")
+    p.add_argument("--workload", default="stack", choices=["stack", "ep", "prefill"],
                    help="stack: config 1 (default); ep: config 2, one DeepSeek-V3-shaped layer "
                         "expert-sharded over the GPUs, 64 tokens per GPU")
     return p.parse_args()
@@ -304,6 +306,9 @@ def run_single(args, dev) -> dict:
                           "frac_of_measured_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
         del g0
 
+    if not args.skip_extra and args.config3_layers > 0:
+        out["config3"] = run_config3(args, dev, args.config3_layers)
+
     # CPU baseline + parity on the same bytes: layer 0, token 0
     if not args.skip_cpu:
         threads = len(os.sched_getaffinity(0))
@@ -326,6 +331,91 @@ def run_single(args, dev) -> dict:
     out["gpu_launches_per_step"] = len(seq) * args.layers + 1
     del g
     return out
+
+
+def run_config3(args, dev, k: int) -> dict:
+    """Config 3 on one GPU: a resident k-layer slice of the DeepSeek-V3-shaped stack
+    (7168 / 2048, 256 experts, top-8, shared expert, Zipf(1.1) routing), prefill of
+    4096 tokens on the tensor-core path, then 128 decode steps at batch 32 on the decode
+    path (one CUDA graph per step).  The 58-layer pool (368 GB) does not fit one GPU:
+    times are normalised per layer (x 58 / k)."""
+    import numpy as np
+    import torch
+    from wisp_b200 import converter as cv
+    from wisp_b200.moe import MoEStack
+    shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=256, top_k=8, shared_inter=2048,
+                        n_layers=k)
+    t0 = time.time()
+    st = MoEStack(shape, SEED + 3, device=dev, zipf_s=1.1)
+    setup_s = time.time() - t0
+    Tp, Bd, steps = 4096, 32, 128
+    xp0 = cv.make_input(shape, Tp, SEED + 3).to(dev)
+    xp = xp0.clone()
+    for _ in range(2):
+        xp.copy_(xp0)
+        st.prefill_stack(xp)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    ms = []
+    with ClockSampler(dev.index or 0) as clk:
+        for _ in range(reps):
+            xp.copy_(xp0)  # a flush of L2 too: 117 MB
+            e0.record()
+            st.prefill_stack(xp)
+            e1.record()
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
+    pre_ms = statistics.median(ms)
+    status = st.prefill_status()
+    _, idx, _ = st.prefill_stack(xp0.clone(), routing=True)
+    torch.cuda.synchronize()
+    H, I, E, K = 7168, 2048, 256, 8
+    flops_layer = 2 * 3 * H * I * (Tp * K + Tp) + 2 * H * E * Tp
+    tflops = k * flops_layer / pre_ms / 1e9
+    # decode: batch 32, one graph per step
+    xd0 = cv.make_input(shape, Bd, SEED + 5).to(dev)
+    xd = xd0.clone()
+    st.workspace(Bd)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        st.stack(xd)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.stack(xd)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    xd.copy_(xd0)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1) / steps
+    dstatus = st.status()
+    del g
+    scale = 58.0 / k
+    total_ms = (pre_ms + steps * dec_ms) * scale
+    cnt = np.bincount(idx[0].cpu().numpy().reshape(-1), minlength=E)
+    return {
+        "workload": f"config3: DeepSeek-V3-shaped stack, resident {k}-layer slice, prefill "
+                    f"{Tp} tokens (tensor-core grouped GEMM) then {steps} decode steps at batch "
+                    f"{Bd}; times x58/{k} for the 58-layer stack (368 GB does not fit one GPU)",
+        "layers_resident": k, "setup_s": round(setup_s, 1),
+        "prefill_ms_per_layer": round(pre_ms / k, 3),
+        "prefill_tokens_per_s": round(Tp / (pre_ms * scale) * 1e3, 1),
+        "prefill_tflops": round(tflops, 1),
+        "prefill_frac_of_measured_bf16": round(tflops / peaks()["bf16_tflops"], 4),
+        "decode_ms_per_layer_step": round(dec_ms / k, 4),
+        "decode_tokens_per_s": round(Bd / (dec_ms * scale) * 1e3, 1),
+        "config3_total_ms": round(total_ms, 1),
+        "config3_tokens_per_s": round((Tp + steps * Bd) / total_ms * 1e3, 1),
+        "max_tokens_per_expert_layer0": int(cnt.max()),
+        "status": int(status | dstatus), "clocks": clk.summary(),
+    }
 
 
 def C_void_p_array(events):
@@ -367,7 +457,7 @@ def main_ours(args):
         "gpu_launches": r["gpu_launches_per_step"] * args.steps,
         "step_hbm_gbs": round(r["step_gbs"], 1), "kernel_ms_mean": r["kernel_ms_mean"],
     }
-    for k in ("e2e", "per_batch", "config0", "cpu_baseline", "parity"):
+    for k in ("e2e", "per_batch", "config0", "config3", "cpu_baseline", "parity"):
         if k in r:
             line[k] = r[k]
     print(json.dumps(line), flush=True)
@@ -454,6 +544,29 @@ def main_ep(args):
             "clocks": clk.summary()}), flush=True)
 
 
+def main_prefill(args):
+    """Config 3 as the headline line (one GPU; see run_config3)."""
+    import torch
+    from wisp_b200 import build
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    build.build()
+    k = args.config3_layers or 4
+    r = run_config3(args, dev, k)
+    print(json.dumps({
+        "metric": "DeepSeek-V3-shaped 58-block stack: prefill 4096 + 128 decode steps at batch "
+                  "32, tokens/s", "value": r["config3_tokens_per_s"], "unit": "tokens/s",
+        "n_gpus": 1, "steps": 1, "warmup": 2, "ms_per_step": r["config3_total_ms"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4xf16",
+        "data": "synthetic (seeded N(0,0.02) weights quantised int4 gs64; fp16 N(0,1) inputs)",
+        "config": {"workload": r["workload"], "parallelism": "single GPU (per-layer normalised)"},
+        "roofline": {"bound": "tensor", "achieved": r["prefill_tflops"],
+                     "peak": peaks()["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": r["prefill_frac_of_measured_bf16"], "traffic": None,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops), of measured"},
+        "clocks": r["clocks"], "config3": r}), flush=True)
+
+
 def main_reference(args):
     """The reference's own CPU implementation (run_moe, built from its sources), all host
     threads, bounded sample: each step = 1 token through one Mixtral-shaped block, the
@@ -514,5 +627,7 @@ if __name__ == "__main__":
         main_reference(a)
     elif a.workload == "ep":
         main_ep(a)
+    elif a.workload == "prefill":
+        main_prefill(a)
     else:
         main_ours(a)

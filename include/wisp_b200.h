@@ -241,6 +241,22 @@ WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x,
                                    void* workspace, size_t workspace_bytes,
                                    cudaStream_t stream, WispErrCtx* err);
 
+/* New: stack of n_layers blocks on the prefill path -- per layer l,
+ * x <- x + MoE_l(rmsnorm(x; norm_w_l, eps)) (the FFN half of decode_step,
+ * csrc/core/wisp_engine.c:1563-1570, attention = identity), each block by
+ * wisp_moe_prefill_forward's kernels.  x [T,H] fp32 device, in place;
+ * topk_idx/topk_w optional device [n_layers, T, top_k].  Launch-only.
+ * workspace: wisp_moe_prefill_stack_workspace_bytes bytes, 1024-byte aligned;
+ * its first word is the status word (wisp_moe_status), accumulated over the
+ * layers. */
+size_t wisp_moe_prefill_stack_workspace_bytes(const WispMoeLayer* layers,
+                                              int n_layers, int T);
+WispError wisp_moe_prefill_stack_forward(const WispMoeLayer* layers, int n_layers,
+                                         float eps, float* x, int T, int* topk_idx,
+                                         float* topk_w, void* workspace,
+                                         size_t workspace_bytes, cudaStream_t stream,
+                                         WispErrCtx* err);
+
 /* No counterpart in the reference.  wisp_moe_block_forward without a
  * workspace argument, for callers that cannot allocate device memory: a host
  * binding the library through a plain C FFI with no device allocator of its

@@ -89,3 +89,42 @@ def test_deepseek_shaped_prefill_matches_oracle(cuda):
     nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
     if nd == 0:
         check_outputs(y.cpu().numpy(), yr)
+
+
+@pytest.mark.parametrize("T", [96, 333])
+def test_prefill_stack_matches_oracle(cuda, T):
+    """x <- x + MoE_l(rmsnorm(x)) over 3 layers on the tensor-core path against the
+    oracle's per-layer recipe (rmsnorm, block, residual)."""
+    H = 512
+    shape = cv.MoEShape(hidden=H, inter=384, n_experts=16, top_k=4, shared_inter=384, n_layers=3)
+    st = MoEStack(shape, seed=19, device=cuda, zipf_s=1.1)
+    x0 = torch.randn(T, H, generator=torch.Generator().manual_seed(4)).half().float()
+    x = x0.clone().to(cuda)
+    _, idx, _ = st.prefill_stack(x, routing=True)
+    torch.cuda.synchronize()
+    assert st.prefill_status() == 0
+    xr = x0.numpy().copy()
+    ones = np.ones(H, np.float16).view(np.uint16)
+    for l in range(shape.n_layers):
+        Wb, bb = st.host_router(l)
+        xn = np.empty_like(xr)
+        for t in range(T):
+            orc.port_lib().oracle_rmsnorm(xr[t].ctypes.data, ones.ctypes.data, xn[t].ctypes.data,
+                                          H, np.float32(shape.rms_eps))
+        yl, il, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(l), 4, xn,
+                                              shared=st.host_shared(l))
+        check_routing(idx[l].cpu().numpy(), il, Wb, bb, xn)
+        xr = xr + yl
+    check_outputs(x.cpu().numpy(), xr)
+
+
+def test_prefill_stack_matches_decode_stack(cuda):
+    """The tensor-core stack and the decode stream stack agree on the same tokens."""
+    shape = cv.MoEShape(hidden=256, inter=256, n_experts=8, top_k=2, n_layers=4)
+    st = MoEStack(shape, seed=23, device=cuda, random_bias=True)
+    x0 = torch.randn(16, 256, generator=torch.Generator().manual_seed(9)).to(cuda)
+    a = st.prefill_stack(x0.clone())
+    b = st.stack(x0.clone())
+    torch.cuda.synchronize()
+    assert st.prefill_status() == 0 and st.status() == 0
+    check_outputs(a.cpu().numpy(), b.cpu().numpy())

@@ -775,6 +775,51 @@ prefill_scatter_kernel(PArgs P, PWs W, int T, const float* __restrict__ x, float
     }
 }
 
+// Between stacked blocks (the FFN half of decode_step, csrc/core/wisp_engine.c
+// :1563-1570, attention = identity): x[t] += y[t] (the previous block's
+// output, when `add`), then xn[t] = rmsnorm(x[t]) * w (cpu_rmsnorm,
+// wisp_engine.c:415-422), when `norm`.  One CTA per token.
+__global__ void __launch_bounds__(256)
+prefill_norm_kernel(float* __restrict__ x, const float* __restrict__ y,
+                    const __half* __restrict__ w, float* __restrict__ xn, int H, float eps,
+                    int add, int norm) {
+    pdl_wait();
+    pdl_launch();
+    const int t = blockIdx.x, tid = threadIdx.x;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)t * H);
+    const float4* yr = reinterpret_cast<const float4*>(y + (size_t)t * H);
+    __shared__ float red[8];
+    float ss = 0.f;
+    for (int i = tid; i < H / 4; i += 256) {
+        float4 v = xr[i];
+        if (add) {
+            const float4 d = yr[i];
+            v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
+            xr[i] = v;
+        }
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    if (!norm) return;
+    ss = wisp_route::warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float sc = 1.0f / sqrtf(tot / (float)H + eps);
+    float4* on = reinterpret_cast<float4*>(xn + (size_t)t * H);
+    const __half2* w2 = reinterpret_cast<const __half2*>(w);
+    for (int i = tid; i < H / 4; i += 256) {
+        float4 v = xr[i];
+        v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+        if (w) {
+            const float2 a = __half22float2(w2[2 * i]), b = __half22float2(w2[2 * i + 1]);
+            v.x *= a.x; v.y *= a.y; v.z *= b.x; v.w *= b.y;
+        }
+        on[i] = v;
+    }
+}
+
 // ------------------------------------------------------------------------
 // the grouped GEMM
 // ------------------------------------------------------------------------
@@ -1258,7 +1303,7 @@ cudaError_t ensure_gemm_attrs() {
 // Route x, then run the experts; x [T, H] fp32 is the MoE input (normalised).
 WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int T,
                         int* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
-                        cudaStream_t stream, WispErrCtx* err) {
+                        bool reset_status, cudaStream_t stream, WispErrCtx* err) {
     WispError ce = check_prefill_layer(layer, T, err);
     if (ce != WISP_OK) return ce;
     const PArgs P = make_pargs(layer);
@@ -1284,7 +1329,9 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
         return WISP_ERR_CUDA;
     }
     WB_CUDA_RET(ensure_gemm_attrs(), err);
-    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, L.counters + 256, stream), err);
+    // the plan kernel rewrites the tile counters; the status word accumulates
+    // over the blocks of a stack
+    if (reset_status) WB_CUDA_RET(cudaMemsetAsync(W.status, 0, sizeof(int), stream), err);
     const int sms = wb::sm_count();
     if (T >= kRouterTcMinT) {
         // hi/lo halves of x live in the (not yet used) activation-row buffer
@@ -1337,12 +1384,78 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     return WISP_OK;
 }
 
+// Workspace of the stack: one block's workspace, then xn and y [T, H] fp32.
+size_t stack_ws_bytes(const WispMoeLayer* l, int T, size_t* block_bytes) {
+    const WispExpertMeta& m = l->meta;
+    const size_t b = al(make_playout(T, (int)m.cols[0], (int)m.rows[0], l->n_experts,
+                                     l->top_k).total, 1024);
+    if (block_bytes) *block_bytes = b;
+    return b + 2 * al((size_t)T * m.cols[0] * sizeof(float), 1024);
+}
+
 }  // namespace
 
 extern "C" size_t wisp_moe_prefill_workspace_bytes(const WispMoeLayer* layer, int T) {
     if (!layer || T <= 0) return 0;
     const WispExpertMeta& m = layer->meta;
     return make_playout(T, (int)m.cols[0], (int)m.rows[0], layer->n_experts, layer->top_k).total;
+}
+
+extern "C" size_t wisp_moe_prefill_stack_workspace_bytes(const WispMoeLayer* layers, int n_layers,
+                                                         int T) {
+    if (!layers || n_layers <= 0 || T <= 0) return 0;
+    size_t best = 0;
+    for (int i = 0; i < n_layers; ++i) best = std::max(best, stack_ws_bytes(&layers[i], T, nullptr));
+    return best;
+}
+
+extern "C" WispError wisp_moe_prefill_stack_forward(const WispMoeLayer* layers, int n_layers,
+                                                    float eps, float* x, int T, int* topk_idx,
+                                                    float* topk_w, void* workspace,
+                                                    size_t workspace_bytes, cudaStream_t stream,
+                                                    WispErrCtx* err) {
+    if (!layers || n_layers <= 0 || !x || T <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill_stack: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    const int H = (int)layers[0].meta.cols[0];
+    for (int l = 0; l < n_layers; ++l)
+        if ((int)layers[l].meta.cols[0] != H) {
+            WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill_stack: layers differ in hidden size");
+            return WISP_ERR_INVALID_ARG;
+        }
+    size_t bb = 0;
+    const size_t need = stack_ws_bytes(&layers[0], T, &bb);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 1023)) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                   "prefill_stack: workspace %zu bytes (need %zu, 1024-byte aligned)",
+                   workspace_bytes, need);
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill_stack: x must be 16-byte aligned");
+        return WISP_ERR_INVALID_ARG;
+    }
+    char* ws = static_cast<char*>(workspace);
+    float* xn = reinterpret_cast<float*>(ws + bb);
+    float* y = reinterpret_cast<float*>(ws + bb + al((size_t)T * H * sizeof(float), 1024));
+    const int K = layers[0].top_k;
+    for (int l = 0; l < n_layers; ++l) {
+        WB_CUDA_RET(wb::launch_pdl(prefill_norm_kernel, dim3(T), dim3(256), 0, stream, x,
+                                   (const float*)y,
+                                   static_cast<const __half*>(layers[l].norm_w), xn, H, eps,
+                                   l > 0 ? 1 : 0, 1),
+                    err);
+        WispError r = prefill_block(&layers[l], xn, y, T,
+                                    topk_idx ? topk_idx + (size_t)l * T * K : nullptr,
+                                    topk_w ? topk_w + (size_t)l * T * K : nullptr, workspace, bb,
+                                    l == 0, stream, err);
+        if (r != WISP_OK) return r;
+    }
+    WB_CUDA_RET(wb::launch_pdl(prefill_norm_kernel, dim3(T), dim3(256), 0, stream, x,
+                               (const float*)y, (const __half*)nullptr, xn, H, eps, 1, 0),
+                err);
+    return WISP_OK;
 }
 
 extern "C" WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x, float* y,
@@ -1353,6 +1466,6 @@ extern "C" WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const f
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: NULL layer, x or y");
         return WISP_ERR_INVALID_ARG;
     }
-    return prefill_block(layer, x, y, T, topk_idx, topk_w, workspace, workspace_bytes, stream,
-                         err);
+    return prefill_block(layer, x, y, T, topk_idx, topk_w, workspace, workspace_bytes, true,
+                         stream, err);
 }

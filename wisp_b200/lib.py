@@ -70,6 +70,10 @@ _SIGS = {
     "wisp_moe_prefill_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                            C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_moe_prefill_stack_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int, C.c_int]),
+    "wisp_moe_prefill_stack_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_float, C.c_void_p,
+                                                 C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                 C.c_size_t, C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),

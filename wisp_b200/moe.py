@@ -195,7 +195,8 @@ class MoEStack:
         return (y, idx, w) if routing else y
 
     def prefill_workspace(self, T: int) -> torch.Tensor:
-        need = int(lib().wisp_moe_prefill_workspace_bytes(C.byref(self._c_layers[0]), T)) + 1024
+        need = int(lib().wisp_moe_prefill_stack_workspace_bytes(C.byref(self._c_layers), self.L,
+                                                                 T)) + 1024
         if getattr(self, "_pws", None) is None or self._pws.numel() < need:
             self._pws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._pws
@@ -218,6 +219,26 @@ class MoEStack:
             torch.cuda.current_stream().cuda_stream, C.byref(err))
         check(rc, err)
         return (y, idx, w) if routing else y
+
+    def prefill_stack(self, x: torch.Tensor, routing: bool = False, layers: int | None = None):
+        """x <- x + MoE_l(rmsnorm(x)) for every layer on the tensor-core path
+        (``wisp_moe_prefill_stack_forward``), in place, on the current stream."""
+        T = x.shape[0]
+        n = layers or self.L
+        idx = w = None
+        if routing:
+            idx = torch.empty((n, T, self.shape.top_k), dtype=torch.int32, device=self.device)
+            w = torch.empty((n, T, self.shape.top_k), dtype=torch.float32, device=self.device)
+        ws = self.prefill_workspace(T)
+        off = (-ws.data_ptr()) % 1024
+        err = WispErrCtx()
+        rc = lib().wisp_moe_prefill_stack_forward(
+            C.byref(self._c_layers), n, self.shape.rms_eps, x.data_ptr(), T,
+            idx.data_ptr() if routing else None, w.data_ptr() if routing else None,
+            ws.data_ptr() + off, ws.numel() - off, torch.cuda.current_stream().cuda_stream,
+            C.byref(err))
+        check(rc, err)
+        return (x, idx, w) if routing else x
 
     def prefill_status(self) -> int:
         ws = getattr(self, "_pws", None)
