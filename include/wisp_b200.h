@@ -184,9 +184,10 @@ WispError wisp_moe_block_forward(const WispMoeLayer* layer, const float* x,
 
 /* The two halves of wisp_moe_block_forward, for callers that must see the
  * routing on the host between them (e.g. to fetch the routed experts into
- * the table first): _route quantises x and runs router + top-k + the
- * expert-tile plan; _experts runs gate/up, down and the combine on the plan
- * the preceding _route left in the SAME workspace (same x, T, layer shape,
+ * the table first): _route quantises x and runs router + top-k (the expert
+ * table is not read); _experts builds the expert-tile plan from that routing
+ * -- reading the table then, after the caller's fetch -- and runs gate/up,
+ * down and the combine, in the SAME workspace (same x, T, layer shape,
  * stream; topk_idx/topk_w the same buffers or both NULL). */
 WispError wisp_moe_block_route(const WispMoeLayer* layer, const float* x,
                                int T, int* topk_idx, float* topk_w,
@@ -256,6 +257,37 @@ WispError wisp_moe_prefill_stack_forward(const WispMoeLayer* layers, int n_layer
                                          float* topk_w, void* workspace,
                                          size_t workspace_bytes, cudaStream_t stream,
                                          WispErrCtx* err);
+
+/* New: an expert pool in pinned host memory streamed into a device cache of
+ * n_slots slots under LRU (the oversubscribed configuration).  Replaces the
+ * synchronous VRAM fill of wisp_expert_fetch (csrc/core/wisp_engine.c
+ * :891-1078) for a pool held in RAM: a miss is one cudaMemcpyAsync of the
+ * tiled blob from the pool into its slot on one of two transfer streams, and
+ * events order everything (no host synchronisation):
+ *   ensure     -- make ids[n] of `layer` resident; `compute` waits for their
+ *                 copies; *hits / *misses of this call;
+ *   prefetch   -- start copies for experts predicted for a later layer;
+ *   layer_done -- the layer's kernels are queued on `compute`: slots they read
+ *                 are not overwritten before those kernels finish.
+ * wisp_stream_table(layer) is the device pointer table [n_experts] to put in
+ * WispMoeLayer.expert_blobs (NULL entries: not resident).  Host blobs must be
+ * tiled (wisp_expert_tile layout), stay valid and pinned while registered.
+ * stats: hits, misses, prefetched, prefetched-then-used, bytes copied, slots. */
+typedef struct WispStreamCache WispStreamCache;
+WispStreamCache* wisp_stream_create(int n_layers, int n_experts, size_t blob_bytes,
+                                    size_t n_slots, WispErrCtx* err);
+void wisp_stream_destroy(WispStreamCache* c);
+WispError wisp_stream_register(WispStreamCache* c, int layer, int expert,
+                               const void* host_blob, WispErrCtx* err);
+const void* const* wisp_stream_table(WispStreamCache* c, int layer);
+WispError wisp_stream_ensure(WispStreamCache* c, int layer, const int* ids, int n,
+                             cudaStream_t compute, int* hits, int* misses,
+                             WispErrCtx* err);
+WispError wisp_stream_prefetch(WispStreamCache* c, int layer, const int* ids, int n,
+                               int* issued, WispErrCtx* err);
+WispError wisp_stream_layer_done(WispStreamCache* c, int layer, cudaStream_t compute,
+                                 WispErrCtx* err);
+void wisp_stream_stats(WispStreamCache* c, uint64_t* out6);
 
 /* No counterpart in the reference.  wisp_moe_block_forward without a
  * workspace argument, for callers that cannot allocate device memory: a host

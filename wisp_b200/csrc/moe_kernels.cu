@@ -522,19 +522,6 @@ ep_combine_kernel(float* y, const float* rows, const int* ridx, const float* w, 
     }
 }
 
-// Re-read every tile's blob pointer from the expert table (for a plan built
-// before the table was filled: the host-driven miss path).
-__global__ void __launch_bounds__(kThreads)
-resolve_kernel(LayerArgs L, Ws W) {
-    pdl_wait();
-    pdl_launch();
-    const int n = __ldcg(W.counters + C_NTILES);
-    for (int t = threadIdx.x; t < n; t += kThreads) {
-        const int e = __ldcg(&W.tiles[t].expert);
-        W.tiles[t].blob = checked_blob(L, W, e);
-    }
-}
-
 __global__ void __launch_bounds__(kThreads)
 router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
     pdl_wait();
@@ -1871,8 +1858,8 @@ cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t 
 }
 
 cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* xin,
-                          cudaStream_t s) {
-    const int mt = plan_tokens(a, T);
+                          cudaStream_t s, bool plan = true) {
+    const int mt = plan ? plan_tokens(a, T) : 0;
     const int nsl = (a.H + kSlice - 1) / kSlice;
     const int blocks = (a.E * nsl + kWarps - 1) / kWarps;
     return launch(router_kernel, dim3(blocks), dim3(kThreads), router_smem(a.E), s, a, W, T, mt,
@@ -1884,24 +1871,25 @@ cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* x
 // prep over T tokens (one cluster per token).  P_ROUTE is added when the
 // router runs inside prep; otherwise the separate router kernel follows.
 cudaError_t launch_prep(const LayerArgs& a, const Ws& W, int T, int flags, float* x, float* y,
-                        float eps, int prevK, int prev_sh, int prev_kp, cudaStream_t s) {
+                        float eps, int prevK, int prev_sh, int prev_kp, cudaStream_t s,
+                        bool plan = true) {
     const int cs = prep_cluster(a.H, a.gs);
     hook_mark(s);
     return launch_pdl_cluster(prep_kernel, dim3(T * cs), dim3(kPrepThreads),
                               prep_smem_bytes(a.H, cs, a.E), s, cs, a, W, T, flags, x, y, eps,
-                              prevK, prev_sh, prev_kp, plan_tokens(a, T));
+                              prevK, prev_sh, prev_kp, plan ? plan_tokens(a, T) : 0);
 }
 
 // Routing of a layer whose input prep is about to quantise: the router in
 // prep, or prep then the router kernel on `xin`.
 cudaError_t launch_prep_route(const LayerArgs& a, const Ws& W, int T, int flags, float* x,
                               float eps, int prevK, int prev_sh, int prev_kp, const float* xin,
-                              cudaStream_t s) {
+                              cudaStream_t s, bool plan = true) {
     const bool fused = route_in_prep(a, T);
     cudaError_t e = launch_prep(a, W, T, flags | (fused ? (int)P_ROUTE : 0), x, nullptr, eps,
-                                prevK, prev_sh, prev_kp, s);
+                                prevK, prev_sh, prev_kp, s, plan);
     if (e != cudaSuccess || fused) return e;
-    return launch_router(a, W, T, xin, s);
+    return launch_router(a, W, T, xin, s, plan);
 }
 
 }  // namespace
@@ -1966,7 +1954,8 @@ static bool aligned_io(const void* p) { return (reinterpret_cast<uintptr_t>(p) &
 // prep (quantise x) + router/top-k/plan for one layer.
 static WispError block_route(const WispMoeLayer* layer, const float* x, int T, int* topk_idx,
                              float* topk_w, void* workspace, size_t workspace_bytes,
-                             cudaStream_t stream, WispErrCtx* err, LayerArgs* a_out, Ws* w_out) {
+                             cudaStream_t stream, WispErrCtx* err, LayerArgs* a_out, Ws* w_out,
+                             bool plan = true) {
     WispError ce = common_checks(layer, 1, T, workspace, workspace_bytes, err);
     if (ce != WISP_OK) return ce;
     if (!x || !aligned_io(x)) {
@@ -1981,7 +1970,7 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
     WB_CUDA_RET(ensure_attrs(a.H), err);
     WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
     WB_CUDA_RET(launch_prep_route(a, W, T, (int)P_QUANT, const_cast<float*>(x), 0.f, 0, 0, 1, x,
-                                  stream),
+                                  stream, plan),
                 err);
     *a_out = a;
     *w_out = W;
@@ -1990,9 +1979,7 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
 
 // gate/up + down + combine, on the plan the preceding route left in the workspace.
 static WispError block_experts(const LayerArgs& a, const Ws& W, int T, const float* x, float* y,
-                               cudaStream_t stream, WispErrCtx* err, bool resolve = false) {
-    if (resolve)
-        WB_CUDA_RET(launch(resolve_kernel, dim3(1), dim3(kThreads), 0, stream, a, W), err);
+                               cudaStream_t stream, WispErrCtx* err) {
     WB_CUDA_RET(launch_streams(a, W, T, stream), err);
     Ws Wc = W;
     Wc.prev_idx = W.topk_idx;
@@ -2025,10 +2012,12 @@ extern "C" WispError wisp_moe_block_route(const WispMoeLayer* layer, const float
                                           int* topk_idx, float* topk_w, void* workspace,
                                           size_t workspace_bytes, cudaStream_t stream,
                                           WispErrCtx* err) {
+    // routing only: the expert plan is built by wisp_moe_block_experts once the
+    // caller has made the routed experts resident
     LayerArgs a;
     Ws W;
     WispError r = block_route(layer, x, T, topk_idx, topk_w, workspace, workspace_bytes, stream,
-                              err, &a, &W);
+                              err, &a, &W, /*plan=*/false);
     if (r == WISP_OK) hook_mark(stream);
     return r;
 }
@@ -2049,7 +2038,10 @@ extern "C" WispError wisp_moe_block_experts(const WispMoeLayer* layer, const flo
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    return block_experts(a, W, T, x, y, stream, err, /*resolve=*/true);
+    WB_CUDA_RET(launch(plan_kernel, dim3(1), dim3(kThreads), router_smem(a.E), stream, a, W, T,
+                       plan_tokens(a, T)),
+                err);
+    return block_experts(a, W, T, x, y, stream, err);
 }
 
 extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_layers, float eps,

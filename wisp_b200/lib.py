@@ -74,6 +74,19 @@ _SIGS = {
     "wisp_moe_prefill_stack_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_float, C.c_void_p,
                                                  C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                                  C.c_size_t, C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_stream_create": (C.c_void_p, [C.c_int, C.c_int, C.c_size_t, C.c_size_t,
+                                        C.POINTER(WispErrCtx)]),
+    "wisp_stream_destroy": (None, [C.c_void_p]),
+    "wisp_stream_register": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                       C.POINTER(WispErrCtx)]),
+    "wisp_stream_table": (C.c_void_p, [C.c_void_p, C.c_int]),
+    "wisp_stream_ensure": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_stream_prefetch": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                       C.POINTER(WispErrCtx)]),
+    "wisp_stream_layer_done": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p,
+                                         C.POINTER(WispErrCtx)]),
+    "wisp_stream_stats": (None, [C.c_void_p, C.c_void_p]),
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),
