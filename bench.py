@@ -56,6 +56,12 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--config3-layers", type=int, default=4,
                    help="resident DeepSeek-shaped layers of the config-3 leg (0 = skip)")
+    p.add_argument("--c3-total-layers", type=int, default=58,
+                   help="layers of the config-3 stack split over the ranks")
+    p.add_argument("--prefill-micro", type=int, default=512,
+                   help="config-3 prefill micro-batch (tokens)")
+    p.add_argument("--c3-prefill-steps", type=int, default=3)
+    p.add_argument("--c3-decode-steps", type=int, default=32)
     p.add_argument("--stream-layers", type=int, default=16,
                    help="layers of the config-4 host pool (6.3 GB each)")
     p.add_argument("--stream-steps", type=int, default=512)
@@ -548,7 +554,11 @@ def main_ep(args):
 
 
 def main_prefill(args):
-    """Config 3 as the headline line (one GPU; see run_config3)."""
+    """Config 3 as the headline line: one GPU (run_config3, per-layer normalised) or the
+    layer pipeline over N GPUs (wisp_b200.pipeline.bench_prefill_main)."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        from wisp_b200 import pipeline
+        return pipeline.bench_prefill_main(args)
     import torch
     from wisp_b200 import build
     dev = torch.device("cuda", 0)

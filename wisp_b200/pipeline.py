@@ -221,3 +221,149 @@ def bench_main(args) -> None:
                     "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": (launches_per_layer(shape, mb) * per + 1) * M * args.steps * world,
         }), flush=True)
+
+
+def layer_split(L: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous (first layer, count) per rank; the first L % world ranks get one more."""
+    base, extra = divmod(L, world)
+    out, l0 = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((l0, n))
+        l0 += n
+    return out
+
+
+def graphs_for(run_one, bufs):
+    """One CUDA graph per buffer of `run_one(buf)` (warmed once outside capture)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        tmp = bufs[0].clone()
+        run_one(tmp)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graphs = []
+    for b in bufs:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_one(b)
+        graphs.append(g)
+    return graphs
+
+
+def bench_prefill_main(args) -> None:
+    """Config 3 over N GPUs: the 58-layer DeepSeek-V3-shaped stack split into contiguous
+    layer ranges, prefill of 4096 tokens in micro-batches on the tensor-core path and
+    decode at batch 32 on the stream kernels, both as a ring of micro-batches over NCCL
+    (steady-state throughput: every stage busy).  Config-3 time = 4096 / prefill rate +
+    128 * 32 / decode rate."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from . import build
+    from . import converter as cv
+    from .benchutil import ClockSampler, peaks
+    from .moe import MoEStack
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if rank == 0:
+        build.build()
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    dist.barrier()
+    build.build()
+
+    seed = 20251201 + 3
+    L = args.c3_total_layers
+    l0, nl = layer_split(L, world)[rank]
+    shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=256, top_k=8, shared_inter=2048,
+                        n_layers=L)
+    t0 = time.time()
+    stack = MoEStack(shape, seed, device=dev, zipf_s=1.1, n_layers=nl, layer0=l0)
+    setup_s = time.time() - t0
+    groups = [dist.new_group(list(range(world))), dist.new_group(list(range(world)))]
+    Tp, Bd, dsteps = 4096, 32, 128
+    mbp = args.prefill_micro
+    Mp = Tp // mbp
+    mbd = max(1, Bd // max(world, 1))
+    Md = Bd // mbd
+    pin = [cv.make_input(shape, mbp, seed + 100 + m).to(dev) for m in range(Mp)]
+    din = [cv.make_input(shape, mbd, seed + 200 + m).to(dev) for m in range(Md)]
+    pbufs = [x.clone() for x in pin]
+    stack.prefill_workspace(mbp)
+    pgraphs = graphs_for(stack.prefill_stack, pbufs)
+    ppipe = LayerPipeline(lambda m: pgraphs[m].replay(), pbufs, rank, world, groups)
+    dpipe = LayerPipeline.for_stack(stack, din, rank, world, groups)
+
+    def timed(pipe, steps):
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(steps):
+            pipe.step(first=False, last=False)
+        pipe.drain()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item() / steps
+
+    # prime both rings, then time steady state
+    for pipe, w in ((ppipe, 2), (dpipe, max(3, args.warmup))):
+        for s in range(w):
+            pipe.step(first=s == 0, last=False)
+        pipe.drain()
+    with ClockSampler(local) as clk:
+        p_ms = timed(ppipe, args.c3_prefill_steps)
+        d_ms = timed(dpipe, args.c3_decode_steps)
+    status = stack.prefill_status() | stack.status()
+    st_t = torch.tensor([status], device=dev)
+    dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
+    ppipe.close()
+    dpipe.close()
+    pgraphs.clear()
+    del ppipe, dpipe
+    torch.cuda.synchronize()
+    dist.barrier()
+    for g in groups:
+        dist.destroy_process_group(g)
+    dist.destroy_process_group()
+    if rank == 0:
+        H, I, E, K = 7168, 2048, 256, 8
+        flops = L * (2 * 3 * H * I * (Tp * K + Tp) + 2 * H * E * Tp)
+        p_tps = Tp * 1000.0 / p_ms
+        d_tps = Bd * 1000.0 / d_ms
+        total_ms = Tp / p_tps * 1e3 + dsteps * Bd / d_tps * 1e3
+        tflops_gpu = flops / (p_ms * 1e-3) / 1e12 / world
+        pk = peaks()
+        print(json.dumps({
+            "metric": "DeepSeek-V3-shaped 58-block stack: prefill 4096 + 128 decode steps at "
+                      "batch 32, tokens/s", "value": round((Tp + dsteps * Bd) / total_ms * 1e3, 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.c3_prefill_steps,
+            "warmup": 2, "ms_per_step": round(total_ms, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4xf16",
+            "data": "synthetic (seeded N(0,0.02) weights quantised int4 gs64; fp16 N(0,1) "
+                    "inputs)",
+            "config": {"workload": f"config3: DeepSeek-V3-shaped {L}-layer stack, layer "
+                                   f"pipeline over {world} GPUs; prefill {Tp} tokens in {Mp} "
+                                   f"micro-batches of {mbp}; decode batch {Bd} in {Md} "
+                                   f"micro-batches of {mbd}; steady-state ring",
+                       "parallelism": f"pp{world}", "layers_per_rank":
+                       [n for _, n in layer_split(L, world)]},
+            "prefill_tokens_per_s": round(p_tps, 1), "prefill_ms": round(p_ms, 2),
+            "prefill_tflops_per_gpu": round(tflops_gpu, 1),
+            "decode_tokens_per_s": round(d_tps, 1), "decode_ms_per_step": round(d_ms, 3),
+            "roofline": {"bound": "tensor", "achieved": round(tflops_gpu, 1),
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(tflops_gpu / pk["bf16_tflops"], 4), "traffic": None,
+                         "peak_source": pk["source"]},
+            "status": int(st_t.item()), "setup_s": round(setup_s, 1),
+            "clocks": clk.summary()}), flush=True)
