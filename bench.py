@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--config3-layers", type=int, default=4,
                    help="resident DeepSeek-shaped layers of the config-3 leg (0 = skip)")
+    p.add_argument("--c3-experts", type=int, default=256,
+                   help="routed experts per config-3 layer (fewer: a small case for ncu)")
     p.add_argument("--c3-total-layers", type=int, default=58,
                    help="layers of the config-3 stack split over the ranks")
     p.add_argument("--prefill-micro", type=int, default=512,
@@ -352,7 +354,8 @@ def run_config3(args, dev, k: int) -> dict:
     import torch
     from wisp_b200 import converter as cv
     from wisp_b200.moe import MoEStack
-    shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=256, top_k=8, shared_inter=2048,
+    E = args.c3_experts
+    shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=E, top_k=8, shared_inter=2048,
                         n_layers=k)
     t0 = time.time()
     st = MoEStack(shape, SEED + 3, device=dev, zipf_s=1.1)
@@ -379,7 +382,7 @@ def run_config3(args, dev, k: int) -> dict:
     status = st.prefill_status()
     _, idx, _ = st.prefill_stack(xp0.clone(), routing=True)
     torch.cuda.synchronize()
-    H, I, E, K = 7168, 2048, 256, 8
+    H, I, K = 7168, 2048, 8
     flops_layer = 2 * 3 * H * I * (Tp * K + Tp) + 2 * H * E * Tp
     tflops = k * flops_layer / pre_ms / 1e9
     # decode: batch 32, one graph per step
@@ -410,7 +413,8 @@ def run_config3(args, dev, k: int) -> dict:
     total_ms = (pre_ms + steps * dec_ms) * scale
     cnt = np.bincount(idx[0].cpu().numpy().reshape(-1), minlength=E)
     return {
-        "workload": f"config3: DeepSeek-V3-shaped stack, resident {k}-layer slice, prefill "
+        "workload": f"config3: DeepSeek-V3-shaped stack ({E} routed experts), resident "
+                    f"{k}-layer slice, prefill "
                     f"{Tp} tokens (tensor-core grouped GEMM) then {steps} decode steps at batch "
                     f"{Bd}; times x58/{k} for the 58-layer stack (368 GB does not fit one GPU)",
         "layers_resident": k, "setup_s": round(setup_s, 1),

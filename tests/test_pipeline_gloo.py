@@ -63,3 +63,15 @@ def test_ring_applies_every_rank_in_order(world, M, steps):
                 v = v * 2.0 + (r + 1)
         want.append(v)
     assert got == want
+
+
+def test_layer_split_covers_the_stack_contiguously():
+    from wisp_b200.pipeline import layer_split
+    for L, world in ((58, 8), (58, 4), (58, 2), (32, 8), (7, 3), (4, 4)):
+        parts = layer_split(L, world)
+        assert len(parts) == world
+        assert parts[0][0] == 0
+        for (a, n), (b, _) in zip(parts, parts[1:]):
+            assert a + n == b
+        assert sum(n for _, n in parts) == L
+        assert max(n for _, n in parts) - min(n for _, n in parts) <= 1

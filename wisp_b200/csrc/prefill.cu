@@ -116,25 +116,27 @@ struct PWs {
     int R, max_gu, max_dn;
 };
 
-// Ring depths.  WS: weight staging (smem); BS: activation tiles (smem, deep:
-// their loads are the longest-latency step); S: dequantised weight tiles in
-// TMEM (NMAT x 32 columns each); NACC: accumulator buffers (TMEM, 128 columns
-// per matrix).  TMEM: 256 accumulator columns + S * NMAT * 32 = 256 A columns.
+// A stage covers kKG quant groups (K = 128).  Ring depths in stages -- WS: weight
+// staging (smem); BS: activation tiles (smem, deep: their loads are the
+// longest-latency step); S: dequantised weight tiles in TMEM (NMAT * kKG * 32
+// columns each); NACC: accumulator buffers (TMEM, 128 columns per matrix).
+// TMEM: 256 accumulator columns + S * NMAT * kKG * 32 = 256 A columns.
+constexpr int kKG = 2;
 template <int NMAT>
 struct GCfg;
 template <>
 struct GCfg<2> {  // gate + up
-    static constexpr int WS = 8, BS = 8, S = 4, NACC = 1;
+    static constexpr int WS = 4, BS = 4, S = 2, NACC = 1;
 };
 template <>
 struct GCfg<1> {  // down
-    static constexpr int WS = 16, BS = 8, S = 8, NACC = 2;
+    static constexpr int WS = 8, BS = 4, S = 4, NACC = 2;
 };
 
 template <int NMAT>
 constexpr size_t gemm_smem_bytes() {
     using C = GCfg<NMAT>;
-    return 1024 + (size_t)C::BS * kBTile + (size_t)C::WS * NMAT * kWStage + 1024;
+    return 1024 + (size_t)C::BS * kKG * kBTile + (size_t)C::WS * NMAT * kKG * kWStage + 1024;
 }
 
 // ------------------------------------------------------------------------
@@ -831,8 +833,8 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~(uintptr_t)1023);
     uint8_t* sB = base;
-    uint8_t* sW = sB + C::BS * kBTile;
-    uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * kWStage);
+    uint8_t* sW = sB + C::BS * kKG * kBTile;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * kKG * kWStage);
     uint64_t* w_empty = w_full + C::WS;
     uint64_t* a_full = w_empty + C::WS;   // dequantised tile in TMEM
     uint64_t* a_empty = a_full + C::S;
@@ -880,7 +882,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
     pdl_launch();
     const int ntiles = __ldcg(W.counters + (NMAT == 2 ? 0 : 1));
     const PTile* tiles = NMAT == 2 ? W.tiles_gu : W.tiles_dn;
-    const int KB = (NMAT == 2 ? P.H : P.I) / kBK;
+    const int KS = (NMAT == 2 ? P.H : P.I) / (kBK * kKG);  // stages per tile
     int* status = W.status;
 
     if (warp == kWProdWarp) {
@@ -898,18 +900,19 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                     tmap_acquire(maps[m][0]);
                     tmap_acquire(maps[m][1]);
                 }
-                for (int kb = 0; kb < KB; ++kb, ++wi) {
+                for (int ks = 0; ks < KS; ++ks, ++wi) {
                     const int s = wi % C::WS;
                     if (!wait1_lazy(&w_empty[s], ((wi / C::WS) & 1) ^ 1, s_abort, status)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&w_full[s], NMAT * kWStage);
+                    mbar_expect_tx(&w_full[s], NMAT * kKG * kWStage);
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m) {
-                        uint8_t* dst = sW + (s * NMAT + m) * kWStage;
-                        tma3d(dst, maps[m][0], 0, kb, tl.mt * 16, &w_full[s]);
-                        tma3d(dst + kWCodes, maps[m][1], 0, kb, tl.mt * 16, &w_full[s]);
+                        // [16 blocks][kKG groups] of codes, then of scale/zero pairs
+                        uint8_t* dst = sW + (s * NMAT + m) * kKG * kWStage;
+                        tma3d(dst, maps[m][0], 0, ks * kKG, tl.mt * 16, &w_full[s]);
+                        tma3d(dst + kKG * kWCodes, maps[m][1], 0, ks * kKG, tl.mt * 16, &w_full[s]);
                     }
                 }
             }
@@ -923,21 +926,24 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
             for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
                 const PTile tl = tiles[t];
                 const int nmma = (tl.n + 15) & ~15;
-                for (int kb = 0; kb < KB; ++kb, ++bi) {
+                for (int ks = 0; ks < KS; ++ks, ++bi) {
                     const int s = bi % C::BS;
                     if (!wait1_lazy(&b_empty[s], ((bi / C::BS) & 1) ^ 1, s_abort, status)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&b_full[s], (uint32_t)nmma * 128);
-                    int off = 0;
+                    mbar_expect_tx(&b_full[s], (uint32_t)(kKG * nmma * 128));
 #pragma unroll
-                    for (int i = kBoxes - 1; i >= 0; --i) {
-                        const int h = 16 << i;
-                        if ((nmma - off) >= h) {
-                            tma2d(sB + s * kBTile + off * 128, &bm.box[i], kb * kBK, tl.row0 + off,
-                                  &b_full[s]);
-                            off += h;
+                    for (int g = 0; g < kKG; ++g) {
+                        int off = 0;
+#pragma unroll
+                        for (int i = kBoxes - 1; i >= 0; --i) {
+                            const int h = 16 << i;
+                            if ((nmma - off) >= h) {
+                                tma2d(sB + (s * kKG + g) * kBTile + off * 128, &bm.box[i],
+                                      (ks * kKG + g) * kBK, tl.row0 + off, &b_full[s]);
+                                off += h;
+                            }
                         }
                     }
                 }
@@ -958,7 +964,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 if (!wait1(&acc_empty[buf], ((ci / C::NACC) & 1) ^ 1, s_abort, status)) break;
                 tc_fence_after();
                 const uint32_t d0 = tmem + (uint32_t)((NMAT == 2 ? 0 : buf) * kNT);
-                for (int kb = 0; kb < KB; ++kb, ++si) {
+                for (int ks = 0; ks < KS; ++ks, ++si) {
                     const int s = si % C::S, sb = si % C::BS;
                     if (!wait1(&a_full[s], (si / C::S) & 1, s_abort, status) ||
                         !wait1(&b_full[sb], (si / C::BS) & 1, s_abort, status)) {
@@ -966,14 +972,18 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bd = bdesc0 + (uint64_t)(sb * (kBTile >> 4));
-                    const uint32_t at = tmem + kAcol0 + (uint32_t)(s * NMAT * 32);
+                    const uint64_t bd = bdesc0 + (uint64_t)(sb * kKG * (kBTile >> 4));
+                    const uint32_t at = tmem + kAcol0 + (uint32_t)(s * NMAT * kKG * 32);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
+                    for (int g = 0; g < kKG; ++g)
 #pragma unroll
-                        for (int m = 0; m < NMAT; ++m)
-                            mma_ts(d0 + (uint32_t)(m * kNT), at + (uint32_t)(m * 32 + k * 8),
-                                   bd + (uint64_t)(2 * k), id, (kb | k) ? 1u : 0u);
+                        for (int k = 0; k < 4; ++k)
+#pragma unroll
+                            for (int m = 0; m < NMAT; ++m)
+                                mma_ts(d0 + (uint32_t)(m * kNT),
+                                       at + (uint32_t)((m * kKG + g) * 32 + k * 8),
+                                       bd + (uint64_t)(g * (kBTile >> 4) + 2 * k), id,
+                                       (ks | g | k) ? 1u : 0u);
                     mma_commit(&a_empty[s]);
                     mma_commit(&b_empty[sb]);
                 }
@@ -1029,19 +1039,23 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
         }
     } else {
         // dequantisers: warp (g, q) writes TMEM lanes 32q..32q+31 (weight rows) of
-        // part g of each stage: gate/up -> matrix g/2, half g%2 of the 64-wide
-        // group (16 columns); down -> quarter g (8 columns)
-        const int dw = warp - kDqWarp0, q = warp & 3, g = dw >> 2;
+        // part g of each group of the stage: gate/up -> matrix g/2, half g%2 of the
+        // 64-wide group (16 columns); down -> quarter g (8 columns)
+        const int dw = warp - kDqWarp0, q = warp & 3, gw = dw >> 2;
         const int r = q * 32 + lane;
-        const int mat = NMAT == 2 ? (g >> 1) : 0;
-        constexpr int PW = NMAT == 2 ? 4 : 2;  // code words per thread and stage
-        const int part = NMAT == 2 ? (g & 1) : g;
+        const int mat = NMAT == 2 ? (gw >> 1) : 0;
+        constexpr int PW = NMAT == 2 ? 4 : 2;  // code words per thread and group
+        const int part = NMAT == 2 ? (gw & 1) : gw;
         const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + kAcol0 +
-                                   (uint32_t)(mat * 32 + part * PW * 4);
+                                   (uint32_t)(mat * kKG * 32 + part * PW * 4);
+        // smem staging of one matrix: [16 blocks][kKG groups][8 rows][8 code words],
+        // then [16 blocks][kKG groups][8 rows] (scale, zero) words
+        const int cw0 = ((r >> 3) * kKG) * 64 + (r & 7) * 8 + part * PW;
+        const int sw0 = kKG * kWCodes / 4 + ((r >> 3) * kKG) * 8 + (r & 7);
         uint32_t wi = 0, ai = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
-            for (int kb = 0; kb < KB; ++kb, ++wi, ++ai) {
+            for (int ks = 0; ks < KS; ++ks, ++wi, ++ai) {
                 const int ws = wi % C::WS, as = ai % C::S;
                 if (!wait_warp(&w_full[ws], (wi / C::WS) & 1, s_abort, status) ||
                     !wait_warp(&a_empty[as], ((ai / C::S) & 1) ^ 1, s_abort, status)) {
@@ -1049,30 +1063,30 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                     break;
                 }
                 tc_fence_after();
-                const uint32_t* st =
-                    reinterpret_cast<const uint32_t*>(sW + (ws * NMAT + mat) * kWStage);
-                const uint32_t szw = st[kWCodes / 4 + r];
-                const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFFu)));
-                const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
-                uint32_t v[PW];
-                if (PW == 4) {
-                    const uint4 c4 = *reinterpret_cast<const uint4*>(st + r * 8 + part * 4);
-                    v[0] = c4.x; v[1] = c4.y; v[2] = c4.z; v[3] = c4.w;
-                } else {
-                    const uint2 c2 = *reinterpret_cast<const uint2*>(st + r * 8 + part * 2);
-                    v[0] = c2.x; v[1] = c2.y;
-                }
-                const uint32_t ta = lane_addr + (uint32_t)(as * NMAT * 32);
-                if (PW == 4) {
-                    uint32_t o[16];
+                const uint32_t* st = reinterpret_cast<const uint32_t*>(
+                    sW + (ws * NMAT + mat) * kKG * kWStage);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) dequant_cols(v[i], s2, z2, o + 4 * i);
-                    tmem_st16(ta, o);
-                } else {
-                    uint32_t o[8];
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) dequant_cols(v[i], s2, z2, o + 4 * i);
-                    tmem_st8(ta, o);
+                for (int g = 0; g < kKG; ++g) {
+                    const uint32_t szw = st[sw0 + g * 8];
+                    const __half2 s2 =
+                        __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFFu)));
+                    const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
+                    const uint32_t ta = lane_addr + (uint32_t)((as * NMAT * kKG + g) * 32);
+                    if (PW == 4) {
+                        const uint4 c4 = *reinterpret_cast<const uint4*>(st + cw0 + g * 64);
+                        uint32_t o[16];
+                        dequant_cols(c4.x, s2, z2, o);
+                        dequant_cols(c4.y, s2, z2, o + 4);
+                        dequant_cols(c4.z, s2, z2, o + 8);
+                        dequant_cols(c4.w, s2, z2, o + 12);
+                        tmem_st16(ta, o);
+                    } else {
+                        const uint2 c2 = *reinterpret_cast<const uint2*>(st + cw0 + g * 64);
+                        uint32_t o[8];
+                        dequant_cols(c2.x, s2, z2, o);
+                        dequant_cols(c2.y, s2, z2, o + 4);
+                        tmem_st8(ta, o);
+                    }
                 }
                 tmem_st_wait();
                 tc_fence_before();
@@ -1251,9 +1265,9 @@ bool weight_templates(const PArgs& P, const WispExpertMeta& m, void* anchor, WTe
         const cuuint64_t rows = m.rows[mat], cols = m.cols[mat];
         const cuuint64_t G = cols / 64, nblk = rows / 8, block_bytes = 4 * cols + 32 * G;
         const cuuint64_t dc[3] = {64, G, nblk}, sc[2] = {256, block_bytes};
-        const cuuint32_t bc[3] = {64, 1, 16};
+        const cuuint32_t bc[3] = {64, (cuuint32_t)kKG, 16};
         const cuuint64_t ds[3] = {8, G, nblk}, ss[2] = {32, block_bytes};
-        const cuuint32_t bs[3] = {8, 1, 16};
+        const cuuint32_t bs[3] = {8, (cuuint32_t)kKG, 16};
         if (!encode(&t->m[mat * 2], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, dc, sc, bc,
                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
             !encode(&t->m[mat * 2 + 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, ds, ss, bs,
