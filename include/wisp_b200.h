@@ -242,6 +242,18 @@ WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x,
                                    void* workspace, size_t workspace_bytes,
                                    cudaStream_t stream, WispErrCtx* err);
 
+/* New: the routed experts only, on the tensor-core path, for a routing the
+ * caller supplies -- y[t] = sum_j w[t,j] * expert_{idx[t,j]}(x[t]) over K slots
+ * (idx < 0: skipped), no router, no shared expert.  The expert-parallel owner of
+ * dispatched rows calls it with K = 1 and w = 1 (the counterpart of
+ * wisp_moe_experts_routed for many rows per expert).  workspace:
+ * wisp_moe_prefill_routed_workspace_bytes(layer, T, K), 1024-byte aligned. */
+size_t wisp_moe_prefill_routed_workspace_bytes(const WispMoeLayer* layer, int T, int K);
+WispError wisp_moe_prefill_routed(const WispMoeLayer* layer, const float* x, float* y,
+                                  int T, int K, const int* topk_idx, const float* topk_w,
+                                  void* workspace, size_t workspace_bytes,
+                                  cudaStream_t stream, WispErrCtx* err);
+
 /* New: stack of n_layers blocks on the prefill path -- per layer l,
  * x <- x + MoE_l(rmsnorm(x; norm_w_l, eps)) (the FFN half of decode_step,
  * csrc/core/wisp_engine.c:1563-1570, attention = identity), each block by

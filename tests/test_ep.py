@@ -104,3 +104,30 @@ def test_ep_layer_matches_block_and_oracle(cuda, B):
                                           shared=st.host_shared(0))
     if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.cpu().numpy()) == 0:
         check_outputs(y.cpu().numpy(), yr, tight=False)
+
+
+@pytest.mark.gpu
+def test_ep_layer_tensor_path_for_many_rows(cuda):
+    """At 64 tokens x top-8 the rank receives 512 rows: its experts run on the
+    tensor-core path (wisp_moe_prefill_routed); the result matches the fused block and
+    the oracle."""
+    from oracle import oracle as orc
+    from wisp_b200 import converter as cv
+    from wisp_b200.ep import EPLayer
+    from wisp_b200.moe import MoEStack
+    from parity import check_outputs, check_routing
+    shape = cv.MoEShape(hidden=1024, inter=512, n_experts=32, top_k=8, shared_inter=512)
+    ep = EPLayer(shape, 43, 0, 1, cuda, zipf_s=1.1)
+    assert 64 * 8 >= max(ep.TENSOR_MIN_ROWS, ep.TENSOR_MIN_PER_EXPERT * ep.per)
+    st = MoEStack(shape, 43, device=cuda, zipf_s=1.1)
+    x = cv.make_input(shape, 64, 10).to(cuda)
+    y, idx, w = ep.forward(x)
+    yb, ib, _ = st.block(0, x, routing=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(idx.cpu().numpy(), ib.cpu().numpy())
+    check_outputs(y.cpu().numpy(), yb.cpu().numpy())
+    Wb, bb = st.host_router(0)
+    yr, ir, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
+                                          shared=st.host_shared(0))
+    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.cpu().numpy()) == 0:
+        check_outputs(y.cpu().numpy(), yr)

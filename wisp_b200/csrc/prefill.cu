@@ -1192,10 +1192,10 @@ PWs make_pws(void* ws, const PLayout& L) {
 // The layer's geometry must suit the tensor-core tiles: tiled int4 experts with
 // 64-element groups, 128-row tiles of every matrix, a shared expert (if any) of
 // the routed experts' shape.
-WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err) {
+WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err, bool route = true) {
     const WispExpertMeta& m = l->meta;
     const int H = (int)m.cols[0], I = (int)m.rows[0];
-    if (!l->expert_blobs || !l->router_w || !m.valid || T <= 0) {
+    if (!l->expert_blobs || (route && !l->router_w) || !m.valid || T <= 0) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: missing layer pointers or T <= 0");
         return WISP_ERR_INVALID_ARG;
     }
@@ -1315,12 +1315,25 @@ cudaError_t ensure_gemm_attrs() {
 }
 
 // Route x, then run the experts; x [T, H] fp32 is the MoE input (normalised).
+// One block.  route: run the router (else topk_idx/topk_w [T, K] are the caller's
+// routing, K = k_override, and the shared expert is left out: the expert-parallel
+// owner of routed rows).
 WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int T,
                         int* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
-                        bool reset_status, cudaStream_t stream, WispErrCtx* err) {
-    WispError ce = check_prefill_layer(layer, T, err);
+                        bool reset_status, cudaStream_t stream, WispErrCtx* err,
+                        bool route = true, int k_override = 0) {
+    WispError ce = check_prefill_layer(layer, T, err, route);
     if (ce != WISP_OK) return ce;
-    const PArgs P = make_pargs(layer);
+    PArgs P = make_pargs(layer);
+    if (!route) {
+        if (!topk_idx || !topk_w || k_override <= 0 || k_override > 64) {
+            WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                       "prefill_routed: routing arrays and 1 <= K <= 64 required");
+            return WISP_ERR_INVALID_ARG;
+        }
+        P.K = k_override;
+        P.has_shared = 0;
+    }
     const PLayout L = make_playout(T, P.H, P.I, P.E, P.K);
     if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 1023)) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
@@ -1347,7 +1360,9 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     // over the blocks of a stack
     if (reset_status) WB_CUDA_RET(cudaMemsetAsync(W.status, 0, sizeof(int), stream), err);
     const int sms = wb::sm_count();
-    if (T >= kRouterTcMinT) {
+    if (!route) {
+        // routing given: straight to the plan
+    } else if (T >= kRouterTcMinT) {
         // hi/lo halves of x live in the (not yet used) activation-row buffer
         __half* hi = W.xs;
         __half* lo = W.xs + (size_t)T * P.H;
@@ -1379,10 +1394,12 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
                                    W.logits, T, P.E, P.H),
                     err);
     }
-    WB_CUDA_RET(wb::launch_pdl(route_topk_kernel, dim3(std::min((T + 7) / 8, 4 * sms)), dim3(256),
-                               (size_t)8 * 2 * P.E * 4, stream, (const float*)W.logits,
-                               P.router_bias, T, P.E, P.K, W.idx, W.w),
-                err);
+    if (route)
+        WB_CUDA_RET(wb::launch_pdl(route_topk_kernel, dim3(std::min((T + 7) / 8, 4 * sms)),
+                                   dim3(256), (size_t)8 * 2 * P.E * 4, stream,
+                                   (const float*)W.logits, P.router_bias, T, P.E, P.K, W.idx,
+                                   W.w),
+                    err);
     WB_CUDA_RET(wb::launch_pdl(prefill_plan_kernel, dim3(1), dim3(kPlanThreads),
                                (size_t)5 * (P.E + 2) * 4, stream, P, W, T, wt),
                 err);
@@ -1470,6 +1487,26 @@ extern "C" WispError wisp_moe_prefill_stack_forward(const WispMoeLayer* layers, 
                                (const float*)y, (const __half*)nullptr, xn, H, eps, 1, 0),
                 err);
     return WISP_OK;
+}
+
+extern "C" size_t wisp_moe_prefill_routed_workspace_bytes(const WispMoeLayer* layer, int T,
+                                                          int K) {
+    if (!layer || T <= 0 || K <= 0) return 0;
+    const WispExpertMeta& m = layer->meta;
+    return make_playout(T, (int)m.cols[0], (int)m.rows[0], layer->n_experts, K).total;
+}
+
+extern "C" WispError wisp_moe_prefill_routed(const WispMoeLayer* layer, const float* x, float* y,
+                                             int T, int K, const int* topk_idx,
+                                             const float* topk_w, void* workspace,
+                                             size_t workspace_bytes, cudaStream_t stream,
+                                             WispErrCtx* err) {
+    if (!layer || !x || !y) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill_routed: NULL layer, x or y");
+        return WISP_ERR_INVALID_ARG;
+    }
+    return prefill_block(layer, x, y, T, const_cast<int*>(topk_idx), const_cast<float*>(topk_w),
+                         workspace, workspace_bytes, true, stream, err, /*route=*/false, K);
 }
 
 extern "C" WispError wisp_moe_prefill_forward(const WispMoeLayer* layer, const float* x, float* y,

@@ -145,12 +145,34 @@ class EPLayer:
                                    torch.cuda.current_stream().cuda_stream, C.byref(err)), err)
         return idx, w
 
+    # this rank's experts run on the tensor-core path (each routed expert streamed
+    # once per 128 rows) instead of the decode kernels (once per 4-row tile) from
+    # TENSOR_MIN_ROWS rows and TENSOR_MIN_PER_EXPERT rows per local expert: the ranks
+    # holding the hot experts of a Zipf-skewed routing get hundreds of rows each
+    TENSOR_MIN_ROWS = 256
+    TENSOR_MIN_PER_EXPERT = 8
+
     def experts(self, layer, x, eid, wt):
         """y[r] = sum_j wt[r,j] * E_eid[r,j](x[r]) for this rank's experts."""
         import torch
         from .lib import WispErrCtx, check, lib
         y = torch.empty_like(x)
         if x.shape[0] == 0:
+            return y
+        R, K = x.shape[0], eid.shape[1]
+        if (R >= self.TENSOR_MIN_ROWS and layer.n_experts > 1
+                and R >= self.TENSOR_MIN_PER_EXPERT * layer.n_experts):
+            need = int(lib().wisp_moe_prefill_routed_workspace_bytes(C.byref(layer), R, K)) + 1024
+            if getattr(self, "_pws", None) is None or self._pws.numel() < need:
+                self._pws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            off = (-self._pws.data_ptr()) % 1024
+            err = WispErrCtx()
+            check(lib().wisp_moe_prefill_routed(C.byref(layer), x.data_ptr(), y.data_ptr(), R, K,
+                                                eid.data_ptr(), wt.data_ptr(),
+                                                self._pws.data_ptr() + off,
+                                                self._pws.numel() - off,
+                                                torch.cuda.current_stream().cuda_stream,
+                                                C.byref(err)), err)
             return y
         ws = self._workspace(layer, x.shape[0])
         err = WispErrCtx()
