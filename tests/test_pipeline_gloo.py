@@ -75,3 +75,51 @@ def test_layer_split_covers_the_stack_contiguously():
             assert a + n == b
         assert sum(n for _, n in parts) == L
         assert max(n for _, n in parts) - min(n for _, n in parts) <= 1
+
+
+def _two_rings_main(rank, world, port, out):
+    """Two rings on the same process groups, one after the other, with the protocol
+    of the config-3 bench: ring_prime then ring_finish each."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from wisp_b200.pipeline import LayerPipeline, ring_finish, ring_prime
+    groups = [dist.new_group(list(range(world))), dist.new_group(list(range(world)))]
+    res = []
+    for M, warm, steps in ((3, 2, 3), (2, 3, 2)):
+        bufs = [torch.full((2, 2), float(m)) for m in range(M)]
+
+        def run(m, bufs=bufs):
+            bufs[m].add_(1.0)
+
+        pipe = LayerPipeline(run, bufs, rank, world, groups)
+        ring_prime(pipe, warm)
+        ring_finish(pipe, steps)
+        pipe.close()
+        res.append([b[0, 0].item() for b in bufs])
+    if rank == world - 1:
+        out.put(res)
+    dist.barrier()
+    for g in groups:
+        dist.destroy_process_group(g)
+    dist.destroy_process_group()
+
+
+def test_two_rings_back_to_back_leave_no_unmatched_send():
+    """A ring left with sends in flight would block the next one (both ranks wait
+    forever); the prime/finish protocol empties each ring before the next starts."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_rings_main, args=(r, world, port, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # every micro-batch went through (warm + steps) passes of both ranks
+    assert got == [[float(m) + (2 + 3) * world for m in range(3)],
+                   [float(m) + (3 + 2) * world for m in range(2)]]

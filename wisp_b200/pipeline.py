@@ -223,6 +223,20 @@ def bench_main(args) -> None:
         }), flush=True)
 
 
+def ring_prime(pipe, warm: int) -> None:
+    """`warm` steps from an empty ring (rank 0 receives nothing on the first)."""
+    for s in range(warm):
+        pipe.step(first=s == 0, last=False)
+
+
+def ring_finish(pipe, steps: int) -> None:
+    """`steps` more steps of a primed ring; the last one sends nothing back, so every
+    send has been matched when this returns and another ring may start."""
+    for s in range(steps):
+        pipe.step(first=False, last=s == steps - 1)
+    pipe.drain()
+
+
 def layer_split(L: int, world: int) -> list[tuple[int, int]]:
     """Contiguous (first layer, count) per rank; the first L % world ranks get one more."""
     base, extra = divmod(L, world)
@@ -275,7 +289,7 @@ def bench_prefill_main(args) -> None:
     torch.cuda.set_device(dev)
     if rank == 0:
         build.build()
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     dist.barrier()
     build.build()
 
@@ -301,29 +315,26 @@ def bench_prefill_main(args) -> None:
     ppipe = LayerPipeline(lambda m: pgraphs[m].replay(), pbufs, rank, world, groups)
     dpipe = LayerPipeline.for_stack(stack, din, rank, world, groups)
 
-    def timed(pipe, steps):
+    def phase(pipe, warm, steps):
+        """Prime the ring, then time `steps` steady-state steps.  Every send is matched:
+        after the first step rank 0 receives what the last rank sent back, and the last
+        timed step sends nothing back (last=True), so the ring is empty afterwards."""
+        ring_prime(pipe, warm)
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for s in range(steps):
-            pipe.step(first=False, last=False)
-        pipe.drain()
+        ring_finish(pipe, steps)
         e1.record()
         torch.cuda.synchronize()
         ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return ms.item() / steps
 
-    # prime both rings, then time steady state
-    for pipe, w in ((ppipe, 2), (dpipe, max(3, args.warmup))):
-        for s in range(w):
-            pipe.step(first=s == 0, last=False)
-        pipe.drain()
     with ClockSampler(local) as clk:
-        p_ms = timed(ppipe, args.c3_prefill_steps)
-        d_ms = timed(dpipe, args.c3_decode_steps)
+        p_ms = phase(ppipe, 2, args.c3_prefill_steps)
+        d_ms = phase(dpipe, max(3, args.warmup), args.c3_decode_steps)
     status = stack.prefill_status() | stack.status()
     st_t = torch.tensor([status], device=dev)
     dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
