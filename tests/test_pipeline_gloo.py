@@ -78,23 +78,23 @@ def test_layer_split_covers_the_stack_contiguously():
 
 
 def _two_rings_main(rank, world, port, out):
-    """Two rings on the same process groups, one after the other, with the protocol
-    of the config-3 bench: ring_prime then ring_finish each."""
+    """Two rings on the same process groups, one after the other, each a complete
+    ring_run (as the config-3 bench drives them)."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    from wisp_b200.pipeline import LayerPipeline, ring_finish, ring_prime
+    from wisp_b200.pipeline import LayerPipeline, ring_run
     groups = [dist.new_group(list(range(world))), dist.new_group(list(range(world)))]
     res = []
-    for M, warm, steps in ((3, 2, 3), (2, 3, 2)):
+    for M, steps in ((3, 2), (2, 3), (3, 1)):
         bufs = [torch.full((2, 2), float(m)) for m in range(M)]
 
         def run(m, bufs=bufs):
             bufs[m].add_(1.0)
 
         pipe = LayerPipeline(run, bufs, rank, world, groups)
-        ring_prime(pipe, warm)
-        ring_finish(pipe, steps)
+        ring_run(pipe, steps)
+        dist.barrier()  # nothing may be in flight here
         pipe.close()
         res.append([b[0, 0].item() for b in bufs])
     if rank == world - 1:
@@ -105,9 +105,9 @@ def _two_rings_main(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_two_rings_back_to_back_leave_no_unmatched_send():
-    """A ring left with sends in flight would block the next one (both ranks wait
-    forever); the prime/finish protocol empties each ring before the next starts."""
+def test_complete_rings_back_to_back():
+    """Each ring_run leaves no send in flight: the next ring receives only its own
+    micro-batches, and every micro-batch went through steps x world passes."""
     world = 2
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
@@ -120,6 +120,5 @@ def test_two_rings_back_to_back_leave_no_unmatched_send():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    # every micro-batch went through (warm + steps) passes of both ranks
-    assert got == [[float(m) + (2 + 3) * world for m in range(3)],
-                   [float(m) + (3 + 2) * world for m in range(2)]]
+    assert got == [[float(m) + steps * world for m in range(M)]
+                   for M, steps in ((3, 2), (2, 3), (3, 1))]

@@ -223,17 +223,14 @@ def bench_main(args) -> None:
         }), flush=True)
 
 
-def ring_prime(pipe, warm: int) -> None:
-    """`warm` steps from an empty ring (rank 0 receives nothing on the first)."""
-    for s in range(warm):
-        pipe.step(first=s == 0, last=False)
-
-
-def ring_finish(pipe, steps: int) -> None:
-    """`steps` more steps of a primed ring; the last one sends nothing back, so every
-    send has been matched when this returns and another ring may start."""
+def ring_run(pipe, steps: int) -> None:
+    """A complete ring of `steps` steps: empty before (rank 0 receives nothing on the
+    first step) and empty after (the last step sends nothing back), so no send is in
+    flight when it returns.  A device-wide synchronisation with a send in flight would
+    wait for a receive the peer has not posted yet (NCCL completes a send larger than
+    its staging buffer only when the receiver arrives): synchronise between rings."""
     for s in range(steps):
-        pipe.step(first=False, last=s == steps - 1)
+        pipe.step(first=s == 0, last=s == steps - 1)
     pipe.drain()
 
 
@@ -315,26 +312,30 @@ def bench_prefill_main(args) -> None:
     ppipe = LayerPipeline(lambda m: pgraphs[m].replay(), pbufs, rank, world, groups)
     dpipe = LayerPipeline.for_stack(stack, din, rank, world, groups)
 
-    def phase(pipe, warm, steps):
-        """Prime the ring, then time `steps` steady-state steps.  Every send is matched:
-        after the first step rank 0 receives what the last rank sent back, and the last
-        timed step sends nothing back (last=True), so the ring is empty afterwards."""
-        ring_prime(pipe, warm)
+    def timed_ring(pipe, steps):
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        ring_finish(pipe, steps)
+        ring_run(pipe, steps)
         e1.record()
         torch.cuda.synchronize()
         ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return ms.item() / steps
+        return ms.item()
+
+    def phase(pipe, warm, s1, s2):
+        """Steady-state time per step: two complete rings of s1 and s2 steps; the
+        difference cancels the fill and drain of the pipeline."""
+        ring_run(pipe, warm)
+        t1 = timed_ring(pipe, s1)
+        t2 = timed_ring(pipe, s2)
+        return (t2 - t1) / (s2 - s1)
 
     with ClockSampler(local) as clk:
-        p_ms = phase(ppipe, 2, args.c3_prefill_steps)
-        d_ms = phase(dpipe, max(3, args.warmup), args.c3_decode_steps)
+        p_ms = phase(ppipe, 2, 2, 2 + args.c3_prefill_steps)
+        d_ms = phase(dpipe, max(3, args.warmup), 4, 4 + args.c3_decode_steps)
     status = stack.prefill_status() | stack.status()
     st_t = torch.tensor([status], device=dev)
     dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
