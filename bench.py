@@ -60,8 +60,8 @@ def parse():
                    help="routed experts per config-3 layer (fewer: a small case for ncu)")
     p.add_argument("--c3-total-layers", type=int, default=58,
                    help="layers of the config-3 stack split over the ranks")
-    p.add_argument("--prefill-micro", type=int, default=512,
-                   help="config-3 prefill micro-batch (tokens)")
+    p.add_argument("--prefill-micro", type=int, default=4096,
+                   help="config-3 prefill micro-batch (tokens) of the multi-GPU ring")
     p.add_argument("--c3-prefill-steps", type=int, default=3)
     p.add_argument("--c3-decode-steps", type=int, default=32)
     p.add_argument("--stream-layers", type=int, default=16,
