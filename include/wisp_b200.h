@@ -224,6 +224,25 @@ WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
                               const float* weights, int T, int K, int H,
                               cudaStream_t stream, WispErrCtx* err);
 
+/* Multi-GPU helpers of the reference (csrc/cuda/multi_gpu.cu:37-160, declared in
+ * csrc/core/wisp_engine.h:656-665), same signatures and codes (0 ok, -1 failure):
+ * a single-process NCCL pipeline -- init builds one communicator per GPU of
+ * gpu_indices (stage i = gpu_indices[i]); send/recv move n fp32 values between
+ * the current device's stage and peer_stage on stream s (issue a matching
+ * send and receive from different host threads) -- and 2-GPU peer access /
+ * peer copies.  NCCL is loaded at first use; without it wisp_nccl_available()
+ * is 0 and the pipeline calls return -1. */
+int  wisp_nccl_available(void);
+int  wisp_pipeline_init(const int* gpu_indices, int n);
+void wisp_pipeline_shutdown(void);
+int  wisp_pipeline_send_activation(const float* x, int n, int peer_stage,
+                                   cudaStream_t s);
+int  wisp_pipeline_recv_activation(float* x, int n, int peer_stage,
+                                   cudaStream_t s);
+int  wisp_peer_enable(int dev_a, int dev_b);
+int  wisp_peer_copy_async(void* dst, int dst_dev, const void* src,
+                          int src_dev, size_t n, cudaStream_t s);
+
 /* New: the block for batched / prefill tokens on the tensor cores (tcgen05).
  * Same contract as wisp_moe_block_forward -- x [T,H] fp32 MoE input (already
  * normalised), y [T,H] fp32 output (overwritten), optional device

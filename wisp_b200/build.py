@@ -24,7 +24,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall,-Wno-unused-function",
           f"-I{ROOT / 'include'}", f"-I{CSRC}"]
-SOURCES = ["moe_kernels.cu", "prefill.cu", "expert_layout.cu", "ref_launchers.cu", "engine.cpp", "tiers.cpp", "stream_cache.cpp"]
+SOURCES = ["moe_kernels.cu", "prefill.cu", "expert_layout.cu", "ref_launchers.cu", "engine.cpp", "tiers.cpp", "stream_cache.cpp",
+           "multi_gpu.cpp"]
 HEADERS = ["internal.h", "tiers.h", "route_common.cuh"]
 
 
@@ -53,7 +54,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
             if ptxas_info or verbose:
                 print(r.stderr, file=sys.stderr)
     if _stale(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -123,6 +123,14 @@ _SIGS = {
                                         C.c_int, C.c_void_p]),
     "async_load_expert": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_nccl_available": (C.c_int, []),
+    "wisp_pipeline_init": (C.c_int, [C.c_void_p, C.c_int]),
+    "wisp_pipeline_shutdown": (None, []),
+    "wisp_pipeline_send_activation": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_pipeline_recv_activation": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_peer_enable": (C.c_int, [C.c_int, C.c_int]),
+    "wisp_peer_copy_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_size_t,
+                                       C.c_void_p]),
     # engine
     "wisp_expert_parse_header": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(WispExpertMeta),
                                            C.POINTER(WispErrCtx)]),
