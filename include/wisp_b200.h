@@ -224,6 +224,17 @@ WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
                               const float* weights, int T, int K, int H,
                               cudaStream_t stream, WispErrCtx* err);
 
+/* New: the converter's int4 quantiser on the GPU (wisp/converter/quantizer.py
+ * :46-86, bit-identical on fp32 input): w [rows, cols] fp32 device, row-major;
+ * per group of group_size consecutive elements zero = (max+min)/2, scale =
+ * max((max-min)/15, 1e-8), codes clamp(round_half_even((x-zero)/scale)+8, 0,
+ * 15) packed low nibble first into packed [rows*cols/2]; scales, zeros fp16
+ * [rows*cols/group_size].  rows*cols must be a multiple of an even group size.
+ * Launch-only. */
+WispError wisp_quantize_int4(const float* w, int rows, int cols, int group_size,
+                             uint8_t* packed, void* scales, void* zeros,
+                             cudaStream_t stream, WispErrCtx* err);
+
 /* Multi-GPU helpers of the reference (csrc/cuda/multi_gpu.cu:37-160, declared in
  * csrc/core/wisp_engine.h:656-665), same signatures and codes (0 ok, -1 failure):
  * a single-process NCCL pipeline -- init builds one communicator per GPU of

@@ -123,6 +123,8 @@ _SIGS = {
                                         C.c_int, C.c_void_p]),
     "async_load_expert": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_quantize_int4": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_nccl_available": (C.c_int, []),
     "wisp_pipeline_init": (C.c_int, [C.c_void_p, C.c_int]),
     "wisp_pipeline_shutdown": (None, []),
