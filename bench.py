@@ -318,7 +318,12 @@ def run_single(args, dev) -> dict:
         del g0
 
     if not args.skip_extra and args.config3_layers > 0:
-        out["config3"] = run_config3(args, dev, args.config3_layers)
+        # an extra leg: its failure is recorded, not fatal to the headline line
+        try:
+            out["config3"] = run_config3(args, dev, args.config3_layers)
+        except Exception as e:  # noqa: BLE001
+            out["config3"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
 
     # CPU baseline + parity on the same bytes: layer 0, token 0
     if not args.skip_cpu:
