@@ -52,6 +52,13 @@ def test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T):
         check_outputs(y.cpu().numpy(), yr)
 
 
+@pytest.mark.parametrize("H,I,E,k,shared,bias,T", [CONFIGS[0], CONFIGS[2], CONFIGS[3]])
+def test_prefill_pairs_match_oracle(cuda, monkeypatch, H, I, E, k, shared, bias, T):
+    """The opt-in gate/up GEMM on SM pairs (cta_group::2, 256-token tiles)."""
+    monkeypatch.setenv("WISP_B200_PREFILL_2SM", "1")
+    test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T)
+
+
 def test_prefill_matches_decode_path(cuda):
     """The tensor-core path and the decode stream kernels agree on the same batch."""
     st = _stack(cuda, 512, 512, 16, 4, True, "zipf", seed=77)
