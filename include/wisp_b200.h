@@ -165,7 +165,20 @@ typedef struct {
     WispExpertMeta shared_meta;        /* host copy; used when shared_blob */
     int n_experts;
     int top_k;
+    int gating;                        /* WISP_GATING_* (0 = the reference's) */
 } WispMoeLayer;
+
+/* Gating rules of WispMoeLayer.gating.
+ *  SOFTMAX: the reference's (router.cu:60-120, wisp_engine.c:520-556):
+ *           p = softmax(logits + bias), k strict-argmax passes (lowest index
+ *           wins ties), w_j = p_j / sum of the selected p.
+ *  SIGMOID: DeepSeek-V3-style scores, s = sigmoid(logits); the experts are
+ *           chosen on s + bias (the bias steers selection only), k strict-argmax
+ *           passes as above, w_j = s_j / sum of the selected s.  No reference
+ *           implementation exists: parity unpinned, tested against its own
+ *           restatement. */
+#define WISP_GATING_SOFTMAX 0
+#define WISP_GATING_SIGMOID 1
 
 /* Bytes of device workspace wisp_moe_block_forward / wisp_moe_stack_forward
  * need for T tokens (max over the layers passed). */
@@ -407,6 +420,12 @@ void wisp_expert_prefetch_hint(WispEngine* eng, int layer_idx,
 WispError wisp_moe_forward(WispEngine* eng, int layer, const float* x,
                            float* y, int T, cudaStream_t stream,
                            WispErrCtx* err);
+/* New: the decode form of wisp_moe_forward: one token, y[H] = MoE_l(x[H]).
+ * With the layer's experts VRAM-resident it enqueues the fused block with no
+ * host synchronisation (graph-capturable); otherwise it takes the miss path of
+ * wisp_moe_forward. */
+WispError wisp_moe_decode(WispEngine* eng, int layer, const float* x, float* y,
+                          cudaStream_t stream, WispErrCtx* err);
 /* New: x <- x + MoE_l(rmsnorm(x)) for layers [layer0, layer0+n). */
 WispError wisp_moe_stack(WispEngine* eng, int layer0, int n_layers, float* x,
                          int T, cudaStream_t stream, WispErrCtx* err);

@@ -38,6 +38,26 @@ def test_engine_block_matches_reference_golden(cuda, golden, golden_dirs, name):
         core.engine_destroy(h)
 
 
+def test_engine_decode_is_forward_of_one_token(cuda, golden, golden_dirs):
+    """wisp_moe_decode == wisp_moe_forward at T = 1 (resident and miss path)."""
+    _, arr = golden
+    x = torch.from_numpy(arr["mx_small.x"][:1].copy()).to(cuda)
+    for pin in (True, False):
+        h = core.engine_create(str(golden_dirs["mx_small"]), 4 * GB if pin else 0, 4 * GB, [0], 1)
+        try:
+            if pin:
+                core.pin_experts(h, 0, 1)
+            y1 = torch.empty_like(x)
+            y2 = torch.empty_like(x)
+            torch.cuda.synchronize()
+            core.moe_forward(h, 0, x.data_ptr(), y1.data_ptr(), 1)
+            core.moe_decode(h, 0, x.data_ptr(), y2.data_ptr())
+            torch.cuda.synchronize()
+            assert torch.equal(y1, y2)
+        finally:
+            core.engine_destroy(h)
+
+
 def test_engine_stack_matches_reference_golden(cuda, golden, golden_dirs):
     _, arr = golden
     h = core.engine_create(str(golden_dirs["mx_small"]), 4 * GB, 4 * GB, [0], 1)

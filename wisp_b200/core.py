@@ -142,6 +142,15 @@ def moe_forward(handle: int, layer: int, x_ptr: int, y_ptr: int, n_tokens: int,
         _raise(err, rc)
 
 
+def moe_decode(handle: int, layer: int, x_ptr: int, y_ptr: int, stream: int = 0) -> None:
+    """y[H] = MoE_layer(x[H]) for one token (``wisp_moe_decode``); device pointers."""
+    err = WispErrCtx()
+    rc = lib().wisp_moe_decode(_engine(handle), layer, x_ptr, y_ptr, stream or None,
+                               C.byref(err))
+    if rc != 0:
+        _raise(err, rc)
+
+
 def moe_stack(handle: int, layer0: int, n_layers: int, x_ptr: int, n_tokens: int,
               stream: int = 0) -> None:
     """x <- x + MoE_l(rmsnorm(x)) for layers [layer0, layer0 + n_layers), in place."""

@@ -913,6 +913,11 @@ extern "C" WispError wisp_moe_forward(WispEngine* e, int layer, const float* x, 
     return moe_forward_impl(e, layer, x, y, T, s, err);
 }
 
+extern "C" WispError wisp_moe_decode(WispEngine* e, int layer, const float* x, float* y,
+                                     cudaStream_t stream, WispErrCtx* err) {
+    return wisp_moe_forward(e, layer, x, y, 1, stream, err);
+}
+
 extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, int T,
                                     cudaStream_t stream, WispErrCtx* err) {
     if (!e || layer0 < 0 || n <= 0 || layer0 + n > e->n_layers || !x || T <= 0) {

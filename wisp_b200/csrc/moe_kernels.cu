@@ -93,6 +93,7 @@ struct LayerArgs {
     int kp;   // K parts of the down projection
     int act_slots;  // token slots of the staged activation tile (min(T, mt))
     int mt;         // tokens per expert tile of the plan (1, 4 or 8)
+    int gating;     // WISP_GATING_* of the layer
 };
 
 struct Ws {
@@ -216,7 +217,7 @@ constexpr int kSlice = 1024;
 __device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, const float* lg,
                            float* sp, int* staken) {
     wisp_route::warp_topk(lg, L.router_bias, L.E, K, sp, staken, W.topk_idx + t * K,
-                          W.topk_w + t * K);
+                          W.topk_w + t * K, L.gating);
 }
 
 // The tiled blob of expert e (E = the shared expert), or NULL with the status
@@ -1509,6 +1510,10 @@ bool check_layer(const WispMoeLayer* ly, int T, WispErrCtx* err) {
                    H, I, gs);
         return false;
     }
+    if (ly->gating != WISP_GATING_SOFTMAX && ly->gating != WISP_GATING_SIGMOID) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe layer: unknown gating %d", ly->gating);
+        return false;
+    }
     if (ly->n_experts <= 0 || ly->n_experts > 1024 || ly->top_k <= 0 ||
         ly->top_k > ly->n_experts || ly->top_k > 64) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe layer: n_experts=%d top_k=%d",
@@ -1607,6 +1612,7 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.K = ly->top_k;
     a.gs = (int)ly->meta.group_size;
     a.has_shared = ly->shared_blob != nullptr;
+    a.gating = ly->gating;
     // Tokens per expert tile: 4 (one MMA column quad).  8-token tiles (two quads,
     // WISP_B200_TILE_TOKENS=8) stream fewer duplicate tiles at larger batches but
     // measured slower on Mixtral shapes at 16 tokens (the consumers become

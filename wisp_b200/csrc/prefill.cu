@@ -14,7 +14,7 @@
 //
 // One block, all on one stream, no host synchronisation:
 //   router_logits_kernel  logits [T, E] in fp32 on the CUDA cores
-//   route_topk_kernel     softmax(+bias) top-k, one warp per token
+//   route_topk_kernel     top-k under the layer's gating rule, one warp per token
 //   prefill_plan_kernel   one CTA: the (token, slot) assignments grouped by
 //                         expert into rows, the tile lists, and the per-expert
 //                         TMA descriptors (a host-encoded template whose global
@@ -97,6 +97,7 @@ struct PArgs {
     unsigned long long mat_off[3];  // packed_off of gate, up, down in a blob
     int H, I, E, K, has_shared;
     int nt_gu;  // tokens per gate/up tile: 256 (2-SM kernel) or 128
+    int gating; // WISP_GATING_* of the layer
 };
 
 struct PWs {
@@ -589,10 +590,11 @@ router_tc_kernel(const __grid_constant__ RouterMaps rm, float* __restrict__ lg, 
     }
 }
 
-// softmax(+bias) top-k per token, one warp per token.
+// top-k per token under the layer's gating rule (softmax(+bias) or sigmoid
+// scores), one warp per token.
 __global__ void __launch_bounds__(256)
 route_topk_kernel(const float* __restrict__ lg, const __half* bias, int T, int E, int K,
-                  int* idx, float* w) {
+                  int* idx, float* w, int gating) {
     pdl_wait();
     pdl_launch();
     extern __shared__ float rs[];
@@ -601,7 +603,7 @@ route_topk_kernel(const float* __restrict__ lg, const __half* bias, int T, int E
     int* staken = reinterpret_cast<int*>(sp + E);
     for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
         wisp_route::warp_topk(lg + (size_t)t * E, bias, E, K, sp, staken, idx + (size_t)t * K,
-                              w + (size_t)t * K);
+                              w + (size_t)t * K, gating);
         __syncwarp();
     }
 }
@@ -1610,6 +1612,10 @@ WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err, boo
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: missing layer pointers or T <= 0");
         return WISP_ERR_INVALID_ARG;
     }
+    if (l->gating != WISP_GATING_SOFTMAX && l->gating != WISP_GATING_SIGMOID) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: unknown gating %d", l->gating);
+        return WISP_ERR_INVALID_ARG;
+    }
     if (!m.tiled || m.group_size != 64 || H % kBM || I % kBM || m.rows[1] != (uint32_t)I ||
         m.cols[1] != (uint32_t)H || m.rows[2] != (uint32_t)H || m.cols[2] != (uint32_t)I) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
@@ -1665,6 +1671,7 @@ PArgs make_pargs(const WispMoeLayer* l) {
     P.E = l->n_experts;
     P.K = l->top_k;
     P.has_shared = l->shared_blob ? 1 : 0;
+    P.gating = l->gating;
     return P;
 }
 
@@ -1823,7 +1830,7 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
         WB_CUDA_RET(wb::launch_pdl(route_topk_kernel, dim3(std::min((T + 7) / 8, 4 * sms)),
                                    dim3(256), (size_t)8 * 2 * P.E * 4, stream,
                                    (const float*)W.logits, P.router_bias, T, P.E, P.K, W.idx,
-                                   W.w),
+                                   W.w, P.gating),
                     err);
     WB_CUDA_RET(wb::launch_pdl(prefill_plan_kernel, dim3(1), dim3(kPlanThreads),
                                (size_t)5 * (P.E + 2) * 4, stream, P, W, T, wt),

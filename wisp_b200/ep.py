@@ -76,7 +76,7 @@ class EPLayer:
     """One expert-sharded MoE layer on this rank's GPU (see the module doc)."""
 
     def __init__(self, shape, seed: int, rank: int, world: int, device, zipf_s=None,
-                 random_bias: bool = False, group=None):
+                 random_bias: bool = False, group=None, gating: int = 0):
         import torch
         from .lib import WispMoeLayer
         from .moe import MoEStack
@@ -87,7 +87,7 @@ class EPLayer:
         self.per = shape.n_experts // world
         ids = range(rank * self.per, (rank + 1) * self.per)
         self.local = MoEStack(shape, seed, device, zipf_s=zipf_s, random_bias=random_bias,
-                              n_layers=1, expert_ids=ids, with_shared=True)
+                              n_layers=1, expert_ids=ids, with_shared=True, gating=gating)
         lw = self.local.layers[0]
         H = shape.hidden
         # routing: the full router, no expert table

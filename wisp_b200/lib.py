@@ -34,7 +34,8 @@ class WispExpertMeta(C.Structure):
 class WispMoeLayer(C.Structure):
     _fields_ = [("meta", WispExpertMeta), ("expert_blobs", C.c_void_p), ("router_w", C.c_void_p),
                 ("router_bias", C.c_void_p), ("norm_w", C.c_void_p), ("shared_blob", C.c_void_p),
-                ("shared_meta", WispExpertMeta), ("n_experts", C.c_int), ("top_k", C.c_int)]
+                ("shared_meta", WispExpertMeta), ("n_experts", C.c_int), ("top_k", C.c_int),
+                ("gating", C.c_int)]
 
 
 class WispError(RuntimeError):
@@ -142,6 +143,8 @@ _SIGS = {
     "wisp_expert_fetch": (C.c_void_p, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(WispErrCtx)]),
     "wisp_expert_prefetch_hint": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
     "wisp_moe_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_void_p, C.POINTER(WispErrCtx)]),
+    "wisp_moe_decode": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_moe_stack": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                  C.POINTER(WispErrCtx)]),

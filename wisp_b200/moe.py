@@ -102,10 +102,11 @@ class MoEStack:
 
     def __init__(self, shape: cv.MoEShape, seed: int, device="cuda", zipf_s: float | None = None,
                  random_bias: bool = False, n_layers: int | None = None, layer0: int = 0,
-                 expert_ids=None, with_shared: bool = True):
+                 expert_ids=None, with_shared: bool = True, gating: int = 0):
         """`expert_ids`: the experts this stack holds (default all; the expert-parallel
         path holds a slice, table entry i = expert expert_ids[i]); `with_shared`: build
-        the shape's shared expert (if any)."""
+        the shape's shared expert (if any); `gating`: 0 the reference's softmax(+bias),
+        1 sigmoid scores (``WISP_GATING_SIGMOID``)."""
         self.shape = shape
         self.device = torch.device(device)
         self.L = n_layers or shape.n_layers
@@ -162,6 +163,7 @@ class MoEStack:
                 c.shared_meta = self.meta
             c.n_experts = E
             c.top_k = shape.top_k
+            c.gating = gating
         self._ws: torch.Tensor | None = None
 
     # ------------------------------------------------------------------
