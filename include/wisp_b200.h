@@ -408,6 +408,14 @@ void wisp_engine_destroy(WispEngine* eng);
  * (WISP_ERR_IO = file missing/short; callers skip the expert). */
 void* wisp_expert_fetch(WispEngine* eng, uint32_t layer_id,
                         uint32_t expert_id, WispErrCtx* err);
+/* New: read a whole expert file into `dst` (capacity `cap`) the way the SSD
+ * tier's miss path does (replaces the fopen/fread of wisp_engine.c:351-380):
+ * O_DIRECT preads straight into `dst` when it is 4096-byte aligned and `cap`
+ * holds the size rounded up to 4096 (a pinned staging buffer), else buffered
+ * sequential preads.  Returns the file size, 0 on error (WISP_ERR_IO in `err`);
+ * *direct (if non-NULL) = 1 when O_DIRECT was used. */
+size_t wisp_read_expert_file(const char* path, void* dst, size_t cap, int* direct,
+                             WispErrCtx* err);
 /* Replaces wisp_expert_prefetch_hint (wisp_engine.c:1162-1177). */
 void wisp_expert_prefetch_hint(WispEngine* eng, int layer_idx,
                                const int* expert_ids, int n);

@@ -16,10 +16,14 @@
 // kernels read; when every expert of a layer is VRAM-resident the whole MoE
 // block runs with no host synchronisation.
 
+#include <errno.h>
+#include <fcntl.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/stat.h>
 #include <time.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <chrono>
@@ -220,28 +224,72 @@ std::string expert_path(const WispEngine* e, uint32_t layer, uint32_t expert) {
 }
 
 // Read an expert file into `dst` (capacity cap). Returns bytes, 0 on error.
+// The SSD tier's miss path (the reference opens the file and freads it per miss,
+// wisp_engine.c:351-380): the file is opened with O_DIRECT and read with large
+// preads straight into the destination, bypassing the page cache, when the
+// destination and its capacity allow it (4096-byte aligned address, capacity >=
+// the size rounded up to 4096 -- the engine's pinned staging buffer does); a
+// filesystem that refuses O_DIRECT (tmpfs, some overlays) or an unaligned
+// destination gets plain sequential preads.  *direct reports which one ran.
+size_t read_file_into(const char* p, void* dst, size_t cap, int* direct, WispErrCtx* err) {
+    constexpr size_t kAlign = 4096, kChunk = (size_t)16 << 20;
+    if (direct) *direct = 0;
+    struct stat sb;
+    if (!p || !dst || stat(p, &sb) != 0) {
+        WB_SET_ERR(err, WISP_ERR_IO, "expert file missing: %s", p ? p : "(null)");
+        return 0;
+    }
+    const size_t n = (size_t)sb.st_size;
+    if (n == 0 || n > cap) {
+        WB_SET_ERR(err, WISP_ERR_IO, "expert file %s size %zu exceeds staging %zu", p, n, cap);
+        return 0;
+    }
+    const size_t padded = (n + kAlign - 1) / kAlign * kAlign;
+    const bool can_direct = (reinterpret_cast<uintptr_t>(dst) % kAlign) == 0 && padded <= cap;
+    int fd = -1;
+    bool use_direct = false;
+#ifdef O_DIRECT
+    if (can_direct) {
+        fd = open(p, O_RDONLY | O_DIRECT);
+        use_direct = fd >= 0;
+    }
+#endif
+    if (fd < 0) fd = open(p, O_RDONLY);
+    if (fd < 0) {
+        WB_SET_ERR(err, WISP_ERR_IO, "expert file missing: %s", p);
+        return 0;
+    }
+    if (!use_direct) posix_fadvise(fd, 0, 0, POSIX_FADV_SEQUENTIAL);
+    char* out = static_cast<char*>(dst);
+    size_t got = 0;
+    const size_t want = use_direct ? padded : n;
+    while (got < want) {
+        const size_t len = std::min(kChunk, want - got);
+        const ssize_t r = pread(fd, out + got, len, (off_t)got);
+        if (r < 0 && errno == EINTR) continue;
+        if (r < 0 && use_direct && got == 0 && errno == EINVAL) {
+            // O_DIRECT accepted at open but not for this read: buffered instead
+            close(fd);
+            fd = open(p, O_RDONLY);
+            use_direct = false;
+            if (fd < 0) break;
+            continue;
+        }
+        if (r <= 0) break;
+        got += (size_t)r;
+        if (use_direct && got >= n) break;  // the last block ends at end of file
+    }
+    if (fd >= 0) close(fd);
+    if (got < n) {
+        WB_SET_ERR(err, WISP_ERR_IO, "short read on %s: %zu of %zu", p, got, n);
+        return 0;
+    }
+    if (direct) *direct = use_direct ? 1 : 0;
+    return n;
+}
+
 size_t read_expert(const std::string& p, void* dst, size_t cap, WispErrCtx* err) {
-    FILE* f = fopen(p.c_str(), "rb");
-    if (!f) {
-        WB_SET_ERR(err, WISP_ERR_IO, "expert file missing: %s", p.c_str());
-        return 0;
-    }
-    fseek(f, 0, SEEK_END);
-    long n = ftell(f);
-    fseek(f, 0, SEEK_SET);
-    if (n <= 0 || (size_t)n > cap) {
-        fclose(f);
-        WB_SET_ERR(err, WISP_ERR_IO, "expert file %s size %ld exceeds staging %zu", p.c_str(),
-                   n, cap);
-        return 0;
-    }
-    size_t got = fread(dst, 1, (size_t)n, f);
-    fclose(f);
-    if (got != (size_t)n) {
-        WB_SET_ERR(err, WISP_ERR_IO, "short read on %s: %zu of %ld", p.c_str(), got, n);
-        return 0;
-    }
-    return got;
+    return read_file_into(p.c_str(), dst, cap, nullptr, err);
 }
 
 bool sections_aligned(const WispExpertMeta& m) {
@@ -521,6 +569,11 @@ WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
 }
 
 }  // namespace
+
+extern "C" size_t wisp_read_expert_file(const char* path, void* dst, size_t cap, int* direct,
+                                        WispErrCtx* err) {
+    return read_file_into(path, dst, cap, direct, err);
+}
 
 // ====================================================================== ABI
 

@@ -141,6 +141,8 @@ _SIGS = {
                                         C.c_int, C.POINTER(WispErrCtx)]),
     "wisp_engine_destroy": (None, [C.c_void_p]),
     "wisp_expert_fetch": (C.c_void_p, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(WispErrCtx)]),
+    "wisp_read_expert_file": (C.c_size_t, [C.c_char_p, C.c_void_p, C.c_size_t,
+                                           C.POINTER(C.c_int), C.POINTER(WispErrCtx)]),
     "wisp_expert_prefetch_hint": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
     "wisp_moe_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                    C.c_void_p, C.POINTER(WispErrCtx)]),
