@@ -119,27 +119,36 @@ struct PWs {
     int R, max_gu, max_dn;
 };
 
-// A stage covers kKG quant groups (K = 128).  Ring depths in stages -- WS: weight
-// staging (smem); BS: activation tiles (smem, deep: their loads are the
-// longest-latency step); S: dequantised weight tiles in TMEM (NMAT * kKG * 32
+// A stage covers KG quant groups (K = 64 * KG).  Ring depths in stages -- WS:
+// weight staging (smem); BS: activation tiles (smem, deep: their loads are the
+// longest-latency step); S: dequantised weight tiles in TMEM (NMAT * KG * 32
 // columns each); NACC: accumulator buffers (TMEM, 128 columns per matrix).
-// TMEM: 256 accumulator columns + S * NMAT * kKG * 32 = 256 A columns.
+// TMEM: 256 accumulator columns + S * NMAT * KG * 32 = 256 A columns.  Every
+// stage carries a fixed cost (the issuing thread's polls, fence and commits, the
+// dequantisers' TMEM-store wait and arrivals), so stages are as large as TMEM
+// allows: gate/up 2 groups (two matrices), down 4 groups when its K has a
+// multiple of 4 groups (up to 2048 tokens), else 2.  kKG is the gate/up (and
+// SM-pair) stage size.
 constexpr int kKG = 2;
-template <int NMAT>
+template <int NMAT, int KG>
 struct GCfg;
 template <>
-struct GCfg<2> {  // gate + up
+struct GCfg<2, 2> {  // gate + up
     static constexpr int WS = 4, BS = 4, S = 2, NACC = 1;
 };
 template <>
-struct GCfg<1> {  // down
+struct GCfg<1, 2> {  // down, K of 2 (mod 4) groups
     static constexpr int WS = 8, BS = 4, S = 4, NACC = 2;
 };
+template <>
+struct GCfg<1, 4> {  // down
+    static constexpr int WS = 4, BS = 2, S = 2, NACC = 2;
+};
 
-template <int NMAT>
+template <int NMAT, int KG>
 constexpr size_t gemm_smem_bytes() {
-    using C = GCfg<NMAT>;
-    return 1024 + (size_t)C::BS * kKG * kBTile + (size_t)C::WS * NMAT * kKG * kWStage + 1024;
+    using C = GCfg<NMAT, KG>;
+    return 1024 + (size_t)C::BS * KG * kBTile + (size_t)C::WS * NMAT * KG * kWStage + 1024;
 }
 
 // ------------------------------------------------------------------------
@@ -836,16 +845,16 @@ __device__ __forceinline__ PTile tiles_at(const PTile* tiles, int t) {
 // ------------------------------------------------------------------------
 // the grouped GEMM
 // ------------------------------------------------------------------------
-template <int NMAT>
+template <int NMAT, int KG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __restrict__ y) {
-    using C = GCfg<NMAT>;
+    using C = GCfg<NMAT, KG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~(uintptr_t)1023);
     uint8_t* sB = base;
-    uint8_t* sW = sB + C::BS * kKG * kBTile;
-    uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * kKG * kWStage);
+    uint8_t* sW = sB + C::BS * KG * kBTile;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(sW + C::WS * NMAT * KG * kWStage);
     uint64_t* w_empty = w_full + C::WS;
     uint64_t* a_full = w_empty + C::WS;   // dequantised tile in TMEM
     uint64_t* a_empty = a_full + C::S;
@@ -893,7 +902,7 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
     pdl_launch();
     const int ntiles = __ldcg(W.counters + (NMAT == 2 ? 0 : 1));
     const PTile* tiles = NMAT == 2 ? W.tiles_gu : W.tiles_dn;
-    const int KS = (NMAT == 2 ? P.H : P.I) / (kBK * kKG);  // stages per tile
+    const int KS = (NMAT == 2 ? P.H : P.I) / (kBK * KG);  // stages per tile
     int* status = W.status;
 
     if (warp == kWProdWarp) {
@@ -917,13 +926,13 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&w_full[s], NMAT * kKG * kWStage);
+                    mbar_expect_tx(&w_full[s], NMAT * KG * kWStage);
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m) {
-                        // [16 blocks][kKG groups] of codes, then of scale/zero pairs
-                        uint8_t* dst = sW + (s * NMAT + m) * kKG * kWStage;
-                        tma3d(dst, maps[m][0], 0, ks * kKG, tl.mt * 16, &w_full[s]);
-                        tma3d(dst + kKG * kWCodes, maps[m][1], 0, ks * kKG, tl.mt * 16, &w_full[s]);
+                        // [16 blocks][KG groups] of codes, then of scale/zero pairs
+                        uint8_t* dst = sW + (s * NMAT + m) * KG * kWStage;
+                        tma3d(dst, maps[m][0], 0, ks * KG, tl.mt * 16, &w_full[s]);
+                        tma3d(dst + KG * kWCodes, maps[m][1], 0, ks * KG, tl.mt * 16, &w_full[s]);
                     }
                 }
             }
@@ -943,16 +952,16 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&b_full[s], (uint32_t)(kKG * nmma * 128));
+                    mbar_expect_tx(&b_full[s], (uint32_t)(KG * nmma * 128));
 #pragma unroll
-                    for (int g = 0; g < kKG; ++g) {
+                    for (int g = 0; g < KG; ++g) {
                         int off = 0;
 #pragma unroll
                         for (int i = kBoxes - 1; i >= 0; --i) {
                             const int h = 16 << i;
                             if ((nmma - off) >= h) {
-                                tma2d(sB + (s * kKG + g) * kBTile + off * 128, &bm.box[i],
-                                      (ks * kKG + g) * kBK, tl.row0 + off, &b_full[s]);
+                                tma2d(sB + (s * KG + g) * kBTile + off * 128, &bm.box[i],
+                                      (ks * KG + g) * kBK, tl.row0 + off, &b_full[s]);
                                 off += h;
                             }
                         }
@@ -983,16 +992,16 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bd = bdesc0 + (uint64_t)(sb * kKG * (kBTile >> 4));
-                    const uint32_t at = tmem + kAcol0 + (uint32_t)(s * NMAT * kKG * 32);
+                    const uint64_t bd = bdesc0 + (uint64_t)(sb * KG * (kBTile >> 4));
+                    const uint32_t at = tmem + kAcol0 + (uint32_t)(s * NMAT * KG * 32);
 #pragma unroll
-                    for (int g = 0; g < kKG; ++g)
+                    for (int g = 0; g < KG; ++g)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
 #pragma unroll
                             for (int m = 0; m < NMAT; ++m)
                                 mma_ts(d0 + (uint32_t)(m * kNT),
-                                       at + (uint32_t)((m * kKG + g) * 32 + k * 8),
+                                       at + (uint32_t)((m * KG + g) * 32 + k * 8),
                                        bd + (uint64_t)(g * (kBTile >> 4) + 2 * k), id,
                                        (ks | g | k) ? 1u : 0u);
                     mma_commit(&a_empty[s]);
@@ -1058,11 +1067,11 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
         constexpr int PW = NMAT == 2 ? 4 : 2;  // code words per thread and group
         const int part = NMAT == 2 ? (gw & 1) : gw;
         const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + kAcol0 +
-                                   (uint32_t)(mat * kKG * 32 + part * PW * 4);
-        // smem staging of one matrix: [16 blocks][kKG groups][8 rows][8 code words],
-        // then [16 blocks][kKG groups][8 rows] (scale, zero) words
-        const int cw0 = ((r >> 3) * kKG) * 64 + (r & 7) * 8 + part * PW;
-        const int sw0 = kKG * kWCodes / 4 + ((r >> 3) * kKG) * 8 + (r & 7);
+                                   (uint32_t)(mat * KG * 32 + part * PW * 4);
+        // smem staging of one matrix: [16 blocks][KG groups][8 rows][8 code words],
+        // then [16 blocks][KG groups][8 rows] (scale, zero) words
+        const int cw0 = ((r >> 3) * KG) * 64 + (r & 7) * 8 + part * PW;
+        const int sw0 = KG * kWCodes / 4 + ((r >> 3) * KG) * 8 + (r & 7);
         uint32_t wi = 0, ai = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
@@ -1075,14 +1084,14 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
                 }
                 tc_fence_after();
                 const uint32_t* st = reinterpret_cast<const uint32_t*>(
-                    sW + (ws * NMAT + mat) * kKG * kWStage);
+                    sW + (ws * NMAT + mat) * KG * kWStage);
 #pragma unroll
-                for (int g = 0; g < kKG; ++g) {
+                for (int g = 0; g < KG; ++g) {
                     const uint32_t szw = st[sw0 + g * 8];
                     const __half2 s2 =
                         __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFFu)));
                     const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
-                    const uint32_t ta = lane_addr + (uint32_t)((as * NMAT * kKG + g) * 32);
+                    const uint32_t ta = lane_addr + (uint32_t)((as * NMAT * KG + g) * 32);
                     if (PW == 4) {
                         const uint4 c4 = *reinterpret_cast<const uint4*>(st + cw0 + g * 64);
                         uint32_t o[16];
@@ -1689,14 +1698,17 @@ bool encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* addr, cons
 // (scale, zero) pairs [16 blocks][8 x 4 B] of one quant group, as 32-bit words
 // over (word, group, 8-row block).  `anchor`: any 16-byte aligned device address
 // (replaced per expert on the device).
-bool weight_templates(const PArgs& P, const WispExpertMeta& m, void* anchor, WTemplates* t) {
+// The boxes span one stage's groups: kKG for gate/up, `kg_down` for down.
+bool weight_templates(const PArgs& P, const WispExpertMeta& m, void* anchor, WTemplates* t,
+                      int kg_down) {
     for (int mat = 0; mat < 3; ++mat) {
         const cuuint64_t rows = m.rows[mat], cols = m.cols[mat];
         const cuuint64_t G = cols / 64, nblk = rows / 8, block_bytes = 4 * cols + 32 * G;
+        const cuuint32_t kg = (cuuint32_t)(mat == 2 ? kg_down : kKG);
         const cuuint64_t dc[3] = {64, G, nblk}, sc[2] = {256, block_bytes};
-        const cuuint32_t bc[3] = {64, (cuuint32_t)kKG, 16};
+        const cuuint32_t bc[3] = {64, kg, 16};
         const cuuint64_t ds[3] = {8, G, nblk}, ss[2] = {32, block_bytes};
-        const cuuint32_t bs[3] = {8, (cuuint32_t)kKG, 16};
+        const cuuint32_t bs[3] = {8, kg, 16};
         if (!encode(&t->m[mat * 2], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, dc, sc, bc,
                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
             !encode(&t->m[mat * 2 + 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, anchor, ds, ss, bs,
@@ -1722,13 +1734,17 @@ bool row_maps(__half* rows_base, int R, int cols, BMaps* b) {
 
 cudaError_t ensure_gemm_attrs() {
     static cudaError_t e = [] {
-        cudaError_t r = cudaFuncSetAttribute(grouped_gemm_kernel<2>,
+        cudaError_t r = cudaFuncSetAttribute(grouped_gemm_kernel<2, 2>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)gemm_smem_bytes<2>());
+                                             (int)gemm_smem_bytes<2, 2>());
         if (r == cudaSuccess)
-            r = cudaFuncSetAttribute(grouped_gemm_kernel<1>,
+            r = cudaFuncSetAttribute(grouped_gemm_kernel<1, 2>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)gemm_smem_bytes<1>());
+                                     (int)gemm_smem_bytes<1, 2>());
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(grouped_gemm_kernel<1, 4>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)gemm_smem_bytes<1, 4>());
         if (r == cudaSuccess)
             r = cudaFuncSetAttribute(prefill_plan_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 5 * 1026 * 4);
@@ -1782,7 +1798,14 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     if (topk_w) W.w = topk_w;
     WTemplates wt;
     BMaps bx, bh;
-    if (!weight_templates(P, layer->meta, W.xs, &wt) || !row_maps(W.xs, L.R, P.H, &bx) ||
+    // down stages of 4 groups when its K (= I) has a multiple of 4 groups, up to
+    // 2048 tokens (measured on the DeepSeek layer: -4.3% at 512 tokens, -3.3% at
+    // 1024, +0.5% at 4096, where the shallower activation ring shows);
+    // WISP_B200_PREFILL_DOWN_KG=2 keeps 2
+    int kg_down = (P.I / 64) % 4 == 0 && T <= 2048 ? 4 : 2;
+    if (const char* v = getenv("WISP_B200_PREFILL_DOWN_KG"))
+        if (atoi(v) == 2) kg_down = 2;
+    if (!weight_templates(P, layer->meta, W.xs, &wt, kg_down) || !row_maps(W.xs, L.R, P.H, &bx) ||
         !row_maps(W.hs, L.R, P.I, &bh)) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed or unavailable");
         return WISP_ERR_CUDA;
@@ -1843,12 +1866,17 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
                                            kGemm2Smem, stream, 2, P, W, bx),
                     err);
     else
-        WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<2>, dim3(sms), dim3(kGemmThreads),
-                                   gemm_smem_bytes<2>(), stream, P, W, bx, y),
+        WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<2, 2>, dim3(sms), dim3(kGemmThreads),
+                                   gemm_smem_bytes<2, 2>(), stream, P, W, bx, y),
                     err);
-    WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1>, dim3(sms), dim3(kGemmThreads),
-                               gemm_smem_bytes<1>(), stream, P, W, bh, y),
-                err);
+    if (kg_down == 4)
+        WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1, 4>, dim3(sms), dim3(kGemmThreads),
+                                   gemm_smem_bytes<1, 4>(), stream, P, W, bh, y),
+                    err);
+    else
+        WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1, 2>, dim3(sms), dim3(kGemmThreads),
+                                   gemm_smem_bytes<1, 2>(), stream, P, W, bh, y),
+                    err);
     return WISP_OK;
 }
 
