@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--prefill-micro", type=int, default=4096,
                    help="config-3 prefill micro-batch (tokens) of the multi-GPU ring")
     p.add_argument("--c3-prefill-steps", type=int, default=3)
+    p.add_argument("--c3-prefill-tokens", type=int, default=4096,
+                   help="prefill tokens of the one-GPU config-3 leg (config 3 is 4096; fewer: "
+                        "a profiling case for the smaller-batch kernel variants)")
     p.add_argument("--c3-decode-steps", type=int, default=32)
     p.add_argument("--stream-layers", type=int, default=16,
                    help="layers of the config-4 host pool (6.3 GB each)")
@@ -365,7 +368,7 @@ def run_config3(args, dev, k: int) -> dict:
     t0 = time.time()
     st = MoEStack(shape, SEED + 3, device=dev, zipf_s=1.1)
     setup_s = time.time() - t0
-    Tp, Bd, steps = 4096, 32, 128
+    Tp, Bd, steps = args.c3_prefill_tokens, 32, 128
     xp0 = cv.make_input(shape, Tp, SEED + 3).to(dev)
     xp = xp0.clone()
     for _ in range(2):
