@@ -59,6 +59,14 @@ def test_prefill_pairs_match_oracle(cuda, monkeypatch, H, I, E, k, shared, bias,
     test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T)
 
 
+@pytest.mark.parametrize("kg", ["2", "4"])
+def test_prefill_down_stage_sizes_match_oracle(cuda, monkeypatch, kg):
+    """The down GEMM with stages of 2 and of 4 quant groups (WISP_B200_PREFILL_DOWN_KG
+    forces the choice the rows-per-expert rule would make)."""
+    monkeypatch.setenv("WISP_B200_PREFILL_DOWN_KG", kg)
+    test_prefill_matches_oracle(cuda, *CONFIGS[3])
+
+
 def test_prefill_matches_decode_path(cuda):
     """The tensor-core path and the decode stream kernels agree on the same batch."""
     st = _stack(cuda, 512, 512, 16, 4, True, "zipf", seed=77)

@@ -127,8 +127,8 @@ struct PWs {
 // stage carries a fixed cost (the issuing thread's polls, fence and commits, the
 // dequantisers' TMEM-store wait and arrivals), so stages are as large as TMEM
 // allows: gate/up 2 groups (two matrices), down 4 groups when its K has a
-// multiple of 4 groups (up to 2048 tokens), else 2.  kKG is the gate/up (and
-// SM-pair) stage size.
+// multiple of 4 groups and the expert tiles are thin, else 2.  kKG is the
+// gate/up (and SM-pair) stage size.
 constexpr int kKG = 2;
 template <int NMAT, int KG>
 struct GCfg;
@@ -1798,13 +1798,20 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     if (topk_w) W.w = topk_w;
     WTemplates wt;
     BMaps bx, bh;
-    // down stages of 4 groups when its K (= I) has a multiple of 4 groups, up to
-    // 2048 tokens (measured on the DeepSeek layer: -4.3% at 512 tokens, -3.3% at
-    // 1024, +0.5% at 4096, where the shallower activation ring shows);
-    // WISP_B200_PREFILL_DOWN_KG=2 keeps 2
-    int kg_down = (P.I / 64) % 4 == 0 && T <= 2048 ? 4 : 2;
-    if (const char* v = getenv("WISP_B200_PREFILL_DOWN_KG"))
+    // down stages of 4 groups when its K (= I) has a multiple of 4 groups and the
+    // experts' tiles are thin (<= 96 rows per expert on average): measured on the
+    // DeepSeek layer, 4 groups take -4.3% at 18 rows per expert (512 tokens) and
+    // -3.3% at 36 (1024), +0.5% at 143 (4096), and +3.7% in a 32-expert layer at
+    // 280 rows (ncu), where the shallower activation ring shows.
+    // WISP_B200_PREFILL_DOWN_KG=2 / =4 chooses.
+    const int nexp = P.E + (P.has_shared ? 1 : 0);
+    const long long rows_per_expert = (long long)T * (P.K + (P.has_shared ? 1 : 0)) / nexp;
+    const bool kg4_ok = (P.I / 64) % 4 == 0;
+    int kg_down = kg4_ok && rows_per_expert <= 96 ? 4 : 2;
+    if (const char* v = getenv("WISP_B200_PREFILL_DOWN_KG")) {
         if (atoi(v) == 2) kg_down = 2;
+        if (atoi(v) == 4 && kg4_ok) kg_down = 4;
+    }
     if (!weight_templates(P, layer->meta, W.xs, &wt, kg_down) || !row_maps(W.xs, L.R, P.H, &bx) ||
         !row_maps(W.hs, L.R, P.I, &bh)) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed or unavailable");
