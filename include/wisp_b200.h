@@ -166,6 +166,16 @@ typedef struct {
     int n_experts;
     int top_k;
     int gating;                        /* WISP_GATING_* (0 = the reference's) */
+    /* The shared expert in the form the reference converter writes it:
+     * fp16-dense layers.{i}.shared.{gate,up,down} (gate/up [shared_inter, H],
+     * down [H, shared_inter], row-major, 16-byte aligned; shared_inter a
+     * multiple of 8), run always-on with weight 1 before the routed experts
+     * (csrc/core/wisp_engine.c:1443-1450).  NULL when absent; set at most one
+     * of shared_blob and shared_gate. */
+    const wisp_half* shared_gate;
+    const wisp_half* shared_up;
+    const wisp_half* shared_down;
+    int shared_inter;
 } WispMoeLayer;
 
 /* Gating rules of WispMoeLayer.gating.
@@ -236,6 +246,21 @@ WispError wisp_moe_route(const WispMoeLayer* layer, const float* x, int T,
 WispError wisp_moe_ep_combine(float* y, const float* rows, const int* row_idx,
                               const float* weights, int T, int K, int H,
                               cudaStream_t stream, WispErrCtx* err);
+
+/* Replaces run_dense_mlp (csrc/core/wisp_engine.c:1524-1534) and the dense
+ * shared-expert FFN of run_moe (:1443-1450, op_swiglu_ffn + op_gemv): for T
+ * tokens, y[t] = down . (silu(gate . x[t]) * (up . x[t])) with the fp16-dense
+ * weights the reference converter writes as layers.{i}.shared.{gate,up,down}
+ * (gate/up [inter, hidden], down [hidden, inter], row-major), fp32 math.
+ * x, y [T, hidden] fp32 device (16-byte aligned, not aliased); inter and
+ * hidden multiples of 8.  workspace: wisp_dense_ffn_workspace_bytes(inter, T)
+ * device bytes (the SwiGLU activations).  Launch-only. */
+size_t wisp_dense_ffn_workspace_bytes(int inter, int T);
+WispError wisp_dense_ffn_forward(const wisp_half* gate, const wisp_half* up,
+                                 const wisp_half* down, int inter, int hidden,
+                                 const float* x, float* y, int T, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t stream,
+                                 WispErrCtx* err);
 
 /* New: the converter's int4 quantiser on the GPU (wisp/converter/quantizer.py
  * :46-86, bit-identical on fp32 input): w [rows, cols] fp32 device, row-major;
@@ -358,6 +383,12 @@ WispError wisp_moe_block_forward_static(const WispMoeLayer* layer,
                                         const float* x, float* y, int T,
                                         int* topk_idx, float* topk_w,
                                         cudaStream_t stream, WispErrCtx* err);
+/* The device-side status word (bits as wisp_moe_status) that the last
+ * wisp_moe_block_forward_static call on the current device left in the fixed
+ * array: a caller of that entry has no workspace pointer to pass to
+ * wisp_moe_status.  Synchronises `stream` (the stream of that call); -1 when the
+ * read fails.  Allocates nothing. */
+int wisp_moe_block_static_status(cudaStream_t stream);
 
 /* Stack of n_layers blocks: per layer l, x <- x + MoE_l(rmsnorm(x; norm_w_l,
  * eps)).  x [T,H] is updated in place.  topk_idx/topk_w optional, device

@@ -16,11 +16,16 @@
  *   swiglu            -- g/(1+expf(-g)) * u (wisp_engine.c:428-433)
  *   gemv_f16          -- dense fp16 GEMV for the shared expert (:389-400)
  *   moe_block         -- run_moe's CPU branch: router, zero acc, shared expert
- *                        (w = 1), routed experts in top-k order
- *                        (wisp_engine.c:1411-1493, 1383-1409)
+ *                        (w = 1), routed experts in top-k order; an expert
+ *                        whose blob is absent (file unreadable: fetch gives
+ *                        WISP_ERR_IO) is skipped (wisp_engine.c:1411-1493,
+ *                        1473-1477, 1383-1409)
+ *   dense_ffn         -- run_dense_mlp: the fp16-dense SwiGLU FFN of a
+ *                        router-less layer (wisp_engine.c:1524-1534)
  *   rmsnorm           -- double sum of squares, float scale (:415-422)
- *   stack             -- x += moe(rmsnorm(x)) per layer (decode_step's FFN
- *                        half, :1563-1570, attention taken as identity)
+ *   stack             -- x += ffn(rmsnorm(x)) per layer, ffn = dense_ffn for
+ *                        a router-less layer else moe_block (decode_step's
+ *                        FFN half, :1563-1570, attention taken as identity)
  *
  * Expert blobs are in the .bin layout (wisp/converter/partitioner.py:11-26):
  * 120-byte header, then packed|scales|zeros for gate, up, down.
@@ -176,6 +181,7 @@ int oracle_moe_block(const uint16_t* router_w, const uint16_t* router_bias,
     int max_i = shared_inter;
     for (int e = 0; e < E; e++) {
         QView v[3];
+        if (!blobs[e]) continue; /* absent file: skipped when routed */
         if (!blob_views(blobs[e], v)) return 6;
         if ((int)v[0].rows > max_i) max_i = (int)v[0].rows;
     }
@@ -198,7 +204,7 @@ int oracle_moe_block(const uint16_t* router_w, const uint16_t* router_bias,
             for (int i = 0; i < H; i++) acc[i] += 1.0f * yy[i];
         }
         for (int j = 0; j < k; j++) {
-            if (ti[j] < 0) continue;
+            if (ti[j] < 0 || !blobs[ti[j]]) continue; /* run_moe: IO miss -> skip */
             QView v[3];
             uint32_t gs = blob_views(blobs[ti[j]], v);
             gemv_int4(&v[0], gs, xt, g);
@@ -211,6 +217,83 @@ int oracle_moe_block(const uint16_t* router_w, const uint16_t* router_bias,
         if (w) memcpy(w + (size_t)t * k, tw, (size_t)k * sizeof(float));
     }
     free(g); free(u); free(h); free(yy); free(ti); free(tw);
+    return 0;
+}
+
+/* The expert half of run_moe on a given routing (idx/w [T,k]; idx < 0 or an
+ * absent blob: skipped): zero acc, fp16 shared expert (w = 1), then the routed
+ * experts in slot order -- the same arithmetic as oracle_moe_block, used to
+ * check a token whose routing differs from the reference's only by a near-tie
+ * against the experts it was actually routed to. */
+int oracle_experts_routed(int E, int H, int k, const uint8_t* const* blobs,
+                          const uint16_t* shared_gate, const uint16_t* shared_up,
+                          const uint16_t* shared_down, int shared_inter,
+                          const float* x, int T, const int* idx, const float* w,
+                          float* y, int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    int max_i = shared_inter;
+    for (int e = 0; e < E; e++) {
+        QView v[3];
+        if (!blobs[e]) continue;
+        if (!blob_views(blobs[e], v)) return 6;
+        if ((int)v[0].rows > max_i) max_i = (int)v[0].rows;
+    }
+    float* g = (float*)malloc((size_t)max_i * sizeof(float));
+    float* u = (float*)malloc((size_t)max_i * sizeof(float));
+    float* h = (float*)malloc((size_t)max_i * sizeof(float));
+    float* yy = (float*)malloc((size_t)H * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        const float* xt = x + (size_t)t * H;
+        float* acc = y + (size_t)t * H;
+        memset(acc, 0, (size_t)H * sizeof(float));
+        if (shared_gate && shared_up && shared_down) {
+            gemv_f16(shared_gate, xt, g, shared_inter, H);
+            gemv_f16(shared_up, xt, u, shared_inter, H);
+            swiglu(g, u, h, shared_inter);
+            gemv_f16(shared_down, h, yy, H, shared_inter);
+            for (int i = 0; i < H; i++) acc[i] += 1.0f * yy[i];
+        }
+        for (int j = 0; j < k; j++) {
+            const int e = idx[(size_t)t * k + j];
+            if (e < 0 || e >= E || !blobs[e]) continue;
+            QView v[3];
+            uint32_t gs = blob_views(blobs[e], v);
+            gemv_int4(&v[0], gs, xt, g);
+            gemv_int4(&v[1], gs, xt, u);
+            swiglu(g, u, h, (int)v[0].rows);
+            gemv_int4(&v[2], gs, h, yy);
+            const float wj = w[(size_t)t * k + j];
+            for (int i = 0; i < H; i++) acc[i] += wj * yy[i];
+        }
+    }
+    free(g); free(u); free(h); free(yy);
+    return 0;
+}
+
+/* run_dense_mlp for T tokens: y = down . (silu(gate . x) * (up . x)), gate/up
+ * [inter, H], down [H, inter] fp16 bits. */
+int oracle_dense_ffn(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                     int inter, int H, const float* x, int T, float* y, int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    float* g = (float*)malloc((size_t)inter * sizeof(float));
+    float* u = (float*)malloc((size_t)inter * sizeof(float));
+    float* h = (float*)malloc((size_t)inter * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        const float* xt = x + (size_t)t * H;
+        gemv_f16(gate, xt, g, inter, H);
+        gemv_f16(up, xt, u, inter, H);
+        swiglu(g, u, h, inter);
+        gemv_f16(down, h, y + (size_t)t * H, H, inter);
+    }
+    free(g); free(u); free(h);
     return 0;
 }
 
@@ -241,6 +324,51 @@ int oracle_stack(int L, const uint16_t* const* router_w,
                                       E, H, k, blobs + (size_t)l * E, NULL, NULL,
                                       NULL, 0, xn, 1, f, idx ? idx + o : NULL,
                                       w ? w + o : NULL, threads);
+            if (rc) { free(xn); free(f); return rc; }
+            for (int i = 0; i < H; i++) xt[i] += f[i];
+        }
+    }
+    free(xn);
+    free(f);
+    return 0;
+}
+
+/* Stack over layers of any kind: router_w[l] NULL = a dense-MLP layer whose FFN
+ * is shared_*[l] alone; else an MoE layer with the fp16 shared expert
+ * shared_*[l] (NULL = none).  blobs [L][E] flattened (NULL = absent file).
+ * idx/w (optional) [T, L, k]; a dense layer leaves -1 / 0 there. */
+int oracle_stack_layers(int L, const uint16_t* const* router_w,
+                        const uint16_t* const* router_bias,
+                        const uint16_t* const* norm_w, float eps, int E, int H, int k,
+                        const uint8_t* const* blobs, const uint16_t* const* shared_gate,
+                        const uint16_t* const* shared_up,
+                        const uint16_t* const* shared_down, const int* shared_inter,
+                        const float* x_in, float* x, int T, int* idx, float* w,
+                        int threads) {
+    float* xn = (float*)malloc((size_t)H * sizeof(float));
+    float* f = (float*)malloc((size_t)H * sizeof(float));
+    if (x != x_in) memcpy(x, x_in, (size_t)T * H * sizeof(float));
+    for (int t = 0; t < T; t++) {
+        float* xt = x + (size_t)t * H;
+        for (int l = 0; l < L; l++) {
+            oracle_rmsnorm(xt, norm_w[l], xn, H, eps);
+            size_t o = ((size_t)t * L + l) * k;
+            int rc;
+            const int si = shared_inter ? shared_inter[l] : 0;
+            if (!router_w[l]) {
+                rc = oracle_dense_ffn(shared_gate[l], shared_up[l], shared_down[l], si, H, xn,
+                                      1, f, threads);
+                for (int j = 0; j < k; j++) {
+                    if (idx) idx[o + j] = -1;
+                    if (w) w[o + j] = 0.f;
+                }
+            } else {
+                rc = oracle_moe_block(router_w[l], router_bias ? router_bias[l] : NULL, E, H,
+                                      k, blobs + (size_t)l * E,
+                                      si ? shared_gate[l] : NULL, si ? shared_up[l] : NULL,
+                                      si ? shared_down[l] : NULL, si, xn, 1, f,
+                                      idx ? idx + o : NULL, w ? w + o : NULL, threads);
+            }
             if (rc) { free(xn); free(f); return rc; }
             for (int i = 0; i < H; i++) xt[i] += f[i];
         }

@@ -40,6 +40,20 @@ def port_lib() -> C.CDLL:
         _port.oracle_router_topk.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                              C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
         _port.oracle_rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float]
+        f = _port.oracle_experts_routed
+        f.restype = C.c_int
+        f.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                      C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                      C.c_void_p, C.c_int]
+        f = _port.oracle_dense_ffn
+        f.restype = C.c_int
+        f.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                      C.c_int, C.c_void_p, C.c_int]
+        f = _port.oracle_stack_layers
+        f.restype = C.c_int
+        f.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_int, C.c_int,
+                      C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                      C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int]
         _port.oracle_dequant.argtypes = [C.c_void_p, C.c_int, C.c_long, C.c_void_p]
     return _port
 
@@ -76,7 +90,9 @@ def host_threads() -> int:
 
 
 class Model:
-    """A converted model directory held in host memory."""
+    """A converted model directory held in host memory.  An expert whose file is
+    absent is held as None (the reference's fetch fails with WISP_ERR_IO and
+    run_moe skips it); a layer without a router is a dense-MLP layer."""
 
     def __init__(self, path: str | Path):
         from safetensors.numpy import load_file
@@ -90,8 +106,18 @@ class Model:
         self.eps = float(a.get("rms_norm_eps", 1e-6))
         self.dense = {k: v.view(np.uint16) for k, v in
                       load_file(str(self.path / "dense" / "model_dense.safetensors")).items()}
-        self.blobs = [[np.fromfile(self.path / "experts" / f"L{l:03d}_E{e:05d}.bin", dtype=np.uint8)
-                       for e in range(self.E)] for l in range(self.n_layers)]
+        def blob(l, e):
+            p = self.path / "experts" / f"L{l:03d}_E{e:05d}.bin"
+            return np.fromfile(p, dtype=np.uint8) if p.exists() else None
+        self.blobs = [[blob(l, e) for e in range(self.E)] for l in range(self.n_layers)]
+
+    def is_dense(self, layer: int) -> bool:
+        return self.d(f"layers.{layer}.router") is None
+
+    def shared(self, layer: int):
+        """(gate, up, down) fp16 bits of the layer's shared.* tensors, or None."""
+        t = tuple(self.d(f"layers.{layer}.shared.{n}") for n in ("gate", "up", "down"))
+        return None if any(a is None for a in t) else t
 
     def d(self, name: str):
         return self.dense.get(name)
@@ -99,13 +125,22 @@ class Model:
 
 def port_moe_block(m: Model, layer: int, x: np.ndarray, threads: int | None = None,
                    with_shared: bool = True):
-    """The restated block on x [T,H] fp32 -> (y [T,H], idx [T,k], w [T,k])."""
+    """The restated block on x [T,H] fp32 -> (y [T,H], idx [T,k], w [T,k]); a dense-MLP
+    layer gives its FFN with idx -1 and w 0."""
     lib = port_lib()
     x = np.ascontiguousarray(x, dtype=np.float32)
     T = x.shape[0]
     y = np.zeros((T, m.H), np.float32)
     idx = np.zeros((T, m.k), np.int32)
     w = np.zeros((T, m.k), np.float32)
+    if m.is_dense(layer):
+        sg, su, sd = m.shared(layer)
+        rc = lib.oracle_dense_ffn(_ptr(sg), _ptr(su), _ptr(sd), sg.shape[0], m.H, _ptr(x), T,
+                                  _ptr(y), threads or host_threads())
+        if rc:
+            raise RuntimeError(f"oracle_dense_ffn failed: {rc}")
+        idx[:] = -1
+        return y, idx, w
     blobs = _ptr_array(m.blobs[layer])
     sg, su, sd = (m.d(f"layers.{layer}.shared.{n}") for n in ("gate", "up", "down"))
     si = sg.shape[0] if (sg is not None and with_shared) else 0
@@ -144,6 +179,30 @@ def port_moe_block_arrays(router_w: np.ndarray, router_bias: np.ndarray | None, 
     return y, idx, w
 
 
+def port_experts_routed(blobs: list, H: int, idx: np.ndarray, w: np.ndarray, x: np.ndarray,
+                        shared=None, threads: int | None = None) -> np.ndarray:
+    """The expert half of the restated block on a given routing (idx/w [T,k]):
+    y = [shared(x)] + sum_j w_j * E_idx_j(x), skipping idx < 0 and absent blobs."""
+    lib = port_lib()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, k = idx.shape
+    y = np.zeros((T, H), np.float32)
+    sg = su = sd = None
+    si = 0
+    if shared is not None:
+        sg, su, sd = (np.ascontiguousarray(a) for a in shared)
+        si = sg.shape[0]
+    bp = _ptr_array(blobs)
+    rc = lib.oracle_experts_routed(len(blobs), H, k, _ptr(bp), _ptr(sg), _ptr(su), _ptr(sd), si,
+                                   _ptr(x), T, _ptr(idx), _ptr(w), _ptr(y),
+                                   threads or host_threads())
+    if rc:
+        raise RuntimeError(f"oracle_experts_routed failed: {rc}")
+    return y
+
+
 def port_stack(m: Model, x: np.ndarray, layers: int | None = None, threads: int | None = None):
     """x <- x + moe_l(rmsnorm(x)) for l < layers -> (x_out, idx [T,L,k], w [T,L,k])."""
     lib = port_lib()
@@ -158,8 +217,12 @@ def port_stack(m: Model, x: np.ndarray, layers: int | None = None, threads: int 
     rbp = _ptr_array(rb) if any(b is not None for b in rb) else None
     nw = _ptr_array([m.d(f"layers.{l}.post_norm") for l in range(L)])
     bl = _ptr_array([b for l in range(L) for b in m.blobs[l]])
-    rc = lib.oracle_stack(L, _ptr(rw), _ptr(rbp), _ptr(nw), m.eps, m.E, m.H, m.k, _ptr(bl),
-                          _ptr(x), _ptr(out), T, _ptr(idx), _ptr(w), threads or host_threads())
+    sh = [m.shared(l) for l in range(L)]
+    sg, su, sd = (_ptr_array([s[i] if s is not None else None for s in sh]) for i in range(3))
+    si = np.array([s[0].shape[0] if s is not None else 0 for s in sh], dtype=np.int32)
+    rc = lib.oracle_stack_layers(L, _ptr(rw), _ptr(rbp), _ptr(nw), m.eps, m.E, m.H, m.k,
+                                 _ptr(bl), _ptr(sg), _ptr(su), _ptr(sd), _ptr(si), _ptr(x),
+                                 _ptr(out), T, _ptr(idx), _ptr(w), threads or host_threads())
     if rc:
         raise RuntimeError(f"oracle_stack failed: {rc}")
     return out, idx, w

@@ -34,9 +34,17 @@ void ref_close(void* h) { wisp_engine_destroy((WispEngine*)h); }
 int ref_hidden(void* h) { return ((WispEngine*)h)->cfg.hidden; }
 int ref_top_k(void* h) { return ((WispEngine*)h)->cfg.top_k; }
 
+/* The FFN of one layer as decode_step runs it (wisp_engine.c:1564-1568):
+ * run_dense_mlp for a router-less layer, else run_moe. */
+static WispError ref_ffn(WispEngine* eng, int layer, WispErrCtx* err) {
+    if (eng->layers[layer].is_dense_mlp) return run_dense_mlp(eng, layer);
+    return run_moe(eng, layer, err);
+}
+
 /* One MoE block on T tokens (T sequential run_moe calls: the reference has
- * no batched path).  x: [T,H] normalised input; y: [T,H] block output
- * (buf_ffn); idx/w: [T,k] routing (host_topk_*).  Returns WispError. */
+ * no batched path; a dense-MLP layer runs run_dense_mlp and leaves idx/w
+ * at -1/0).  x: [T,H] normalised input; y: [T,H] block output (buf_ffn);
+ * idx/w: [T,k] routing (host_topk_*).  Returns WispError. */
 int ref_moe(void* h, int layer, const float* x, int T, float* y, int* idx,
             float* w) {
     WispEngine* eng = (WispEngine*)h;
@@ -45,17 +53,21 @@ int ref_moe(void* h, int layer, const float* x, int T, float* y, int* idx,
         WispErrCtx err;
         memset(&err, 0, sizeof(err));
         memcpy(eng->buf_norm, x + (size_t)t * H, (size_t)H * sizeof(float));
-        WispError e = run_moe(eng, layer, &err);
+        WispError e = ref_ffn(eng, layer, &err);
         if (e != WISP_OK) return (int)e;
         memcpy(y + (size_t)t * H, eng->buf_ffn, (size_t)H * sizeof(float));
-        if (idx) memcpy(idx + (size_t)t * K, eng->host_topk_idx, (size_t)K * sizeof(int));
-        if (w) memcpy(w + (size_t)t * K, eng->host_topk_w, (size_t)K * sizeof(float));
+        const int dense = eng->layers[layer].is_dense_mlp;
+        for (int j = 0; j < K; j++) {
+            if (idx) idx[(size_t)t * K + j] = dense ? -1 : eng->host_topk_idx[j];
+            if (w) w[(size_t)t * K + j] = dense ? 0.f : eng->host_topk_w[j];
+        }
     }
     return 0;
 }
 
 /* The FFN half of decode_step (wisp_engine.c:1563-1570) over a layer range
  * with attention taken as identity: per layer x <- x + run_moe(rmsnorm(x)).
+ * Dense-MLP layers run run_dense_mlp, as decode_step does.
  * x: [T,H] updated in place. idx/w (optional): [T, n_layers, k]. */
 int ref_stack(void* h, int layer0, int n_layers, float* x, int T, int* idx,
               float* w) {
@@ -70,12 +82,15 @@ int ref_stack(void* h, int layer0, int n_layers, float* x, int T, int* idx,
             memset(&err, 0, sizeof(err));
             cpu_rmsnorm(xt, eng->layers[layer].post_norm, eng->buf_norm, H,
                         c->rms_eps);
-            WispError e = run_moe(eng, layer, &err);
+            WispError e = ref_ffn(eng, layer, &err);
             if (e != WISP_OK) return (int)e;
             cpu_residual_add(xt, eng->buf_ffn, H);
             size_t o = ((size_t)t * n_layers + l) * K;
-            if (idx) memcpy(idx + o, eng->host_topk_idx, (size_t)K * sizeof(int));
-            if (w) memcpy(w + o, eng->host_topk_w, (size_t)K * sizeof(float));
+            const int dense = eng->layers[layer].is_dense_mlp;
+            for (int j = 0; j < K; j++) {
+                if (idx) idx[o + j] = dense ? -1 : eng->host_topk_idx[j];
+                if (w) w[o + j] = dense ? 0.f : eng->host_topk_w[j];
+            }
         }
     }
     return 0;

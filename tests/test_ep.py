@@ -88,7 +88,7 @@ def test_ep_layer_matches_block_and_oracle(cuda, B):
     from wisp_b200 import converter as cv
     from wisp_b200.ep import EPLayer
     from wisp_b200.moe import MoEStack
-    from parity import check_outputs, check_routing
+    from parity import check_block, check_outputs
     shape = cv.MoEShape(hidden=1024, inter=512, n_experts=32, top_k=8, shared_inter=512)
     ep = EPLayer(shape, 41, 0, 1, cuda, zipf_s=1.1)
     st = MoEStack(shape, 41, device=cuda, zipf_s=1.1)
@@ -100,10 +100,10 @@ def test_ep_layer_matches_block_and_oracle(cuda, B):
     assert np.array_equal(idx.cpu().numpy(), ib.cpu().numpy())
     np.testing.assert_allclose(y.cpu().numpy(), yb.cpu().numpy(), rtol=1e-5, atol=1e-6)
     Wb, bb = st.host_router(0)
-    yr, ir, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
-                                          shared=st.host_shared(0))
-    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.cpu().numpy()) == 0:
-        check_outputs(y.cpu().numpy(), yr, tight=False)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
+                                           shared=st.host_shared(0))
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.cpu().numpy(), st.host_blobs(0), shared=st.host_shared(0), tight=False)
 
 
 @pytest.mark.gpu
@@ -115,7 +115,7 @@ def test_ep_layer_tensor_path_for_many_rows(cuda):
     from wisp_b200 import converter as cv
     from wisp_b200.ep import EPLayer
     from wisp_b200.moe import MoEStack
-    from parity import check_outputs, check_routing
+    from parity import check_block, check_outputs
     shape = cv.MoEShape(hidden=1024, inter=512, n_experts=32, top_k=8, shared_inter=512)
     ep = EPLayer(shape, 43, 0, 1, cuda, zipf_s=1.1)
     assert 64 * 8 >= max(ep.TENSOR_MIN_ROWS, ep.TENSOR_MIN_PER_EXPERT * ep.per)
@@ -127,7 +127,7 @@ def test_ep_layer_tensor_path_for_many_rows(cuda):
     assert np.array_equal(idx.cpu().numpy(), ib.cpu().numpy())
     check_outputs(y.cpu().numpy(), yb.cpu().numpy())
     Wb, bb = st.host_router(0)
-    yr, ir, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
-                                          shared=st.host_shared(0))
-    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.cpu().numpy()) == 0:
-        check_outputs(y.cpu().numpy(), yr)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.cpu().numpy(),
+                                           shared=st.host_shared(0))
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.cpu().numpy(), st.host_blobs(0), shared=st.host_shared(0))

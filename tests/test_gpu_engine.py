@@ -117,10 +117,21 @@ def test_promotion_after_three_ram_hits(cuda, golden, golden_dirs):
 
 
 def test_fetch_errors_and_prefetch(cuda, golden_dirs, tmp_path):
+    """A routed expert whose file is missing is skipped and the others are combined
+    (run_moe, csrc/core/wisp_engine.c:1473-1477): the output equals the oracle's with
+    that expert left out, and differs from the full model's."""
     import shutil
+    from oracle import oracle as orc
     d = tmp_path / "m"
     shutil.copytree(golden_dirs["mx_small"], d)
     (d / "experts" / "L000_E00003.bin").unlink()
+    m = orc.Model(d)
+    full = orc.Model(golden_dirs["mx_small"])
+    # tokens that route expert 3 in layer 0
+    x = np.random.default_rng(5).standard_normal((64, m.H)).astype(np.float32)
+    _, idx, _ = orc.port_moe_block(full, 0, x)
+    x = x[(idx == 3).any(axis=1)][:3]
+    assert len(x) > 0
     h = core.engine_create(str(d), 0, 4 * GB, [0], 1)
     try:
         core.expert_prefetch_hint(h, 1, [0, 1, 2, 99, -1])
@@ -130,13 +141,44 @@ def test_fetch_errors_and_prefetch(cuda, golden_dirs, tmp_path):
                 break
             time.sleep(0.02)
         assert core.get_ram_used_bytes(h) > 0
-        # a routed expert whose file is missing surfaces as an IO error
-        x = torch.zeros(1, 128, device=cuda)
-        x[0, :] = 1.0
-        y = torch.empty_like(x)
-        try:
-            core.moe_forward(h, 0, x.data_ptr(), y.data_ptr(), 1)
-        except RuntimeError as e:
-            assert "[2]" in str(e)
+        y = run_block(h, 0, x, cuda)
+        y_skip, _, _ = orc.port_moe_block(m, 0, x)
+        y_full, _, _ = orc.port_moe_block(full, 0, x)
+        check_outputs(y, y_skip)
+        assert np.abs(y_full - y_skip).max() > 10 * np.abs(y - y_skip).max()
+        # the fetch ABI itself reports the missing expert as WISP_ERR_IO
+        import ctypes as C
+        from wisp_b200.lib import WispErrCtx, lib
+        err = WispErrCtx()
+        assert not lib().wisp_expert_fetch(core._engine(h), 0, 3, C.byref(err))
+        assert err.code == 2
+    finally:
+        core.engine_destroy(h)
+
+
+@pytest.mark.parametrize("vram", [4 * GB, 0])
+def test_engine_on_reference_converted_dir(cuda, golden, ref_conv_dir, vram):
+    """A model directory in the form the reference converter writes for a real
+    checkpoint -- fp16 real-valued shared experts (layers.i.shared.*, no int4 copy), a
+    router-less dense-MLP layer, one routed expert file absent -- through
+    engine_create -> moe_forward (every layer) and moe_stack, against the reference
+    engine's own outputs on it (golden, made with run_moe / run_dense_mlp).  With the
+    experts pinned (fused path for the complete layer, miss path for the layer with
+    the absent file) and with a zero VRAM budget (every expert through the miss path)."""
+    meta, arr = golden
+    rc = meta["ref_conv"]
+    L = rc["shape"]["n_layers"]
+    h = core.engine_create(str(ref_conv_dir), vram, 4 * GB, [0], 1)
+    try:
+        if vram:
+            core.pin_experts(h, 0, L)
+        x = arr["ref_conv.x"]
+        for l in range(L):
+            y = run_block(h, l, x, cuda)
+            check_outputs(y, arr[f"ref_conv.L{l}.y"])
+        xs = torch.from_numpy(x).to(cuda)
+        core.moe_stack(h, 0, L, xs.data_ptr(), x.shape[0])
+        torch.cuda.synchronize()
+        check_outputs(xs.cpu().numpy(), arr["ref_conv.stack_x"])
     finally:
         core.engine_destroy(h)

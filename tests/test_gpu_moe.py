@@ -18,7 +18,7 @@ from wisp_b200.moe import MoEStack
 
 pytestmark = pytest.mark.gpu
 
-from parity import check_outputs, check_routing  # noqa: E402
+from parity import check_block, check_outputs, check_routing  # noqa: E402
 
 
 CONFIGS = [
@@ -43,10 +43,8 @@ def test_block_matches_oracle(cuda, H, I, E, k, gs, bias, T):
     assert st.status() == 0
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy())
-    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
-    if nd == 0:
-        np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-6)
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0))
 
 
 @pytest.mark.parametrize("T", [1, 4, 16])
@@ -115,9 +113,8 @@ def test_mixtral_block_matches_oracle(cuda, T):
     assert st.status() == 0
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 2, x.numpy())
-    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
-    if nd == 0:
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0))
 
 
 @pytest.mark.parametrize("H,I,gs", [(128, 256, 64), (192, 96, 32), (512, 256, 128),
@@ -180,8 +177,8 @@ def test_separate_router_kernel_path(cuda, T, monkeypatch):
     assert st.status() == 0
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 4, x.numpy())
-    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0))
     xs = x.clone().to(cuda)
     xs2 = x.clone().to(cuda)
     st.stack(xs)
@@ -206,8 +203,8 @@ def test_eight_token_tiles(cuda, T, monkeypatch):
     assert st.status() == 0
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 2, x.numpy())
-    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0))
 
 
 @pytest.mark.parametrize("H,I,E,T", [(1024, 512, 64, 8),
@@ -225,7 +222,78 @@ def test_deepseek_shaped_block_with_shared_expert(cuda, H, I, E, T):
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.numpy(),
                                            shared=st.host_shared(0))
-    if check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy()) == 0:
-        np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-6)
-        # the shared expert's weights are fp16-rounded dequantised int4 in the oracle
-        check_outputs(y.cpu().numpy(), yr, tight=False)
+    # the shared expert's weights are fp16-rounded dequantised int4 in the oracle
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0), shared=st.host_shared(0), tight=False)
+
+
+@pytest.mark.parametrize("H,I,E,k,si,T", [(256, 128, 16, 4, 128, 3), (1024, 512, 32, 8, 1024, 9),
+                                          (512, 256, 8, 2, 96, 1)])
+def test_fp16_dense_shared_expert_matches_oracle(cuda, H, I, E, k, si, T):
+    """The shared expert in the reference converter's form (real-valued fp16-dense
+    layers.i.shared.*, wisp_engine.c:1443-1450): block, stack and the tensor-core
+    prefill path against the oracle, which computes it exactly as the reference does."""
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=E, top_k=k, shared_inter=si, n_layers=2)
+    st = MoEStack(shape, seed=H + si + T, device=cuda, random_bias=True, shared_form="fp16")
+    x = cv.make_input(shape, T, 13)
+    y, idx, w = st.block(0, x.to(cuda), routing=True)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    Wb, bb = st.host_router(0)
+    sh = st.host_shared(0)
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy(), shared=sh)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0), shared=sh)
+    # the shared term is really there: without it the output is far off
+    y_ns, _, _ = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy())
+    assert np.abs(y_ns - yr).max() > 100 * np.abs(y.cpu().numpy() - yr).max()
+    # stack: x <- x + moe(rmsnorm(x)) per layer, fp16 shared in each
+    xs = x.clone().to(cuda)
+    st.stack(xs)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    xr = x.numpy().copy()
+    ones = np.ones(H, np.float16).view(np.uint16)
+    for l in range(2):
+        Wl, bl = st.host_router(l)
+        xn = np.empty_like(xr)
+        for t in range(T):
+            orc.port_lib().oracle_rmsnorm(xr[t].ctypes.data, ones.ctypes.data, xn[t].ctypes.data,
+                                          H, np.float32(shape.rms_eps))
+        yl, _, _ = orc.port_moe_block_arrays(Wl, bl, st.host_blobs(l), k, xn,
+                                             shared=st.host_shared(l))
+        xr = xr + yl
+    check_outputs(xs.cpu().numpy(), xr)
+    # prefill path (tensor cores for the routed experts, the dense GEMVs for the shared)
+    if H % 128 == 0 and I % 128 == 0:
+        yp, ip, wp = st.prefill(0, x.to(cuda), routing=True)
+        torch.cuda.synchronize()
+        assert st.prefill_status() == 0
+        check_block(yp.cpu().numpy(), ip.cpu().numpy(), wp.cpu().numpy(), yr, ir, wr, Wb, bb,
+                    x.numpy(), st.host_blobs(0), shared=sh)
+
+
+def test_dense_ffn_entry_matches_oracle(cuda):
+    """wisp_dense_ffn_forward (run_dense_mlp, wisp_engine.c:1524-1534) on T tokens."""
+    import ctypes as C
+    from wisp_b200.lib import WispErrCtx, lib
+    H, inter = 512, 1000
+    for T in (1, 11):
+        wts = cv.make_dense_ffn(H, inter, 0, 99, 2)
+        g, u, d = (t.to(cuda) for t in wts.values())
+        x = cv.make_input(cv.MoEShape(H, 64, 2, 1), T, 4).to(cuda)
+        y = torch.empty_like(x)
+        ws = torch.empty(lib().wisp_dense_ffn_workspace_bytes(inter, T), dtype=torch.uint8,
+                         device=cuda)
+        err = WispErrCtx()
+        rc = lib().wisp_dense_ffn_forward(g.data_ptr(), u.data_ptr(), d.data_ptr(), inter, H,
+                                          x.data_ptr(), y.data_ptr(), T, ws.data_ptr(), ws.numel(),
+                                          torch.cuda.current_stream().cuda_stream, C.byref(err))
+        assert rc == 0, err.message.decode()
+        torch.cuda.synchronize()
+        yr = np.zeros((T, H), np.float32)
+        xh = x.cpu().numpy()
+        bits = [t.numpy().view(np.uint16) for t in wts.values()]
+        assert orc.port_lib().oracle_dense_ffn(*(b.ctypes.data for b in bits), inter, H,
+                                               xh.ctypes.data, T, yr.ctypes.data, 4) == 0
+        check_outputs(y.cpu().numpy(), yr)

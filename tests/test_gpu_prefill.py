@@ -17,7 +17,7 @@ from wisp_b200.moe import MoEStack
 
 pytestmark = pytest.mark.gpu
 
-from parity import check_outputs, check_routing  # noqa: E402
+from parity import check_block, check_outputs, check_routing  # noqa: E402
 
 CONFIGS = [
     # H, I, E, k, shared, bias, T
@@ -46,10 +46,8 @@ def test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T):
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy(),
                                            shared=st.host_shared(0) if shared else None)
-    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
-    if nd == 0:
-        np.testing.assert_allclose(w.cpu().numpy(), wr, rtol=1e-5, atol=1e-6)
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0), shared=st.host_shared(0) if shared else None)
 
 
 @pytest.mark.parametrize("H,I,E,k,shared,bias,T", [CONFIGS[0], CONFIGS[2], CONFIGS[3]])
@@ -101,9 +99,8 @@ def test_deepseek_shaped_prefill_matches_oracle(cuda):
     Wb, bb = st.host_router(0)
     yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 8, x.numpy(),
                                            shared=st.host_shared(0))
-    nd = check_routing(idx.cpu().numpy(), ir, Wb, bb, x.numpy())
-    if nd == 0:
-        check_outputs(y.cpu().numpy(), yr)
+    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
+                x.numpy(), st.host_blobs(0), shared=st.host_shared(0))
 
 
 @pytest.mark.parametrize("T", [96, 333])

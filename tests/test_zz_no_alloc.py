@@ -3,9 +3,12 @@
 The entry point runs the same kernels as wisp_moe_block_forward in a fixed device
 array inside the library.  The GPU test calls both through the C ABI on the same
 inputs and compares them within the parity tolerances, twice in a row (the second
-call reuses the array the first one left behind).  The CPU test checks that a
-request larger than the array is refused before any GPU work.  This file is
-collected last so it also runs after every other test has used the device.
+call reuses the array the first one left behind); after each static call it reads
+the status word through wisp_moe_block_static_status (0 = no misaligned or missing
+expert, no plan overflow, no timed-out wait) and compares the output with the CPU
+oracle too.  The CPU test checks that a request larger than the array is refused
+before any GPU work.  This file is collected last so it also runs after every other
+test has used the device.
 """
 
 import ctypes as C
@@ -18,7 +21,7 @@ from wisp_b200 import converter as cv
 from wisp_b200.lib import WispErrCtx, WispMoeLayer, lib
 from wisp_b200.moe import MoEStack
 
-from parity import MAX_ABS, REL_L2, rel_l2
+from parity import MAX_ABS, REL_L2, check_block, rel_l2
 
 LIMIT = 8 << 20
 
@@ -42,14 +45,21 @@ def test_static_matches_workspace_entry(cuda, H, I, E, k, T):
     torch.cuda.synchronize()
     assert st.status() == 0
     y_ref, idx_ref, w_ref = y_ref.cpu().numpy(), idx_ref.cpu().numpy(), w_ref.cpu().numpy()
+    from oracle import oracle as orc
+    Wb, bb = st.host_router(0)
+    blobs = st.host_blobs(0)
+    yo, io, wo = orc.port_moe_block_arrays(Wb, bb, blobs, k, x.cpu().numpy())
     for _ in range(2):
         y = torch.full_like(x, float("nan"))
         idx = torch.full((T, k), -7, dtype=torch.int32, device=cuda)
         w = torch.zeros((T, k), dtype=torch.float32, device=cuda)
         rc, err = call_static(st, x, y, idx, w)
         assert rc == 0, err.message.decode()
+        assert lib().wisp_moe_block_static_status(torch.cuda.current_stream().cuda_stream) == 0
         torch.cuda.synchronize()
         yg = y.cpu().numpy()
+        check_block(yg, idx.cpu().numpy(), w.cpu().numpy(), yo, io, wo, Wb, bb,
+                    x.cpu().numpy(), blobs)
         assert np.array_equal(idx.cpu().numpy(), idx_ref)
         np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=1e-6, atol=1e-7)
         assert np.isfinite(yg).all()

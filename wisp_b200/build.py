@@ -24,9 +24,9 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall,-Wno-unused-function",
           f"-I{ROOT / 'include'}", f"-I{CSRC}"]
-SOURCES = ["moe_kernels.cu", "prefill.cu", "expert_layout.cu", "quantize.cu", "ref_launchers.cu", "engine.cpp", "tiers.cpp", "stream_cache.cpp",
+SOURCES = ["moe_kernels.cu", "dense_ffn.cu", "prefill.cu", "expert_layout.cu", "quantize.cu", "ref_launchers.cu", "engine.cpp", "tiers.cpp", "stream_cache.cpp",
            "multi_gpu.cpp"]
-HEADERS = ["internal.h", "tiers.h", "route_common.cuh"]
+HEADERS = ["internal.h", "tiers.h", "route_common.cuh", "dense_ffn.h"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

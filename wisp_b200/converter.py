@@ -286,16 +286,39 @@ def _safetensors_bytes(tensors: dict[str, torch.Tensor]) -> bytes:
     return struct.pack("<Q", len(hj)) + hj + b"".join(blobs)
 
 
+def make_dense_ffn(hidden: int, inter: int, layer: int, seed: int, tag: int,
+                   std: float = 0.02) -> dict[str, torch.Tensor]:
+    """fp16 SwiGLU weights (gate/up ``[inter, hidden]``, down ``[hidden, inter]``) drawn
+    N(0, std) and rounded to fp16, the form the reference converter stores shared
+    experts and dense-MLP layers in (real-valued, not int4-representable).  ``tag``
+    separates the shared expert (1) from a dense-MLP layer (2)."""
+    dims = {"gate": (inter, hidden), "up": (inter, hidden), "down": (hidden, inter)}
+    return {name: _normal(dims[name], std, seed + 8_000_000 + (layer * 3 + m) * 4 + tag,
+                          "cpu").half()
+            for m, name in enumerate(MAT_ORDER)}
+
+
 def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias: bool = False,
-                    zipf_s: float | None = None, shared_int4: bool = True, vocab: int = 16) -> Path:
+                    zipf_s: float | None = None, shared_int4: bool = True, vocab: int = 16,
+                    shared_form: str = "int4", dense_layers=(), dense_inter: int = 0,
+                    missing=()) -> Path:
     """Write a converted-model directory (manifest, dense safetensors, expert blobs).
 
     The dense file carries what the reference loader requires (``embed_tokens``,
     ``final_norm``, ``lm_head``, per-layer ``input_norm``/``post_norm``/``attn.o_proj``)
-    plus the router.  Norm weights are ones.  When the shape has a shared expert it
-    is stored fp16-dense under ``layers.i.shared.*`` as the dequantised int4 weights
-    (the reference runs shared experts dense) and, with ``shared_int4``, also as an
-    int4 blob ``experts/L{layer}_shared.bin`` that this engine prefers.
+    plus the router.  Norm weights are ones.  When the shape has a shared expert:
+
+    * ``shared_form="int4"``: it is quantised like a routed expert and stored
+      fp16-dense under ``layers.i.shared.*`` as the dequantised int4 weights (the
+      reference runs shared experts dense) and, with ``shared_int4``, also as an int4
+      blob ``experts/L{layer}_shared.bin`` that this engine prefers;
+    * ``shared_form="fp16"``: real-valued fp16 weights under ``layers.i.shared.*``
+      only (``make_dense_ffn``), as the reference converter writes a checkpoint's
+      shared expert.
+
+    ``dense_layers``: layers written without a router whose FFN is an fp16-dense
+    SwiGLU of ``dense_inter`` rows under ``layers.i.shared.*`` (the reference's
+    dense-MLP layers).  ``missing``: (layer, expert) pairs whose blob is not written.
     """
     root = Path(path)
     (root / "experts").mkdir(parents=True, exist_ok=True)
@@ -307,10 +330,15 @@ def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias
         "lm_head": _normal((vocab, H), 0.02, seed + 2, "cpu").half(),
     }
     blob_bytes = 0
+    missing = {tuple(m) for m in missing}
     for layer in range(shape.n_layers):
         dense[f"layers.{layer}.input_norm"] = torch.ones(H, dtype=torch.float16)
         dense[f"layers.{layer}.post_norm"] = torch.ones(H, dtype=torch.float16)
         dense[f"layers.{layer}.attn.o_proj"] = torch.zeros(1, 1, dtype=torch.float16)
+        if layer in dense_layers:
+            for name, t in make_dense_ffn(H, dense_inter, layer, seed, 2).items():
+                dense[f"layers.{layer}.shared.{name}"] = t
+            continue
         dense[f"layers.{layer}.router"] = make_router(shape, layer, seed)
         if router_bias or zipf_s is not None:
             dense[f"layers.{layer}.router_bias"] = (
@@ -318,9 +346,13 @@ def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias
                 else _normal((shape.n_experts,), 0.5, seed + 3 + layer, "cpu").half())
         for e in range(shape.n_experts):
             blob = expert_blob(layer, e, make_expert(shape, layer, e, seed))
-            (root / "experts" / expert_filename(layer, e)).write_bytes(blob)
             blob_bytes = max(blob_bytes, len(blob))
-        if shape.shared_inter:
+            if (layer, e) not in missing:
+                (root / "experts" / expert_filename(layer, e)).write_bytes(blob)
+        if shape.shared_inter and shared_form == "fp16":
+            for name, t in make_dense_ffn(H, shape.shared_inter, layer, seed, 1).items():
+                dense[f"layers.{layer}.shared.{name}"] = t
+        elif shape.shared_inter:
             sh = make_shared_expert(shape, layer, seed)
             for name in MAT_ORDER:
                 dense[f"layers.{layer}.shared.{name}"] = dequantize_int4(sh[name]).half()

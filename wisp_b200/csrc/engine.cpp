@@ -4,8 +4,15 @@
 // Model directory: manifest.json (keys found by name anywhere in the file,
 // as the reference's strstr scan does, wisp_engine.c:1601-1657),
 // dense/model_dense.safetensors (fp16: layers.i.router, router_bias,
-// post_norm; wisp_engine.c:1698-1813) and experts/L%03u_E%05u.bin blobs.  An
-// int4 shared expert is read from experts/L%03u_shared.bin (same layout).
+// post_norm, shared.{gate,up,down}; wisp_engine.c:1698-1813) and
+// experts/L%03u_E%05u.bin blobs.  The shared expert is run in the form the
+// reference converter writes it, fp16-dense layers.i.shared.*, unless this
+// build's int4 copy experts/L%03u_shared.bin (same .bin layout, a quarter of
+// the bytes) is present.  A layer without a router is a dense-MLP layer
+// (wisp_engine.c:1757): its FFN is the fp16-dense shared.* SwiGLU alone
+// (run_dense_mlp, :1524-1534).  A routed expert whose file cannot be read
+// (WISP_ERR_IO) is skipped and the others are combined, as run_moe does
+// (:1473-1477, 1502-1506).
 //
 // Expert tiers (policy of wisp_engine.c:920-1078): VRAM LRU (fixed slots in
 // one device arena), RAM LRU (pinned host blobs), SSD files.  A RAM hit is
@@ -35,6 +42,7 @@
 #include <thread>
 #include <vector>
 
+#include "dense_ffn.h"
 #include "internal.h"
 #include "tiers.h"
 
@@ -158,6 +166,12 @@ struct LayerDev {
     wisp_half* post_norm = nullptr;
     void* shared_blob = nullptr;
     WispExpertMeta shared_meta{};
+    // fp16-dense shared expert / dense-MLP weights (layers.i.shared.*)
+    wisp_half* shared_gate = nullptr;
+    wisp_half* shared_up = nullptr;
+    wisp_half* shared_down = nullptr;
+    int shared_inter = 0;
+    bool dense_mlp = false;       // no router: the layer's FFN is shared.* alone
     void** d_table = nullptr;     // device [E]
     std::vector<void*> h_table;   // host mirror
     std::vector<uint8_t> in_vram; // expert is VRAM-resident (not ring-served)
@@ -186,6 +200,16 @@ struct WispEngine {
     // workspace of the fused kernels
     void* ws = nullptr;
     size_t ws_bytes = 0;
+    // per-call device buffers of the miss path and the layer-by-layer stack,
+    // grown on demand and kept: routing [T, K], xn and ffn [T, H], dense h
+    int* d_idx = nullptr;
+    float* d_w = nullptr;
+    float* d_xn = nullptr;
+    float* d_ffn = nullptr;
+    float* d_dh = nullptr;
+    size_t cap_route = 0, cap_rows = 0, cap_dh = 0;
+    std::vector<int> h_idx;        // host copy of the routing (miss path)
+    cudaEvent_t order_ev = nullptr;  // orders the compute stream before a caller's stream
     // prefetch worker
     std::thread worker;
     std::mutex q_mu;
@@ -492,7 +516,7 @@ void prefetch_loop(WispEngine* e) {
 }
 
 WispError load_half(WispEngine* e, const StFile& st, const std::string& name, wisp_half** out,
-                    bool required, WispErrCtx* err) {
+                    bool required, WispErrCtx* err, std::vector<int64_t>* shape = nullptr) {
     StTensor t;
     if (!st.find(name, &t)) {
         if (required) {
@@ -512,7 +536,35 @@ WispError load_half(WispEngine* e, const StFile& st, const std::string& name, wi
     }
     WB_CUDA_RET(cudaMalloc(out, t.bytes), err);
     WB_CUDA_RET(cudaMemcpy(*out, host.data(), t.bytes, cudaMemcpyHostToDevice), err);
+    if (shape) *shape = t.shape;
     (void)e;
+    return WISP_OK;
+}
+
+// The fp16-dense shared.{gate,up,down} of layer l (gate/up [si, H], down
+// [H, si]; wisp_engine.c:1748-1756).  Absent tensors leave the pointers NULL.
+WispError load_dense_shared(WispEngine* e, const StFile& st, int l, WispErrCtx* err) {
+    LayerDev& d = e->L[l];
+    const std::string p = "layers." + std::to_string(l) + ".shared.";
+    std::vector<int64_t> sg, su, sd;
+    WispError r = load_half(e, st, p + "gate", &d.shared_gate, false, err, &sg);
+    if (r == WISP_OK) r = load_half(e, st, p + "up", &d.shared_up, false, err, &su);
+    if (r == WISP_OK) r = load_half(e, st, p + "down", &d.shared_down, false, err, &sd);
+    if (r != WISP_OK) return r;
+    if (!d.shared_gate && !d.shared_up && !d.shared_down) return WISP_OK;
+    const int si = sg.size() == 2 ? (int)sg[0] : 0;
+    const bool ok = d.shared_gate && d.shared_up && d.shared_down && sg.size() == 2 &&
+                    su.size() == 2 && sd.size() == 2 && sg[1] == e->H && su[0] == si &&
+                    su[1] == e->H && sd[0] == e->H && sd[1] == si &&
+                    wb::dense_ffn_shape_ok(d.shared_gate, d.shared_up, d.shared_down, si, e->H);
+    if (!ok) {
+        WB_SET_ERR(err, WISP_ERR_MODEL,
+                   "layer %d: shared.{gate,up,down} must be fp16 [si,%d], [si,%d], [%d,si] with "
+                   "si a multiple of 8",
+                   l, e->H, e->H, e->H);
+        return WISP_ERR_MODEL;
+    }
+    d.shared_inter = si;
     return WISP_OK;
 }
 
@@ -540,13 +592,60 @@ WispMoeLayer layer_desc(WispEngine* e, int l) {
     d.norm_w = e->L[l].post_norm;
     d.shared_blob = e->L[l].shared_blob;
     d.shared_meta = e->L[l].shared_meta;
+    if (!d.shared_blob && e->L[l].shared_gate) {
+        d.shared_gate = e->L[l].shared_gate;
+        d.shared_up = e->L[l].shared_up;
+        d.shared_down = e->L[l].shared_down;
+        d.shared_inter = e->L[l].shared_inter;
+    }
     d.n_experts = e->E;
     d.top_k = e->K;
     return d;
 }
 
 bool layer_resident(WispEngine* e, int l) {
-    return e->meta[l].valid && e->L[l].n_vram == e->E;
+    return !e->L[l].dense_mlp && e->meta[l].valid && e->L[l].n_vram == e->E;
+}
+
+// Grow the engine's per-call device buffers to T tokens.  A grown buffer
+// replaces the old one after the device is idle (cudaFree synchronises).
+WispError ensure_bufs(WispEngine* e, int T, int si, WispErrCtx* err) {
+    const size_t route = (size_t)T * e->K, rows = (size_t)T * e->H, dh = (size_t)T * si;
+    if (route > e->cap_route) {
+        cudaFree(e->d_idx);
+        cudaFree(e->d_w);
+        e->d_idx = nullptr;
+        e->d_w = nullptr;
+        e->cap_route = 0;
+        WB_CUDA_RET(cudaMalloc(&e->d_idx, route * sizeof(int)), err);
+        WB_CUDA_RET(cudaMalloc(&e->d_w, route * sizeof(float)), err);
+        e->cap_route = route;
+    }
+    if (rows > e->cap_rows) {
+        cudaFree(e->d_xn);
+        cudaFree(e->d_ffn);
+        e->d_xn = e->d_ffn = nullptr;
+        e->cap_rows = 0;
+        WB_CUDA_RET(cudaMalloc(&e->d_xn, rows * sizeof(float)), err);
+        WB_CUDA_RET(cudaMalloc(&e->d_ffn, rows * sizeof(float)), err);
+        e->cap_rows = rows;
+    }
+    if (dh > e->cap_dh) {
+        cudaFree(e->d_dh);
+        e->d_dh = nullptr;
+        e->cap_dh = 0;
+        WB_CUDA_RET(cudaMalloc(&e->d_dh, dh * sizeof(float)), err);
+        e->cap_dh = dh;
+    }
+    return WISP_OK;
+}
+
+// Work queued on the compute stream (expert-table updates) precedes what the
+// caller queues next on `s`.
+void order_after_compute(WispEngine* e, cudaStream_t s) {
+    if (s == e->compute) return;
+    cudaEventRecord(e->order_ev, e->compute);
+    cudaStreamWaitEvent(s, e->order_ev, 0);
 }
 
 WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
@@ -697,6 +796,7 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
     e->max_expert_bytes = e->expert_bytes + e->expert_bytes / 4 + 4096;
     ce = cudaStreamCreateWithFlags(&e->compute, cudaStreamNonBlocking);
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->transfer, cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->order_ev, cudaEventDisableTiming);
     if (ce == cudaSuccess) ce = cudaHostAlloc(&e->staging, e->max_expert_bytes, 0);
     if (ce == cudaSuccess) ce = cudaMalloc(&e->d_stage, e->max_expert_bytes + 264);
     if (ce == cudaSuccess) e->d_stage += 8;  // blob at 8 (mod 16), like every slot
@@ -718,10 +818,22 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
     for (int l = 0; l < e->n_layers; ++l) {
         std::string p = "layers." + std::to_string(l) + ".";
         LayerDev& d = e->L[l];
-        if (load_half(e.get(), st, p + "router", &d.router, true, err) != WISP_OK ||
+        if (load_half(e.get(), st, p + "router", &d.router, false, err) != WISP_OK ||
             load_half(e.get(), st, p + "router_bias", &d.router_bias, false, err) != WISP_OK ||
-            load_half(e.get(), st, p + "post_norm", &d.post_norm, false, err) != WISP_OK ||
-            load_shared(e.get(), l, err) != WISP_OK) {
+            load_half(e.get(), st, p + "post_norm", &d.post_norm, false, err) != WISP_OK) {
+            wisp_engine_destroy(e.release());
+            return nullptr;
+        }
+        d.dense_mlp = d.router == nullptr;
+        // the int4 shared blob when this build's converter wrote one, else the
+        // reference's fp16-dense shared.* (also the whole FFN of a dense-MLP layer)
+        WispError sr = d.dense_mlp ? WISP_OK : load_shared(e.get(), l, err);
+        if (sr == WISP_OK && !d.shared_blob) sr = load_dense_shared(e.get(), st, l, err);
+        if (sr == WISP_OK && d.dense_mlp && !d.shared_gate) {
+            WB_SET_ERR(err, WISP_ERR_MODEL, "layer %d: no router and no dense MLP weights", l);
+            sr = WISP_ERR_MODEL;
+        }
+        if (sr != WISP_OK) {
             wisp_engine_destroy(e.release());
             return nullptr;
         }
@@ -777,9 +889,18 @@ extern "C" void wisp_engine_destroy(WispEngine* e) {
         cudaFree(d.router_bias);
         cudaFree(d.post_norm);
         if (d.shared_blob) cudaFree(static_cast<char*>(d.shared_blob) - 8);
+        cudaFree(d.shared_gate);
+        cudaFree(d.shared_up);
+        cudaFree(d.shared_down);
         cudaFree(d.d_table);
     }
     if (e->ws) cudaFree(e->ws);
+    cudaFree(e->d_idx);
+    cudaFree(e->d_w);
+    cudaFree(e->d_xn);
+    cudaFree(e->d_ffn);
+    cudaFree(e->d_dh);
+    if (e->order_ev) cudaEventDestroy(e->order_ev);
     if (e->staging) cudaFreeHost(e->staging);
     if (e->d_stage) cudaFree(e->d_stage - 8);
     if (e->compute) cudaStreamDestroy(e->compute);
@@ -815,6 +936,7 @@ extern "C" int wisp_engine_pin_experts(WispEngine* e, int layer0, int n, WispErr
     std::lock_guard<std::mutex> g(e->fetch_mu);
     int resident = 0;
     for (int l = layer0; l < layer0 + n && l < e->n_layers; ++l) {
+        if (e->L[l].dense_mlp) continue;  // no routed experts
         for (int x = 0; x < e->E; ++x) {
             if (e->L[l].in_vram[x]) {
                 ++resident;
@@ -869,6 +991,18 @@ extern "C" void wisp_engine_dims(WispEngine* e, int* hidden, int* n_experts, int
 
 static WispError moe_forward_impl(WispEngine* e, int l, const float* x, float* y, int T,
                                   cudaStream_t s, WispErrCtx* err) {
+    LayerDev& ld = e->L[l];
+    if (ld.dense_mlp) {
+        // run_dense_mlp (wisp_engine.c:1524-1534): the fp16-dense SwiGLU FFN alone
+        WispError br = ensure_bufs(e, T, ld.shared_inter, err);
+        if (br != WISP_OK) return br;
+        WB_CUDA_RET(wb::launch_dense_ffn(reinterpret_cast<const __half*>(ld.shared_gate),
+                                     reinterpret_cast<const __half*>(ld.shared_up),
+                                     reinterpret_cast<const __half*>(ld.shared_down),
+                                     ld.shared_inter, e->H, x, e->H, e->d_dh, y, e->H, T, s),
+                    err);
+        return WISP_OK;
+    }
     if (!e->meta[l].valid) {
         // nothing of this layer parsed yet: the layout is in any blob's header
         std::lock_guard<std::mutex> g(e->fetch_mu);
@@ -888,63 +1022,64 @@ static WispError moe_forward_impl(WispEngine* e, int l, const float* x, float* y
                                       err);
     // miss path: the fused router decides, the host fetches what it chose, then the
     // expert kernels run on that same plan
-    int* d_idx = nullptr;
-    float* d_w = nullptr;
-    WB_CUDA_RET(cudaMallocAsync(&d_idx, (size_t)T * e->K * sizeof(int), s), err);
-    WB_CUDA_RET(cudaMallocAsync(&d_w, (size_t)T * e->K * sizeof(float), s), err);
-    r = wisp_moe_block_route(&d[0], x, T, d_idx, d_w, e->ws, e->ws_bytes, s, err);
-    std::vector<int> idx((size_t)T * e->K, -1);
-    if (r == WISP_OK) {
-        cudaError_t ce = cudaMemcpyAsync(idx.data(), d_idx, idx.size() * sizeof(int),
-                                         cudaMemcpyDeviceToHost, s);
-        if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
-        if (ce != cudaSuccess) {
-            WB_SET_ERR(err, WISP_ERR_CUDA, "router readback: %s", cudaGetErrorString(ce));
-            r = WISP_ERR_CUDA;
-        }
+    r = ensure_bufs(e, T, 0, err);
+    if (r != WISP_OK) return r;
+    r = wisp_moe_block_route(&d[0], x, T, e->d_idx, e->d_w, e->ws, e->ws_bytes, s, err);
+    if (r != WISP_OK) return r;
+    std::vector<int>& idx = e->h_idx;
+    idx.assign((size_t)T * e->K, -1);
+    cudaError_t ce = cudaMemcpyAsync(idx.data(), e->d_idx, idx.size() * sizeof(int),
+                                     cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) {
+        WB_SET_ERR(err, WISP_ERR_CUDA, "router readback: %s", cudaGetErrorString(ce));
+        return WISP_ERR_CUDA;
     }
-    if (r == WISP_OK) {
-        std::vector<int> uniq;
-        for (int v : idx)
-            if (v >= 0) uniq.push_back(v);
-        std::sort(uniq.begin(), uniq.end());
-        uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
-        std::vector<uint64_t> keep;
-        for (int v : uniq) keep.push_back(wb::Lru::key((uint32_t)l, (uint32_t)v));
+    std::vector<int> uniq;
+    for (int v : idx)
+        if (v >= 0) uniq.push_back(v);
+    std::sort(uniq.begin(), uniq.end());
+    uniq.erase(std::unique(uniq.begin(), uniq.end()), uniq.end());
+    std::vector<uint64_t> keep;
+    for (int v : uniq) keep.push_back(wb::Lru::key((uint32_t)l, (uint32_t)v));
+    std::vector<int> missing;
+    {
         int ring_used = 0;
         std::lock_guard<std::mutex> g(e->fetch_mu);
         for (int v : uniq) {
             WispErrCtx fe{};
             void* p = fetch_locked(e, (uint32_t)l, (uint32_t)v, keep, &fe);
             if (!p) {
+                // run_moe skips an expert whose file cannot be read and combines
+                // the others (wisp_engine.c:1473-1477, 1502-1506)
+                if (fe.code == WISP_ERR_IO) {
+                    missing.push_back(v);
+                    continue;
+                }
                 if (err) *err = fe;
-                r = fe.code == WISP_OK ? WISP_ERR_EXPERT_MISS : fe.code;
-                break;
+                return fe.code == WISP_OK ? WISP_ERR_EXPERT_MISS : fe.code;
             }
             if (!e->L[l].in_vram[v] && ++ring_used > (int)e->ring.size()) {
                 WB_SET_ERR(err, WISP_ERR_OOM,
                            "layer %d routes %zu cold experts for %d tokens; raise the VRAM "
                            "budget (scratch ring holds %zu)",
                            l, uniq.size(), T, e->ring.size());
-                r = WISP_ERR_OOM;
-                break;
+                return WISP_ERR_OOM;
             }
         }
     }
-    if (r == WISP_OK) {
-        // table updates were queued on the compute stream
-        if (s != e->compute) {
-            cudaEvent_t ev;
-            cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-            cudaEventRecord(ev, e->compute);
-            cudaStreamWaitEvent(s, ev, 0);
-            cudaEventDestroy(ev);
-        }
-        r = wisp_moe_block_experts(&d[0], x, y, T, d_idx, d_w, e->ws, e->ws_bytes, s, err);
+    if (!missing.empty()) {
+        // the skipped experts' slots leave the plan and the combine (index -1); the
+        // other weights stay as routed, as in the reference
+        for (int& v : idx)
+            if (std::binary_search(missing.begin(), missing.end(), v)) v = -1;
+        WB_CUDA_RET(cudaMemcpyAsync(e->d_idx, idx.data(), idx.size() * sizeof(int),
+                                    cudaMemcpyHostToDevice, s),
+                    err);
     }
-    cudaFreeAsync(d_idx, s);
-    cudaFreeAsync(d_w, s);
-    return r;
+    // table updates were queued on the compute stream
+    order_after_compute(e, s);
+    return wisp_moe_block_experts(&d[0], x, y, T, e->d_idx, e->d_w, e->ws, e->ws_bytes, s, err);
 }
 
 extern "C" WispError wisp_moe_forward(WispEngine* e, int layer, const float* x, float* y, int T,
@@ -955,14 +1090,8 @@ extern "C" WispError wisp_moe_forward(WispEngine* e, int layer, const float* x, 
     }
     cudaSetDevice(e->device);
     cudaStream_t s = stream ? stream : e->compute;
-    if (s != e->compute) {
-        // pending table updates on the compute stream must land first
-        cudaEvent_t ev;
-        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-        cudaEventRecord(ev, e->compute);
-        cudaStreamWaitEvent(s, ev, 0);
-        cudaEventDestroy(ev);
-    }
+    // pending table updates on the compute stream must land first
+    order_after_compute(e, s);
     return moe_forward_impl(e, layer, x, y, T, s, err);
 }
 
@@ -979,38 +1108,31 @@ extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, 
     }
     cudaSetDevice(e->device);
     cudaStream_t s = stream ? stream : e->compute;
-    bool all = true;
-    for (int l = layer0; l < layer0 + n; ++l) all = all && layer_resident(e, l);
+    order_after_compute(e, s);
     WispError r = WISP_OK;
-    if (all) {
-        if (s != e->compute) {
-            cudaEvent_t ev;
-            cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-            cudaEventRecord(ev, e->compute);
-            cudaStreamWaitEvent(s, ev, 0);
-            cudaEventDestroy(ev);
+    for (int l = layer0; l < layer0 + n && r == WISP_OK;) {
+        // a run of VRAM-resident MoE layers: one fused stack, no host synchronisation
+        int j = l;
+        while (j < layer0 + n && layer_resident(e, j)) ++j;
+        if (j > l) {
+            std::vector<WispMoeLayer> d;
+            for (int q = l; q < j; ++q) d.push_back(layer_desc(e, q));
+            r = ensure_ws(e, d, T, err);
+            if (r == WISP_OK)
+                r = wisp_moe_stack_forward(d.data(), j - l, e->eps, x, T, nullptr, nullptr, e->ws,
+                                           e->ws_bytes, s, err);
+            l = j;
+            continue;
         }
-        std::vector<WispMoeLayer> d;
-        for (int l = layer0; l < layer0 + n; ++l) d.push_back(layer_desc(e, l));
-        r = ensure_ws(e, d, T, err);
-        if (r == WISP_OK)
-            r = wisp_moe_stack_forward(d.data(), n, e->eps, x, T, nullptr, nullptr, e->ws,
-                                       e->ws_bytes, s, err);
-    } else {
-        // layer by layer with the miss path: xn = rmsnorm(x); x += moe(xn)
-        float *xn = nullptr, *f = nullptr;
-        size_t bytes = (size_t)T * e->H * sizeof(float);
-        WB_CUDA_RET(cudaMallocAsync(&xn, bytes, s), err);
-        WB_CUDA_RET(cudaMallocAsync(&f, bytes, s), err);
-        for (int l = layer0; l < layer0 + n && r == WISP_OK; ++l) {
-            for (int t = 0; t < T; ++t)
-                wisp_gpu_rmsnorm(x + (size_t)t * e->H, e->L[l].post_norm, xn + (size_t)t * e->H,
-                                 e->H, e->eps, s);
-            r = moe_forward_impl(e, l, xn, f, T, s, err);
-            if (r == WISP_OK) wisp_gpu_residual_add(x, f, T * e->H, s);
-        }
-        cudaFreeAsync(xn, s);
-        cudaFreeAsync(f, s);
+        // one layer with the miss path or a dense MLP: xn = rmsnorm(x); x += ffn(xn)
+        r = ensure_bufs(e, T, 0, err);
+        if (r != WISP_OK) break;
+        WB_CUDA_RET(wb::launch_rmsnorm_rows(x, reinterpret_cast<const __half*>(e->L[l].post_norm),
+                                        e->d_xn, e->H, e->eps, T, s),
+                    err);
+        r = moe_forward_impl(e, l, e->d_xn, e->d_ffn, T, s, err);
+        if (r == WISP_OK) WB_CUDA_RET(wb::launch_add_rows(x, e->d_ffn, (size_t)T * e->H, s), err);
+        ++l;
     }
     std::lock_guard<std::mutex> g(e->stats_mu);
     e->tok_ns[e->tok_head] = now_ns();

@@ -49,6 +49,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "dense_ffn.h"
 #include "internal.h"
 #include "route_common.cuh"
 
@@ -89,7 +90,12 @@ struct LayerArgs {
     const __half* norm_w;
     MatOff mat[3];
     MatOff smat[3];
-    int H, I, E, K, gs, has_shared;
+    const __half* sg;  // fp16-dense shared expert (has_shared == 2): gate/up [si, H]
+    const __half* su;
+    const __half* sd;  // down [H, si]
+    int si;
+    int H, I, E, K, gs;
+    int has_shared;  // 0 none, 1 int4 blob (a tile of the plan), 2 fp16 dense (dense_ffn.cu)
     int kp;   // K parts of the down projection
     int act_slots;  // token slots of the staged activation tile (min(T, mt))
     int mt;         // tokens per expert tile of the plan (1, 4 or 8)
@@ -110,7 +116,8 @@ struct Ws {
     uint4* xq;      // [T][H/32][4]  activation digits
     float4* xqp;    // [T][H/gs]     (k/254, sum of quantised x, 0, 0) per group
     float* h;       // [A][I]
-    float* ypart;   // [kp][A][H]
+    float* hs;      // [T][si] the fp16-dense shared expert's SwiGLU activations
+    float* ypart;   // [kp][A][H]; a dense shared expert writes part 0 of its rows
     int A;          // assignment capacity
     int max_tiles;
 };
@@ -283,7 +290,7 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
     __syncthreads();
     int base = s_cnt[kWarps + warp] + incl - local;
     const int routed_tiles = s_cnt[2 * kWarps];
-    const int shared_tiles = L.has_shared ? (T + mt - 1) / mt : 0;
+    const int shared_tiles = L.has_shared == 1 ? (T + mt - 1) / mt : 0;
     const int total = routed_tiles + shared_tiles;
     if (total > W.max_tiles) {
         if (tid == 0) {
@@ -377,8 +384,10 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             // reference order: shared expert first (weight 1), then top-k order
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             if (prev_shared) {
+                // int4 shared expert: one ypart per down K part; fp16-dense: part 0
                 const size_t a = (size_t)T * prevK + t;
-                for (int p = 0; p < prev_kp; ++p) {
+                const int np = prev_shared == 2 ? 1 : prev_kp;
+                for (int p = 0; p < np; ++p) {
                     const float4 yv = reinterpret_cast<const float4*>(
                         W.ypart + p * part_stride + a * H)[i0 + i];
                     acc.x += yv.x; acc.y += yv.y; acc.z += yv.z; acc.w += yv.w;
@@ -1405,13 +1414,13 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
 // ------------------------------------------------------------------------
 struct Layout {
     size_t status, counters, tok_cnt, logits, topk_idx, topk_w, pidx, pw, tiles,
-        xn, xq, xqp, h, ypart, total;
+        xn, xq, xqp, h, hs, ypart, total;
     int A, max_tiles;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-Layout make_layout(int T, int H, int I, int E, int K, bool shared) {
+Layout make_layout(int T, int H, int I, int E, int K, bool shared, int si = 0) {
     Layout l{};
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -1434,6 +1443,7 @@ Layout make_layout(int T, int H, int I, int E, int K, bool shared) {
     l.xq = take((size_t)T * (H / kChunk) * 64);
     l.xqp = take((size_t)T * (H / kChunk) * sizeof(float4));  // >= per-group params
     l.h = take((size_t)l.A * I * sizeof(float));
+    l.hs = take((size_t)T * si * sizeof(float));
     l.ypart = take((size_t)kMaxKp * l.A * H * sizeof(float));
     l.total = o;
     return l;
@@ -1455,6 +1465,7 @@ Ws make_ws(void* base, const Layout& l) {
     w.xq = reinterpret_cast<uint4*>(b + l.xq);
     w.xqp = reinterpret_cast<float4*>(b + l.xqp);
     w.h = reinterpret_cast<float*>(b + l.h);
+    w.hs = reinterpret_cast<float*>(b + l.hs);
     w.ypart = reinterpret_cast<float*>(b + l.ypart);
     w.A = l.A;
     w.max_tiles = l.max_tiles;
@@ -1528,6 +1539,18 @@ bool check_layer(const WispMoeLayer* ly, int T, WispErrCtx* err) {
     if (!ly->expert_blobs || !ly->router_w) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe layer: NULL expert table or router");
         return false;
+    }
+    if (ly->shared_gate || ly->shared_up || ly->shared_down) {
+        if (ly->shared_blob ||
+            !dense_ffn_shape_ok(ly->shared_gate, ly->shared_up, ly->shared_down,
+                                ly->shared_inter, H)) {
+            WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                       "moe layer: fp16-dense shared expert needs gate, up and down (16-byte "
+                       "aligned), shared_inter a positive multiple of 8 (got %d), and no int4 "
+                       "shared blob beside it",
+                       ly->shared_inter);
+            return false;
+        }
     }
     if (ly->shared_blob) {
         const WispExpertMeta& s = ly->shared_meta;
@@ -1611,7 +1634,11 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.E = ly->n_experts;
     a.K = ly->top_k;
     a.gs = (int)ly->meta.group_size;
-    a.has_shared = ly->shared_blob != nullptr;
+    a.has_shared = ly->shared_blob ? 1 : (ly->shared_gate ? 2 : 0);
+    a.sg = reinterpret_cast<const __half*>(ly->shared_gate);
+    a.su = reinterpret_cast<const __half*>(ly->shared_up);
+    a.sd = reinterpret_cast<const __half*>(ly->shared_down);
+    a.si = a.has_shared == 2 ? ly->shared_inter : 0;
     a.gating = ly->gating;
     // Tokens per expert tile: 4 (one MMA column quad).  8-token tiles (two quads,
     // WISP_B200_TILE_TOKENS=8) stream fewer duplicate tiles at larger batches but
@@ -1623,7 +1650,7 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
         a.act_slots = std::min(T, mtk);
         const long long tiles =
             std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
-            (a.has_shared ? (T + mtk - 1) / mtk : 0);
+            (a.has_shared == 1 ? (T + mtk - 1) / mtk : 0);
         a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, mtk);
     };
     int want = 4;
@@ -1872,6 +1899,16 @@ cudaError_t launch_router(const LayerArgs& a, const Ws& W, int T, const float* x
                   xin, nsl);
 }
 
+// The fp16-dense shared expert of a layer (has_shared == 2) on its input xin
+// [T, H]: h into W.hs, the result into part 0 of the shared rows of ypart
+// (assignments T*K + t), which the combine adds first with weight 1.
+cudaError_t launch_dense_shared(const LayerArgs& a, const Ws& W, int T, const float* xin,
+                                cudaStream_t s) {
+    if (a.has_shared != 2) return cudaSuccess;
+    return launch_dense_ffn(a.sg, a.su, a.sd, a.si, a.H, xin, a.H, W.hs,
+                            W.ypart + (size_t)T * a.K * a.H, a.H, T, s, hook_mark);
+}
+
 // Run one layer's router + expert kernels.  The layer's input is already
 // quantised in W.xq (and xin holds the router input).
 // prep over T tokens (one cluster per token).  P_ROUTE is added when the
@@ -1918,8 +1955,10 @@ extern "C" size_t wisp_moe_workspace_bytes(const WispMoeLayer* layers, int n_lay
     size_t best = 0;
     for (int i = 0; i < n_layers; ++i) {
         const WispMoeLayer& l = layers[i];
+        const bool dense_sh = l.shared_gate != nullptr;
         Layout lo = make_layout(T, (int)l.meta.cols[0], (int)l.meta.rows[0], l.n_experts,
-                                l.top_k, l.shared_blob != nullptr);
+                                l.top_k, l.shared_blob != nullptr || dense_sh,
+                                dense_sh ? l.shared_inter : 0);
         best = std::max(best, lo.total);
     }
     return best;
@@ -1969,7 +2008,7 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
         return WISP_ERR_INVALID_ARG;
     }
     LayerArgs a = layer_args(layer, T, dev_info().sms);
-    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared != 0, a.si);
     Ws W = make_ws(workspace, lo);
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
@@ -1986,6 +2025,7 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
 // gate/up + down + combine, on the plan the preceding route left in the workspace.
 static WispError block_experts(const LayerArgs& a, const Ws& W, int T, const float* x, float* y,
                                cudaStream_t stream, WispErrCtx* err) {
+    WB_CUDA_RET(launch_dense_shared(a, W, T, x, stream), err);
     WB_CUDA_RET(launch_streams(a, W, T, stream), err);
     Ws Wc = W;
     Wc.prev_idx = W.topk_idx;
@@ -2039,7 +2079,7 @@ extern "C" WispError wisp_moe_block_experts(const WispMoeLayer* layer, const flo
         return WISP_ERR_INVALID_ARG;
     }
     LayerArgs a = layer_args(layer, T, dev_info().sms);
-    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared != 0, a.si);
     Ws W = make_ws(workspace, lo);
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
@@ -2067,25 +2107,26 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
         }
     }
     // the workspace layout is sized for the largest layer; all layers share it
-    int maxI = 0, maxE = 0, maxK = 0;
+    int maxI = 0, maxE = 0, maxK = 0, maxSI = 0;
     bool anysh = false;
     for (int l = 0; l < n_layers; ++l) {
         maxI = std::max(maxI, (int)layers[l].meta.rows[0]);
         maxE = std::max(maxE, layers[l].n_experts);
         maxK = std::max(maxK, layers[l].top_k);
-        anysh = anysh || layers[l].shared_blob;
+        anysh = anysh || layers[l].shared_blob || layers[l].shared_gate;
+        if (layers[l].shared_gate) maxSI = std::max(maxSI, layers[l].shared_inter);
     }
     const int H = (int)layers[0].meta.cols[0];
     WB_CUDA_RET(ensure_attrs(H), err);
     {
-        const Layout lo0 = make_layout(T, H, maxI, maxE, maxK, anysh);
+        const Layout lo0 = make_layout(T, H, maxI, maxE, maxK, anysh, maxSI);
         WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo0.counters + kCounters * sizeof(int), stream),
                     err);
     }
     int prevK = 0, prev_sh = 0, prev_kp = 1;
     for (int l = 0; l < n_layers; ++l) {
         LayerArgs a = layer_args(&layers[l], T, dev_info().sms);
-        Layout lo = make_layout(T, H, maxI, maxE, maxK, anysh);
+        Layout lo = make_layout(T, H, maxI, maxE, maxK, anysh, maxSI);
         Ws W = make_ws(workspace, lo);
         // the previous layer's routing is read (per token, before this
         // layer's routing of the same token is written) by prep's combine
@@ -2100,6 +2141,7 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
         WB_CUDA_RET(launch_prep_route(a, Wp, T, flags, x, eps, prevK, prev_sh, prev_kp, W.xn,
                                       stream),
                     err);
+        WB_CUDA_RET(launch_dense_shared(a, W, T, W.xn, stream), err);
         WB_CUDA_RET(launch_streams(a, W, T, stream), err);
         prevK = a.K;
         prev_sh = a.has_shared;
@@ -2137,7 +2179,7 @@ extern "C" WispError wisp_moe_experts_routed(const WispMoeLayer* layer, const fl
     WispError ce = common_checks(&chk, 1, T, workspace, workspace_bytes, err);
     if (ce != WISP_OK) return ce;
     LayerArgs a = layer_args(layer, T, dev_info().sms);
-    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared != 0, a.si);
     Ws W = make_ws(workspace, lo);
     W.topk_idx = const_cast<int*>(topk_idx);
     W.topk_w = const_cast<float*>(topk_w);
@@ -2166,7 +2208,7 @@ extern "C" WispError wisp_moe_route(const WispMoeLayer* layer, const float* x, i
     WispError ce = common_checks(&chk, 1, T, workspace, workspace_bytes, err);
     if (ce != WISP_OK) return ce;
     LayerArgs a = layer_args(&chk, T, dev_info().sms);
-    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared);
+    Layout lo = make_layout(T, a.H, a.I, a.E, a.K, a.has_shared != 0, a.si);
     Ws W = make_ws(workspace, lo);
     W.topk_idx = topk_idx;
     W.topk_w = topk_w;
@@ -2275,4 +2317,16 @@ extern "C" WispError wisp_moe_block_forward_static(const WispMoeLayer* layer, co
     if (!ws) return WISP_ERR_CUDA;
     return wisp_moe_block_forward(layer, x, y, T, topk_idx, topk_w, ws, kStaticScratchBytes,
                                   stream, err);
+}
+
+// Status word of the last wisp_moe_block_forward_static call on the current
+// device (the first int of the fixed array; bits as wisp_moe_status).  A caller
+// of the static entry has no workspace pointer to hand wisp_moe_status, so this
+// reads it through the array's cached address.  Synchronises `stream`; -1 when
+// the read fails.
+extern "C" int wisp_moe_block_static_status(cudaStream_t stream) {
+    WispErrCtx err{};
+    void* ws = block_scratch(&err);
+    if (!ws) return -1;
+    return wisp_moe_status(ws, stream);
 }

@@ -52,6 +52,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "dense_ffn.h"
 #include "internal.h"
 #include "route_common.cuh"
 
@@ -1556,11 +1557,13 @@ size_t al(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct PLayout {
     size_t status, counters, logits, idx, w, cnt, seg, row_tok, row_w, row_of, tiles_gu, tiles_dn,
-        wmaps, xs, hs, total;
+        wmaps, xs, hs, dh, dy, total;
     int R, max_gu, max_dn;
 };
 
-PLayout make_playout(int T, int H, int I, int E, int K) {
+// si > 0: the layer's shared expert is fp16-dense (dense_ffn.cu), with its
+// SwiGLU activations dh [T, si] and output dy [T, H] (fp32) in the workspace.
+PLayout make_playout(int T, int H, int I, int E, int K, int si = 0) {
     PLayout L{};
     const int R = T * K + T;
     const int nt_max = (R + kNT - 1) / kNT + E + 2;  // token tiles over all experts
@@ -1583,6 +1586,8 @@ PLayout make_playout(int T, int H, int I, int E, int K) {
     L.wmaps = o; o = al(o + (size_t)(E + 1) * kMaps * sizeof(CUtensorMap), 1024);
     L.xs = o; o = al(o + (size_t)R * H * 2, 1024);
     L.hs = o; o = al(o + (size_t)R * I * 2, 1024);
+    L.dh = o; o = al(o + (size_t)T * si * 4, 1024);
+    L.dy = o; o = al(o + (size_t)(si ? T : 0) * H * 4, 1024);
     L.total = o;
     return L;
 }
@@ -1643,6 +1648,17 @@ WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err, boo
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: n_experts %d / top_k %d out of range",
                    l->n_experts, l->top_k);
         return WISP_ERR_INVALID_ARG;
+    }
+    if (l->shared_gate || l->shared_up || l->shared_down) {
+        if (l->shared_blob ||
+            !wb::dense_ffn_shape_ok(l->shared_gate, l->shared_up, l->shared_down,
+                                    l->shared_inter, H)) {
+            WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
+                       "prefill: fp16-dense shared expert needs gate, up and down (16-byte "
+                       "aligned), shared_inter a positive multiple of 8, and no int4 shared "
+                       "blob beside it");
+            return WISP_ERR_INVALID_ARG;
+        }
     }
     if (l->shared_blob) {
         const WispExpertMeta& s = l->shared_meta;
@@ -1782,7 +1798,9 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
         P.K = k_override;
         P.has_shared = 0;
     }
-    const PLayout L = make_playout(T, P.H, P.I, P.E, P.K);
+    // fp16-dense shared expert: CUDA-core GEMVs after the routed experts (dense_ffn.cu)
+    const int dense_si = route && layer->shared_gate ? layer->shared_inter : 0;
+    const PLayout L = make_playout(T, P.H, P.I, P.E, P.K, dense_si);
     if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 1023)) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
                    "prefill: workspace %zu bytes (need %zu, 1024-byte aligned)", workspace_bytes,
@@ -1884,6 +1902,17 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
         WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1, 2>, dim3(sms), dim3(kGemmThreads),
                                    gemm_smem_bytes<1, 2>(), stream, P, W, bh, y),
                     err);
+    if (dense_si) {
+        char* b = static_cast<char*>(workspace);
+        float* dy = reinterpret_cast<float*>(b + L.dy);
+        WB_CUDA_RET(wb::launch_dense_ffn(static_cast<const __half*>(layer->shared_gate),
+                                         static_cast<const __half*>(layer->shared_up),
+                                         static_cast<const __half*>(layer->shared_down),
+                                         dense_si, P.H, x, P.H, reinterpret_cast<float*>(b + L.dh),
+                                         dy, P.H, T, stream),
+                    err);
+        WB_CUDA_RET(wb::launch_add_rows(y, dy, (size_t)T * P.H, stream), err);
+    }
     return WISP_OK;
 }
 
@@ -1891,7 +1920,8 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
 size_t stack_ws_bytes(const WispMoeLayer* l, int T, size_t* block_bytes) {
     const WispExpertMeta& m = l->meta;
     const size_t b = al(make_playout(T, (int)m.cols[0], (int)m.rows[0], l->n_experts,
-                                     l->top_k).total, 1024);
+                                     l->top_k, l->shared_gate ? l->shared_inter : 0).total,
+                        1024);
     if (block_bytes) *block_bytes = b;
     return b + 2 * al((size_t)T * m.cols[0] * sizeof(float), 1024);
 }
@@ -1901,7 +1931,9 @@ size_t stack_ws_bytes(const WispMoeLayer* l, int T, size_t* block_bytes) {
 extern "C" size_t wisp_moe_prefill_workspace_bytes(const WispMoeLayer* layer, int T) {
     if (!layer || T <= 0) return 0;
     const WispExpertMeta& m = layer->meta;
-    return make_playout(T, (int)m.cols[0], (int)m.rows[0], layer->n_experts, layer->top_k).total;
+    return make_playout(T, (int)m.cols[0], (int)m.rows[0], layer->n_experts, layer->top_k,
+                        layer->shared_gate ? layer->shared_inter : 0)
+        .total;
 }
 
 extern "C" size_t wisp_moe_prefill_stack_workspace_bytes(const WispMoeLayer* layers, int n_layers,
@@ -1927,8 +1959,13 @@ extern "C" WispError wisp_moe_prefill_stack_forward(const WispMoeLayer* layers, 
             WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill_stack: layers differ in hidden size");
             return WISP_ERR_INVALID_ARG;
         }
-    size_t bb = 0;
-    const size_t need = stack_ws_bytes(&layers[0], T, &bb);
+    // one block's workspace sized for the largest layer, then xn and y
+    size_t bb = 0, need = 0;
+    for (int l = 0; l < n_layers; ++l) {
+        size_t b = 0;
+        need = std::max(need, stack_ws_bytes(&layers[l], T, &b));
+        bb = std::max(bb, b);
+    }
     if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 1023)) {
         WB_SET_ERR(err, WISP_ERR_INVALID_ARG,
                    "prefill_stack: workspace %zu bytes (need %zu, 1024-byte aligned)",

@@ -35,7 +35,8 @@ class WispMoeLayer(C.Structure):
     _fields_ = [("meta", WispExpertMeta), ("expert_blobs", C.c_void_p), ("router_w", C.c_void_p),
                 ("router_bias", C.c_void_p), ("norm_w", C.c_void_p), ("shared_blob", C.c_void_p),
                 ("shared_meta", WispExpertMeta), ("n_experts", C.c_int), ("top_k", C.c_int),
-                ("gating", C.c_int)]
+                ("gating", C.c_int), ("shared_gate", C.c_void_p), ("shared_up", C.c_void_p),
+                ("shared_down", C.c_void_p), ("shared_inter", C.c_int)]
 
 
 class WispError(RuntimeError):
@@ -95,6 +96,7 @@ _SIGS = {
     "wisp_moe_block_forward_static": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                                 C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.POINTER(WispErrCtx)]),
+    "wisp_moe_block_static_status": (C.c_int, [C.c_void_p]),
     "wisp_moe_stack_forward": (C.c_int, [C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_int,
                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                          C.c_void_p, C.POINTER(WispErrCtx)]),
@@ -124,6 +126,10 @@ _SIGS = {
                                         C.c_int, C.c_void_p]),
     "async_load_expert": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_dense_ffn_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "wisp_dense_ffn_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                         C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t,
+                                         C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_quantize_int4": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(WispErrCtx)]),
     "wisp_nccl_available": (C.c_int, []),

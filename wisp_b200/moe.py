@@ -95,6 +95,7 @@ class LayerWeights:
     table: torch.Tensor           # int64 [E] device blob pointers
     slots: list[int]
     shared_slot: int | None = None
+    shared_dense: tuple | None = None  # fp16 (gate, up, down) device tensors
 
 
 class MoEStack:
@@ -102,11 +103,14 @@ class MoEStack:
 
     def __init__(self, shape: cv.MoEShape, seed: int, device="cuda", zipf_s: float | None = None,
                  random_bias: bool = False, n_layers: int | None = None, layer0: int = 0,
-                 expert_ids=None, with_shared: bool = True, gating: int = 0):
+                 expert_ids=None, with_shared: bool = True, gating: int = 0,
+                 shared_form: str = "int4"):
         """`expert_ids`: the experts this stack holds (default all; the expert-parallel
         path holds a slice, table entry i = expert expert_ids[i]); `with_shared`: build
-        the shape's shared expert (if any); `gating`: 0 the reference's softmax(+bias),
-        1 sigmoid scores (``WISP_GATING_SIGMOID``)."""
+        the shape's shared expert (if any) -- `shared_form` "int4" (an int4 blob like the
+        routed experts) or "fp16" (real-valued fp16-dense weights, the form the reference
+        converter writes, ``converter.make_dense_ffn``); `gating`: 0 the reference's
+        softmax(+bias), 1 sigmoid scores (``WISP_GATING_SIGMOID``)."""
         self.shape = shape
         self.device = torch.device(device)
         self.L = n_layers or shape.n_layers
@@ -117,7 +121,8 @@ class MoEStack:
         probe = cv.make_expert(cv.MoEShape(shape.hidden, shape.inter, E, shape.top_k,
                                            shape.group_size), 0, 0, seed, device=self.device)
         self.blob_bytes = blob_bytes_of(probe)
-        n_slots = self.L * E + (self.L if has_shared else 0)
+        dense_shared = has_shared and shared_form == "fp16"
+        n_slots = self.L * E + (self.L if has_shared and not dense_shared else 0)
         self.arena = ExpertArena(n_slots, self.blob_bytes, self.device)
         self.layers: list[LayerWeights] = []
         slot = 0
@@ -130,7 +135,11 @@ class MoEStack:
                 slots.append(slot)
                 slot += 1
             sh = None
-            if has_shared:
+            sd = None
+            if dense_shared:
+                sd = tuple(t.to(self.device) for t in
+                           cv.make_dense_ffn(shape.hidden, shape.shared_inter, l, seed, 1).values())
+            elif has_shared:
                 self.arena.write(slot, l, 0xFFFF, cv.make_shared_expert(shape, l, seed, self.device))
                 sh = slot
                 slot += 1
@@ -146,7 +155,7 @@ class MoEStack:
             self.layers.append(LayerWeights(router, bias, torch.ones(shape.hidden,
                                                                      dtype=torch.float16,
                                                                      device=self.device),
-                                            table, slots, sh))
+                                            table, slots, sh, sd))
         torch.cuda.synchronize(self.device)
         head = self.arena.blob(0)[:cv.HEADER_BYTES].cpu().numpy().tobytes()
         self.meta = parse_meta(head, self.blob_bytes)
@@ -161,6 +170,9 @@ class MoEStack:
             if lw.shared_slot is not None:
                 c.shared_blob = self.arena.ptr(lw.shared_slot)
                 c.shared_meta = self.meta
+            if lw.shared_dense is not None:
+                c.shared_gate, c.shared_up, c.shared_down = (t.data_ptr() for t in lw.shared_dense)
+                c.shared_inter = shape.shared_inter
             c.n_experts = E
             c.top_k = shape.top_k
             c.gating = gating
@@ -283,6 +295,8 @@ class MoEStack:
         """The shared expert of layer l as fp16 dense gate/up/down (raw bits, the
         form the reference computes it in), or None."""
         lw = self.layers[l]
+        if lw.shared_dense is not None:
+            return tuple(t.cpu().numpy().view(np.uint16) for t in lw.shared_dense)
         if lw.shared_slot is None:
             return None
         q = cv.qmats_from_blob(cv.untile_blob(self.arena.blob(lw.shared_slot).cpu().numpy()))
