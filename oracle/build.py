@@ -3,8 +3,9 @@
 * ``oracle/_build/libmoe_oracle.so`` -- the C restatement in ``moe_oracle.c``.
 * ``oracle/_ref/libwisp_ref.so``     -- the reference's own CPU MoE path, compiled
   from its sources where they lie (``csrc/core/*.c`` of the reference checkout)
-  plus ``ref_harness.c``.  Only built when the reference checkout is present;
-  elsewhere (the GPU box) the prebuilt file that travelled with the repo is used.
+  plus ``ref_harness.c``.  Built only when the caller names the checkout (argument
+  ``ref_root`` or the environment variable ``WISP_REFERENCE_ROOT``); otherwise the
+  prebuilt file that travelled with the repo is used, if there is one.
 
 Both use the same flags, ``-O3 -fopenmp -ffp-contract=off`` and no ``-march``,
 so the two compute every float in the same order with the same instructions.
@@ -18,7 +19,6 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("WISP_REFERENCE_ROOT", "/" + "root/reference"))
 CFLAGS = ["-O3", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared", "-std=gnu11", "-w"]
 
 PORT_SO = HERE / "_build" / "libmoe_oracle.so"
@@ -39,10 +39,17 @@ def build_port() -> Path:
     return PORT_SO
 
 
-def build_ref() -> Path | None:
-    core = REF_ROOT / "csrc" / "core"
-    if not (core / "wisp_engine.c").exists():
+def build_ref(ref_root: str | Path | None = None) -> Path | None:
+    """Compile the reference harness from the checkout at ``ref_root`` (default: the
+    environment variable WISP_REFERENCE_ROOT).  Without a checkout, the prebuilt
+    library if present, else None.  A named checkout without the engine source is an
+    error."""
+    root = ref_root or os.environ.get("WISP_REFERENCE_ROOT")
+    if not root:
         return REF_SO if REF_SO.exists() else None
+    core = Path(root) / "csrc" / "core"
+    if not (core / "wisp_engine.c").exists():
+        raise FileNotFoundError(f"reference checkout {root}: {core / 'wisp_engine.c'} not found")
     REF_SO.parent.mkdir(parents=True, exist_ok=True)
     srcs = [HERE / "ref_harness.c", core / "lru_cache.c", core / "double_buffer.c",
             core / "mem_pool.c"]
@@ -53,11 +60,11 @@ def build_ref() -> Path | None:
     return REF_SO
 
 
-def build() -> None:
+def build(ref_root: str | Path | None = None) -> None:
     build_port()
-    build_ref()
+    build_ref(ref_root)
 
 
 if __name__ == "__main__":
-    build()
+    build(sys.argv[1] if len(sys.argv) > 1 else None)
     print(PORT_SO, REF_SO if REF_SO.exists() else "(reference not built)", file=sys.stderr)

@@ -64,7 +64,10 @@ def check_block(y_gpu, idx_gpu, w_gpu, y_ref, idx_ref, w_ref, Wbits, bias_bits, 
     same = (idx_gpu == idx_ref).all(axis=1)
     if same.any():
         if weights:
-            np.testing.assert_allclose(w_gpu[same], w_ref[same], rtol=1e-5, atol=1e-6)
+            # router logits are fp32 sums over H in another order than the reference's
+            # sequential sum (about 1e-5 apart at H = 7168), which moves the softmax
+            # weights by about that much relative to each other
+            np.testing.assert_allclose(w_gpu[same], w_ref[same], rtol=1e-4, atol=1e-6)
         check_outputs(y_gpu[same], y_ref[same], tight)
     if (~same).any():
         y_alt = orc.port_experts_routed(blobs, x.shape[1], idx_gpu[~same], w_gpu[~same],

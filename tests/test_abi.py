@@ -39,7 +39,9 @@ def test_library_exports_every_declared_symbol(built_lib):
 
 
 def test_version_and_selftests(built_lib):
-    assert b"sm_100a" in lib().wisp_b200_version()
+    from wisp_b200 import build
+    v = lib().wisp_b200_version().decode()
+    assert "sm_100a" in v and v.endswith("src:" + build.source_hash())
     assert core._selftest_lru() is True
     for _ in range(5):
         assert core._selftest_double_buffer() is True

@@ -1207,4 +1207,5 @@ extern "C" double wisp_tok_per_sec(WispEngine* e) {
     return span ? (double)(n - 1) * 1e9 / (double)span : 0.0;
 }
 
-extern "C" const char* wisp_b200_version(void) { return "wisp_b200 0.1.0 sm_100a"; }
+// wisp_b200_version() is generated at build time (wisp_b200/build.py): it carries
+// a hash of the sources the library was built from.

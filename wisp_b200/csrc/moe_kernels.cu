@@ -26,7 +26,7 @@
 // (expert_layout.cu).  Each CTA owns a contiguous range of units (two 8-row
 // blocks over a K range); its producer thread fills a ring of shared-memory
 // stages with four cp.async.bulk (TMA) copies per unit and stages each tile's
-// activations, eight consumer warps split the unit's K range on the tensor
+// activations, sixteen consumer warps split the unit's K range on the tensor
 // cores, and a reducer warp sums their partials.
 //
 // Int4 arithmetic on the tensor cores.  Activations are split per quant
