@@ -163,46 +163,21 @@ def test_untiled_blobs_are_refused_on_the_device(cuda):
     assert st.status() == 0
 
 
-@pytest.mark.parametrize("T", [1, 5])
-def test_separate_router_kernel_path(cuda, T, monkeypatch):
-    """Layers whose router would be re-read too often inside prep use the
-    separate router kernel: force it and check block and stack against the
-    oracle."""
-    monkeypatch.setenv("WISP_B200_PREP_ROUTER_BYTES", "0")
-    shape = cv.MoEShape(hidden=256, inter=512, n_experts=16, top_k=4, n_layers=2)
+@pytest.mark.parametrize("T", [17])
+def test_separate_router_kernel_path(cuda, T):
+    """A layer whose router would be re-read more than 32 MB inside prep
+    (T * E * H * 2 bytes) routes with the separate router kernel: block and
+    stack against the oracle."""
+    H, I, E, k = 2048, 256, 512, 4
+    assert T * E * H * 2 > 32 << 20
+    shape = cv.MoEShape(hidden=H, inter=I, n_experts=E, top_k=k, n_layers=2)
     st = MoEStack(shape, seed=19, device=cuda, random_bias=True)
-    x = (torch.randn(T, 256, generator=torch.Generator().manual_seed(T))).half().float()
+    x = (torch.randn(T, H, generator=torch.Generator().manual_seed(T))).half().float()
     y, idx, w = st.block(0, x.to(cuda), routing=True)
     torch.cuda.synchronize()
     assert st.status() == 0
     Wb, bb = st.host_router(0)
-    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 4, x.numpy())
-    check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
-                x.numpy(), st.host_blobs(0))
-    xs = x.clone().to(cuda)
-    xs2 = x.clone().to(cuda)
-    st.stack(xs)
-    monkeypatch.delenv("WISP_B200_PREP_ROUTER_BYTES")
-    st.stack(xs2)
-    torch.cuda.synchronize()
-    assert st.status() == 0
-    # the two router placements sum the logits in different orders
-    np.testing.assert_allclose(xs.cpu().numpy(), xs2.cpu().numpy(), rtol=1e-4, atol=1e-5)
-
-
-@pytest.mark.parametrize("T", [6, 16])
-def test_eight_token_tiles(cuda, T, monkeypatch):
-    """The 8-token tile kernels (two MMA column quads; WISP_B200_TILE_TOKENS=8)
-    against the oracle, with tiles of more and of fewer than 4 tokens."""
-    monkeypatch.setenv("WISP_B200_TILE_TOKENS", "8")
-    shape = cv.MoEShape(hidden=512, inter=1024, n_experts=4, top_k=2)
-    st = MoEStack(shape, seed=23 + T, device=cuda, random_bias=True)
-    x = (torch.randn(T, 512, generator=torch.Generator().manual_seed(T))).half().float()
-    y, idx, w = st.block(0, x.to(cuda), routing=True)
-    torch.cuda.synchronize()
-    assert st.status() == 0
-    Wb, bb = st.host_router(0)
-    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), 2, x.numpy())
+    yr, ir, wr = orc.port_moe_block_arrays(Wb, bb, st.host_blobs(0), k, x.numpy())
     check_block(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), yr, ir, wr, Wb, bb,
                 x.numpy(), st.host_blobs(0))
 

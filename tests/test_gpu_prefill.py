@@ -50,19 +50,11 @@ def test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T):
                 x.numpy(), st.host_blobs(0), shared=st.host_shared(0) if shared else None)
 
 
-@pytest.mark.parametrize("H,I,E,k,shared,bias,T", [CONFIGS[0], CONFIGS[2], CONFIGS[3]])
-def test_prefill_pairs_match_oracle(cuda, monkeypatch, H, I, E, k, shared, bias, T):
-    """The opt-in gate/up GEMM on SM pairs (cta_group::2, 256-token tiles)."""
-    monkeypatch.setenv("WISP_B200_PREFILL_2SM", "1")
-    test_prefill_matches_oracle(cuda, H, I, E, k, shared, bias, T)
-
-
-@pytest.mark.parametrize("kg", ["2", "4"])
-def test_prefill_down_stage_sizes_match_oracle(cuda, monkeypatch, kg):
-    """The down GEMM with stages of 2 and of 4 quant groups (WISP_B200_PREFILL_DOWN_KG
-    forces the choice the rows-per-expert rule would make)."""
-    monkeypatch.setenv("WISP_B200_PREFILL_DOWN_KG", kg)
-    test_prefill_matches_oracle(cuda, *CONFIGS[3])
+@pytest.mark.parametrize("T", [300, 700])
+def test_prefill_down_stage_sizes_match_oracle(cuda, T):
+    """The down GEMM's stage size follows the rows per expert: 4 quant groups
+    per stage at 300 tokens (82 rows per expert), 2 at 700 (191 rows)."""
+    test_prefill_matches_oracle(cuda, 1024, 512, 32, 8, True, "zipf", T)
 
 
 def test_prefill_matches_decode_path(cuda):

@@ -59,7 +59,7 @@ namespace wb {
 namespace {
 
 constexpr int kChunk = 32;      // elements per MMA k-slice (16 packed bytes)
-constexpr int kMT = 8;          // max tokens per expert tile (two MMA column quads)
+constexpr int kMT = 4;          // tokens per expert tile (one MMA column quad)
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
@@ -134,11 +134,6 @@ __device__ __forceinline__ void pdl_launch() {
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-    return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
     return v;
 }
 __device__ __forceinline__ bool aligned16(const void* p) {
@@ -220,36 +215,60 @@ __device__ __forceinline__ void quantize_row(const float4* src, int n, int gs, i
 constexpr int kSlice = 1024;
 
 // Softmax + top-k of token t from its logits lg[E] (without the bias), by one
-// warp; sp/staken: [E] shared scratch of this warp (rule: route_common.cuh).
-__device__ void topk_token(const LayerArgs& L, const Ws& W, int t, int K, const float* lg,
-                           float* sp, int* staken) {
-    wisp_route::warp_topk(lg, L.router_bias, L.E, K, sp, staken, W.topk_idx + t * K,
-                          W.topk_w + t * K, L.gating);
+// warp, into W.topk_idx / W.topk_w (rule: route_common.cuh); sp: [E] shared
+// scratch of this warp; bias: the layer's bias as fp16 or as a float copy in
+// shared memory, NULL for none.
+template <typename BiasT>
+__device__ wisp_route::TopkLane topk_token(const LayerArgs& L, const Ws& W, int t, int K,
+                                           const float* lg, float* sp, const BiasT* bias) {
+    return wisp_route::warp_topk(lg, bias, L.E, K, sp, W.topk_idx + t * K, W.topk_w + t * K,
+                                 L.gating);
 }
 
 // The tiled blob of expert e (E = the shared expert), or NULL with the status
 // flagged: ST_EXPERT for an index out of range or a NULL table entry,
 // ST_LAYOUT for a blob whose header is not the tiled layout's (version 2).
 constexpr uint32_t kTiledVersion = 2;
-__device__ const unsigned char* checked_blob(const LayerArgs& L, const Ws& W, int e) {
+__device__ __forceinline__ const unsigned char* blob_ptr(const LayerArgs& L, int e) {
     const void* b = nullptr;
     if (e == L.E)
         b = L.shared_blob;
     else if (e >= 0 && e < L.E)
         b = L.blobs[e];
-    if (!b) {
-        atomicOr(W.status, ST_EXPERT);
-        return nullptr;
-    }
-    if (__ldg(reinterpret_cast<const uint32_t*>(b) + 1) != kTiledVersion) {
-        atomicOr(W.status, ST_LAYOUT);
-        return nullptr;
-    }
     return static_cast<const unsigned char*>(b);
 }
+// Check code of a blob pointer: 0, ST_EXPERT (NULL) or ST_LAYOUT.
+__device__ __forceinline__ int blob_code(const unsigned char* b) {
+    if (!b) return ST_EXPERT;
+    return __ldg(reinterpret_cast<const uint32_t*>(b) + 1) != kTiledVersion ? ST_LAYOUT : 0;
+}
+// Loads kept where they are written (volatile asm): issued early, their
+// results used much later, so their latency overlaps other work.
+__device__ __forceinline__ uint32_t ld_early_u32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_early_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ const unsigned char* checked_blob(const LayerArgs& L, const Ws& W, int e) {
+    const unsigned char* b = blob_ptr(L, e);
+    const int code = blob_code(b);
+    if (code) atomicOr(W.status, code);
+    return code ? nullptr : b;
+}
 
+// Tiles of up to mt tokens per routed expert (and the shared expert's
+// tiles).  pblob / pcode: the experts' blob pointers and check codes probed
+// earlier (indices 0..E, E = the shared expert), or NULL to probe here.
 __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
-                           int* s_idx, int* s_cnt) {
+                           int* s_idx, int* s_cnt, const unsigned char* const* pblob = nullptr,
+                           const int* pcode = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = L.K, E = L.E, NA = T * K;
     for (int a = tid; a < NA; a += kThreads) s_idx[a] = __ldcg(W.topk_idx + a);
@@ -304,7 +323,12 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
         if (e >= E || my_tiles[r] == 0) continue;
         Tile tl;
         tl.expert = e;
-        tl.blob = checked_blob(L, W, e);
+        if (pblob) {
+            if (pcode[e]) atomicOr(W.status, pcode[e]);
+            tl.blob = pcode[e] ? nullptr : pblob[e];
+        } else {
+            tl.blob = checked_blob(L, W, e);
+        }
         tl.m = 0;
         int ti = base;
         for (int a = 0; a < NA; ++a) {
@@ -322,7 +346,12 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
     for (int s = tid; s < shared_tiles; s += kThreads) {
         Tile tl;
         tl.expert = E;
-        tl.blob = checked_blob(L, W, E);
+        if (pblob) {
+            if (pcode[E]) atomicOr(W.status, pcode[E]);
+            tl.blob = pcode[E] ? nullptr : pblob[E];
+        } else {
+            tl.blob = checked_blob(L, W, E);
+        }
         tl.m = 0;
         for (int t = s * mt; t < T && tl.m < mt; ++t) {
             tl.tok[tl.m] = t;
@@ -331,9 +360,37 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
         }
         W.tiles[routed_tiles + s] = tl;
     }
-    if (tid == 0) {
-        W.counters[C_NTILES] = total;
+    if (tid == 0) W.counters[C_NTILES] = total;
+}
+
+// The plan of a single token (T == 1, K + 1 <= 32), by one warp from the
+// lanes' top-k results: one tile per routed slot j (lane j: token 0,
+// assignment j), then the int4 shared expert's tile (assignment K).
+__device__ void plan_one_token(const LayerArgs& L, const Ws& W, const wisp_route::TopkLane& r,
+                               const unsigned char* const* pblob, const int* pcode) {
+    const int lane = threadIdx.x & 31, K = L.K;
+    int e = -1, asg = 0;
+    if (lane < K) {
+        e = r.i0;
+        asg = lane;
+    } else if (lane == K && L.has_shared == 1) {
+        e = L.E;
+        asg = K;
     }
+    const unsigned live = __ballot_sync(kFull, e >= 0);
+    if (e >= 0) {
+        Tile tl;
+        tl.expert = e;
+        tl.m = 1;
+#pragma unroll
+        for (int i = 0; i < kMT; ++i) tl.tok[i] = tl.asg[i] = 0;
+        tl.asg[0] = asg;
+        const int code = pcode[e];
+        if (code) atomicOr(W.status, code);
+        tl.blob = code ? nullptr : pblob[e];
+        W.tiles[__popc(live & ((1u << lane) - 1u))] = tl;
+    }
+    if (lane == 0) W.counters[C_NTILES] = __popc(live);
 }
 
 // ------------------------------------------------------------------------
@@ -349,10 +406,19 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
 enum { P_COMBINE = 1, P_RESID = 2, P_NORM = 4, P_QUANT = 8, P_ROUTE = 16 };
 constexpr int kPrepThreads = 256;
 
-__host__ __device__ inline size_t prep_smem_bytes(int H, int cs, int E) {
-    return (size_t)(H / cs) * sizeof(float) + (size_t)E * sizeof(float) +
-           (size_t)(kMaxPlanAssign + 64 > 3 * E ? kMaxPlanAssign + 64 : 3 * E) * sizeof(int);
+// Shared memory of prep: the row slice, partial logits, the top-k / plan
+// scratch, then (8-byte aligned) the probed blob pointers and check codes
+// [E + 1] and the bias as floats [E].
+__host__ __device__ inline size_t prep_tail_off(int H, int cs, int E) {
+    const size_t o = (size_t)(H / cs) * sizeof(float) + (size_t)E * sizeof(float) +
+                     (size_t)(kMaxPlanAssign + 64 > 3 * E ? kMaxPlanAssign + 64 : 3 * E) * sizeof(int);
+    return (o + 7) & ~size_t(7);
 }
+__host__ __device__ inline size_t prep_smem_bytes(int H, int cs, int E) {
+    return prep_tail_off(H, cs, E) + (size_t)(E + 1) * (sizeof(void*) + sizeof(int)) +
+           (size_t)E * sizeof(float);
+}
+constexpr int kProbeSlots = 5;  // experts 0..E (E <= 1024) over 256 threads
 
 __global__ void __launch_bounds__(kPrepThreads)
 prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, int prevK,
@@ -360,8 +426,6 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
-    pdl_wait();
-    pdl_launch();
     const int t = blockIdx.x / cs;
     const int H = L.H, E = L.E;
     const int n4 = H / 4 / cs, i0 = rank * n4;  // this CTA's float4 range of the row
@@ -371,6 +435,44 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     float4* sx4 = smem4;                                // [n4] the slice
     float* s_lg = reinterpret_cast<float*>(sx4 + n4);  // [E] partial router logits
     int* s_scr = reinterpret_cast<int*>(s_lg + E);      // top-k / plan scratch (rank 0)
+    unsigned char* tail = reinterpret_cast<unsigned char*>(smem4) + prep_tail_off(H, cs, E);
+    const unsigned char** s_blob = reinterpret_cast<const unsigned char**>(tail);  // [E + 1]
+    int* s_bcode = reinterpret_cast<int*>(s_blob + E + 1);                          // [E + 1]
+    float* s_bias = reinterpret_cast<float*>(s_bcode + E + 1);                      // [E]
+    // Rank 0 of a routing prep with a plan: the layer's weights (bias) and the
+    // expert table are not written by the kernels of this stream, so they are
+    // read before the PDL wait; the blob headers are probed after it, while
+    // the router runs, so the plan needs no dependent global loads.
+    const bool planner = (flags & P_ROUTE) && rank == 0 && mt != 0;
+    const unsigned char* pb[kProbeSlots];
+    uint32_t phdr[kProbeSlots];
+    if ((flags & P_ROUTE) && rank == 0 && L.router_bias)
+        for (int e = tid; e < E; e += kPrepThreads) s_bias[e] = __half2float(L.router_bias[e]);
+#pragma unroll
+    for (int i = 0; i < kProbeSlots; ++i) {
+        const int e = tid + i * kPrepThreads;
+        pb[i] = (planner && e <= E) ? blob_ptr(L, e) : nullptr;
+    }
+    // The router rows of this warp's first expert (this CTA's slice, two
+    // 16-byte words per lane) and the norm weights of this thread's first
+    // float4 are static: in registers before the wait, so the previous
+    // kernel's tail hides their latency.
+    const uint4* wr_rows = reinterpret_cast<const uint4*>(L.router_w);
+    uint4 rw0 = make_uint4(0, 0, 0, 0), rw1 = make_uint4(0, 0, 0, 0);
+    if ((flags & P_ROUTE) && warp < E) {
+        const uint4* row = wr_rows + ((size_t)warp * H + (size_t)i0 * 4) / 8;
+        if (lane < n4 / 2) rw0 = ld_early_v4(row + lane);
+        if (lane + 32 < n4 / 2) rw1 = ld_early_v4(row + lane + 32);
+    }
+    uint2 nwv = make_uint2(0, 0);
+    if ((flags & P_NORM) && L.norm_w && tid < n4)
+        nwv = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half2*>(L.norm_w) +
+                                              2 * (i0 + tid));
+    pdl_wait();
+#pragma unroll
+    for (int i = 0; i < kProbeSlots; ++i)
+        phdr[i] = pb[i] ? ld_early_u32(reinterpret_cast<const uint32_t*>(pb[i]) + 1) : 0u;
+    pdl_launch();
     __shared__ float red[nw];
     __shared__ float s_ss;
     __shared__ int s_last;
@@ -439,7 +541,10 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             float4 v = sx4[i];
             v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
             if (L.norm_w) {
-                const float2 a = __half22float2(nw2[2 * i]), b = __half22float2(nw2[2 * i + 1]);
+                uint2 nv = nwv;  // prefetched for the first float4
+                if (i != tid) nv = *reinterpret_cast<const uint2*>(nw2 + 2 * i);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&nv.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&nv.y));
                 v.x *= a.x; v.y *= a.y; v.z *= b.x; v.w *= b.y;
             }
             sx4[i] = v;
@@ -458,7 +563,9 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             const uint4* row = wr + ((size_t)e * H + (size_t)i0 * 4) / 8;
             float acc = 0.f;
             for (int c = lane; c < n4 / 2; c += 32) {
-                const uint4 wv = __ldg(row + c);
+                // the first expert's first two words were prefetched
+                const uint4 wv = e == warp && c < lane + 64 ? (c == lane ? rw0 : rw1)
+                                                             : __ldg(row + c);
                 const float4 a = sx4[2 * c], b = sx4[2 * c + 1];
                 const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
                 float2 f = __half22float2(w2[0]);
@@ -483,11 +590,27 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     }
     if (cs > 1 && (flags & (P_NORM | P_ROUTE))) cl.sync();  // peers read; CTAs may leave
     if (!(flags & P_ROUTE) || rank != 0) return;
+    if (planner) {
+#pragma unroll
+        for (int i = 0; i < kProbeSlots; ++i) {
+            const int e = tid + i * kPrepThreads;
+            if (e <= E) {
+                s_blob[e] = pb[i];
+                s_bcode[e] = !pb[i] ? ST_EXPERT : (phdr[i] != kTiledVersion ? ST_LAYOUT : 0);
+            }
+        }
+    }
     __syncthreads();
-    if (warp == 0)
-        topk_token(L, W, t, L.K, reinterpret_cast<const float*>(s_scr + 2 * E),
-                   reinterpret_cast<float*>(s_scr), s_scr + E);
-    if (mt == 0) return;  // routing only, no plan
+    const bool one = T == 1 && L.K + 1 <= 32;  // the one-token plan
+    if (warp == 0) {
+        const float* lg = reinterpret_cast<const float*>(s_scr + 2 * E);
+        float* sp = reinterpret_cast<float*>(s_scr);
+        const wisp_route::TopkLane r =
+            L.router_bias ? topk_token(L, W, t, L.K, lg, sp, s_bias)
+                          : topk_token(L, W, t, L.K, lg, sp, static_cast<const float*>(nullptr));
+        if (mt != 0 && one) plan_one_token(L, W, r, s_blob, s_bcode);
+    }
+    if (mt == 0 || one) return;  // routing only, or the plan is written
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -496,7 +619,7 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    build_plan(L, W, T, mt, s_scr, s_scr + kMaxPlanAssign);
+    build_plan(L, W, T, mt, s_scr, s_scr + kMaxPlanAssign, s_blob, s_bcode);
     if (tid == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
 }
 
@@ -590,7 +713,6 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
     __threadfence();
     {
         float* sp = reinterpret_cast<float*>(smem) + (size_t)warp * 3 * E;
-        int* staken = smem + (size_t)warp * 3 * E + E;
         float* lg = sp + 2 * E;
         for (int t = warp; t < T; t += kWarps) {
             for (int e = lane; e < E; e += 32) {
@@ -600,7 +722,7 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
                 lg[e] = v;
             }
             __syncwarp();
-            topk_token(L, W, t, L.K, lg, sp, staken);
+            topk_token(L, W, t, L.K, lg, sp, L.router_bias);
             __syncwarp();
         }
     }
@@ -702,6 +824,34 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint3
         : "memory");
 }
 
+// 16-byte copies through the load/store path (cp.async), completion tracked
+// by an mbarrier: the fp32 activation rows of the down projection take this
+// path so that they do not queue in the copy engine behind the weight stages
+// the CTA filled before its PDL wait.
+__device__ __forceinline__ void ldgsts16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void ldgsts_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+// The warp copies `rows` fp32 rows of `bytes` each (src_row(t) -> dst + t *
+// bytes) and makes `bar` (expected count 1) complete when they have landed.
+template <typename SrcRow>
+__device__ __forceinline__ void copy_rows_lsu(uint8_t* dst, uint32_t bytes, int rows,
+                                              SrcRow src_row, uint64_t* bar) {
+    const int lane = threadIdx.x & 31;
+    const int n16 = (int)(bytes / 16);
+    for (int t = 0; t < rows; ++t) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(src_row(t));
+        for (int i = lane; i < n16; i += 32) ldgsts16(dst + (size_t)t * bytes + i * 16, src + i * 16);
+    }
+    ldgsts_arrive(bar);  // every lane: one pending arrival, released when its copies land
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
 // A streaming CTA: warp 0 = producer (lane 0), warp 1 = reducer, warps
 // 2 .. kNcw+1 = tensor-core consumers.
 constexpr int kNcw = 16;                          // consumer warps per CTA
@@ -741,11 +891,6 @@ __host__ __device__ inline uint32_t act_row_bytes(int ng, int npg, bool f32) {
 __host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32, int slots) {
     return (uint32_t)slots * (act_row_bytes(ng, npg, f32) + (f32 ? 0u : (uint32_t)ng * 16u));
 }
-// Per consumer warp scratch of the float path: one group of every slot in
-// the quantised word layout, and its (k/254, S).
-__host__ __device__ inline uint32_t qs_warp_bytes(int npg, int mt) {
-    return (uint32_t)mt * (npg * 64u + 16u);
-}
 
 // Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
 // the end; the tile's token count and assignment ids (for the reducer).
@@ -754,12 +899,12 @@ struct UnitInfo {
     int asg[kMT];
 };
 
+
 // Shared memory of a streaming CTA.
 struct StreamSmem {
     uint8_t* stages;   // [n_stages][stage_bytes]
     float2* red;       // [n_stages][kNcw][32] consumer partials
     uint8_t* act;      // activation tile (act_bytes_of)
-    uint8_t* qs;       // [kNcw][qs_warp_bytes] (float path)
     float2* kp;        // [kNcw][NGmax][kMT] (k/254, S) of each warp's groups
     UnitInfo* info;    // [n_stages]
     uint64_t* full;    // [n_stages] weights landed (tx)
@@ -767,7 +912,7 @@ struct StreamSmem {
     uint64_t* empty;   // [n_stages] stage reusable (reducer)
     uint64_t* act_full;
     uint64_t* act_empty;
-    uint32_t stage_bytes, act_row, act_bytes, qs_warp;
+    uint32_t stage_bytes, act_row, act_bytes;
     int act_slots;
     int n_stages;
 };
@@ -778,11 +923,11 @@ __host__ __device__ constexpr size_t red_bytes_per_stage(int mt) {
 // (k/254, S) pairs: every group of a unit's K range x the tile width.
 __host__ __device__ constexpr size_t kp_bytes(int mt) { return (size_t)(kMaxPartK / 32) * mt * 8; }
 __host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage_bytes,
-                                                     uint32_t act_bytes, uint32_t qs_bytes,
-                                                     int mt) {
+                                                     uint32_t act_bytes, int mt) {
     return (size_t)n_stages * (stage_bytes + red_bytes_per_stage(mt) + sizeof(UnitInfo) + 24) +
-           (act_bytes + 127) / 128 * 128 + qs_bytes + kp_bytes(mt) + 16 + 128;
+           (act_bytes + 127) / 128 * 128 + kp_bytes(mt) + 16 + 128;
 }
+// The float path (down) quantises its rows in place in the activation tile.
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
                                                   uint32_t stage_bytes, const Geo& geo, int npg,
                                                   bool f32, int slots, int mt) {
@@ -792,14 +937,11 @@ __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
     s.act_row = act_row_bytes(geo.ng, npg, f32);
     s.act_bytes = act_bytes_of(geo.ng, npg, f32, slots);
     s.act_slots = slots;
-    s.qs_warp = f32 ? qs_warp_bytes(npg, mt) : 0u;
     size_t o = 0;
     s.stages = base;
     o += (size_t)n_stages * stage_bytes;
     s.act = base + o;
     o += (s.act_bytes + 127) / 128 * 128;
-    s.qs = base + o;
-    o += (size_t)kNcw * s.qs_warp;
     s.red = reinterpret_cast<float2*>(base + o);
     o += (size_t)n_stages * red_bytes_per_stage(mt);
     s.kp = reinterpret_cast<float2*>(base + o);
@@ -864,10 +1006,17 @@ struct UnitAddr {
     size_t coff[4];
 };
 
+// With `first_act_elsewhere` another warp loads the range's first
+// activation tile (the down kernel's reducer, right after the PDL wait), and
+// the producer issues only kPrePdlStages stages before it waits for the
+// previous kernel itself: a full ring on every SM at that moment would queue
+// the small activation loads behind ~28 MB of weight copies, and the down
+// projection is bound by its consumers once h is complete, not by DRAM.
+constexpr int kPrePdlStages = 2;
 template <typename Dummy = void>
 __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
                         int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
-                        const UnitAddr& ua) {
+                        const UnitAddr& ua, bool first_act_elsewhere = false) {
     const int lane = threadIdx.x & 31;
     const uint32_t tx = 2 * geo.bbytes, zb = (uint32_t)geo.ng * 32u;
     const bool f32 = as.xf != nullptr;
@@ -892,9 +1041,13 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
         if (mis && lane == 0) atomicOr(W.status, ST_ALIGN);
     };
     if (u_begin < u_end) start_tile();
-    int it = 0, tiles_done = 0, s = 0;
+    int it = 0, tiles_done = 0, s = 0, issued = 0;
     uint32_t ph = 0;
     bool ok = true, act_due = true, waited_pdl = !act_after_pdl;
+    if (first_act_elsewhere && u_begin < u_end) {
+        act_due = false;
+        tiles_done = 1;
+    }
     // barrier waits by lane 0, result shared with the warp
     auto wait0 = [&](uint64_t* bar, uint32_t parity) -> bool {
         int v = 1;
@@ -909,16 +1062,21 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             waited_pdl = true;
         }
         if (tiles_done > 0 && !wait0(S.act_empty, (tiles_done - 1) & 1)) return false;
+        if (f32) {
+            copy_rows_lsu(S.act, rowb, cur.m, [&](int t) {
+                const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
+                return as.xf + (size_t)row * as.row_elems + (size_t)as.kg0 * as.gs;
+            }, S.act_full);
+            ++tiles_done;
+            act_due = false;
+            return true;
+        }
         if (lane == 0) mbar_expect_tx(S.act_full, (uint32_t)cur.m * (rowb + pb));
         __syncwarp();
-        const int per = f32 ? 1 : 2, t = lane / per;
+        const int t = lane / 2;
         if (t < cur.m) {
             const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
-            if (f32) {
-                bulk_g2s_plain(S.act + t * rowb,
-                               as.xf + (size_t)row * as.row_elems + (size_t)as.kg0 * as.gs, rowb,
-                               S.act_full);
-            } else if ((lane & 1) == 0) {
+            if ((lane & 1) == 0) {
                 bulk_g2s_plain(S.act + t * rowb,
                                as.xq + ((size_t)row * as.nchk + (size_t)as.kg0 * as.npg) * 64,
                                rowb, S.act_full);
@@ -972,8 +1130,18 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
         __syncwarp();
         if (tile_ok && lane < 4)
             bulk_g2s(S.stages + (size_t)s * S.stage_bytes + dst_off, p, csize, &S.full[s], pol);
+        ++issued;
         p += ua.ustride;
         ++r;
+        if (first_act_elsewhere && !waited_pdl && it + 1 >= kPrePdlStages) {
+            pdl_wait();
+            waited_pdl = true;
+            // a tile that began before this point still needs its activations
+            if (act_due && !issue_act()) {
+                ok = false;
+                break;
+            }
+        }
         // a deferred first activation tile: once the stages are full, or before
         // the tile or the range ends
         if (act_due && !waited_pdl &&
@@ -989,8 +1157,8 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
     if (!ok && lane == 0) {
         atomicOr(W.status, ST_TIMEOUT);
         // a consumer stopped early: let every issued copy land before exiting
-        for (int k = 0; k < S.n_stages && k < it; ++k) {
-            const int j = it - 1 - k;
+        for (int k = 0; k < S.n_stages && k < issued; ++k) {
+            const int j = issued - 1 - k;
             mbar_wait(&S.full[j % S.n_stages], (j / S.n_stages) & 1);
         }
         if (tiles_done > 0) mbar_wait(S.act_full, (tiles_done - 1) & 1);
@@ -1051,9 +1219,11 @@ __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
 // (block B) for token slot q in fp32, and per unit writes its partial to the
 // stage's reduction slot.
 // ------------------------------------------------------------------------
+// d += A.B (pure: not volatile, so the compiler may interleave the MMAs of
+// independent groups).
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                        uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
@@ -1147,57 +1317,75 @@ __device__ __forceinline__ void load_act(WarpAct<NPG, NG, MT>& A, float2* kp_w,
     __syncwarp();
 }
 
-// Float path: quantise the warp's groups of the staged fp32 rows (slots
-// t < m) with the activation quantiser (quantize_block, one group of a slot
-// per gs/4 lanes), one group at a time through the warp's scratch, and take
-// the B fragments and (k/254, S) pairs from there.
+
+// Float rows (down): the warp quantises its groups [g0, g0 + n) of the
+// first `rows` rows of the activation tile in place, once per tile, right
+// after they land -- a group's gs fp32 values (gs*4 bytes)
+// become its NPG digit chunks (NPG*64 bytes) followed by its (k/254, S)
+// float4.  Each (row, group) item takes gs/4 lanes; two passes of items are
+// quantised together (independent shuffle chains); lanes past the last item
+// redo it (same data, same bytes written).  Every read of a batch happens
+// before the batch's writes, and items never overlap.
+template <int NPG>
+__device__ __forceinline__ void quant_rows_in_place(const StreamSmem& S, int rows, int g0,
+                                                    int n) {
+    constexpr int kGs = 32 * NPG, kLpb = kGs / 4, kPer = 32 / kLpb;
+    const int lane = threadIdx.x & 31, pos = (lane % kLpb) * 4;
+    const int items = rows * n;
+    for (int i0 = 0; i0 < items; i0 += 2 * kPer) {
+        const int ia = min(i0 + lane / kLpb, items - 1);
+        const int ib = min(i0 + kPer + lane / kLpb, items - 1);
+        const int ra = ia / n, rb = ib / n;
+        uint8_t* ga = S.act + (size_t)ra * S.act_row + (size_t)(g0 + ia - ra * n) * (kGs * 4);
+        uint8_t* gb = S.act + (size_t)rb * S.act_row + (size_t)(g0 + ib - rb * n) * (kGs * 4);
+        const float4 va = *reinterpret_cast<const float4*>(ga + pos * 4);
+        const float4 vb = *reinterpret_cast<const float4*>(gb + pos * 4);
+        __syncwarp();
+        quantize_block(va, kLpb, reinterpret_cast<uint32_t*>(ga + (pos / kChunk) * 64),
+                       reinterpret_cast<float4*>(ga + NPG * 64), pos == 0);
+        quantize_block(vb, kLpb, reinterpret_cast<uint32_t*>(gb + (pos / kChunk) * 64),
+                       reinterpret_cast<float4*>(gb + NPG * 64), pos == 0);
+        __syncwarp();
+    }
+}
+
+// B fragments and (k/254, S) pairs of the warp's groups for a tile of m
+// tokens whose fp32 rows (slots 0..m-1 of the activation tile) were
+// quantised in place: group G of a slot at G * gs*4 bytes, its NPG digit
+// chunks first, then its float4.
 template <int NPG, int NG, int MT>
-__device__ __forceinline__ void load_act_quant(WarpAct<NPG, NG, MT>& A, float2* kp_w,
-                                               const StreamSmem& S, int g0, int n, int m,
-                                               int cw) {
+__device__ __forceinline__ void load_act_inplace(WarpAct<NPG, NG, MT>& A, float2* kp_w,
+                                                 const StreamSmem& S, int g0, int n, int m) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     const int bd = g & 1;
-    constexpr int kGs = 32 * NPG, kLpb = kGs / 4, kPer = 32 / kLpb;  // lanes / group, groups / pass
-    uint8_t* qs = S.qs + cw * S.qs_warp;
-    float4* qpar = reinterpret_cast<float4*>(qs + MT * NPG * 64);
-    const float* rows = reinterpret_cast<const float*>(S.act);
-    const int row_elems = (int)(S.act_row / 4);
+    constexpr uint32_t kGstride = NPG * 128u;
+    const uint32_t act = smem_addr(S.act);
 #pragma unroll
-    for (int G = 0; G < NG; ++G) {
+    for (int h = 0; h < MT / 4; ++h) {
+        const int bt = 4 * h + (g >> 1);
+        const uint32_t base = act + (bt < m ? bt : 0) * S.act_row + bd * 32;
 #pragma unroll
-        for (int p0 = 0; p0 < MT; p0 += kPer) {
-            if (p0 < m) {
-                const int t = p0 + lane / kLpb, pos = (lane % kLpb) * 4;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (G < n && t < m)
-                    v = *reinterpret_cast<const float4*>(rows + t * row_elems + (g0 + G) * kGs + pos);
-                quantize_block(v, kLpb,
-                               reinterpret_cast<uint32_t*>(qs + t * (NPG * 64) + (pos / kChunk) * 64),
-                               qpar + t, pos == 0);
-            }
-        }
-        __syncwarp();
-#pragma unroll
-        for (int h = 0; h < MT / 4; ++h) {
-            const int bt = 4 * h + (g >> 1);
-            const uint32_t qbase = smem_addr(qs) + bt * (NPG * 64) + bd * 32;
+        for (int G = 0; G < NG; ++G) {
 #pragma unroll
             for (int i = 0; i < NPG; ++i) {
                 const int wi = q * NPG + i;
-                A.b[G][i][h] = (G < n && bt < m) ? lds64(qbase + (wi >> 2) * 64 + (wi & 3) * 8)
-                                                 : make_uint2(0u, 0u);
+                A.b[G][i][h] = (G < n && bt < m)
+                                   ? lds64(base + (g0 + G) * kGstride + (wi >> 2) * 64 + (wi & 3) * 8)
+                                   : make_uint2(0u, 0u);
             }
         }
-        if (lane < MT) {
-            float2 v = make_float2(0.f, 0.f);
-            if (G < n && lane < m) {
-                const float4 pr = qpar[lane];
-                v = make_float2(pr.x, pr.y);
-            }
-            kp_w[G * MT + lane] = v;
-        }
-        __syncwarp();
     }
+    for (int e = lane; e < NG * MT; e += 32) {
+        const int G = e / MT, t = e - G * MT;
+        float2 v = make_float2(0.f, 0.f);
+        if (G < n && t < m) {
+            const float4 p = *reinterpret_cast<const float4*>(
+                S.act + (size_t)t * S.act_row + (size_t)(g0 + G) * kGstride + NPG * 64);
+            v = make_float2(p.x, p.y);
+        }
+        kp_w[e] = v;
+    }
+    __syncwarp();
 }
 
 // This warp's partial dot products of a unit: acc[h].x = MMA row g (block A),
@@ -1235,16 +1423,10 @@ __device__ __forceinline__ void mma_unit(uint32_t st, const Geo& geo, int g0,
             a[1] = wh.w[i] & 0x0F0F0F0Fu;
             a[2] = (wl.w[i] >> 4) & 0x0F0F0F0Fu;
             a[3] = (wh.w[i] >> 4) & 0x0F0F0F0Fu;
-            // one accumulator per MMA (independent, so they overlap), summed in int
+            // the group's slices accumulate in the MMA; the groups are
+            // independent chains the compiler interleaves
 #pragma unroll
-            for (int h = 0; h < NQ; ++h) {
-                int di[4] = {0, 0, 0, 0};
-                mma_s8(di, a, A.b[G][i][h].x, A.b[G][i][h].y);
-                d[h][0] += di[0];
-                d[h][1] += di[1];
-                d[h][2] += di[2];
-                d[h][3] += di[3];
-            }
+            for (int h = 0; h < NQ; ++h) mma_s8(d[h], a, A.b[G][i][h].x, A.b[G][i][h].y);
         }
         // row += s * (k/254 * (254*A + B) - 8*S) + z * S
 #pragma unroll
@@ -1285,10 +1467,12 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
                 if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
                 break;
             }
-            if constexpr (F32)
-                load_act_quant<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m, cw);
-            else
+            if constexpr (F32) {
+                quant_rows_in_place<NPG>(S, inf.m, g0, n);
+                load_act_inplace<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m);
+            } else {
                 load_act<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m);
+            }
             if (lane == 0) mbar_arrive(S.act_empty);
             ++tiles;
         }
@@ -1296,11 +1480,7 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
 #pragma unroll
         for (int h = 0; h < MT / 4; ++h) part[h] = make_float2(0.f, 0.f);
         if (!(uf & kSkip)) {
-            // the second token quad only for tiles of more than 4 tokens (uniform)
-            if (MT == 8 && inf.m > 4)
-                mma_unit<NPG, NG, MT, MT / 4>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
-            else
-                mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+            mma_unit<NPG, NG, MT, MT / 4>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
         }
         float2* red = S.red + ((size_t)s * kNcw + cw) * 32 * (MT / 4);
 #pragma unroll
@@ -1323,7 +1503,8 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int H = L.H, I = L.I, gs = L.gs;
     const Geo geo = make_geo(H / gs, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots, MT);
+    const StreamSmem S =
+        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots, MT);
     stream_init(S);
     pdl_wait();
     pdl_launch();
@@ -1369,7 +1550,8 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int H = L.H, I = L.I, gs = L.gs;
     const int ngp = I / gs / kp;  // groups per part
     const Geo geo = make_geo(ngp, gs);
-    const StreamSmem S = stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots, MT);
+    const StreamSmem S =
+        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots, MT);
     stream_init(S);
     // Weights, the expert table and the tile plan (written by the router,
     // which completed before the gate/up kernel could start) do not depend on
@@ -1393,11 +1575,24 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const size_t p_off = (size_t)pi * geo.pbytes;
             const ActSrc as{nullptr, nullptr, W.h, I / kChunk, I / gs, pi * ngp, NPG, gs, I, true};
             const UnitAddr ua{L.mat[2].packed, 2 * bb, {p_off, z_off, bb + p_off, bb + z_off}};
-            produce(S, W, b, e, upt, ntiles, geo, as, true, ua);
+            produce(S, W, b, e, upt, ntiles, geo, as, true, ua, true);
         }
         return;
     }
     if (warp == 1) {
+        {
+            // the first activation tile of the range, as soon as h is complete
+            const int j = blockIdx.x / kp;
+            const int b = (int)(total * j / cpp), e = (int)(total * (j + 1) / cpp);
+            if (b < e) {
+                Tile tl;
+                load_tile(W.tiles + b / upt, tl);
+                pdl_wait();
+                copy_rows_lsu(S.act, act_row_bytes(ngp, NPG, true), tl.m, [&](int t) {
+                    return W.h + (size_t)tl.asg[t] * I + (size_t)pi * ngp * gs;
+                }, S.act_full);
+            }
+        }
         reduce_units<MT>(S, W, [&](int u, int asg, int g, float2 v) {
             const size_t row = (size_t)(u % upt) * 16 + g;
             float* dst = W.ypart + ((size_t)pi * W.A + asg) * H + row;
@@ -1603,16 +1798,15 @@ StreamCfg plan_stream(const Geo& geo, int npg, bool f32, int slots, int mt) {
     StreamCfg c;
     c.stage_bytes = stage_bytes_of(geo);
     const uint32_t act = act_bytes_of(geo.ng, npg, f32, slots);
-    const uint32_t qs = f32 ? kNcw * qs_warp_bytes(npg, mt) : 0u;
     int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
     want = std::max(2, std::min(kMaxStages, want));
     c.stages = 0;
     for (int st = want; st >= 2; --st)
-        if (stream_smem_bytes(st, c.stage_bytes, act, qs, mt) <= kSmemPerCta) {
+        if (stream_smem_bytes(st, c.stage_bytes, act, mt) <= kSmemPerCta) {
             c.stages = st;
             break;
         }
-    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, qs, mt);
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, mt);
     return c;
 }
 
@@ -1640,33 +1834,12 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.sd = reinterpret_cast<const __half*>(ly->shared_down);
     a.si = a.has_shared == 2 ? ly->shared_inter : 0;
     a.gating = ly->gating;
-    // Tokens per expert tile: 4 (one MMA column quad).  8-token tiles (two quads,
-    // WISP_B200_TILE_TOKENS=8) stream fewer duplicate tiles at larger batches but
-    // measured slower on Mixtral shapes at 16 tokens (the consumers become
-    // issue-bound); they need groups x NPG <= 8 per warp.
-    const int npg = a.gs / kChunk;
-    auto choose = [&](int mtk) {
-        a.mt = mtk;
-        a.act_slots = std::min(T, mtk);
-        const long long tiles =
-            std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
-            (a.has_shared == 1 ? (T + mtk - 1) / mtk : 0);
-        a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, mtk);
-    };
-    int want = 4;
-    if (const char* v = getenv("WISP_B200_TILE_TOKENS")) want = (atoi(v) == 8 && T > 4) ? 8 : 4;
-    choose(want);
-    if (a.mt == 8 && (ng_bucket(npg, a.H / a.gs) * npg > 8 ||
-                      ng_bucket(npg, a.I / a.gs / a.kp) * npg > 8))
-        choose(4);
-    // tuning override: WISP_B200_DOWN_PARTS=<kp>, used when it is a valid split
-    if (const char* v = getenv("WISP_B200_DOWN_PARTS")) {
-        const int kp = atoi(v), G = a.I / a.gs;
-        if (kp >= 1 && kp <= kMaxKp && G % kp == 0 && a.I / kp <= kMaxPartK &&
-            ng_bucket(a.gs / kChunk, G / kp) &&
-            plan_stream(make_geo(G / kp, a.gs), a.gs / kChunk, true, a.act_slots, a.mt).stages >= 2)
-            a.kp = kp;
-    }
+    // Tokens per expert tile: 4 (one MMA column quad).
+    a.mt = kMT;
+    a.act_slots = std::min(T, kMT);
+    const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
+                            (a.has_shared == 1 ? (T + kMT - 1) / kMT : 0);
+    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, kMT);
     return a;
 }
 
@@ -1775,13 +1948,10 @@ int prep_cluster(int H, int gs) {
 }
 
 // Router inside prep (every token's cluster reads the whole router matrix)
-// unless that re-reads more than 32 MB (the environment variable
-// WISP_B200_PREP_ROUTER_BYTES overrides the limit); then the separate router
-// kernel, which reads it once for all tokens.
+// unless that re-reads more than 32 MB; then the separate router kernel,
+// which reads it once for all tokens.
 bool route_in_prep(const LayerArgs& a, int T) {
-    size_t limit = (size_t)32 << 20;
-    if (const char* v = getenv("WISP_B200_PREP_ROUTER_BYTES")) limit = strtoull(v, nullptr, 10);
-    return (size_t)T * a.E * a.H * 2 <= limit;
+    return (size_t)T * a.E * a.H * 2 <= ((size_t)32 << 20);
 }
 
 int plan_tokens(const LayerArgs& a, int T) { return T == 1 ? 1 : a.mt; }
@@ -1827,64 +1997,46 @@ cudaError_t launch_down(const LayerArgs& a, const Ws& W, cudaStream_t s) {
 }
 
 cudaError_t launch_gateup_any(int npg, int ng, int mt, const LayerArgs& a, const Ws& W,
-                          cudaStream_t s) {
+                              cudaStream_t s) {
     switch (mt * 1000 + npg * 100 + ng) {
         case 4101: return launch_gateup<1, 1, 4>(a, W, s);
-        case 8101: return launch_gateup<1, 1, 8>(a, W, s);
         case 4102: return launch_gateup<1, 2, 4>(a, W, s);
-        case 8102: return launch_gateup<1, 2, 8>(a, W, s);
         case 4104: return launch_gateup<1, 4, 4>(a, W, s);
-        case 8104: return launch_gateup<1, 4, 8>(a, W, s);
         case 4108: return launch_gateup<1, 8, 4>(a, W, s);
-        case 8108: return launch_gateup<1, 8, 8>(a, W, s);
         case 4116: return launch_gateup<1, 16, 4>(a, W, s);
         case 4201: return launch_gateup<2, 1, 4>(a, W, s);
-        case 8201: return launch_gateup<2, 1, 8>(a, W, s);
         case 4202: return launch_gateup<2, 2, 4>(a, W, s);
-        case 8202: return launch_gateup<2, 2, 8>(a, W, s);
         case 4204: return launch_gateup<2, 4, 4>(a, W, s);
-        case 8204: return launch_gateup<2, 4, 8>(a, W, s);
         case 4207: return launch_gateup<2, 7, 4>(a, W, s);
         case 4208: return launch_gateup<2, 8, 4>(a, W, s);
         case 4401: return launch_gateup<4, 1, 4>(a, W, s);
-        case 8401: return launch_gateup<4, 1, 8>(a, W, s);
         case 4402: return launch_gateup<4, 2, 4>(a, W, s);
-        case 8402: return launch_gateup<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
 
 cudaError_t launch_down_any(int npg, int ng, int mt, const LayerArgs& a, const Ws& W,
-                          cudaStream_t s) {
+                            cudaStream_t s) {
     switch (mt * 1000 + npg * 100 + ng) {
         case 4101: return launch_down<1, 1, 4>(a, W, s);
-        case 8101: return launch_down<1, 1, 8>(a, W, s);
         case 4102: return launch_down<1, 2, 4>(a, W, s);
-        case 8102: return launch_down<1, 2, 8>(a, W, s);
         case 4104: return launch_down<1, 4, 4>(a, W, s);
-        case 8104: return launch_down<1, 4, 8>(a, W, s);
         case 4108: return launch_down<1, 8, 4>(a, W, s);
-        case 8108: return launch_down<1, 8, 8>(a, W, s);
         case 4116: return launch_down<1, 16, 4>(a, W, s);
         case 4201: return launch_down<2, 1, 4>(a, W, s);
-        case 8201: return launch_down<2, 1, 8>(a, W, s);
         case 4202: return launch_down<2, 2, 4>(a, W, s);
-        case 8202: return launch_down<2, 2, 8>(a, W, s);
         case 4204: return launch_down<2, 4, 4>(a, W, s);
-        case 8204: return launch_down<2, 4, 8>(a, W, s);
         case 4207: return launch_down<2, 7, 4>(a, W, s);
         case 4208: return launch_down<2, 8, 4>(a, W, s);
         case 4401: return launch_down<4, 1, 4>(a, W, s);
-        case 8401: return launch_down<4, 1, 8>(a, W, s);
         case 4402: return launch_down<4, 2, 4>(a, W, s);
-        case 8402: return launch_down<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
 
 cudaError_t launch_streams(const LayerArgs& a, const Ws& W, int T, cudaStream_t s) {
-    (void)T;
     const int npg = a.gs / kChunk;
+    (void)T;
     cudaError_t e = launch_gateup_any(npg, ng_bucket(npg, a.H / a.gs), a.mt, a, W, s);
     if (e != cudaSuccess) return e;
     return launch_down_any(npg, ng_bucket(npg, a.I / a.gs / a.kp), a.mt, a, W, s);

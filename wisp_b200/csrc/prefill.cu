@@ -97,7 +97,6 @@ struct PArgs {
     const __half* router_bias;
     unsigned long long mat_off[3];  // packed_off of gate, up, down in a blob
     int H, I, E, K, has_shared;
-    int nt_gu;  // tokens per gate/up tile: 256 (2-SM kernel) or 128
     int gating; // WISP_GATING_* of the layer
 };
 
@@ -129,7 +128,7 @@ struct PWs {
 // dequantisers' TMEM-store wait and arrivals), so stages are as large as TMEM
 // allows: gate/up 2 groups (two matrices), down 4 groups when its K has a
 // multiple of 4 groups and the expert tiles are thin, else 2.  kKG is the
-// gate/up (and SM-pair) stage size.
+// gate/up stage size.
 constexpr int kKG = 2;
 template <int NMAT, int KG>
 struct GCfg;
@@ -610,9 +609,8 @@ route_topk_kernel(const float* __restrict__ lg, const __half* bias, int T, int E
     extern __shared__ float rs[];
     const int warp = threadIdx.x >> 5;
     float* sp = rs + (size_t)warp * 2 * E;
-    int* staken = reinterpret_cast<int*>(sp + E);
     for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
-        wisp_route::warp_topk(lg + (size_t)t * E, bias, E, K, sp, staken, idx + (size_t)t * K,
+        wisp_route::warp_topk(lg + (size_t)t * E, bias, E, K, sp, idx + (size_t)t * K,
                               w + (size_t)t * K, gating);
         __syncwarp();
     }
@@ -674,9 +672,8 @@ prefill_plan_kernel(PArgs P, PWs W, int T, const __grid_constant__ WTemplates tm
             s_tgu[e] = tg;
             s_tdn[e] = td;
             const int nt = (s_cnt[e] + kNT - 1) / kNT;
-            const int ntg = (s_cnt[e] + P.nt_gu - 1) / P.nt_gu;
             run += s_cnt[e];
-            tg += ntg * mt_gu;
+            tg += nt * mt_gu;
             td += nt * mt_dn;
         }
         s_seg[NE] = run;
@@ -726,12 +723,11 @@ prefill_plan_kernel(PArgs P, PWs W, int T, const __grid_constant__ WTemplates tm
             int e = lo;
             while (e + 1 < NE && base[e + 1] <= i) ++e;
             const int local = i - base[e], nt = local / mt_per;
-            const int ntk = pass ? kNT : P.nt_gu;  // tokens per tile of this list
             PTile tl;
             tl.e = e;
             tl.mt = local - nt * mt_per;
-            tl.row0 = s_seg[e] + nt * ntk;
-            tl.n = min(ntk, s_cnt[e] - nt * ntk);
+            tl.row0 = s_seg[e] + nt * kNT;
+            tl.n = min(kNT, s_cnt[e] - nt * kNT);
             out[i] = tl;
         }
     }
@@ -1130,408 +1126,6 @@ grouped_gemm_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm, float* __r
 }
 
 // ------------------------------------------------------------------------
-// gate/up on SM pairs (tcgen05.mma.cta_group::2)
-//
-// A cluster of two CTAs handles 128 features x up to 256 tokens of one expert:
-// CTA 0 holds the 128 gate rows and CTA 1 the 128 up rows of those features
-// (M = 256 per MMA), each dequantising only its matrix into its own TMEM;
-// each loads half of the token rows (B is split by N across the pair).  The
-// leader (rank 0) issues kind::f16 MMAs with A from TMEM and N up to 256, so
-// one instruction covers both SMs: half the MMA issue and half the
-// dequantisation per SM of the one-CTA kernel.  Its commits are multicast to
-// both CTAs; the peer's dequant warps and a relay of its activation copies
-// arrive on the leader's barriers remotely.  D_gate lives in CTA 0 and D_up in
-// CTA 1, so for SwiGLU each CTA sends the accumulator columns of the other
-// half of the tokens to the peer's shared memory and finishes its own half.
-// ------------------------------------------------------------------------
-constexpr int kNT2 = 256;                // tokens per tile of the pair
-constexpr int kWS2 = 6, kBS2 = 3, kS2 = 4;
-constexpr size_t kX2 = (size_t)128 * 128 * 4;  // exchange buffer: 128 rows x 128 columns
-constexpr size_t kGemm2Smem = 1024 + (size_t)kBS2 * kKG * kBTile + (size_t)kWS2 * kKG * kWStage +
-                              kX2 + 1024;
-
-__device__ __forceinline__ uint32_t cta_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-// arrive on the barrier at `local`'s offset in CTA `rank` of the cluster
-__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     peer_addr(saddr(bar), rank))
-                 : "memory");
-}
-// The same with the default (.release.cta) semantics, the form CUTLASS's
-// ClusterBarrier::arrive(cta_id) issues: the cheap per-stage signal of the pipeline
-// rings (TMEM writes are ordered by tcgen05.fence::before_thread_sync before it).
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t rank) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(peer_addr(saddr(bar), rank))
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_cluster(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(saddr(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// bounded waits (one thread / whole warp) on barriers other CTAs arrive on
-__device__ bool wait1_cl(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* status) {
-    uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_cluster(b, parity)) return true;
-        if ((it & 63) == 63) {
-            if (*abort_flag) return false;
-            const uint64_t t = gtimer();
-            if (t0 == 0) {
-                t0 = t;
-            } else if (t - t0 > kWaitNs) {
-                *abort_flag = 1;
-                atomicOr(status, ST_TIMEOUT);
-                return false;
-            }
-        }
-    }
-}
-__device__ bool wait_warp_cl(uint64_t* b, uint32_t parity, volatile int* abort_flag,
-                             int* status) {
-    const int lane = threadIdx.x & 31;
-    uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        if (__all_sync(kFull, mbar_try_cluster(b, parity))) return true;
-        if ((it & 15) == 15) {
-            __nanosleep(64);
-            int stop = 0;
-            if (lane == 0) {
-                if (*abort_flag) {
-                    stop = 1;
-                } else {
-                    const uint64_t t = gtimer();
-                    if (t0 == 0) {
-                        t0 = t;
-                    } else if (t - t0 > kWaitNs) {
-                        *abort_flag = 1;
-                        atomicOr(status, ST_TIMEOUT);
-                        stop = 1;
-                    }
-                }
-            }
-            if (__shfl_sync(kFull, stop, 0)) return false;
-        }
-    }
-}
-__device__ __forceinline__ void mma_commit_mc(uint64_t* bar) {  // both CTAs of the pair
-    asm volatile(
-        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], m;\n\t}" ::"r"(saddr(bar))
-        : "memory");
-}
-__device__ __forceinline__ void mma_ts2(uint32_t d, uint32_t a, uint64_t b, uint32_t id,
-                                        uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5},"
-        " p;\n\t}" ::"r"(d),
-        "r"(a), "l"(b), "r"(id), "r"(acc), "r"(0u)
-        : "memory");
-}
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-                 ::: "memory");
-}
-
-__global__ void __launch_bounds__(kGemmThreads, 1)
-gateup2_kernel(PArgs P, PWs W, const __grid_constant__ BMaps bm) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~(uintptr_t)1023);
-    uint8_t* sB = base;                                   // [kBS2][kKG][kBTile]
-    uint8_t* sW = sB + kBS2 * kKG * kBTile;               // [kWS2][kKG * kWStage]
-    float* xbuf = reinterpret_cast<float*>(sW + kWS2 * kKG * kWStage);  // [128 col][128 row]
-    uint64_t* w_full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + kX2);
-    uint64_t* w_empty = w_full + kWS2;
-    uint64_t* a_full = w_empty + kWS2;   // leader: 16 local + 16 peer dequant warps
-    uint64_t* a_empty = a_full + kS2;    // multicast commit
-    uint64_t* b_full = a_empty + kS2;    // local TMA
-    uint64_t* b_peer = b_full + kBS2;    // leader: the peer's half landed (relay)
-    uint64_t* b_empty = b_peer + kBS2;   // multicast commit
-    uint64_t* acc_full = b_empty + kBS2; // multicast commit
-    uint64_t* acc_empty = acc_full + 1;  // leader: 4 local + 4 peer epilogue warps
-    uint64_t* x_full = acc_empty + 1;    // the peer wrote my exchange buffer
-    uint64_t* x_free = x_full + 1;       // the peer consumed its exchange buffer
-    uint64_t* drain = x_free + 1;
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
-    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t rank = cta_rank(), peer = rank ^ 1u;
-    const bool leader = rank == 0;
-    if (tid == 0) {
-        for (int i = 0; i < kWS2; ++i) {
-            mbar_init(&w_full[i], 1);
-            mbar_init(&w_empty[i], kDqWarps);
-        }
-        for (int i = 0; i < kS2; ++i) {
-            mbar_init(&a_full[i], 2 * kDqWarps);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < kBS2; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_peer[i], 1);
-            mbar_init(&b_empty[i], 1);
-        }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 8);
-        mbar_init(x_full, 4);
-        mbar_init(x_free, 4);
-        mbar_init(drain, 1);
-        *s_abort = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
-                         saddr(s_tmem))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
-    tc_fence_after();
-    const uint32_t tmem = *s_tmem;
-    pdl_wait();
-    pdl_launch();
-    const int ntiles = __ldcg(W.counters + 0);
-    const int nclusters = gridDim.x / 2, cid = blockIdx.x / 2;
-    const int KS = P.H / (kBK * kKG);
-    int* status = W.status;
-
-    if (warp == kWProdWarp) {
-        if (lane == 0) {
-            uint32_t wi = 0;
-            bool ok = true;
-            for (int t = cid; ok && t < ntiles; t += nclusters) {
-                const PTile tl = tiles_at(W.tiles_gu, t);
-                const CUtensorMap* mc = W.wmaps + tl.e * kMaps + rank * 2;  // gate or up
-                tmap_acquire(mc);
-                tmap_acquire(mc + 1);
-                for (int ks = 0; ks < KS; ++ks, ++wi) {
-                    const int s = wi % kWS2;
-                    if (!wait1_lazy(&w_empty[s], ((wi / kWS2) & 1) ^ 1, s_abort, status)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(&w_full[s], kKG * kWStage);
-                    uint8_t* dst = sW + s * kKG * kWStage;
-                    tma3d(dst, mc, 0, ks * kKG, tl.mt * 16, &w_full[s]);
-                    tma3d(dst + kKG * kWCodes, mc + 1, 0, ks * kKG, tl.mt * 16, &w_full[s]);
-                }
-            }
-            const uint32_t first = wi > (uint32_t)kWS2 ? wi - kWS2 : 0;
-            for (uint32_t i = first; i < wi; ++i) wait_drain(&w_full[i % kWS2], (i / kWS2) & 1);
-        }
-    } else if (warp == kBProdWarp) {
-        if (lane == 0) {
-            uint32_t bi = 0;
-            bool ok = true;
-            for (int t = cid; ok && t < ntiles; t += nclusters) {
-                const PTile tl = tiles_at(W.tiles_gu, t);
-                const int nmma = (tl.n + 31) & ~31, nh = nmma / 2;
-                const int r0 = tl.row0 + (int)rank * nh;  // this CTA's half of the tokens
-                for (int ks = 0; ks < KS; ++ks, ++bi) {
-                    const int s = bi % kBS2;
-                    if (!wait1_lazy(&b_empty[s], ((bi / kBS2) & 1) ^ 1, s_abort, status)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(&b_full[s], (uint32_t)(kKG * nh * 128));
-#pragma unroll
-                    for (int g = 0; g < kKG; ++g) {
-                        int off = 0;
-#pragma unroll
-                        for (int i = kBoxes - 1; i >= 0; --i) {
-                            const int h = 16 << i;
-                            if ((nh - off) >= h) {
-                                tma2d(sB + (s * kKG + g) * kBTile + off * 128, &bm.box[i],
-                                      (ks * kKG + g) * kBK, r0 + off, &b_full[s]);
-                                off += h;
-                            }
-                        }
-                    }
-                }
-            }
-            const uint32_t first = bi > (uint32_t)kBS2 ? bi - kBS2 : 0;
-            for (uint32_t i = first; i < bi; ++i) wait_drain(&b_full[i % kBS2], (i / kBS2) & 1);
-        }
-    } else if (warp == kMmaWarp) {
-        if (lane == 0 && leader) {
-            uint32_t si = 0, ci = 0;
-            bool ok = true;
-            const uint64_t bdesc0 = sdesc(saddr(sB));
-            for (int t = cid; ok && t < ntiles; t += nclusters, ++ci) {
-                const PTile tl = tiles_at(W.tiles_gu, t);
-                const int nmma = (tl.n + 31) & ~31;
-                const uint32_t id = (1u << 4) | ((uint32_t)(nmma >> 3) << 17) | (16u << 24);
-                if (!wait1_cl(acc_empty, (ci & 1) ^ 1, s_abort, status)) break;
-                tc_fence_after();
-                for (int ks = 0; ks < KS; ++ks, ++si) {
-                    const int sa = si % kS2, sb = si % kBS2;
-                    if (!wait1(&a_full[sa], (si / kS2) & 1, s_abort, status) ||
-                        !wait1(&b_full[sb], (si / kBS2) & 1, s_abort, status) ||
-                        !wait1(&b_peer[sb], (si / kBS2) & 1, s_abort, status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t bd = bdesc0 + (uint64_t)(sb * kKG * (kBTile >> 4));
-                    const uint32_t at = tmem + kAcol0 + (uint32_t)(sa * kKG * 32);
-#pragma unroll
-                    for (int g = 0; g < kKG; ++g)
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            mma_ts2(tmem, at + (uint32_t)(g * 32 + k * 8),
-                                    bd + (uint64_t)(g * (kBTile >> 4) + 2 * k), id,
-                                    (ks | g | k) ? 1u : 0u);
-                    mma_commit_mc(&a_empty[sa]);
-                    mma_commit_mc(&b_empty[sb]);
-                }
-                if (ok) mma_commit_mc(acc_full);
-            }
-            mma_commit_mc(drain);
-            wait_drain(drain, 0);
-        } else if (lane == 0) {
-            // peer: relay the completion of this CTA's activation copies to the leader
-            uint32_t bi = 0;
-            bool ok = true;
-            for (int t = cid; ok && t < ntiles; t += nclusters)
-                for (int ks = 0; ks < KS; ++ks, ++bi) {
-                    if (!wait1(&b_full[bi % kBS2], (bi / kBS2) & 1, s_abort, status)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_remote(&b_peer[bi % kBS2], 0);
-                }
-        }
-    } else if (warp < 4) {
-        // epilogue: warp q owns TMEM lanes 32q..32q+31 = features of the tile
-        const int q = warp, row = q * 32 + lane;
-        const uint32_t xpeer = peer_addr(saddr(xbuf), peer);
-        uint32_t ci = 0;
-        for (int t = cid; t < ntiles; t += nclusters, ++ci) {
-            const PTile tl = tiles_at(W.tiles_gu, t);
-            const int nmma = (tl.n + 31) & ~31, nh = nmma / 2;
-            if (!wait_warp_lazy(acc_full, ci & 1, s_abort, status)) break;
-            tc_fence_after();
-            const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-            // 1. the columns the peer finishes: rank 0 sends gate [nh, nmma), rank 1 up [0, nh)
-            if (!wait_warp_cl(x_free, (ci & 1) ^ 1, s_abort, status)) break;
-            const int sb0 = leader ? nh : 0;
-            for (int c = 0; c < nh; c += 16) {
-                float v[16];
-                tmem_ld16(lane_base + sb0 + c, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    st_cluster_f32(xpeer + (uint32_t)(((c + j) * 128 + row) * 4), v[j]);
-            }
-            asm volatile("fence.acq_rel.cluster;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(x_full, peer);
-            // 2. this CTA's half: own accumulator + the peer's values
-            if (!wait_warp_cl(x_full, ci & 1, s_abort, status)) break;
-            const int mb0 = leader ? 0 : nh;
-            const int f = tl.mt * kBM + row;
-            const int fp = kperm(f);
-            for (int c = 0; c < nh; c += 16) {
-                float v[16];
-                tmem_ld16(lane_base + mb0 + c, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = mb0 + c + j;
-                    if (col < tl.n) {
-                        const float o = xbuf[(c + j) * 128 + row];
-                        const float g = leader ? v[j] : o, u = leader ? o : v[j];
-                        const float h = g / (1.0f + expf(-g)) * u;
-                        W.hs[(size_t)(tl.row0 + col) * P.I + fp] = __float2half_rn(h);
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(x_free, peer);  // my buffer may be refilled
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc_empty, 0);
-        }
-    } else {
-        // dequantisers: one matrix per CTA; warp (part, q): TMEM lanes 32q.. (weight
-        // rows), quarter `part` of each group (8 columns)
-        const int dw = warp - kDqWarp0, q = warp & 3, part = dw >> 2;
-        const int r = q * 32 + lane;
-        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + kAcol0 + (uint32_t)(part * 8);
-        const int cw0 = ((r >> 3) * kKG) * 64 + (r & 7) * 8 + part * 2;
-        const int sw0 = kKG * kWCodes / 4 + ((r >> 3) * kKG) * 8 + (r & 7);
-        uint32_t wi = 0, ai = 0;
-        bool ok = true;
-        for (int t = cid; ok && t < ntiles; t += nclusters) {
-            for (int ks = 0; ks < KS; ++ks, ++wi, ++ai) {
-                const int ws = wi % kWS2, as = ai % kS2;
-                if (!wait_warp(&w_full[ws], (wi / kWS2) & 1, s_abort, status) ||
-                    !wait_warp(&a_empty[as], ((ai / kS2) & 1) ^ 1, s_abort, status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t* st = reinterpret_cast<const uint32_t*>(sW + ws * kKG * kWStage);
-#pragma unroll
-                for (int g = 0; g < kKG; ++g) {
-                    const uint32_t szw = st[sw0 + g * 8];
-                    const __half2 s2 =
-                        __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFFu)));
-                    const __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
-                    const uint2 c2 = *reinterpret_cast<const uint2*>(st + cw0 + g * 64);
-                    uint32_t o[8];
-                    dequant_cols(c2.x, s2, z2, o);
-                    dequant_cols(c2.y, s2, z2, o + 4);
-                    tmem_st8(lane_addr + (uint32_t)((as * kKG + g) * 32), o);
-                }
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    if (leader)
-                        mbar_arrive(&a_full[as]);
-                    else
-                        mbar_arrive_remote(&a_full[as], 0);
-                    mbar_arrive(&w_empty[ws]);
-                }
-            }
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    cluster_sync_all();  // no MMA, copy or remote access of the pair is left
-    if (warp == kMmaWarp) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem)
-                     : "memory");
-    }
-}
-
-// ------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -1673,19 +1267,8 @@ WispError check_prefill_layer(const WispMoeLayer* l, int T, WispErrCtx* err, boo
     return WISP_OK;
 }
 
-// gate/up on SM pairs (gateup2_kernel) unless WISP_B200_PREFILL_2SM=0
-// The gate/up GEMM on SM pairs (gateup2_kernel) instead of one CTA per tile: opt-in
-// with WISP_B200_PREFILL_2SM=1, read at every call.  The pair form is correct but
-// slower at every measured size (its cta_group::2 MMAs issue at about 94-100 cycles
-// each against 45-64 for the one-CTA form at the same N).
-bool use_pairs() {
-    const char* v = getenv("WISP_B200_PREFILL_2SM");
-    return v && atoi(v) != 0;
-}
-
 PArgs make_pargs(const WispMoeLayer* l) {
     PArgs P;
-    P.nt_gu = use_pairs() ? kNT2 : kNT;
     P.blobs = l->expert_blobs;
     P.shared_blob = l->shared_blob;
     P.router_w = static_cast<const __half*>(l->router_w);
@@ -1768,9 +1351,6 @@ cudaError_t ensure_gemm_attrs() {
             r = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kRouterSmem);
         if (r == cudaSuccess)
-            r = cudaFuncSetAttribute(gateup2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kGemm2Smem);
-        if (r == cudaSuccess)
             r = cudaFuncSetAttribute(route_topk_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 1024 * 4);
         return r;
@@ -1821,15 +1401,10 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     // DeepSeek layer, 4 groups take -4.3% at 18 rows per expert (512 tokens) and
     // -3.3% at 36 (1024), +0.5% at 143 (4096), and +3.7% in a 32-expert layer at
     // 280 rows (ncu), where the shallower activation ring shows.
-    // WISP_B200_PREFILL_DOWN_KG=2 / =4 chooses.
     const int nexp = P.E + (P.has_shared ? 1 : 0);
     const long long rows_per_expert = (long long)T * (P.K + (P.has_shared ? 1 : 0)) / nexp;
     const bool kg4_ok = (P.I / 64) % 4 == 0;
     int kg_down = kg4_ok && rows_per_expert <= 96 ? 4 : 2;
-    if (const char* v = getenv("WISP_B200_PREFILL_DOWN_KG")) {
-        if (atoi(v) == 2) kg_down = 2;
-        if (atoi(v) == 4 && kg4_ok) kg_down = 4;
-    }
     if (!weight_templates(P, layer->meta, W.xs, &wt, kg_down) || !row_maps(W.xs, L.R, P.H, &bx) ||
         !row_maps(W.hs, L.R, P.I, &bh)) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed or unavailable");
@@ -1886,14 +1461,9 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     WB_CUDA_RET(wb::launch_pdl(prefill_scatter_kernel, dim3(T), dim3(256), 0, stream, P, W, T, x,
                                y),
                 err);
-    if (P.nt_gu == kNT2)
-        WB_CUDA_RET(wb::launch_pdl_cluster(gateup2_kernel, dim3(2 * (sms / 2)), dim3(kGemmThreads),
-                                           kGemm2Smem, stream, 2, P, W, bx),
-                    err);
-    else
-        WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<2, 2>, dim3(sms), dim3(kGemmThreads),
-                                   gemm_smem_bytes<2, 2>(), stream, P, W, bx, y),
-                    err);
+    WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<2, 2>, dim3(sms), dim3(kGemmThreads),
+                               gemm_smem_bytes<2, 2>(), stream, P, W, bx, y),
+                err);
     if (kg_down == 4)
         WB_CUDA_RET(wb::launch_pdl(grouped_gemm_kernel<1, 4>, dim3(sms), dim3(kGemmThreads),
                                    gemm_smem_bytes<1, 4>(), stream, P, W, bh, y),

@@ -31,29 +31,41 @@ constexpr int kGatingSigmoid = 1;
 
 __device__ __forceinline__ float sigmoid_score(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// One token by one warp.  lg[E]: logits without the bias; sp/staken: [E]
-// scratch of this warp (shared memory).  Lane 0 writes out_idx[K] / out_w[K]
-// (-1 / 0 for a slot no expert could fill).  K <= 64.
-__device__ inline void warp_topk(const float* lg, const __half* bias, int E, int K, float* sp,
-                                 int* staken, int* out_idx, float* out_w,
-                                 int gating = kGatingSoftmax) {
+// Result of warp_topk held by each lane: the selections of slots `lane` and
+// `lane + 32` (index -1 and weight 0 for a slot no expert could fill, or
+// past K), weights already normalised.
+struct TopkLane {
+    int i0, i1;
+    float w0, w1;
+};
+
+__device__ __forceinline__ float bias_at(const __half* b, int e) { return __half2float(b[e]); }
+__device__ __forceinline__ float bias_at(const float* b, int e) { return b[e]; }
+
+// One token by one warp.  lg[E]: logits without the bias; bias: [E] fp16 or
+// fp32 (NULL: none); sp: [E] scratch of this warp (shared memory).  The
+// selected experts are tracked in a per-lane bit mask (element lane + 32 i
+// is bit i, so E <= 1024) and each slot's result stays in the registers of
+// lane slot % 32, so no per-thread arrays are needed.  When out_idx is not
+// NULL the lanes write out_idx[K] / out_w[K].  K <= 64.
+template <typename BiasT>
+__device__ inline TopkLane warp_topk(const float* lg, const BiasT* bias, int E, int K, float* sp,
+                                     int* out_idx, float* out_w, int gating = kGatingSoftmax) {
     const int lane = threadIdx.x & 31;
     const bool sig = gating == kGatingSigmoid;
     if (sig) {
         // selection scores; the weights come from the scores without the bias
         for (int e = lane; e < E; e += 32) {
             float v = sigmoid_score(lg[e]);
-            if (bias) v += __half2float(bias[e]);
+            if (bias) v += bias_at(bias, e);
             sp[e] = v;
-            staken[e] = 0;
         }
     } else {
         float mx = -1e30f;
         for (int e = lane; e < E; e += 32) {
             float v = lg[e];
-            if (bias) v += __half2float(bias[e]);
+            if (bias) v += bias_at(bias, e);
             sp[e] = v;
-            staken[e] = 0;
             mx = fmaxf(mx, v);
         }
         mx = warp_max(mx);
@@ -67,15 +79,16 @@ __device__ inline void warp_topk(const float* lg, const __half* bias, int E, int
         for (int e = lane; e < E; e += 32) sp[e] = sp[e] / den;
     }
     __syncwarp();
+    uint32_t taken = 0u;
     float wsum = 0.f;
-    float wsel[64];
-    int isel[64];
+    TopkLane r{-1, -1, 0.f, 0.f};
     for (int j = 0; j < K; ++j) {
         float bv = sig ? -INFINITY : -1.f;
         int be = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
+        int i = 0;
+        for (int e = lane; e < E; e += 32, ++i) {
             const float v = sp[e];
-            if (!staken[e] && v > bv) {
+            if (!((taken >> i) & 1u) && v > bv) {
                 bv = v;
                 be = e;
             }
@@ -91,21 +104,34 @@ __device__ inline void warp_topk(const float* lg, const __half* bias, int E, int
             }
         }
         if (sig ? be == 0x7fffffff : bv < 0.f) be = -1;
-        if (lane == 0 && be >= 0) staken[be] = 1;
-        __syncwarp();
+        if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
         const float wv = sig ? (be >= 0 ? sigmoid_score(lg[be]) : 0.f) : bv;
-        wsel[j] = wv;
-        isel[j] = be;
-        if (be >= 0) wsum += wv;
+        if (j == lane) {
+            r.i0 = be;
+            r.w0 = wv;
+        } else if (j == lane + 32) {
+            r.i1 = be;
+            r.w1 = wv;
+        }
+        if (be >= 0) wsum += wv;  // every lane holds the same sum, in slot order
     }
-    if (lane == 0) {
-        for (int j = 0; j < K; ++j) {
-            float wj = isel[j] >= 0 ? wsel[j] : 0.f;
-            if (wsum > 0.f) wj = wj / wsum;
-            out_idx[j] = isel[j];
-            out_w[j] = wj;
+    r.w0 = r.i0 >= 0 ? r.w0 : 0.f;
+    r.w1 = r.i1 >= 0 ? r.w1 : 0.f;
+    if (wsum > 0.f) {
+        r.w0 = r.w0 / wsum;
+        r.w1 = r.w1 / wsum;
+    }
+    if (out_idx) {
+        if (lane < K) {
+            out_idx[lane] = r.i0;
+            out_w[lane] = r.w0;
+        }
+        if (lane + 32 < K) {
+            out_idx[lane + 32] = r.i1;
+            out_w[lane + 32] = r.w1;
         }
     }
+    return r;
 }
 
 }  // namespace wisp_route
