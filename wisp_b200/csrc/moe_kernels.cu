@@ -131,6 +131,13 @@ __device__ __forceinline__ void pdl_wait() {
 __device__ __forceinline__ void pdl_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Split cluster barrier (all threads of every CTA of the cluster).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
@@ -406,11 +413,11 @@ __device__ void plan_one_token(const LayerArgs& L, const Ws& W, const wisp_route
 enum { P_COMBINE = 1, P_RESID = 2, P_NORM = 4, P_QUANT = 8, P_ROUTE = 16 };
 constexpr int kPrepThreads = 256;
 
-// Shared memory of prep: the row slice, partial logits, the top-k / plan
-// scratch, then (8-byte aligned) the probed blob pointers and check codes
-// [E + 1] and the bias as floats [E].
+// Shared memory of prep: the row slice, the cluster's partial logits [cs][E]
+// (gathered in rank 0), the top-k / plan scratch, then (8-byte aligned) the
+// probed blob pointers and check codes [E + 1] and the bias as floats [E].
 __host__ __device__ inline size_t prep_tail_off(int H, int cs, int E) {
-    const size_t o = (size_t)(H / cs) * sizeof(float) + (size_t)E * sizeof(float) +
+    const size_t o = (size_t)(H / cs) * sizeof(float) + (size_t)cs * E * sizeof(float) +
                      (size_t)(kMaxPlanAssign + 64 > 3 * E ? kMaxPlanAssign + 64 : 3 * E) * sizeof(int);
     return (o + 7) & ~size_t(7);
 }
@@ -433,8 +440,8 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     constexpr int nw = kPrepThreads / 32;
     extern __shared__ float4 smem4[];
     float4* sx4 = smem4;                                // [n4] the slice
-    float* s_lg = reinterpret_cast<float*>(sx4 + n4);  // [E] partial router logits
-    int* s_scr = reinterpret_cast<int*>(s_lg + E);      // top-k / plan scratch (rank 0)
+    float* s_lg = reinterpret_cast<float*>(sx4 + n4);  // [cs][E] partial logits (rank 0)
+    int* s_scr = reinterpret_cast<int*>(s_lg + cs * E); // top-k / plan scratch (rank 0)
     unsigned char* tail = reinterpret_cast<unsigned char*>(smem4) + prep_tail_off(H, cs, E);
     const unsigned char** s_blob = reinterpret_cast<const unsigned char**>(tail);  // [E + 1]
     int* s_bcode = reinterpret_cast<int*>(s_blob + E + 1);                          // [E + 1]
@@ -468,13 +475,20 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     if ((flags & P_NORM) && L.norm_w && tid < n4)
         nwv = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half2*>(L.norm_w) +
                                               2 * (i0 + tid));
+    // Partial sums are pushed into the shared memory of the CTAs that read them
+    // (distributed shared memory stores) before a cluster barrier, so no CTA
+    // reads a peer's memory and none has to wait for its peers to finish
+    // reading; the first remote store waits for this arrival of every CTA of
+    // the cluster, i.e. for all of them to have started.
+    const bool remote = cs > 1 && (flags & (P_NORM | P_ROUTE));
+    if (remote) cluster_arrive_relaxed();
     pdl_wait();
 #pragma unroll
     for (int i = 0; i < kProbeSlots; ++i)
         phdr[i] = pb[i] ? ld_early_u32(reinterpret_cast<const uint32_t*>(pb[i]) + 1) : 0u;
     pdl_launch();
     __shared__ float red[nw];
-    __shared__ float s_ss;
+    __shared__ float s_ssv[8];  // partial sums of squares of the cluster, by rank
     __shared__ int s_last;
     float4* xt = reinterpret_cast<float4*>(x + (size_t)t * H) + i0;
 
@@ -485,27 +499,40 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
         if (flags & P_COMBINE) {
             // reference order: shared expert first (weight 1), then top-k order
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            // every part of an assignment is loaded before they are summed
+            // (in part order)
+            float4 yp[kMaxKp];
             if (prev_shared) {
                 // int4 shared expert: one ypart per down K part; fp16-dense: part 0
                 const size_t a = (size_t)T * prevK + t;
                 const int np = prev_shared == 2 ? 1 : prev_kp;
-                for (int p = 0; p < np; ++p) {
-                    const float4 yv = reinterpret_cast<const float4*>(
-                        W.ypart + p * part_stride + a * H)[i0 + i];
-                    acc.x += yv.x; acc.y += yv.y; acc.z += yv.z; acc.w += yv.w;
-                }
+#pragma unroll
+                for (int p = 0; p < kMaxKp; ++p)
+                    if (p < np)
+                        yp[p] = reinterpret_cast<const float4*>(W.ypart + p * part_stride +
+                                                                a * H)[i0 + i];
+#pragma unroll
+                for (int p = 0; p < kMaxKp; ++p)
+                    if (p < np) {
+                        acc.x += yp[p].x; acc.y += yp[p].y; acc.z += yp[p].z; acc.w += yp[p].w;
+                    }
             }
             for (int j = 0; j < prevK; ++j) {
                 // loads do not wait for the routing; an unrouted slot is skipped by a select
                 const bool live = __ldg(W.prev_idx + t * prevK + j) >= 0;
                 const float wj = __ldg(W.prev_w + t * prevK + j);
                 const size_t a = (size_t)t * prevK + j;
-                float4 yj = reinterpret_cast<const float4*>(W.ypart + a * H)[i0 + i];
-                for (int p = 1; p < prev_kp; ++p) {
-                    const float4 yv = reinterpret_cast<const float4*>(
-                        W.ypart + p * part_stride + a * H)[i0 + i];
-                    yj.x += yv.x; yj.y += yv.y; yj.z += yv.z; yj.w += yv.w;
-                }
+#pragma unroll
+                for (int p = 0; p < kMaxKp; ++p)
+                    if (p < prev_kp)
+                        yp[p] = reinterpret_cast<const float4*>(W.ypart + p * part_stride +
+                                                                a * H)[i0 + i];
+                float4 yj = yp[0];
+#pragma unroll
+                for (int p = 1; p < kMaxKp; ++p)
+                    if (p < prev_kp) {
+                        yj.x += yp[p].x; yj.y += yp[p].y; yj.z += yp[p].z; yj.w += yp[p].w;
+                    }
                 if (live) {
                     acc.x += wj * yj.x; acc.y += wj * yj.y; acc.z += wj * yj.z; acc.w += wj * yj.w;
                 }
@@ -526,14 +553,15 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
-        if (tid == 0) {
+        if (remote) cluster_wait();  // peers started (the arrival at entry)
+        if (tid < cs) {
             float v = 0.f;
             for (int w = 0; w < nw; ++w) v += red[w];
-            s_ss = v;
+            *cl.map_shared_rank(&s_ssv[rank], tid) = v;  // into CTA tid's copy
         }
-        cl.sync();  // every CTA's partial sum of squares is in place
+        cl.sync();  // every CTA holds every partial sum of squares
         float tot = 0.f;
-        for (int r = 0; r < cs; ++r) tot += *cl.map_shared_rank(&s_ss, r);
+        for (int r = 0; r < cs; ++r) tot += s_ssv[r];
         const float sc = 1.0f / sqrtf(tot / (float)H + eps);
         float4* xn = reinterpret_cast<float4*>(W.xn + (size_t)t * H) + i0;
         const __half2* nw2 = reinterpret_cast<const __half2*>(L.norm_w) + 2 * i0;
@@ -557,6 +585,7 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
                      W.xq + ((size_t)t * (H / kChunk) + (size_t)i0 * 4 / kChunk) * 4,
                      W.xqp + (size_t)t * (H / L.gs) + (size_t)i0 * 4 / L.gs);
     if (flags & P_ROUTE) {
+        if (remote && !(flags & P_NORM)) cluster_wait();  // peers started
         // partial logits of this slice: warp per expert
         const uint4* wr = reinterpret_cast<const uint4*>(L.router_w);
         for (int e = warp; e < E; e += nw) {
@@ -578,17 +607,16 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
                 acc = fmaf(f.x, b.z, acc); acc = fmaf(f.y, b.w, acc);
             }
             acc = warp_sum(acc);
-            if (lane == 0) s_lg[e] = acc;
+            if (lane == 0) *cl.map_shared_rank(&s_lg[rank * E + e], 0) = acc;  // to rank 0
         }
-        cl.sync();  // every CTA's partial logits are in place
+        cl.sync();  // rank 0 holds every CTA's partial logits; the others may leave
         if (rank == 0)
             for (int e = tid; e < E; e += kPrepThreads) {
                 float v = 0.f;
-                for (int r = 0; r < cs; ++r) v += cl.map_shared_rank(s_lg, r)[e];
+                for (int r = 0; r < cs; ++r) v += s_lg[r * E + e];
                 s_scr[2 * E + e] = __float_as_int(v);
             }
     }
-    if (cs > 1 && (flags & (P_NORM | P_ROUTE))) cl.sync();  // peers read; CTAs may leave
     if (!(flags & P_ROUTE) || rank != 0) return;
     if (planner) {
 #pragma unroll
@@ -1927,7 +1955,8 @@ cudaError_t ensure_attrs(int H) {
     if (done[dev & 63]) return cudaSuccess;
     (void)H;
     cudaError_t e = cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)prep_smem_bytes(kMaxHidden, 1, 1024));
+                                         (int)std::max(prep_smem_bytes(kMaxHidden, 1, 1024),
+                                                       prep_smem_bytes(kMaxHidden, 8, 1024)));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)router_smem(1024));

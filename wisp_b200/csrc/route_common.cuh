@@ -17,10 +17,17 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kAll, v, o);
     return v;
 }
+// Order-preserving map of floats to unsigned integers (and back), so a
+// single redux.sync finds a warp maximum.
+__device__ __forceinline__ uint32_t float_key(float v) {
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 __device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kAll, v, o));
-    return v;
+    return key_float(__reduce_max_sync(kAll, float_key(v)));
 }
 
 // Gating rules (WispMoeLayer.gating): 0 the reference's softmax(+bias); 1
@@ -93,16 +100,12 @@ __device__ inline TopkLane warp_topk(const float* lg, const BiasT* bias, int E, 
                 be = e;
             }
         }
-        // warp argmax: larger value wins, equal values -> lower index
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(kAll, bv, o);
-            const int oe = __shfl_xor_sync(kAll, be, o);
-            if (ov > bv || (ov == bv && oe < be)) {
-                bv = ov;
-                be = oe;
-            }
-        }
+        // warp argmax: the largest value (one redux over an order-preserving
+        // integer image of the floats), and among the lanes holding it the
+        // lowest expert index (a second redux) -- the strict '>' rule
+        const uint32_t key = float_key(bv), kmax = __reduce_max_sync(kAll, key);
+        be = (int)__reduce_min_sync(kAll, key == kmax ? (uint32_t)be : 0x7fffffffu);
+        bv = key_float(kmax);
         if (sig ? be == 0x7fffffff : bv < 0.f) be = -1;
         if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
         const float wv = sig ? (be >= 0 ? sigmoid_score(lg[be]) : 0.f) : bv;
