@@ -6,13 +6,15 @@ RMSNorm and the residual between blocks; attention = identity).  Seeded syntheti
 weights (N(0, 0.02), quantised by the reference quantiser's rule) and inputs (fp16
 N(0,1) upcast to fp32), generated on the GPU.
 
-N = 1: the whole stack on one GPU, one CUDA graph per step.
+N = 1: the whole stack on one GPU, one CUDA graph per step, the global batch of 16
+tokens in one pass (the configuration's 4-micro-batch schedule on one GPU, which only
+serialises, is reported beside it as `pipeline_4mb`).
 N > 1 (torchrun): layer pipeline -- rank r owns layers [32r/N, 32(r+1)/N); the global
-batch (16 tokens per GPU) is split into N micro-batches of 16 tokens that flow rank to
-rank with NCCL send/recv (torch.distributed), and the last rank hands each micro-batch
-back to rank 0 for the next decode step.  Decode streams the routed experts' weights
-once per micro-batch, so micro-batches are as large as keeping every stage busy allows
-(M = N).  Per-GPU work is fixed, so scaling is weak: global batch = 16 * N.
+batch of 16 tokens is split into the configuration's 4 micro-batches of 4 that flow
+rank to rank with NCCL send/recv (torch.distributed), and the last rank hands each
+micro-batch back to rank 0 for the next decode step.  Total work is fixed, so the
+scaling is strong; the weak-scaling ring (16 tokens per GPU, N micro-batches of 16) is
+reported beside it as `weak_scaling`.
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference engine's own
 CPU run_moe (oracle/_ref, built from the reference sources) on a bounded sample of the
@@ -47,10 +49,10 @@ def parse():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--batch", type=int, default=16, help="tokens per decode step per GPU")
+    p.add_argument("--batch", type=int, default=16, help="global batch of a decode step")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--micro", type=int, default=0,
-                   help="tokens per pipeline micro-batch (default: the per-GPU batch)")
+                   help="tokens per pipeline micro-batch (default: a quarter of the batch)")
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--skip-extra", action="store_true", help="no per-batch / e2e / profile legs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -466,13 +468,14 @@ def main_ours(args):
     line = {
         "metric": METRIC, "value": round(r["value"], 2), "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4xf32",
         "precision": "int4 weights with fp16 scale/zero per 64; activations entered as two "
                      "int8 digits per quant group (|error| <= 1.6e-5 * max|x| of the group), "
                      "exact int32 MMA sums, fp32 epilogue, combine and norm",
         "data": "synthetic (seeded N(0,0.02) weights quantised int4 gs64; fp16 N(0,1) inputs)",
         "config": {"workload": f"config1: Mixtral-8x7B-shaped stack, {args.layers} MoE blocks, "
-                               f"decode batch {args.batch}, attention=identity, RMSNorm eps 1e-5",
+                               f"decode global batch {args.batch} in one pass on one GPU, "
+                               f"attention=identity, RMSNorm eps 1e-5",
                    "global_batch": args.batch, "layers": args.layers, "hidden": 4096,
                    "inter": 14336, "experts": 8, "top_k": 2, "group_size": 64,
                    "parallelism": "single GPU", "l2": "weights per step (>=6 GB) exceed L2",
@@ -484,13 +487,21 @@ def main_ours(args):
     for k in ("e2e", "per_batch", "config0", "config3", "cpu_baseline", "parity"):
         if k in r:
             line[k] = r[k]
+    q = r.get("per_batch", {}).get(str(max(1, args.batch // 4)))
+    if q and args.batch % 4 == 0:
+        # the configuration's 4 micro-batches on one GPU run one after another
+        line["pipeline_4mb"] = {"tokens_per_s": round(args.batch * 1000.0 / (4 * q["ms_per_step"]), 1),
+                                "ms_per_step": round(4 * q["ms_per_step"], 4),
+                                "micro_batches": 4, "micro_batch": args.batch // 4}
     print(json.dumps(line), flush=True)
 
 
 def main_ep(args):
     """Config 2: one DeepSeek-V3-shaped MoE layer (256 routed experts, top-8, shared
     expert, Zipf(1.1) router bias) expert-sharded over N GPUs (256/N experts each),
-    decode batch 64 per GPU, NCCL all-to-all dispatch and combine (wisp_b200.ep)."""
+    decode batch 64 in total (64/N tokens routed on each GPU), three NCCL all-to-alls
+    per step (wisp_b200.ep.Dispatch); the total work is fixed, so the scaling is strong.
+    The weak-scaling figure (64 tokens per GPU) is reported beside it."""
     import datetime
     import numpy as np
     import torch
@@ -508,12 +519,13 @@ def main_ep(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
         dist.barrier()
-    B = 64
+    B_total = 64
+    if B_total % world:
+        raise SystemExit(f"64 tokens do not split over {world} GPUs")
     shape = cv.MoEShape(hidden=7168, inter=2048, n_experts=256, top_k=8, shared_inter=2048)
     ep = EPLayer(shape, SEED, rank, world, dev, zipf_s=1.1)
-    x = cv.make_input(shape, B, SEED + 100 * rank).to(dev)
 
-    def timed(steps):
+    def timed(x, steps):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -528,44 +540,56 @@ def main_ep(args):
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return ms.item()
 
-    for _ in range(max(3, args.warmup)):
-        ep.forward(x)
-    with ClockSampler(local) as clk:
-        ms = timed(args.steps)
-    # algorithmic bytes on this GPU per step: distinct local experts routed to it by any
-    # rank + the shared expert + the router
-    _, idx, _ = ep.forward(x)
-    ids = torch.as_tensor(idx.cpu().numpy().reshape(-1))
+    def measure(B):
+        x = cv.make_input(shape, B, SEED + 100 * rank).to(dev)
+        for _ in range(max(3, args.warmup)):
+            ep.forward(x)
+        with ClockSampler(local) as clk:
+            ms = timed(x, args.steps)
+        # algorithmic bytes on this GPU per step: distinct local experts routed to it by
+        # any rank + the shared expert + the router
+        _, idx, _ = ep.forward(x)
+        ids = idx.reshape(-1).to(dev)
+        if world > 1:
+            allidx = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(allidx, ids)
+            ids = torch.cat(allidx)
+        ids = ids.cpu().numpy()
+        mine = np.unique(ids[(ids >= rank * ep.per) & (ids < (rank + 1) * ep.per)])
+        blob = ep.local.blob_bytes - cv.HEADER_BYTES
+        step_bytes = (len(mine) + 1) * blob + shape.n_experts * shape.hidden * 2
+        tb = torch.tensor([float(step_bytes)], device=dev)
+        if world > 1:
+            dist.all_reduce(tb, op=dist.ReduceOp.MAX)
+        return ms, tb.item(), clk.summary()
+
+    ms, tb, clocks = measure(B_total // world)
+    ms_w, tb_w, _ = measure(B_total)
     if world > 1:
-        allidx = [torch.empty_like(ids.to(dev)) for _ in range(world)]
-        dist.all_gather(allidx, ids.to(dev))
-        ids = torch.cat([a.cpu() for a in allidx])
-    ids = ids.numpy()
-    mine = np.unique(ids[(ids >= rank * ep.per) & (ids < (rank + 1) * ep.per)])
-    blob = ep.local.blob_bytes - cv.HEADER_BYTES
-    step_bytes = (len(mine) + 1) * blob + shape.n_experts * shape.hidden * 2
-    tb = torch.tensor([float(step_bytes)], device=dev)
-    if world > 1:
-        dist.all_reduce(tb, op=dist.ReduceOp.MAX)
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         pk = peaks()
-        gbs = tb.item() / (ms * 1e-3) / 1e9
+        gbs = tb / (ms * 1e-3) / 1e9
         print(json.dumps({
             "metric": "MoE-block decode tokens/s (DeepSeek-V3-shaped layer, expert parallel)",
-            "value": round(B * world * 1000.0 / ms, 2), "unit": "tokens/s", "n_gpus": world,
+            "value": round(B_total * 1000.0 / ms, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int4xf32", "data": "synthetic (seeded; Zipf(1.1) router bias)",
             "config": {"workload": f"config2: DeepSeek-V3-shaped MoE layer (H 7168, 256 experts "
-                                   f"top-8 + shared, inter 2048), decode batch {B} per GPU, "
-                                   f"experts sharded over {world} GPU(s), NCCL all-to-all",
-                       "global_batch": B * world, "parallelism": f"ep{world}"},
+                                   f"top-8 + shared, inter 2048), decode batch {B_total} in "
+                                   f"total ({B_total // world} per GPU), experts sharded over "
+                                   f"{world} GPU(s), 3 NCCL all-to-alls per step",
+                       "global_batch": B_total, "parallelism": f"ep{world}"},
             "roofline": {"bound": "hbm", "kernel": "whole step, most loaded GPU",
                          "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None},
-            "clocks": clk.summary()}), flush=True)
+            "clocks": clocks,
+            "weak_scaling": {"tokens_per_s": round(B_total * world * 1000.0 / ms_w, 2),
+                             "ms_per_step": round(ms_w, 4), "tokens_per_gpu": B_total,
+                             "hbm_gbs_most_loaded": round(tb_w / (ms_w * 1e-3) / 1e9, 1)}}),
+              flush=True)
 
 
 def main_prefill(args):

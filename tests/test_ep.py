@@ -12,18 +12,32 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from wisp_b200.ep import dispatch_plan, exchange, exchange_back
+from wisp_b200.ep import Dispatch, dispatch_plan
 
 
 def test_dispatch_plan_orders_by_owner_then_token_then_slot():
-    idx = np.array([[5, 0, -1], [1, 7, 4], [6, 2, 3]], dtype=np.int32)
-    order, counts, tokens, eid, row_idx = dispatch_plan(idx, per=4, world=2)
+    idx = torch.tensor([[5, 0, -1], [1, 7, 4], [6, 2, 3]], dtype=torch.int32)
+    order, counts, tokens, eid, owner, row_idx = dispatch_plan(idx, per=4, world=2)
     assert counts.tolist() == [4, 4]
     # owner 0: (0,1)=0 (1,0)=1 (2,1)=2 (2,2)=3 ; owner 1: (0,0)=5 (1,1)=7 (1,2)=4 (2,0)=6
-    assert order.tolist() == [1, 3, 7, 8, 0, 4, 5, 6]
-    assert tokens.tolist() == [0, 1, 2, 2, 0, 1, 1, 2]
-    assert eid.tolist() == [0, 1, 2, 3, 1, 3, 0, 2]
+    assert order.tolist()[:8] == [1, 3, 7, 8, 0, 4, 5, 6]
+    assert order.tolist()[8] == 2 and owner.tolist()[8] == 2  # the unrouted slot, last
+    assert tokens.tolist()[:8] == [0, 1, 2, 2, 0, 1, 1, 2]
+    assert eid.tolist()[:8] == [0, 1, 2, 3, 1, 3, 0, 2]
     assert row_idx.tolist() == [[4, 0, -1], [1, 5, 6], [7, 2, 3]]
+
+
+def test_single_rank_dispatch_keeps_rows_and_ids():
+    """World size 1: no collective; the rows and local expert ids come back in send
+    order and `back` is the identity."""
+    idx = torch.tensor([[2, 0], [-1, 3], [1, 2]], dtype=torch.int32)
+    x = torch.arange(12, dtype=torch.float32).view(3, 4)
+    d = Dispatch(x, idx, per=4, world=1)
+    assert d.send_counts == [5] and d.recv_counts == [5]
+    # send order: (0,0)=2 (0,1)=0 (1,1)=3 (2,0)=1 (2,1)=2
+    assert d.eids.view(-1).tolist() == [2, 0, 3, 1, 2]
+    assert torch.equal(d.rows, x[[0, 0, 1, 2, 2]])
+    assert d.back(d.rows) is d.rows
 
 
 def _free_port() -> int:
@@ -42,18 +56,15 @@ def _ep_rank(rank, world, port, out):
     idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(B)]).int()
     idx[1, 1] = -1  # an unrouted slot
     w = torch.rand(B, K, generator=g)
-    order, counts, tokens, eid, row_idx = dispatch_plan(idx.numpy(), per, world)
-    send = x[torch.as_tensor(tokens)]
-    recv, rcl = exchange(send, counts, H)
-    eids, _ = exchange(torch.as_tensor(eid).view(-1, 1).float(), counts, 1)
+    d = Dispatch(x, idx, per, world)
     # stand-in expert e (global id rank*per + local): y = (e + 1) * x + e
-    ge = eids.view(-1) + rank * per
-    rows = recv * (ge + 1).view(-1, 1) + ge.view(-1, 1)
-    back = exchange_back(rows, counts, rcl)
+    ge = d.eids.view(-1).float() + rank * per
+    rows = d.rows * (ge + 1).view(-1, 1) + ge.view(-1, 1)
+    back = d.back(rows)
     y = torch.zeros(B, H)
     for t in range(B):
         for j in range(K):
-            r = int(row_idx[t, j])
+            r = int(d.row_idx[t, j])
             if r >= 0:
                 y[t] += w[t, j] * back[r]
     # what the experts compute directly on this rank's tokens

@@ -43,6 +43,7 @@ def test_pipeline_send_recv_two_gpus():
     L = lib()
     if not L.wisp_nccl_available():
         pytest.skip("NCCL not loadable")
+    dev0 = torch.cuda.current_device()
     assert L.wisp_peer_enable(0, 1) in (0, -1)
     devs = (C.c_int * 2)(0, 1)
     assert L.wisp_pipeline_init(devs, 2) == 0
@@ -66,5 +67,7 @@ def test_pipeline_send_recv_two_gpus():
     for t in th:
         t.join(timeout=60)
     L.wisp_pipeline_shutdown()
+    # the library leaves the caller's current device as it found it
+    assert torch.cuda.current_device() == dev0
     assert rc == [0, 0]
     assert torch.equal(x1.cpu(), x0.cpu())

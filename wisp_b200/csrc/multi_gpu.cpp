@@ -93,7 +93,13 @@ extern "C" int wisp_pipeline_init(const int* gpu_indices, int n) {
     std::lock_guard<std::mutex> g(p.mu);
     if (!p.comms.empty()) return -1;  // already initialised: shut down first
     std::vector<ncclComm_t> comms((size_t)n, nullptr);
-    if (N.comm_init_all(comms.data(), n, gpu_indices) != ncclSuccess) return -1;
+    // NCCL selects each communicator's device while it builds them: the caller's
+    // current device is restored afterwards
+    int cur = 0;
+    cudaGetDevice(&cur);
+    const ncclResult_t r = N.comm_init_all(comms.data(), n, gpu_indices);
+    cudaSetDevice(cur);
+    if (r != ncclSuccess) return -1;
     p.devs.assign(gpu_indices, gpu_indices + n);
     p.comms = comms;
     return 0;
@@ -103,9 +109,12 @@ extern "C" void wisp_pipeline_shutdown(void) {
     Nccl& N = nccl();
     Pipeline& p = pipe();
     std::lock_guard<std::mutex> g(p.mu);
+    int cur = 0;
+    cudaGetDevice(&cur);
     if (N.ok)
         for (ncclComm_t c : p.comms)
             if (c) N.comm_destroy(c);
+    cudaSetDevice(cur);  // as in init: the caller's current device is kept
     p.comms.clear();
     p.devs.clear();
 }

@@ -766,7 +766,9 @@ prefill_scatter_kernel(PArgs P, PWs W, int T, const float* __restrict__ x, float
     const int t = blockIdx.x, K = P.K, H = P.H;
     __shared__ int rows[65];
     if (threadIdx.x < K) rows[threadIdx.x] = W.row_of[t * K + threadIdx.x];
-    if (threadIdx.x == 0) rows[K] = W.cnt[P.E] > 0 ? W.seg[P.E] + t : -1;
+    // the shared expert's rows exist only with one (the plan writes its count
+    // and segment only then; a routing-given call has none)
+    if (threadIdx.x == 0) rows[K] = P.has_shared && W.cnt[P.E] > 0 ? W.seg[P.E] + t : -1;
     __syncthreads();
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
     float4* yr = reinterpret_cast<float4*>(y + (size_t)t * H);

@@ -6,70 +6,122 @@ routes its own tokens.
 One step on a rank (tokens x [B, H] fp32 on its GPU):
 
 1. route (``wisp_moe_route``, the full router): top-k expert ids and weights per token;
-2. dispatch: the (token, slot) assignments are ordered by owner rank, counts are
-   exchanged, and the token rows travel to the owners with one NCCL all-to-all
-   (``torch.distributed.all_to_all_single``) together with their local expert ids;
+2. dispatch (``Dispatch``): the (token, slot) assignments are ordered by owner rank on
+   the device; one fixed-size NCCL all-to-all carries, to each owner, the number of
+   rows it will receive and their local expert ids; one small device-to-host read gives
+   both count vectors; the token rows travel with a second all-to-all
+   (``torch.distributed.all_to_all_single``);
 3. each owner runs its experts on the rows it received (``wisp_moe_experts_routed``,
    one expert per row, weight 1);
-4. the result rows travel back with the reverse all-to-all;
+4. the result rows travel back with the third, reverse all-to-all;
 5. the home rank adds the shared expert (computed on its own tokens meanwhile) and the
    gate-weighted rows in top-k order (``wisp_moe_ep_combine``) -- the reference's
    combine order (shared first, then the routed experts in top-k order,
    csrc/core/wisp_engine.c:1443-1522).
 
-The reference declares no expert-parallel path; this one is new.  The bookkeeping of
-step 2 (``dispatch_plan``) is plain numpy so it is tested on CPU with gloo ranks.
+The reference declares no expert-parallel path; this one is new.  Steps 2 and 4 are
+torch operations on whatever device the tensors are on, so the same code is tested on
+CPU with gloo ranks.
 """
 
 from __future__ import annotations
 
 import ctypes as C
 
-import numpy as np
 
-
-def dispatch_plan(idx: np.ndarray, per: int, world: int):
-    """For routing idx [B, K] (expert ids, -1 = none) and `per` experts per rank:
-    the assignments in send order (sorted by owner rank, then token, then slot), the
-    send count per rank, each sent row's token and local expert id, and row_idx [B, K]:
-    the position of assignment (t, j) in the send order (-1 if unrouted)."""
+def dispatch_plan(idx, per: int, world: int):
+    """Device-side bookkeeping (torch ops on idx's device, no host round trip).  For
+    routing idx [B, K] (expert ids, -1 = none) and `per` experts per rank: the send
+    order of the assignments (sorted by owner rank, then token, then slot; unrouted
+    slots last), the send count per rank, each sent row's token and local expert id,
+    its owner, and row_idx [B, K]: the position of assignment (t, j) in the send order
+    (-1 if unrouted)."""
+    import torch
     B, K = idx.shape
-    flat = idx.reshape(-1)
-    live = np.nonzero(flat >= 0)[0]
-    owner = flat[live] // per
-    order = live[np.argsort(owner, kind="stable")]  # stable: token, then slot order
-    counts = np.bincount(flat[order] // per, minlength=world).astype(np.int64)
-    tokens = (order // K).astype(np.int64)
-    local_eid = (flat[order] % per).astype(np.int32)
-    row_idx = np.full(B * K, -1, dtype=np.int32)
-    row_idx[order] = np.arange(order.size, dtype=np.int32)
-    return order, counts, tokens, local_eid, row_idx.reshape(B, K)
+    flat = idx.reshape(-1).long()
+    live = flat >= 0
+    owner = torch.where(live, flat.div(per, rounding_mode="floor"), torch.full_like(flat, world))
+    order = torch.argsort(owner, stable=True)  # stable: token, then slot order
+    counts = torch.bincount(owner, minlength=world + 1)[:world]
+    sorted_owner = owner[order]
+    tokens = order.div(K, rounding_mode="floor")
+    local_eid = torch.where(live[order], flat[order] % per, torch.zeros_like(flat)).int()
+    pos = torch.arange(B * K, device=idx.device)
+    row_idx = torch.full((B * K,), -1, dtype=torch.int32, device=idx.device)
+    row_idx[order] = torch.where(live[order], pos, torch.full_like(pos, -1)).int()
+    return order, counts, tokens, local_eid, sorted_owner, row_idx.view(B, K)
 
 
-def exchange(send, send_counts, row_elems: int, group=None):
-    """all_to_all of `send` rows ([n, row_elems], grouped by destination rank with
-    send_counts[d] rows each); returns (received rows, recv_counts)."""
+def exchange_counts(counts, sorted_owner, local_eid, world: int, cap: int, group=None):
+    """The first all-to-all, of fixed size: to each rank d, [the number of rows this
+    rank will send it, then those rows' local expert ids] (padded to `cap`).  Returns
+    the received [world, 1 + cap] table (row s: what rank s sends here)."""
     import torch
     import torch.distributed as dist
-    sc = torch.as_tensor(send_counts, dtype=torch.int64, device=send.device)
-    rc = torch.empty_like(sc)
-    dist.all_to_all_single(rc, sc, group=group)
-    rcl = rc.cpu().tolist()
-    recv = torch.empty((int(sum(rcl)), row_elems), dtype=send.dtype, device=send.device)
-    dist.all_to_all_single(recv, send, output_split_sizes=rcl,
-                           input_split_sizes=[int(c) for c in send_counts], group=group)
-    return recv, rcl
+    dev = counts.device
+    table = torch.zeros((world, 1 + cap), dtype=torch.int32, device=dev)
+    table[:, 0] = counts.int()
+    start = torch.cumsum(counts, 0) - counts
+    n = sorted_owner.numel()
+    live = sorted_owner < world
+    d = torch.where(live, sorted_owner, torch.zeros_like(sorted_owner))
+    j = torch.arange(n, device=dev) - start[d]
+    dst = torch.where(live, d * (1 + cap) + 1 + j, torch.full_like(j, -1))
+    flat = table.view(-1)
+    keep = dst >= 0
+    flat.index_put_((dst[keep],), local_eid[keep])
+    if world == 1:
+        return table
+    recv = torch.empty_like(table)
+    dist.all_to_all_single(recv, table, group=group)
+    return recv
+
+
+def exchange_rows(send, send_counts, recv_counts, group=None):
+    """all_to_all of `send` rows (grouped by destination, send_counts[d] rows each);
+    recv_counts[s] rows arrive from each rank s (host lists)."""
+    import torch
+    import torch.distributed as dist
+    recv = torch.empty((int(sum(recv_counts)), send.shape[1]), dtype=send.dtype,
+                       device=send.device)
+    dist.all_to_all_single(recv, send, output_split_sizes=list(recv_counts),
+                           input_split_sizes=list(send_counts), group=group)
+    return recv
 
 
 def exchange_back(rows, send_counts, recv_counts, group=None):
     """The reverse all_to_all: rows received per source go back to it."""
-    import torch
-    import torch.distributed as dist
-    out = torch.empty((int(sum(send_counts)), rows.shape[1]), dtype=rows.dtype,
-                      device=rows.device)
-    dist.all_to_all_single(out, rows, output_split_sizes=[int(c) for c in send_counts],
-                           input_split_sizes=list(recv_counts), group=group)
-    return out
+    return exchange_rows(rows, recv_counts, send_counts, group)
+
+
+class Dispatch:
+    """Steps 2-4 of the module doc for one layer call: three collectives (the fixed-size
+    count/expert-id table, the rows out, the rows back) and one small device-to-host
+    read (both count vectors, which the variable all-to-alls need on the host)."""
+
+    def __init__(self, x, idx, per: int, world: int, group=None):
+        import torch
+        B, K = idx.shape
+        self.world, self.group = world, group
+        _, counts, tokens, local_eid, owner, self.row_idx = dispatch_plan(idx, per, world)
+        table = exchange_counts(counts, owner, local_eid, world, B * K, group)
+        both = torch.stack([counts.int(), table[:, 0]]).cpu()  # the one host read
+        self.send_counts = [int(c) for c in both[0]]
+        self.recv_counts = [int(c) for c in both[1]]
+        n_send = sum(self.send_counts)
+        send = x.index_select(0, tokens[:n_send])
+        self.rows = (exchange_rows(send, self.send_counts, self.recv_counts, group)
+                     if world > 1 else send)
+        # local expert ids of the received rows, in source order
+        sel = [s * (1 + B * K) + 1 + j for s in range(world) for j in range(self.recv_counts[s])]
+        self.eids = table.view(-1)[torch.as_tensor(sel, dtype=torch.long,
+                                                   device=x.device)].view(-1, 1)
+
+    def back(self, out_rows):
+        """The expert outputs of the received rows, returned to their home ranks."""
+        if self.world == 1:
+            return out_rows
+        return exchange_back(out_rows, self.send_counts, self.recv_counts, self.group)
 
 
 class EPLayer:
@@ -189,30 +241,20 @@ class EPLayer:
         from .lib import WispErrCtx, check, lib
         B, H = x.shape
         idx, w = self.route(x)
-        order, counts, tokens, local_eid, row_idx = dispatch_plan(
-            idx.cpu().numpy(), self.per, self.world)
-        self.last_counts = counts
-        tok = torch.as_tensor(tokens, device=self.device)
-        send = x.index_select(0, tok) if tokens.size else x[:0]
-        eid_send = torch.as_tensor(local_eid, device=self.device).view(-1, 1)
-        if self.world > 1:
-            recv, rcl = exchange(send, counts, H, self.group)
-            eid_recv, _ = exchange(eid_send, counts, 1, self.group)
-        else:
-            recv, rcl, eid_recv = send, [int(counts[0])], eid_send
-        wt = torch.ones((recv.shape[0], 1), dtype=torch.float32, device=self.device)
-        rows = self.experts(self.expert_layer, recv.contiguous(), eid_recv.contiguous(), wt)
-        back = exchange_back(rows, counts, rcl, self.group) if self.world > 1 else rows
+        dsp = Dispatch(x, idx, self.per, self.world, self.group)
+        self.last_counts = dsp.send_counts
+        wt = torch.ones((dsp.rows.shape[0], 1), dtype=torch.float32, device=self.device)
+        rows = self.experts(self.expert_layer, dsp.rows.contiguous(), dsp.eids.contiguous(), wt)
+        back = dsp.back(rows)
         if self.shared_layer is not None:
             y = self.experts(self.shared_layer, x,
                              torch.zeros((B, 1), dtype=torch.int32, device=self.device),
                              torch.ones((B, 1), dtype=torch.float32, device=self.device))
         else:
             y = torch.zeros_like(x)
-        ridx = torch.as_tensor(row_idx, device=self.device)
         err = WispErrCtx()
         check(lib().wisp_moe_ep_combine(y.data_ptr(), back.data_ptr() if back.numel() else None,
-                                        ridx.data_ptr(), w.data_ptr(), B, idx.shape[1], H,
+                                        dsp.row_idx.data_ptr(), w.data_ptr(), B, idx.shape[1], H,
                                         torch.cuda.current_stream().cuda_stream,
                                         C.byref(err)), err)
         return y, idx, w
