@@ -368,6 +368,10 @@ WispError wisp_stream_prefetch(WispStreamCache* c, int layer, const int* ids, in
 WispError wisp_stream_layer_done(WispStreamCache* c, int layer, cudaStream_t compute,
                                  WispErrCtx* err);
 void wisp_stream_stats(WispStreamCache* c, uint64_t* out6);
+/* Forget every resident expert and zero the statistics (a cold cache), after
+ * the device is idle.  A layer's slots handed out by ensure stay out of
+ * eviction until its layer_done, whatever the caller prefetches in between. */
+void wisp_stream_reset(WispStreamCache* c);
 
 /* No counterpart in the reference.  wisp_moe_block_forward without a
  * workspace argument, for callers that cannot allocate device memory: a host

@@ -2,6 +2,8 @@
 reference engine's own run_moe (golden fixtures), the VRAM/RAM/SSD tier policy, the
 scratch-ring miss path, statistics and the access log."""
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -180,5 +182,72 @@ def test_engine_on_reference_converted_dir(cuda, golden, ref_conv_dir, vram):
         core.moe_stack(h, 0, L, xs.data_ptr(), x.shape[0])
         torch.cuda.synchronize()
         check_outputs(xs.cpu().numpy(), arr["ref_conv.stack_x"])
+    finally:
+        core.engine_destroy(h)
+
+
+def test_stack_with_a_tiny_vram_budget(cuda, golden, golden_dirs):
+    """Three VRAM slots for the 16 experts of a 2-layer stack: every step evicts
+    (write-back to the RAM tier on the transfer stream), serves cool experts through
+    the scratch ring and promotes hot ones after three RAM hits, with no host
+    synchronisation around the uploads; every step matches the reference's stack."""
+    _, arr = golden
+    d = str(golden_dirs["mx_small"])
+    probe = core.engine_create(d, 4 * GB, 4 * GB, [0], 1)
+    try:
+        assert core.pin_experts(probe, 0, 1) == 8
+        slot = core.get_vram_used_bytes(probe) // 8
+    finally:
+        core.engine_destroy(probe)
+    h = core.engine_create(d, 3 * slot, 4 * GB, [0], 1)
+    try:
+        x0 = arr["mx_small.x"]
+        for step in range(6):
+            x = torch.from_numpy(x0).to(cuda)
+            core.moe_stack(h, 0, 2, x.data_ptr(), x.shape[0])
+            torch.cuda.synchronize()
+            check_outputs(x.cpu().numpy(), arr["mx_small.stack_x"])
+        s = core.cache_stats(h)
+        assert s["vram_hits"] > 0 and s["ram_hits"] > 0 and s["ssd_hits"] > 0
+        assert 0 < core.get_vram_used_bytes(h) <= 3 * slot
+    finally:
+        core.engine_destroy(h)
+
+
+def test_learning_cache_prewarms_the_engine(cuda, golden, golden_dirs, tmp_path):
+    """A session's routing drained from the engine's access log into a learning
+    cache, saved; a new engine pre-warmed from it reads those experts into the RAM
+    tier on its worker, so the first forward finds them there (RAM hits, no SSD)."""
+    import time
+    from wisp_b200.learning_cache import LearningCache
+    from wisp_b200.tier_cache import ExpertPredictor, prewarm_engine
+    _, arr = golden
+    d = str(golden_dirs["mx_small"])
+    x = arr["mx_small.x"][:1]
+    lc = LearningCache(tmp_path)
+    h = core.engine_create(d, 0, 4 * GB, [0], 1)
+    try:
+        run_block(h, 0, x, cuda)
+        p = ExpertPredictor(2, 2, lc)
+        assert p.drain_engine_log(h) == 2
+        assert len(p.predict(0)) == 2
+    finally:
+        core.engine_destroy(h)
+    assert lc.save()
+    lc2 = LearningCache(tmp_path)
+    assert lc2.load() == 2
+    h = core.engine_create(d, 0, 4 * GB, [0], 1)
+    try:
+        assert prewarm_engine(h, lc2, 10) == 2
+        blob = (Path(d) / "experts" / "L000_E00000.bin").stat().st_size
+        for _ in range(400):  # the worker thread reads the two files
+            if core.get_ram_used_bytes(h) >= 2 * blob:
+                break
+            time.sleep(0.05)
+        assert core.get_ram_used_bytes(h) >= 2 * blob
+        y = run_block(h, 0, x, cuda)
+        s = core.cache_stats(h)
+        assert s["ssd_hits"] == 0 and s["ram_hits"] == 2
+        check_outputs(y, arr["mx_small.y"][:1])
     finally:
         core.engine_destroy(h)

@@ -210,6 +210,12 @@ struct WispEngine {
     size_t cap_route = 0, cap_rows = 0, cap_dh = 0;
     std::vector<int> h_idx;        // host copy of the routing (miss path)
     cudaEvent_t order_ev = nullptr;  // orders the compute stream before a caller's stream
+    // expert uploads and VRAM write-backs run on the transfer stream without host
+    // synchronisation: up_ev marks the last one issued, the expert kernels wait on
+    // it, and a RAM-tier buffer is freed only after they have drained
+    cudaEvent_t up_ev = nullptr;
+    cudaEvent_t evict_ev = nullptr;  // compute work before a VRAM victim is copied out
+    bool uploads_pending = false;
     // prefetch worker
     std::thread worker;
     std::mutex q_mu;
@@ -334,20 +340,35 @@ void set_table(WispEngine* e, uint32_t layer, uint32_t expert, void* ptr, bool v
                     cudaMemcpyHostToDevice, e->compute);
 }
 
+// Wait for the uploads and write-backs in flight (their host buffers may be
+// about to be freed or reused).
+void drain_uploads(WispEngine* e) {
+    if (!e->uploads_pending) return;
+    cudaStreamSynchronize(e->transfer);
+    e->uploads_pending = false;
+}
+
 void ram_put(WispEngine* e, uint32_t layer, uint32_t expert, void* data, size_t n) {
     if (n > e->ram.capacity()) {
+        drain_uploads(e);
         cudaFreeHost(data);
         return;
     }
     wb::Lru::Entry v;
-    while (e->ram.would_overflow(n) && e->ram.evict(&v)) cudaFreeHost(v.data);
+    while (e->ram.would_overflow(n) && e->ram.evict(&v)) {
+        drain_uploads(e);  // an upload or write-back may still use the victim's buffer
+        cudaFreeHost(v.data);
+    }
     e->ram.put(layer, expert, data, n);
 }
 
 // Host blob -> device slot in the tiled layout the kernels stream, on the
-// transfer stream (synchronised before returning).  A .bin blob is copied to
-// the device staging slot and tiled into `dst`; a blob that is already tiled
-// (a VRAM victim written back to the RAM tier) is copied as is.
+// transfer stream, not waited for: `src` must stay valid until the transfer
+// stream passes it (RAM-tier buffers are freed only after drain_uploads), and
+// whoever runs kernels on the slot waits for up_ev first (wait_uploads).  A .bin
+// blob is copied to the device staging slot and tiled into `dst` (the staging
+// slot is reused in transfer-stream order); a blob that is already tiled (a VRAM
+// victim written back to the RAM tier) is copied as is.
 bool put_tiled(WispEngine* e, void* dst, const void* src, size_t n, WispErrCtx* err) {
     WispExpertMeta m{};
     if (wisp_expert_parse_header(src, n, &m, err) != WISP_OK) return false;
@@ -359,12 +380,18 @@ bool put_tiled(WispEngine* e, void* dst, const void* src, size_t n, WispErrCtx* 
         if (ce == cudaSuccess && wisp_expert_tile(&m, e->d_stage, dst, e->transfer, err) != WISP_OK)
             return false;
     }
-    if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->transfer);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e->up_ev, e->transfer);
     if (ce != cudaSuccess) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "expert upload failed: %s", cudaGetErrorString(ce));
         return false;
     }
+    e->uploads_pending = true;
     return true;
+}
+
+// Kernels queued next on `s` see every upload issued so far.
+void wait_uploads(WispEngine* e, cudaStream_t s) {
+    if (e->uploads_pending) cudaStreamWaitEvent(s, e->up_ev, 0);
 }
 
 // Upload into a ring slot (cool experts: no cache insert, no eviction).
@@ -385,15 +412,22 @@ void* vram_alloc_evicting(WispEngine* e, size_t n, const std::vector<uint64_t>& 
         }
         wb::Lru::Entry v;
         if (!e->vram.evict_except(keep, &v)) return nullptr;
-        // in-flight kernels may still read the victim's slot
-        cudaStreamSynchronize(e->compute);
+        // The victim is copied back to the RAM tier on the transfer stream after the
+        // kernels already queued on the compute stream (they may read its slot); the
+        // slot's next upload follows on the same stream, so it cannot overtake.
+        cudaEventRecord(e->evict_ev, e->compute);
+        cudaStreamWaitEvent(e->transfer, e->evict_ev, 0);
         if (!e->ram.get(v.layer, v.expert, nullptr)) {
             void* host = nullptr;
             if (cudaHostAlloc(&host, v.bytes, cudaHostAllocDefault) == cudaSuccess) {
-                if (cudaMemcpy(host, v.data, v.bytes, cudaMemcpyDeviceToHost) == cudaSuccess)
+                if (cudaMemcpyAsync(host, v.data, v.bytes, cudaMemcpyDeviceToHost, e->transfer) ==
+                    cudaSuccess) {
+                    cudaEventRecord(e->up_ev, e->transfer);
+                    e->uploads_pending = true;
                     ram_put(e, v.layer, v.expert, host, v.bytes);
-                else
+                } else {
                     cudaFreeHost(host);
+                }
             }
         }
         set_table(e, v.layer, v.expert, nullptr, false);
@@ -465,19 +499,25 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
     if (n == 0) return nullptr;
     stat_hit(e, 2, layer, expert);
     if (ensure_meta(e, layer, e->staging, n, err) != WISP_OK) return nullptr;
+    // the RAM-tier copy is the upload's source, so the staging buffer is free for
+    // the next read at once; without one, the upload from staging is waited for
     void* host = nullptr;
     if (cudaHostAlloc(&host, n, cudaHostAllocDefault) == cudaSuccess) {
         memcpy(host, e->staging, n);
         ram_put(e, layer, expert, host, n);
     }
+    const void* src = host ? host : e->staging;
     void* slot = nullptr;
     if (!e->vram.would_overflow(n)) slot = e->arena.alloc();
     if (!slot) {
-        void* p = scratch_serve(e, e->staging, n, err);
+        void* p = scratch_serve(e, src, n, err);
         if (p) set_table(e, layer, expert, p, false);
+        if (!host) drain_uploads(e);
         return p;
     }
-    if (!put_tiled(e, slot, e->staging, n, err)) {
+    const bool up = put_tiled(e, slot, src, n, err);
+    if (!host) drain_uploads(e);
+    if (!up) {
         e->arena.release(slot);
         return nullptr;
     }
@@ -797,6 +837,8 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
     ce = cudaStreamCreateWithFlags(&e->compute, cudaStreamNonBlocking);
     if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->transfer, cudaStreamNonBlocking);
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->order_ev, cudaEventDisableTiming);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->up_ev, cudaEventDisableTiming);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->evict_ev, cudaEventDisableTiming);
     if (ce == cudaSuccess) ce = cudaHostAlloc(&e->staging, e->max_expert_bytes, 0);
     if (ce == cudaSuccess) ce = cudaMalloc(&e->d_stage, e->max_expert_bytes + 264);
     if (ce == cudaSuccess) e->d_stage += 8;  // blob at 8 (mod 16), like every slot
@@ -901,6 +943,8 @@ extern "C" void wisp_engine_destroy(WispEngine* e) {
     cudaFree(e->d_ffn);
     cudaFree(e->d_dh);
     if (e->order_ev) cudaEventDestroy(e->order_ev);
+    if (e->up_ev) cudaEventDestroy(e->up_ev);
+    if (e->evict_ev) cudaEventDestroy(e->evict_ev);
     if (e->staging) cudaFreeHost(e->staging);
     if (e->d_stage) cudaFree(e->d_stage - 8);
     if (e->compute) cudaStreamDestroy(e->compute);
@@ -917,7 +961,10 @@ extern "C" void* wisp_expert_fetch(WispEngine* e, uint32_t layer, uint32_t exper
     }
     cudaSetDevice(e->device);
     std::lock_guard<std::mutex> g(e->fetch_mu);
-    return fetch_locked(e, layer, expert, {}, err);
+    void* p = fetch_locked(e, layer, expert, {}, err);
+    // the reference's contract: the returned slot holds the expert
+    drain_uploads(e);
+    return p;
 }
 
 extern "C" void wisp_expert_prefetch_hint(WispEngine* e, int layer, const int* ids, int n) {
@@ -964,7 +1011,9 @@ extern "C" int wisp_engine_pin_experts(WispEngine* e, int layer0, int n, WispErr
             if (e->vram.would_overflow(bytes)) return resident;
             void* slot = e->arena.alloc();
             if (!slot) return resident;
-            if (!put_tiled(e, slot, host, bytes, &le)) {
+            const bool up = put_tiled(e, slot, host, bytes, &le);
+            if (host == e->staging) drain_uploads(e);  // staging is read into next
+            if (!up) {
                 e->arena.release(slot);
                 if (err) *err = le;
                 return resident;
@@ -974,6 +1023,7 @@ extern "C" int wisp_engine_pin_experts(WispEngine* e, int layer0, int n, WispErr
             ++resident;
         }
     }
+    drain_uploads(e);
     cudaStreamSynchronize(e->compute);
     return resident;
 }
@@ -1077,8 +1127,10 @@ static WispError moe_forward_impl(WispEngine* e, int l, const float* x, float* y
                                     cudaMemcpyHostToDevice, s),
                     err);
     }
-    // table updates were queued on the compute stream
+    // table updates were queued on the compute stream, the uploads on the
+    // transfer stream
     order_after_compute(e, s);
+    wait_uploads(e, s);
     return wisp_moe_block_experts(&d[0], x, y, T, e->d_idx, e->d_w, e->ws, e->ws_bytes, s, err);
 }
 
@@ -1090,8 +1142,9 @@ extern "C" WispError wisp_moe_forward(WispEngine* e, int layer, const float* x, 
     }
     cudaSetDevice(e->device);
     cudaStream_t s = stream ? stream : e->compute;
-    // pending table updates on the compute stream must land first
+    // pending table updates on the compute stream and uploads must land first
     order_after_compute(e, s);
+    wait_uploads(e, s);
     return moe_forward_impl(e, layer, x, y, T, s, err);
 }
 
@@ -1109,6 +1162,7 @@ extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, 
     cudaSetDevice(e->device);
     cudaStream_t s = stream ? stream : e->compute;
     order_after_compute(e, s);
+    wait_uploads(e, s);
     WispError r = WISP_OK;
     for (int l = layer0; l < layer0 + n && r == WISP_OK;) {
         // a run of VRAM-resident MoE layers: one fused stack, no host synchronisation
@@ -1160,6 +1214,7 @@ extern "C" void wisp_cache_stats(WispEngine* e, uint64_t* v, uint64_t* r, uint64
 extern "C" void wisp_cache_clear_all(WispEngine* e) {
     std::lock_guard<std::mutex> g(e->fetch_mu);
     cudaStreamSynchronize(e->compute);
+    drain_uploads(e);  // slots and host buffers about to be released may be in flight
     e->vram.clear([&](const wb::Lru::Entry& v) {
         set_table(e, v.layer, v.expert, nullptr, false);
         e->arena.release(v.data);
@@ -1171,6 +1226,8 @@ extern "C" void wisp_cache_clear_all(WispEngine* e) {
 
 extern "C" int wisp_ram_trim(WispEngine* e, int count) {
     if (!e || count <= 0) return 0;
+    std::lock_guard<std::mutex> g(e->fetch_mu);
+    drain_uploads(e);  // the freed buffers may be sources of uploads in flight
     int freed = 0;
     wb::Lru::Entry v;
     while (freed < count && e->ram.evict(&v)) {

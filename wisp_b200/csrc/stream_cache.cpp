@@ -42,6 +42,10 @@ struct WispStreamCache {
     std::vector<cudaEvent_t> ready;   // recorded after the slot's fill
     std::vector<int> last_use;        // index into use_ev (-1: never read)
     std::vector<uint8_t> from_prefetch;
+    // slots a layer's ensure handed to kernels not yet marked by its layer_done:
+    // not evicted until then, whatever order the caller prefetches in
+    std::vector<uint8_t> pending;
+    std::vector<uint64_t> slot_key;   // (layer, expert) key of the slot's expert
     std::vector<cudaEvent_t> use_ev;  // ring of "layer kernels done" events
     int use_head = 0;
     std::vector<std::vector<int>> layer_slots;  // slots of the last ensure per layer
@@ -64,8 +68,12 @@ constexpr int kUseEvents = 64;
 void* take_slot(WispStreamCache* c, const std::vector<uint64_t>& keep, cudaStream_t s) {
     void* p = c->arena.alloc();
     if (p) return p;
+    std::vector<uint64_t> hold = keep;
+    for (size_t si = 0; si < c->pending.size(); ++si)
+        if (c->pending[si]) hold.push_back(c->slot_key[si]);
+    std::sort(hold.begin(), hold.end());
     wb::Lru::Entry v;
-    if (!c->lru.evict_except(keep, &v)) return nullptr;
+    if (!c->lru.evict_except(hold, &v)) return nullptr;
     // kernels already queued may still read the victim (through the table and
     // the slot): the transfer stream waits for them before touching either
     const int si = c->slot_index(v.data);
@@ -103,6 +111,7 @@ void* fill(WispStreamCache* c, int layer, int e, const std::vector<uint64_t>& ke
     }
     c->last_use[si] = -1;
     c->from_prefetch[si] = prefetch ? 1 : 0;
+    c->slot_key[si] = wb::Lru::key((uint32_t)layer, (uint32_t)e);
     c->lru.put((uint32_t)layer, (uint32_t)e, slot, c->blob_bytes);
     c->bytes += c->blob_bytes;
     return slot;
@@ -169,6 +178,8 @@ extern "C" WispStreamCache* wisp_stream_create(int n_layers, int n_experts, size
     c->ready.assign(n_slots, nullptr);
     c->last_use.assign(n_slots, -1);
     c->from_prefetch.assign(n_slots, 0);
+    c->pending.assign(n_slots, 0);
+    c->slot_key.assign(n_slots, 0);
     for (size_t i = 0; i < n_slots; ++i) cudaEventCreateWithFlags(&c->ready[i], cudaEventDisableTiming);
     c->use_ev.assign(kUseEvents, nullptr);
     for (int i = 0; i < kUseEvents; ++i) cudaEventCreateWithFlags(&c->use_ev[i], cudaEventDisableTiming);
@@ -244,6 +255,7 @@ extern "C" WispError wisp_stream_ensure(WispStreamCache* c, int layer, const int
         const int si = c->slot_index(slot);
         cudaStreamWaitEvent(compute, c->ready[si], 0);
         used.push_back(si);
+        c->pending[si] = 1;
     }
     c->hits += (uint64_t)h;
     c->misses += (uint64_t)m;
@@ -282,8 +294,26 @@ extern "C" WispError wisp_stream_layer_done(WispStreamCache* c, int layer, cudaS
     const int i = c->use_head;
     c->use_head = (c->use_head + 1) % kUseEvents;
     WB_CUDA_RET(cudaEventRecord(c->use_ev[i], compute), err);
-    for (int si : c->layer_slots[layer]) c->last_use[si] = i;
+    for (int si : c->layer_slots[layer]) {
+        c->last_use[si] = i;
+        c->pending[si] = 0;
+    }
     return WISP_OK;
+}
+
+extern "C" void wisp_stream_reset(WispStreamCache* c) {
+    if (!c) return;
+    std::lock_guard<std::mutex> g(c->mu);
+    // every queued reader and copy finishes before the slots are forgotten
+    cudaDeviceSynchronize();
+    c->lru.clear([&](const wb::Lru::Entry& v) { c->arena.release(v.data); });
+    std::fill(c->h_tables.begin(), c->h_tables.end(), nullptr);
+    cudaMemset(c->d_tables, 0, c->h_tables.size() * sizeof(void*));
+    std::fill(c->last_use.begin(), c->last_use.end(), -1);
+    std::fill(c->from_prefetch.begin(), c->from_prefetch.end(), 0);
+    std::fill(c->pending.begin(), c->pending.end(), 0);
+    for (auto& v : c->layer_slots) v.clear();
+    c->hits = c->misses = c->prefetched = c->prefetch_used = c->bytes = 0;
 }
 
 extern "C" void wisp_stream_stats(WispStreamCache* c, uint64_t* out6) {

@@ -89,6 +89,7 @@ _SIGS = {
     "wisp_stream_layer_done": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p,
                                          C.POINTER(WispErrCtx)]),
     "wisp_stream_stats": (None, [C.c_void_p, C.c_void_p]),
+    "wisp_stream_reset": (None, [C.c_void_p]),
     "wisp_moe_prefill_routed_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int, C.c_int]),
     "wisp_moe_prefill_routed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,

@@ -17,6 +17,11 @@ identity, csrc/core/wisp_engine.c:1563-1570; tier policy after wisp_expert_fetch
 5. ``wisp_moe_block_experts`` (plan from the routing, gate/up, down, combine), then
    ``wisp_stream_layer_done`` so the slots it reads are not overwritten early.
 
+With a ``tier_cache.ExpertPredictor`` passed to ``step``, each layer's routing is
+recorded and the next layer's most frequent experts are prefetched beside the
+router lookahead's; ``prewarm`` fills a cold cache from a ``LearningCache``'s hottest
+experts (the reference's warm start).
+
 The shared expert, routers and norms stay resident.
 """
 
@@ -111,7 +116,32 @@ class StreamingStack:
         self._pev = torch.cuda.Event()
         self._T = T
 
-    def step(self, x: torch.Tensor, predict: bool = True) -> dict:
+    def reset(self) -> None:
+        """A cold cache: no expert resident, statistics zeroed."""
+        torch.cuda.synchronize(self.device)
+        lib().wisp_stream_reset(self.cache)
+
+    def prewarm(self, pairs) -> int:
+        """Copy the given (layer, expert) pairs into the cache, hottest first, at
+        most one cache's worth; returns the experts copied."""
+        L = lib()
+        err = WispErrCtx()
+        slots = self.stats()["slots"]
+        by_layer: dict[int, list[int]] = {}
+        for layer, e in list(pairs)[:slots]:
+            if 0 <= layer < self.L and 0 <= e < self.shape.n_experts:
+                by_layer.setdefault(layer, []).append(e)
+        n = 0
+        k = C.c_int(0)
+        for layer, ids in by_layer.items():
+            a = (C.c_int * len(ids))(*ids)
+            check(L.wisp_stream_prefetch(self.cache, layer, a, len(ids), C.byref(k), C.byref(err)),
+                  err)
+            n += k.value
+        torch.cuda.synchronize(self.device)
+        return n
+
+    def step(self, x: torch.Tensor, predict: bool = True, predictor=None) -> dict:
         """x <- x + MoE_l(rmsnorm(x)) for every layer, in place (current stream).
         Returns this step's demand hits / misses and prefetches issued."""
         L = lib()
@@ -141,6 +171,8 @@ class StreamingStack:
                                        C.byref(h), C.byref(m), C.byref(err)), err)
             hits += h.value
             misses += m.value
+            if predictor is not None:
+                predictor.observe(l, self._hidx.view(-1).tolist())
             ahead = predict and l + 1 < self.L
             if ahead:
                 check(L.wisp_moe_route(C.byref(self._c[l + 1]), self._xn.data_ptr(), T,
@@ -157,6 +189,13 @@ class StreamingStack:
                 check(L.wisp_stream_prefetch(self.cache, l + 1, self._hpidx.data_ptr(), T * K,
                                              C.byref(k), C.byref(err)), err)
                 issued += k.value
+                if predictor is not None:
+                    freq = predictor.predict(l + 1)
+                    if freq:
+                        a = (C.c_int * len(freq))(*freq)
+                        check(L.wisp_stream_prefetch(self.cache, l + 1, a, len(freq), C.byref(k),
+                                                     C.byref(err)), err)
+                        issued += k.value
         L.wisp_gpu_residual_add(x.data_ptr(), self._y.data_ptr(), T * H, sp)
         return {"hits": hits, "misses": misses, "prefetched": issued}
 
