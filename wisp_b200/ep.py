@@ -112,10 +112,15 @@ class Dispatch:
         send = x.index_select(0, tokens[:n_send])
         self.rows = (exchange_rows(send, self.send_counts, self.recv_counts, group)
                      if world > 1 else send)
-        # local expert ids of the received rows, in source order
-        sel = [s * (1 + B * K) + 1 + j for s in range(world) for j in range(self.recv_counts[s])]
-        self.eids = table.view(-1)[torch.as_tensor(sel, dtype=torch.long,
-                                                   device=x.device)].view(-1, 1)
+        # local expert ids of the received rows, in source order: received row j
+        # came from the rank s whose count range holds j (no host round trip)
+        n_recv = sum(self.recv_counts)
+        rc = table[:, 0].long()
+        end = torch.cumsum(rc, 0)
+        j = torch.arange(n_recv, device=x.device)
+        src = torch.searchsorted(end, j, right=True)
+        sel = src * (1 + B * K) + 1 + (j - (end - rc)[src])
+        self.eids = table.view(-1)[sel].view(-1, 1)
 
     def back(self, out_rows):
         """The expert outputs of the received rows, returned to their home ranks."""
