@@ -360,7 +360,8 @@ def run_single(args, dev) -> dict:
         out["parity"] = {"idx_equal": bool(np.array_equal(ig.cpu().numpy(), iref)),
                          "max_abs": float(np.abs(yg - yref).max()),
                          "rel_l2": float(np.linalg.norm(yg - yref) / np.linalg.norm(yref))}
-    out["gpu_launches_per_step"] = len(seq) * args.layers + 1
+    # per layer, the final combine, and the zeroing of the workspace state
+    out["gpu_launches_per_step"] = len(seq) * args.layers + 2
     del g
     return out
 

@@ -35,6 +35,14 @@ namespace wb {
 // Number of SMs of the current device (cached per device id).
 int sm_count();
 
+// Zero n_words 32-bit words at p (the status word and counters of a
+// workspace) on `stream` with a one-CTA kernel launched like every other
+// kernel of this library (programmatic dependent launch, griddepcontrol.wait
+// before the stores).  A cudaMemsetAsync is not a grid that a following
+// kernel's griddepcontrol.wait waits for, so it is not used for state that
+// the next kernels read.
+cudaError_t launch_zero_words(int* p, int n_words, cudaStream_t stream);
+
 // Launch `kern` with programmatic dependent launch enabled, so its prologue
 // may overlap the tail of the previous kernel on `stream`; the kernel must
 // call griddepcontrol.wait before touching its predecessor's outputs.

@@ -59,7 +59,9 @@ namespace wb {
 namespace {
 
 constexpr int kChunk = 32;      // elements per MMA k-slice (16 packed bytes)
-constexpr int kMT = 4;          // tokens per expert tile (one MMA column quad)
+constexpr int kMT = 4;          // tokens per MMA column quad
+constexpr int kMaxTile = 8;     // tokens per expert tile: one or two column quads
+constexpr int kWideMaxNg = 4;   // quant groups per consumer warp that two quads fit in registers
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kFull = 0xffffffffu;
@@ -72,9 +74,9 @@ enum { ST_ALIGN = 1, ST_EXPERT = 2, ST_PLAN = 4, ST_TIMEOUT = 8, ST_LAYOUT = 16 
 
 struct Tile {
     int expert;  // 0..E-1, or E for the shared expert
-    int m;       // tokens in the tile (1..kMT)
-    int tok[kMT];
-    int asg[kMT];  // assignment ids: t*K + j, or T*K + t for the shared expert
+    int m;       // tokens in the tile (1..kMaxTile)
+    int tok[kMaxTile];
+    int asg[kMaxTile];  // assignment ids: t*K + j, or T*K + t for the shared expert
     const unsigned char* blob;  // the expert's tiled blob, NULL if unusable (status set)
 };
 
@@ -97,7 +99,7 @@ struct LayerArgs {
     int H, I, E, K, gs;
     int has_shared;  // 0 none, 1 int4 blob (a tile of the plan), 2 fp16 dense (dense_ffn.cu)
     int kp;   // K parts of the down projection
-    int act_slots;  // token slots of the staged activation tile (min(T, mt))
+    int act_slots;  // token slots of the staged activation tile (min(T, kMT))
     int mt;         // tokens per expert tile of the plan (1, 4 or 8)
     int gating;     // WISP_GATING_* of the layer
 };
@@ -390,7 +392,7 @@ __device__ void plan_one_token(const LayerArgs& L, const Ws& W, const wisp_route
         tl.expert = e;
         tl.m = 1;
 #pragma unroll
-        for (int i = 0; i < kMT; ++i) tl.tok[i] = tl.asg[i] = 0;
+        for (int i = 0; i < kMaxTile; ++i) tl.tok[i] = tl.asg[i] = 0;
         tl.asg[0] = asg;
         const int code = pcode[e];
         if (code) atomicOr(W.status, code);
@@ -662,11 +664,23 @@ plan_kernel(LayerArgs L, Ws W, int T, int mt) {
     build_plan(L, W, T, mt, smem, smem + kMaxPlanAssign);
 }
 
+// The status word and counters of a workspace, zeroed in stream order (see
+// launch_zero_words).
+__global__ void __launch_bounds__(256) zero_words_kernel(int* p, int n) {
+    pdl_wait();
+    pdl_launch();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = 0;
+}
+
 // y[t] += sum_j w[t,j] * rows[ridx[t,j]] in j order (ridx < 0: skipped); the
 // combine of the expert-parallel path on the tokens' home GPU.
 __global__ void __launch_bounds__(kPrepThreads)
 ep_combine_kernel(float* y, const float* rows, const int* ridx, const float* w, int T, int K,
                   int H) {
+    // y is the output of the previous kernel (the shared expert's combine),
+    // which may have triggered this launch before finishing
+    pdl_wait();
+    pdl_launch();
     const int t = blockIdx.x;
     if (t >= T) return;
     float4* yt = reinterpret_cast<float4*>(y + (size_t)t * H);
@@ -910,9 +924,11 @@ __host__ __device__ inline size_t block_bytes_of(int cols, int gs) {
     return 4 * (size_t)cols + 32 * (size_t)(cols / gs);
 }
 // Activation tile of a K range of ng groups (NPG 32-element chunks each) for
-// kMT token slots.  Quantised (gate/up): the words [slot][chunk][64 B], then
-// (k/254, S) per group [slot][group][16 B].  Float (down): the fp32 rows
-// [slot][ng * gs], quantised by the consumer warps themselves.
+// kMT token slots: one column quad of an expert tile at a time (a tile of
+// more than kMT tokens stages its second quad once the first is in the
+// consumers' registers).  Quantised (gate/up): the words [slot][chunk][64 B],
+// then (k/254, S) per group [slot][group][16 B].  Float (down): the fp32
+// rows [slot][ng * gs], quantised by the consumer warps themselves.
 __host__ __device__ inline uint32_t act_row_bytes(int ng, int npg, bool f32) {
     return (uint32_t)ng * npg * (f32 ? 128u : 64u);
 }
@@ -921,10 +937,12 @@ __host__ __device__ inline uint32_t act_bytes_of(int ng, int npg, bool f32, int 
 }
 
 // Per-stage unit record written by the producer: unit id (| kSkip), or -1 at
-// the end; the tile's token count and assignment ids (for the reducer).
+// the end; the tile's token count, token and assignment ids (the reducer
+// stores by assignment and stages a second column quad by either).
 struct UnitInfo {
     int u, m, tile;  // tile: the tile whose m/asg the record holds
-    int asg[kMT];
+    int asg[kMaxTile];
+    int tok[kMaxTile];
 };
 
 
@@ -933,13 +951,15 @@ struct StreamSmem {
     uint8_t* stages;   // [n_stages][stage_bytes]
     float2* red;       // [n_stages][kNcw][32] consumer partials
     uint8_t* act;      // activation tile (act_bytes_of)
-    float2* kp;        // [kNcw][NGmax][kMT] (k/254, S) of each warp's groups
+    float2* kp;        // [kNcw][NG][MT] (k/254, S) of each warp's groups
     UnitInfo* info;    // [n_stages]
     uint64_t* full;    // [n_stages] weights landed (tx)
     uint64_t* red_bar; // [n_stages] consumer partials written (kNcw arrivals)
     uint64_t* empty;   // [n_stages] stage reusable (reducer)
-    uint64_t* act_full;
-    uint64_t* act_empty;
+    uint64_t* act_full;   // first column quad of a tile staged (producer)
+    uint64_t* act_empty;  // activation tile read (kNcw arrivals)
+    uint64_t* act_mid;    // first quad read, second may be staged (kNcw arrivals)
+    uint64_t* act_full2;  // second column quad staged (reducer)
     uint32_t stage_bytes, act_row, act_bytes;
     int act_slots;
     int n_stages;
@@ -948,17 +968,19 @@ struct StreamSmem {
 __host__ __device__ constexpr size_t red_bytes_per_stage(int mt) {
     return (size_t)kNcw * 32 * 8 * (mt / 4);
 }
-// (k/254, S) pairs: every group of a unit's K range x the tile width.
-__host__ __device__ constexpr size_t kp_bytes(int mt) { return (size_t)(kMaxPartK / 32) * mt * 8; }
+// (k/254, S) pairs: each consumer warp's ng groups x the tile width.
+__host__ __device__ constexpr size_t kp_bytes(int ng, int mt) {
+    return (size_t)kNcw * ng * mt * 8;
+}
 __host__ __device__ inline size_t stream_smem_bytes(int n_stages, uint32_t stage_bytes,
-                                                     uint32_t act_bytes, int mt) {
+                                                     uint32_t act_bytes, int mt, int ng) {
     return (size_t)n_stages * (stage_bytes + red_bytes_per_stage(mt) + sizeof(UnitInfo) + 24) +
-           (act_bytes + 127) / 128 * 128 + kp_bytes(mt) + 16 + 128;
+           (act_bytes + 127) / 128 * 128 + kp_bytes(ng, mt) + 32 + 128;
 }
 // The float path (down) quantises its rows in place in the activation tile.
 __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
                                                   uint32_t stage_bytes, const Geo& geo, int npg,
-                                                  bool f32, int slots, int mt) {
+                                                  bool f32, int slots, int mt, int ng) {
     StreamSmem s;
     s.stage_bytes = stage_bytes;
     s.n_stages = n_stages;
@@ -973,7 +995,7 @@ __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
     s.red = reinterpret_cast<float2*>(base + o);
     o += (size_t)n_stages * red_bytes_per_stage(mt);
     s.kp = reinterpret_cast<float2*>(base + o);
-    o += kp_bytes(mt);
+    o += kp_bytes(ng, mt);
     s.info = reinterpret_cast<UnitInfo*>(base + o);
     o += (size_t)n_stages * sizeof(UnitInfo);
     o = (o + 7) & ~size_t(7);
@@ -982,6 +1004,8 @@ __device__ __forceinline__ StreamSmem stream_smem(uint8_t* base, int n_stages,
     s.empty = s.red_bar + n_stages;
     s.act_full = s.empty + n_stages;
     s.act_empty = s.act_full + 1;
+    s.act_mid = s.act_full + 2;
+    s.act_full2 = s.act_full + 3;
     return s;
 }
 __device__ __forceinline__ void stream_init(const StreamSmem& S) {
@@ -993,6 +1017,8 @@ __device__ __forceinline__ void stream_init(const StreamSmem& S) {
         }
         mbar_init(S.act_full, 1);
         mbar_init(S.act_empty, kNcw);
+        mbar_init(S.act_mid, kNcw);
+        mbar_init(S.act_full2, 1);
         for (int s = 0; s < S.n_stages; ++s) S.info[s].tile = -1;
         mbar_fence_init();
     }
@@ -1082,16 +1108,17 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
         if (lane == 0) v = mbar_wait(bar, parity) ? 1 : 0;
         return __shfl_sync(kFull, v, 0) != 0;
     };
-    // activation tile of `cur`, once the consumers copied the previous one;
-    // one copy per lane
+    // activation tile of `cur` (its first column quad), once the consumers
+    // copied the previous one; one copy per lane
     auto issue_act = [&]() -> bool {
         if (!waited_pdl) {
             pdl_wait();
             waited_pdl = true;
         }
         if (tiles_done > 0 && !wait0(S.act_empty, (tiles_done - 1) & 1)) return false;
+        const int m0 = min(cur.m, S.act_slots);
         if (f32) {
-            copy_rows_lsu(S.act, rowb, cur.m, [&](int t) {
+            copy_rows_lsu(S.act, rowb, m0, [&](int t) {
                 const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
                 return as.xf + (size_t)row * as.row_elems + (size_t)as.kg0 * as.gs;
             }, S.act_full);
@@ -1099,10 +1126,10 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
             act_due = false;
             return true;
         }
-        if (lane == 0) mbar_expect_tx(S.act_full, (uint32_t)cur.m * (rowb + pb));
+        if (lane == 0) mbar_expect_tx(S.act_full, (uint32_t)m0 * (rowb + pb));
         __syncwarp();
         const int t = lane / 2;
-        if (t < cur.m) {
+        if (t < m0) {
             const int row = as.by_asg ? cur.asg[t] : cur.tok[t];
             if ((lane & 1) == 0) {
                 bulk_g2s_plain(S.act + t * rowb,
@@ -1147,7 +1174,10 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
                 inf.tile = ti;
                 inf.m = cur.m;
 #pragma unroll
-                for (int t = 0; t < kMT; ++t) inf.asg[t] = cur.asg[t];
+                for (int t = 0; t < kMaxTile; ++t) {
+                    inf.asg[t] = cur.asg[t];
+                    inf.tok[t] = cur.tok[t];
+                }
             }
             inf.u = tile_ok ? u : (u | kSkip);
             if (tile_ok)
@@ -1195,11 +1225,15 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
 
 // Reducer (warp 1): per unit, once the consumers' partials are in, sum them in
 // warp order (deterministic) and store the result; then release the stage.
-// out(u, asg, g, sum) is called by lane (g, q) for token slot q < m.
-template <int MT, typename Out>
-__device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
+// out(u, asg, g, sum) is called by lane (g, q) for token slot q < m.  At the
+// first unit of a tile of more than kMT tokens it also stages the tile's
+// second column quad (stage2(inf): copies into the activation tile that
+// complete S.act_full2) once the consumers have read the first (S.act_mid):
+// the weight producer keeps streaming meanwhile.
+template <int MT, typename Out, typename Stage2>
+__device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out, Stage2 stage2) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-    int s = 0;
+    int s = 0, last_tile = -1, wide = 0;
     uint32_t ph = 0;
     for (;;) {
         if (!mbar_wait(&S.full[s], ph)) {
@@ -1209,6 +1243,20 @@ __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
         const UnitInfo& inf = S.info[s];
         const int u = *reinterpret_cast<const volatile int*>(&inf.u);
         if (u == -1) break;
+        if constexpr (MT > kMT) {
+            const int ti = *reinterpret_cast<const volatile int*>(&inf.tile);
+            if (ti != last_tile) {
+                last_tile = ti;
+                if (inf.m > kMT) {
+                    if (!mbar_wait(S.act_mid, wide & 1)) {
+                        if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+                        break;
+                    }
+                    stage2(inf);
+                    ++wide;
+                }
+            }
+        }
         if (!mbar_wait(&S.red_bar[s], ph)) {
             if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
             break;
@@ -1236,6 +1284,8 @@ __device__ void reduce_units(const StreamSmem& S, const Ws& W, Out out) {
             ph ^= 1;
         }
     }
+    // copies of a second quad that no consumer waited for (error paths)
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ------------------------------------------------------------------------
@@ -1309,38 +1359,36 @@ struct WarpAct {
     uint2 b[NG][NPG][MT / 4];  // per token quad: slots 4h .. 4h+3
 };
 
-// Copy the warp's B fragments and (k/254, S) pairs of the current tile from
-// the staged activation tile (slots t < m; the rest are zero).
-template <int NPG, int NG, int MT>
+// Copy the warp's B fragments and (k/254, S) pairs of column quad QH of the
+// current tile from the staged activation tile (slots t < m hold tokens
+// 4*QH + t; the rest are zero).
+template <int NPG, int NG, int MT, int QH>
 __device__ __forceinline__ void load_act(WarpAct<NPG, NG, MT>& A, float2* kp_w,
                                          const StreamSmem& S, int g0, int n, int m) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     const int bd = g & 1;
+    const int bt = g >> 1;
+    const uint32_t base = smem_addr(S.act) + bt * S.act_row + bd * 32;
 #pragma unroll
-    for (int h = 0; h < MT / 4; ++h) {
-        const int bt = 4 * h + (g >> 1);
-        const uint32_t base = smem_addr(S.act) + bt * S.act_row + bd * 32;
+    for (int G = 0; G < NG; ++G) {
 #pragma unroll
-        for (int G = 0; G < NG; ++G) {
-#pragma unroll
-            for (int i = 0; i < NPG; ++i) {
-                const int wi = q * NPG + i;
-                const int chunk = (g0 + G) * NPG + (wi >> 2);
-                A.b[G][i][h] = (G < n && bt < m) ? lds64(base + chunk * 64 + (wi & 3) * 8)
-                                                 : make_uint2(0u, 0u);
-            }
+        for (int i = 0; i < NPG; ++i) {
+            const int wi = q * NPG + i;
+            const int chunk = (g0 + G) * NPG + (wi >> 2);
+            A.b[G][i][QH] = (G < n && bt < m) ? lds64(base + chunk * 64 + (wi & 3) * 8)
+                                              : make_uint2(0u, 0u);
         }
     }
     const float4* par = reinterpret_cast<const float4*>(S.act + S.act_slots * S.act_row);
     const int ngr = (int)(S.act_row / (64u * NPG));  // groups in the range
-    for (int e = lane; e < NG * MT; e += 32) {
-        const int G = e / MT, t = e - G * MT;
+    for (int e = lane; e < NG * kMT; e += 32) {
+        const int G = e / kMT, t = e - G * kMT;
         float2 v = make_float2(0.f, 0.f);
         if (G < n && t < m) {
             const float4 p = par[t * ngr + g0 + G];
             v = make_float2(p.x, p.y);
         }
-        kp_w[e] = v;
+        kp_w[G * MT + QH * kMT + t] = v;
     }
     __syncwarp();
 }
@@ -1377,41 +1425,38 @@ __device__ __forceinline__ void quant_rows_in_place(const StreamSmem& S, int row
     }
 }
 
-// B fragments and (k/254, S) pairs of the warp's groups for a tile of m
-// tokens whose fp32 rows (slots 0..m-1 of the activation tile) were
-// quantised in place: group G of a slot at G * gs*4 bytes, its NPG digit
-// chunks first, then its float4.
-template <int NPG, int NG, int MT>
+// B fragments and (k/254, S) pairs of the warp's groups for column quad QH
+// of a tile, whose m fp32 rows (slots 0..m-1 of the activation tile, tokens
+// 4*QH + t) were quantised in place: group G of a slot at G * gs*4 bytes, its
+// NPG digit chunks first, then its float4.
+template <int NPG, int NG, int MT, int QH>
 __device__ __forceinline__ void load_act_inplace(WarpAct<NPG, NG, MT>& A, float2* kp_w,
                                                  const StreamSmem& S, int g0, int n, int m) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     const int bd = g & 1;
     constexpr uint32_t kGstride = NPG * 128u;
     const uint32_t act = smem_addr(S.act);
+    const int bt = g >> 1;
+    const uint32_t base = act + (bt < m ? bt : 0) * S.act_row + bd * 32;
 #pragma unroll
-    for (int h = 0; h < MT / 4; ++h) {
-        const int bt = 4 * h + (g >> 1);
-        const uint32_t base = act + (bt < m ? bt : 0) * S.act_row + bd * 32;
+    for (int G = 0; G < NG; ++G) {
 #pragma unroll
-        for (int G = 0; G < NG; ++G) {
-#pragma unroll
-            for (int i = 0; i < NPG; ++i) {
-                const int wi = q * NPG + i;
-                A.b[G][i][h] = (G < n && bt < m)
-                                   ? lds64(base + (g0 + G) * kGstride + (wi >> 2) * 64 + (wi & 3) * 8)
-                                   : make_uint2(0u, 0u);
-            }
+        for (int i = 0; i < NPG; ++i) {
+            const int wi = q * NPG + i;
+            A.b[G][i][QH] = (G < n && bt < m)
+                                ? lds64(base + (g0 + G) * kGstride + (wi >> 2) * 64 + (wi & 3) * 8)
+                                : make_uint2(0u, 0u);
         }
     }
-    for (int e = lane; e < NG * MT; e += 32) {
-        const int G = e / MT, t = e - G * MT;
+    for (int e = lane; e < NG * kMT; e += 32) {
+        const int G = e / kMT, t = e - G * kMT;
         float2 v = make_float2(0.f, 0.f);
         if (G < n && t < m) {
             const float4 p = *reinterpret_cast<const float4*>(
                 S.act + (size_t)t * S.act_row + (size_t)(g0 + G) * kGstride + NPG * 64);
             v = make_float2(p.x, p.y);
         }
-        kp_w[e] = v;
+        kp_w[G * MT + QH * kMT + t] = v;
     }
     __syncwarp();
 }
@@ -1478,7 +1523,7 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
     float2* kp_w = S.kp + cw * NG * MT;
     const uint32_t st0 = smem_addr(S.stages), kp = smem_addr(kp_w);
     WarpAct<NPG, NG, MT> A;
-    int tile_end = -1, tiles = 0, s = 0;
+    int tile_end = -1, tiles = 0, wide = 0, s = 0, nq = 1;
     uint32_t ph = 0;
     for (;;) {
         if (!mbar_wait(&S.full[s], ph)) {
@@ -1495,11 +1540,30 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
                 if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
                 break;
             }
+            const int m = inf.m, m0 = min(m, kMT);
             if constexpr (F32) {
-                quant_rows_in_place<NPG>(S, inf.m, g0, n);
-                load_act_inplace<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m);
+                quant_rows_in_place<NPG>(S, m0, g0, n);
+                load_act_inplace<NPG, NG, MT, 0>(A, kp_w, S, g0, n, m0);
             } else {
-                load_act<NPG, NG, MT>(A, kp_w, S, g0, n, inf.m);
+                load_act<NPG, NG, MT, 0>(A, kp_w, S, g0, n, m0);
+            }
+            nq = 1;
+            if constexpr (MT > kMT) {
+                if (m > kMT) {  // the second column quad, staged by the reducer
+                    if (lane == 0) mbar_arrive(S.act_mid);
+                    if (!mbar_wait(S.act_full2, wide & 1)) {
+                        if (lane == 0) atomicOr(W.status, ST_TIMEOUT);
+                        break;
+                    }
+                    ++wide;
+                    if constexpr (F32) {
+                        quant_rows_in_place<NPG>(S, m - kMT, g0, n);
+                        load_act_inplace<NPG, NG, MT, 1>(A, kp_w, S, g0, n, m - kMT);
+                    } else {
+                        load_act<NPG, NG, MT, 1>(A, kp_w, S, g0, n, m - kMT);
+                    }
+                    nq = 2;
+                }
             }
             if (lane == 0) mbar_arrive(S.act_empty);
             ++tiles;
@@ -1508,11 +1572,19 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
 #pragma unroll
         for (int h = 0; h < MT / 4; ++h) part[h] = make_float2(0.f, 0.f);
         if (!(uf & kSkip)) {
-            mma_unit<NPG, NG, MT, MT / 4>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+            if constexpr (MT > kMT) {
+                if (nq == 2)
+                    mma_unit<NPG, NG, MT, 2>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+                else
+                    mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+            } else {
+                mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+            }
         }
         float2* red = S.red + ((size_t)s * kNcw + cw) * 32 * (MT / 4);
 #pragma unroll
-        for (int h = 0; h < MT / 4; ++h) red[h * 32 + lane] = part[h];
+        for (int h = 0; h < MT / 4; ++h)
+            if (h < nq) red[h * 32 + lane] = part[h];
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.red_bar[s]);
         if (++s == S.n_stages) {
@@ -1532,7 +1604,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int H = L.H, I = L.I, gs = L.gs;
     const Geo geo = make_geo(H / gs, gs);
     const StreamSmem S =
-        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots, MT);
+        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, false, L.act_slots, MT, NG);
     stream_init(S);
     pdl_wait();
     pdl_launch();
@@ -1555,10 +1627,30 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
         return;
     }
     if (warp == 1) {
-        reduce_units<MT>(S, W, [&](int u, int asg, int g, float2 v) {
-            const size_t row = (size_t)(u % rbs) * 8 + g;
-            W.h[(size_t)asg * I + row] = v.x / (1.0f + expf(-v.x)) * v.y;
-        });
+        const int lane = threadIdx.x & 31;
+        const uint32_t rowb = act_row_bytes(geo.ng, NPG, false), pb = (uint32_t)geo.ng * 16u;
+        reduce_units<MT>(
+            S, W,
+            [&](int u, int asg, int g, float2 v) {
+                const size_t row = (size_t)(u % rbs) * 8 + g;
+                W.h[(size_t)asg * I + row] = v.x / (1.0f + expf(-v.x)) * v.y;
+            },
+            [&](const UnitInfo& inf) {  // tokens kMT.. of the tile: words, then (k/254, S)
+                const int m2 = inf.m - kMT;
+                for (int t = 0; t < m2; ++t) {
+                    const int tok = inf.tok[kMT + t];
+                    const uint8_t* xw = reinterpret_cast<const uint8_t*>(W.xq) +
+                                        (size_t)tok * (H / kChunk) * 64;
+                    const uint8_t* xp = reinterpret_cast<const uint8_t*>(W.xqp + (size_t)tok * (H / gs));
+                    for (uint32_t i = lane; i < rowb / 16; i += 32)
+                        ldgsts16(S.act + (size_t)t * rowb + i * 16, xw + i * 16);
+                    for (uint32_t i = lane; i < pb / 16; i += 32)
+                        ldgsts16(S.act + (size_t)S.act_slots * rowb + t * pb + i * 16, xp + i * 16);
+                }
+                ldgsts_arrive(S.act_full2);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(S.act_full2);
+            });
         return;
     }
     consume<NPG, NG, MT, false>(S, W, geo, rbs);
@@ -1579,7 +1671,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
     const int ngp = I / gs / kp;  // groups per part
     const Geo geo = make_geo(ngp, gs);
     const StreamSmem S =
-        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots, MT);
+        stream_smem(smem_raw, n_stages, stage_bytes, geo, NPG, true, L.act_slots, MT, NG);
     stream_init(S);
     // Weights, the expert table and the tile plan (written by the router,
     // which completed before the gate/up kernel could start) do not depend on
@@ -1616,17 +1708,25 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
                 Tile tl;
                 load_tile(W.tiles + b / upt, tl);
                 pdl_wait();
-                copy_rows_lsu(S.act, act_row_bytes(ngp, NPG, true), tl.m, [&](int t) {
+                copy_rows_lsu(S.act, act_row_bytes(ngp, NPG, true), min(tl.m, S.act_slots),
+                              [&](int t) {
                     return W.h + (size_t)tl.asg[t] * I + (size_t)pi * ngp * gs;
                 }, S.act_full);
             }
         }
-        reduce_units<MT>(S, W, [&](int u, int asg, int g, float2 v) {
-            const size_t row = (size_t)(u % upt) * 16 + g;
-            float* dst = W.ypart + ((size_t)pi * W.A + asg) * H + row;
-            dst[0] = v.x;
-            dst[8] = v.y;
-        });
+        reduce_units<MT>(
+            S, W,
+            [&](int u, int asg, int g, float2 v) {
+                const size_t row = (size_t)(u % upt) * 16 + g;
+                float* dst = W.ypart + ((size_t)pi * W.A + asg) * H + row;
+                dst[0] = v.x;
+                dst[8] = v.y;
+            },
+            [&](const UnitInfo& inf) {  // rows of assignments kMT.. of the tile
+                copy_rows_lsu(S.act, act_row_bytes(ngp, NPG, true), inf.m - kMT, [&](int t) {
+                    return W.h + (size_t)inf.asg[kMT + t] * I + (size_t)pi * ngp * gs;
+                }, S.act_full2);
+            });
         return;
     }
     consume<NPG, NG, MT, true>(S, W, geo, upt);
@@ -1826,15 +1926,16 @@ StreamCfg plan_stream(const Geo& geo, int npg, bool f32, int slots, int mt) {
     StreamCfg c;
     c.stage_bytes = stage_bytes_of(geo);
     const uint32_t act = act_bytes_of(geo.ng, npg, f32, slots);
+    const int ng = ng_bucket(npg, geo.ng);
     int want = (int)((kInFlight + c.stage_bytes / 2) / c.stage_bytes);
     want = std::max(2, std::min(kMaxStages, want));
     c.stages = 0;
     for (int st = want; st >= 2; --st)
-        if (stream_smem_bytes(st, c.stage_bytes, act, mt) <= kSmemPerCta) {
+        if (stream_smem_bytes(st, c.stage_bytes, act, mt, ng) <= kSmemPerCta) {
             c.stages = st;
             break;
         }
-    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, mt);
+    c.smem = stream_smem_bytes(c.stages, c.stage_bytes, act, mt, ng);
     return c;
 }
 
@@ -1862,12 +1963,23 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.sd = reinterpret_cast<const __half*>(ly->shared_down);
     a.si = a.has_shared == 2 ? ly->shared_inter : 0;
     a.gating = ly->gating;
-    // Tokens per expert tile: 4 (one MMA column quad).
-    a.mt = kMT;
+    // Tokens per expert tile: up to 4 (one MMA column quad) while no expert can
+    // have more (T <= 4); beyond, up to 8, so an expert with 5..8 tokens
+    // streams its weights once instead of twice.  The activation tile stages
+    // one quad at a time either way.
+    // (Two quads hold twice the B fragments in registers: past 4 groups per
+    // consumer warp -- H above 64 quant groups -- they spill, and the layer
+    // keeps 4-token tiles.)
+    const int npg = a.gs / kChunk;
+    a.mt = T > kMT && ng_bucket(npg, a.H / a.gs) <= kWideMaxNg ? kMaxTile : kMT;
     a.act_slots = std::min(T, kMT);
     const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
-                            (a.has_shared == 1 ? (T + kMT - 1) / kMT : 0);
-    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, kMT);
+                            (a.has_shared == 1 ? (T + a.mt - 1) / a.mt : 0);
+    a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, a.mt);
+    if (a.mt == kMaxTile && ng_bucket(npg, a.I / a.gs / a.kp) > kWideMaxNg) {
+        a.mt = kMT;
+        a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, a.mt);
+    }
     return a;
 }
 
@@ -2040,6 +2152,18 @@ cudaError_t launch_gateup_any(int npg, int ng, int mt, const LayerArgs& a, const
         case 4208: return launch_gateup<2, 8, 4>(a, W, s);
         case 4401: return launch_gateup<4, 1, 4>(a, W, s);
         case 4402: return launch_gateup<4, 2, 4>(a, W, s);
+        case 8101: return launch_gateup<1, 1, 8>(a, W, s);
+        case 8102: return launch_gateup<1, 2, 8>(a, W, s);
+        case 8104: return launch_gateup<1, 4, 8>(a, W, s);
+        case 8108: return launch_gateup<1, 8, 8>(a, W, s);
+        case 8116: return launch_gateup<1, 16, 8>(a, W, s);
+        case 8201: return launch_gateup<2, 1, 8>(a, W, s);
+        case 8202: return launch_gateup<2, 2, 8>(a, W, s);
+        case 8204: return launch_gateup<2, 4, 8>(a, W, s);
+        case 8207: return launch_gateup<2, 7, 8>(a, W, s);
+        case 8208: return launch_gateup<2, 8, 8>(a, W, s);
+        case 8401: return launch_gateup<4, 1, 8>(a, W, s);
+        case 8402: return launch_gateup<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
@@ -2059,6 +2183,18 @@ cudaError_t launch_down_any(int npg, int ng, int mt, const LayerArgs& a, const W
         case 4208: return launch_down<2, 8, 4>(a, W, s);
         case 4401: return launch_down<4, 1, 4>(a, W, s);
         case 4402: return launch_down<4, 2, 4>(a, W, s);
+        case 8101: return launch_down<1, 1, 8>(a, W, s);
+        case 8102: return launch_down<1, 2, 8>(a, W, s);
+        case 8104: return launch_down<1, 4, 8>(a, W, s);
+        case 8108: return launch_down<1, 8, 8>(a, W, s);
+        case 8116: return launch_down<1, 16, 8>(a, W, s);
+        case 8201: return launch_down<2, 1, 8>(a, W, s);
+        case 8202: return launch_down<2, 2, 8>(a, W, s);
+        case 8204: return launch_down<2, 4, 8>(a, W, s);
+        case 8207: return launch_down<2, 7, 8>(a, W, s);
+        case 8208: return launch_down<2, 8, 8>(a, W, s);
+        case 8401: return launch_down<4, 1, 8>(a, W, s);
+        case 8402: return launch_down<4, 2, 8>(a, W, s);
         default: return cudaErrorInvalidConfiguration;
     }
 }
@@ -2119,6 +2255,10 @@ cudaError_t launch_prep_route(const LayerArgs& a, const Ws& W, int T, int flags,
 }  // namespace
 
 int sm_count() { return dev_info().sms; }
+
+cudaError_t launch_zero_words(int* p, int n_words, cudaStream_t stream) {
+    return launch_pdl(zero_words_kernel, dim3(1), dim3(256), 0, stream, p, n_words);
+}
 
 }  // namespace wb
 
@@ -2194,7 +2334,9 @@ static WispError block_route(const WispMoeLayer* layer, const float* x, int T, i
     if (topk_idx) W.topk_idx = topk_idx;
     if (topk_w) W.topk_w = topk_w;
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    WB_CUDA_RET(launch_zero_words(static_cast<int*>(workspace),
+                                  (int)((lo.counters + kCounters * sizeof(int)) / 4), stream),
+                err);
     WB_CUDA_RET(launch_prep_route(a, W, T, (int)P_QUANT, const_cast<float*>(x), 0.f, 0, 0, 1, x,
                                   stream, plan),
                 err);
@@ -2301,7 +2443,8 @@ extern "C" WispError wisp_moe_stack_forward(const WispMoeLayer* layers, int n_la
     WB_CUDA_RET(ensure_attrs(H), err);
     {
         const Layout lo0 = make_layout(T, H, maxI, maxE, maxK, anysh, maxSI);
-        WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo0.counters + kCounters * sizeof(int), stream),
+        WB_CUDA_RET(launch_zero_words(static_cast<int*>(workspace),
+                                      (int)((lo0.counters + kCounters * sizeof(int)) / 4), stream),
                     err);
     }
     int prevK = 0, prev_sh = 0, prev_kp = 1;
@@ -2365,7 +2508,9 @@ extern "C" WispError wisp_moe_experts_routed(const WispMoeLayer* layer, const fl
     W.topk_idx = const_cast<int*>(topk_idx);
     W.topk_w = const_cast<float*>(topk_w);
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    WB_CUDA_RET(launch_zero_words(static_cast<int*>(workspace),
+                                  (int)((lo.counters + kCounters * sizeof(int)) / 4), stream),
+                err);
     WB_CUDA_RET(launch_prep(a, W, T, (int)P_QUANT, const_cast<float*>(x), nullptr, 0.f, 0, 0, 1,
                             stream),
                 err);
@@ -2394,7 +2539,9 @@ extern "C" WispError wisp_moe_route(const WispMoeLayer* layer, const float* x, i
     W.topk_idx = topk_idx;
     W.topk_w = topk_w;
     WB_CUDA_RET(ensure_attrs(a.H), err);
-    WB_CUDA_RET(cudaMemsetAsync(workspace, 0, lo.counters + kCounters * sizeof(int), stream), err);
+    WB_CUDA_RET(launch_zero_words(static_cast<int*>(workspace),
+                                  (int)((lo.counters + kCounters * sizeof(int)) / 4), stream),
+                err);
     const int cs = prep_cluster(a.H, a.gs);
     const bool fused = route_in_prep(a, T);
     hook_mark(stream);

@@ -1415,7 +1415,7 @@ WispError prefill_block(const WispMoeLayer* layer, const float* x, float* y, int
     WB_CUDA_RET(ensure_gemm_attrs(), err);
     // the plan kernel rewrites the tile counters; the status word accumulates
     // over the blocks of a stack
-    if (reset_status) WB_CUDA_RET(cudaMemsetAsync(W.status, 0, sizeof(int), stream), err);
+    if (reset_status) WB_CUDA_RET(wb::launch_zero_words(W.status, 1, stream), err);
     const int sms = wb::sm_count();
     if (!route) {
         // routing given: straight to the plan

@@ -242,7 +242,7 @@ def bench_main(args) -> None:
                          "peak_source": pk["source"]},
             "clocks": head["clocks"],
             "e2e": head["e2e"],
-            "gpu_launches": (launches_per_layer(shape, mb) * per + 1) * head["M"] * args.steps
+            "gpu_launches": (launches_per_layer(shape, mb) * per + 2) * head["M"] * args.steps
                             * world,
             "weak_scaling": {"tokens_per_s": round(weak["value"], 2),
                              "ms_per_step": round(weak["ms"], 4), "global_batch": B * world,
