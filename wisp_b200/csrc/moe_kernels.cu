@@ -1025,11 +1025,26 @@ __device__ __forceinline__ void stream_init(const StreamSmem& S) {
     __syncthreads();
 }
 
-__device__ __forceinline__ void load_tile(const Tile* src, Tile& tl) {
-    const int* s = reinterpret_cast<const int*>(src);
-    int* d = reinterpret_cast<int*>(&tl);
+// A tile record as a streaming kernel built for MT-token tiles holds it: the
+// plan's slots past MT are never used there, and not carrying them keeps the
+// producer's copies of the current and next record small.
+template <int MT>
+struct TileView {
+    int m;
+    int tok[MT];
+    int asg[MT];
+    const unsigned char* blob;
+};
+template <int MT>
+__device__ __forceinline__ void load_tile(const Tile* src, TileView<MT>& tl) {
+    tl.m = __ldcg(&src->m);
 #pragma unroll
-    for (int i = 0; i < (int)(sizeof(Tile) / 4); ++i) d[i] = __ldcg(s + i);
+    for (int i = 0; i < MT; ++i) {
+        tl.tok[i] = __ldcg(&src->tok[i]);
+        tl.asg[i] = __ldcg(&src->asg[i]);
+    }
+    tl.blob = reinterpret_cast<const unsigned char*>(
+        __ldcg(reinterpret_cast<const unsigned long long*>(&src->blob)));
 }
 
 // Where the producer finds a tile's activations: quantised rows `xq`
@@ -1067,7 +1082,7 @@ struct UnitAddr {
 // the small activation loads behind ~28 MB of weight copies, and the down
 // projection is bound by its consumers once h is complete, not by DRAM.
 constexpr int kPrePdlStages = 2;
-template <typename Dummy = void>
+template <int MT>
 __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
                         int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
                         const UnitAddr& ua, bool first_act_elsewhere = false) {
@@ -1082,7 +1097,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
     const uint32_t csize = (lane & 1) ? zb : geo.pbytes;
     const size_t coff = lane < 4 ? ua.coff[lane] : 0;
     int ti = u_begin / upt, r = u_begin - ti * upt;
-    Tile cur, nxt;
+    TileView<MT> cur, nxt;
     if (u_begin < u_end) load_tile(W.tiles + ti, cur);
     if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
     const unsigned char* p = nullptr;
@@ -1174,7 +1189,7 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
                 inf.tile = ti;
                 inf.m = cur.m;
 #pragma unroll
-                for (int t = 0; t < kMaxTile; ++t) {
+                for (int t = 0; t < MT; ++t) {
                     inf.asg[t] = cur.asg[t];
                     inf.tok[t] = cur.tok[t];
                 }
@@ -1622,7 +1637,7 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, nullptr, H / kChunk,
                             H / gs, 0, NPG, gs, H, false};
             const UnitAddr ua{off_g, bb, {0, 4 * (size_t)H, off_u - off_g, off_u - off_g + 4 * (size_t)H}};
-            produce(S, W, b, e, rbs, ntiles, geo, as, false, ua);
+            produce<MT>(S, W, b, e, rbs, ntiles, geo, as, false, ua);
         }
         return;
     }
@@ -1695,7 +1710,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const size_t p_off = (size_t)pi * geo.pbytes;
             const ActSrc as{nullptr, nullptr, W.h, I / kChunk, I / gs, pi * ngp, NPG, gs, I, true};
             const UnitAddr ua{L.mat[2].packed, 2 * bb, {p_off, z_off, bb + p_off, bb + z_off}};
-            produce(S, W, b, e, upt, ntiles, geo, as, true, ua, true);
+            produce<MT>(S, W, b, e, upt, ntiles, geo, as, true, ua, true);
         }
         return;
     }
@@ -1705,7 +1720,7 @@ down_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const int j = blockIdx.x / kp;
             const int b = (int)(total * j / cpp), e = (int)(total * (j + 1) / cpp);
             if (b < e) {
-                Tile tl;
+                TileView<kMT> tl;
                 load_tile(W.tiles + b / upt, tl);
                 pdl_wait();
                 copy_rows_lsu(S.act, act_row_bytes(ngp, NPG, true), min(tl.m, S.act_slots),
