@@ -134,6 +134,16 @@ __device__ __forceinline__ void pdl_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 // Split cluster barrier (all threads of every CTA of the cluster).
+// Atomic add with release (this CTA's earlier writes, ordered by a preceding
+// __syncthreads, become visible with it) and acquire (the writes released by
+// earlier adders become visible to this thread, and after a __syncthreads to
+// its CTA): the "last CTA to finish" election without a separate fence.
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+                 : "memory");
+    return old;
+}
 __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
@@ -272,52 +282,68 @@ __device__ const unsigned char* checked_blob(const LayerArgs& L, const Ws& W, in
     return code ? nullptr : b;
 }
 
-// Tiles of up to mt tokens per routed expert (and the shared expert's
-// tiles).  pblob / pcode: the experts' blob pointers and check codes probed
-// earlier (indices 0..E, E = the shared expert), or NULL to probe here.
+// Shared memory of the plan builder, in ints: the routing [NA] (kMaxPlanAssign
+// slots), then per expert its count and its first tile (2E + 2), rounded up.
+__host__ __device__ constexpr int plan_scratch_ints(int E) { return kMaxPlanAssign + 2 * E + 64; }
+
+// Tiles of up to mt tokens per routed expert, in expert order, each expert's
+// tokens in assignment order (then the shared expert's tiles).  pblob / pcode:
+// the experts' blob pointers and check codes probed earlier (indices 0..E,
+// E = the shared expert), or NULL to probe here.  s_idx: kMaxPlanAssign ints,
+// s_cnt: 2E + 2 ints of shared memory.  Every step is spread over the block:
+// one warp ranks each assignment within its expert (a match over 32
+// assignments at a time, in order), one warp scans the experts' tile counts,
+// and the tile records are written field by field by all threads.
 __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
                            int* s_idx, int* s_cnt, const unsigned char* const* pblob = nullptr,
                            const int* pcode = nullptr) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
     const int K = L.K, E = L.E, NA = T * K;
-    for (int a = tid; a < NA; a += kThreads) s_idx[a] = __ldcg(W.topk_idx + a);
+    int* s_off = s_cnt + E + 1;  // [E + 1]: first tile of each expert, then the total
+    for (int a = tid; a < NA; a += nthr) s_idx[a] = __ldcg(W.topk_idx + a);
+    for (int e = tid; e <= E; e += nthr) s_cnt[e] = 0;
     __syncthreads();
-    // tiles per expert; experts e = tid, tid + 256, ... (E <= 1024)
-    int my_tiles[4] = {0, 0, 0, 0};
-    int local = 0;
-    for (int r = 0; r < 4; ++r) {
-        int e = tid + r * kThreads;
-        if (e < E) {
-            int cnt = 0;
-            for (int a = 0; a < NA; ++a) cnt += (s_idx[a] == e);
-            my_tiles[r] = (cnt + mt - 1) / mt;
-            local += my_tiles[r];
+    // rank of each assignment among its expert's (stable): s_idx[a] becomes
+    // e | rank << 10, or -1 for a slot that routes nowhere
+    if (warp == 0) {
+        for (int c = 0; c < NA; c += 32) {
+            const int a = c + lane;
+            const int e = a < NA ? s_idx[a] : -1;
+            const bool ok = e >= 0 && e < E;
+            const unsigned grp = __match_any_sync(kFull, ok ? e : (1 << 20) + lane);
+            const int leader = __ffs(grp) - 1;
+            int base = 0;
+            if (ok && lane == leader) {
+                base = s_cnt[e];
+                s_cnt[e] = base + __popc(grp);
+            }
+            base = __shfl_sync(kFull, base, leader);
+            if (a < NA) s_idx[a] = ok ? (e | ((base + __popc(grp & ((1u << lane) - 1u))) << 10)) : -1;
+            __syncwarp();
         }
     }
-    // block exclusive scan of `local` (experts ordered by thread, then round:
-    // tile order does not affect any result, each row is per-token).
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int v = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += v;
-    }
-    if (lane == 31) s_cnt[warp] = incl;
     __syncthreads();
+    // first tile of each expert: exclusive scan of ceil(count / mt), experts
+    // split into contiguous runs of `per` per lane
     if (warp == 0) {
-        int v = lane < kWarps ? s_cnt[lane] : 0;
-        int inc = v;
+        const int per = (E + 31) / 32, e0 = lane * per, e1 = min(E, e0 + per);
+        int sum = 0;
+        for (int e = e0; e < e1; ++e) sum += (s_cnt[e] + mt - 1) / mt;
+        int inc = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            int u = __shfl_up_sync(kFull, inc, o);
-            if (lane >= o) inc += u;
+            const int v = __shfl_up_sync(kFull, inc, o);
+            if (lane >= o) inc += v;
         }
-        if (lane < kWarps) s_cnt[kWarps + lane] = inc - v;  // exclusive
-        if (lane == kWarps - 1) s_cnt[2 * kWarps] = inc;      // routed total
+        int run = inc - sum;
+        for (int e = e0; e < e1; ++e) {
+            s_off[e] = run;
+            run += (s_cnt[e] + mt - 1) / mt;
+        }
+        if (lane == 31) s_off[E] = inc;
     }
     __syncthreads();
-    int base = s_cnt[kWarps + warp] + incl - local;
-    const int routed_tiles = s_cnt[2 * kWarps];
+    const int routed_tiles = s_off[E];
     const int shared_tiles = L.has_shared == 1 ? (T + mt - 1) / mt : 0;
     const int total = routed_tiles + shared_tiles;
     if (total > W.max_tiles) {
@@ -327,47 +353,47 @@ __device__ void build_plan(const LayerArgs& L, const Ws& W, int T, int mt,
         }
         return;
     }
-    for (int r = 0; r < 4; ++r) {
-        int e = tid + r * kThreads;
-        if (e >= E || my_tiles[r] == 0) continue;
-        Tile tl;
-        tl.expert = e;
+    auto blob_of = [&](int e) -> const unsigned char* {
         if (pblob) {
             if (pcode[e]) atomicOr(W.status, pcode[e]);
-            tl.blob = pcode[e] ? nullptr : pblob[e];
-        } else {
-            tl.blob = checked_blob(L, W, e);
+            return pcode[e] ? nullptr : pblob[e];
         }
-        tl.m = 0;
-        int ti = base;
-        for (int a = 0; a < NA; ++a) {
-            if (s_idx[a] != e) continue;
-            tl.tok[tl.m] = a / K;
-            tl.asg[tl.m] = a;
-            if (++tl.m == mt) {
-                W.tiles[ti++] = tl;
-                tl.m = 0;
-            }
+        return checked_blob(L, W, e);
+    };
+    // tile headers (expert, m, blob) of every expert with tokens
+    for (int e = tid; e < E; e += nthr) {
+        const int cnt = s_cnt[e];
+        if (!cnt) continue;
+        const unsigned char* bp = blob_of(e);
+        for (int j = 0, ti = s_off[e]; j * mt < cnt; ++j, ++ti) {
+            Tile* tl = W.tiles + ti;
+            tl->expert = e;
+            tl->m = min(mt, cnt - j * mt);
+            tl->blob = bp;
         }
-        if (tl.m) W.tiles[ti++] = tl;
-        base = ti;
     }
-    for (int s = tid; s < shared_tiles; s += kThreads) {
-        Tile tl;
-        tl.expert = E;
-        if (pblob) {
-            if (pcode[E]) atomicOr(W.status, pcode[E]);
-            tl.blob = pcode[E] ? nullptr : pblob[E];
-        } else {
-            tl.blob = checked_blob(L, W, E);
+    // each assignment into its slot
+    for (int a = tid; a < NA; a += nthr) {
+        const int v = s_idx[a];
+        if (v < 0) continue;
+        const int e = v & 1023, r = v >> 10;
+        Tile* tl = W.tiles + s_off[e] + r / mt;
+        tl->tok[r % mt] = a / K;
+        tl->asg[r % mt] = a;
+    }
+    if (shared_tiles) {
+        const unsigned char* bp = tid < shared_tiles ? blob_of(E) : nullptr;
+        for (int s2 = tid; s2 < shared_tiles; s2 += nthr) {
+            Tile* tl = W.tiles + routed_tiles + s2;
+            tl->expert = E;
+            tl->m = min(mt, T - s2 * mt);
+            tl->blob = bp;
         }
-        tl.m = 0;
-        for (int t = s * mt; t < T && tl.m < mt; ++t) {
-            tl.tok[tl.m] = t;
-            tl.asg[tl.m] = T * K + t;
-            tl.m++;
+        for (int t = tid; t < T; t += nthr) {
+            Tile* tl = W.tiles + routed_tiles + t / mt;
+            tl->tok[t % mt] = t;
+            tl->asg[t % mt] = T * K + t;
         }
-        W.tiles[routed_tiles + s] = tl;
     }
     if (tid == 0) W.counters[C_NTILES] = total;
 }
@@ -420,7 +446,7 @@ constexpr int kPrepThreads = 256;
 // probed blob pointers and check codes [E + 1] and the bias as floats [E].
 __host__ __device__ inline size_t prep_tail_off(int H, int cs, int E) {
     const size_t o = (size_t)(H / cs) * sizeof(float) + (size_t)cs * E * sizeof(float) +
-                     (size_t)(kMaxPlanAssign + 64 > 3 * E ? kMaxPlanAssign + 64 : 3 * E) * sizeof(int);
+                     (size_t)(plan_scratch_ints(E) > 3 * E ? plan_scratch_ints(E) : 3 * E) * sizeof(int);
     return (o + 7) & ~size_t(7);
 }
 __host__ __device__ inline size_t prep_smem_bytes(int H, int cs, int E) {
@@ -642,13 +668,9 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     }
     if (mt == 0 || one) return;  // routing only, or the plan is written
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        s_last = T == 1 || atomicAdd(W.counters + C_TOK_DONE, 1) == T - 1;
-    }
+    if (tid == 0) s_last = T == 1 || atomic_add_acq_rel(W.counters + C_TOK_DONE, 1) == T - 1;
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     build_plan(L, W, T, mt, s_scr, s_scr + kMaxPlanAssign, s_blob, s_bcode);
     if (tid == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
 }
@@ -746,13 +768,10 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = atomicAdd(W.counters + C_TOK_DONE, 1) == (int)gridDim.x - 1;
-    }
+    if (threadIdx.x == 0)
+        s_last = atomic_add_acq_rel(W.counters + C_TOK_DONE, 1) == (int)gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     {
         float* sp = reinterpret_cast<float*>(smem) + (size_t)warp * 3 * E;
         float* lg = sp + 2 * E;
@@ -768,8 +787,7 @@ router_kernel(LayerArgs L, Ws W, int T, int mt, const float* xin, int nsl) {
             __syncwarp();
         }
     }
-    __syncthreads();
-    __threadfence();
+    __syncthreads();  // this CTA's top-k writes are visible to all its threads
     if (mt == 0) return;  // routing only, no plan
     build_plan(L, W, T, mt, smem, smem + kMaxPlanAssign);
     if (threadIdx.x == 0) W.counters[C_TOK_DONE] = 0;  // ready for the next layer
@@ -2069,7 +2087,7 @@ DevInfo dev_info() {
 }
 
 size_t router_smem(int E) {
-    return std::max((size_t)(kMaxPlanAssign + 64), (size_t)kWarps * 3 * E) * sizeof(int);
+    return std::max((size_t)plan_scratch_ints(E), (size_t)kWarps * 3 * E) * sizeof(int);
 }
 constexpr int kMaxHidden = 8192;
 

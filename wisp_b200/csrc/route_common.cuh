@@ -8,6 +8,8 @@
 
 #include <cuda_fp16.h>
 
+#include <cstdint>
+
 namespace wisp_route {
 
 constexpr unsigned kAll = 0xffffffffu;
