@@ -51,6 +51,72 @@ struct TopkLane {
 __device__ __forceinline__ float bias_at(const __half* b, int e) { return __half2float(b[e]); }
 __device__ __forceinline__ float bias_at(const float* b, int e) { return b[e]; }
 
+// Weights of the selected slots normalised by their sum, and the optional
+// out_idx[K] / out_w[K] stores (the end of both forms of warp_topk).
+__device__ __forceinline__ TopkLane topk_finish(TopkLane r, float wsum, int K, int* out_idx,
+                                                float* out_w) {
+    const int lane = threadIdx.x & 31;
+    r.w0 = r.i0 >= 0 ? r.w0 : 0.f;
+    r.w1 = r.i1 >= 0 ? r.w1 : 0.f;
+    if (wsum > 0.f) {
+        r.w0 = r.w0 / wsum;
+        r.w1 = r.w1 / wsum;
+    }
+    if (out_idx) {
+        if (lane < K) {
+            out_idx[lane] = r.i0;
+            out_w[lane] = r.w0;
+        }
+        if (lane + 32 < K) {
+            out_idx[lane + 32] = r.i1;
+            out_w[lane + 32] = r.w1;
+        }
+    }
+    return r;
+}
+
+// Softmax gating with at most 32 experts: lane e holds expert e's
+// probability in a register, so the passes need no shared memory.  The same
+// operations in the same order as the general form below (max, exp, the
+// butterfly sum, one division per expert, strict '>' with the lowest index
+// winning), so the selections and weights are identical.
+template <typename BiasT>
+__device__ inline TopkLane warp_topk_small(const float* lg, const BiasT* bias, int E, int K,
+                                           int* out_idx, float* out_w) {
+    const int lane = threadIdx.x & 31;
+    const bool live = lane < E;
+    float v = -1e30f;
+    if (live) {
+        v = lg[lane];
+        if (bias) v += bias_at(bias, lane);
+    }
+    const float mx = warp_max(v);
+    float p = live ? expf(v - mx) : 0.f;
+    const float den = warp_sum(p);
+    p = live ? p / den : -1.f;
+    bool taken = false;
+    float wsum = 0.f;
+    TopkLane r{-1, -1, 0.f, 0.f};
+    for (int j = 0; j < K; ++j) {
+        const bool cand = live && !taken && p > -1.f;  // (a NaN is never selected)
+        const uint32_t key = float_key(cand ? p : -1.f), kmax = __reduce_max_sync(kAll, key);
+        int be = (int)__reduce_min_sync(
+            kAll, key == kmax && cand ? (uint32_t)lane : 0x7fffffffu);
+        const float bv = key_float(kmax);
+        if (bv < 0.f) be = -1;
+        if (be == lane) taken = true;
+        if (j == lane) {
+            r.i0 = be;
+            r.w0 = bv;
+        } else if (j == lane + 32) {
+            r.i1 = be;
+            r.w1 = bv;
+        }
+        if (be >= 0) wsum += bv;
+    }
+    return topk_finish(r, wsum, K, out_idx, out_w);
+}
+
 // One token by one warp.  lg[E]: logits without the bias; bias: [E] fp16 or
 // fp32 (NULL: none); sp: [E] scratch of this warp (shared memory).  The
 // selected experts are tracked in a per-lane bit mask (element lane + 32 i
@@ -62,6 +128,7 @@ __device__ inline TopkLane warp_topk(const float* lg, const BiasT* bias, int E, 
                                      int* out_idx, float* out_w, int gating = kGatingSoftmax) {
     const int lane = threadIdx.x & 31;
     const bool sig = gating == kGatingSigmoid;
+    if (!sig && E <= 32) return warp_topk_small(lg, bias, E, K, out_idx, out_w);
     if (sig) {
         // selection scores; the weights come from the scores without the bias
         for (int e = lane; e < E; e += 32) {
@@ -120,23 +187,7 @@ __device__ inline TopkLane warp_topk(const float* lg, const BiasT* bias, int E, 
         }
         if (be >= 0) wsum += wv;  // every lane holds the same sum, in slot order
     }
-    r.w0 = r.i0 >= 0 ? r.w0 : 0.f;
-    r.w1 = r.i1 >= 0 ? r.w1 : 0.f;
-    if (wsum > 0.f) {
-        r.w0 = r.w0 / wsum;
-        r.w1 = r.w1 / wsum;
-    }
-    if (out_idx) {
-        if (lane < K) {
-            out_idx[lane] = r.i0;
-            out_w[lane] = r.w0;
-        }
-        if (lane + 32 < K) {
-            out_idx[lane + 32] = r.i1;
-            out_w[lane + 32] = r.w1;
-        }
-    }
-    return r;
+    return topk_finish(r, wsum, K, out_idx, out_w);
 }
 
 }  // namespace wisp_route
