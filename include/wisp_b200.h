@@ -421,6 +421,53 @@ void wisp_moe_profile_events(void* events, int n_events);
 int wisp_moe_profile_count(void);
 
 /* ====================================================================== *
+ * 2c. The decoder step's kernels (decoder.cu)
+ * ====================================================================== */
+/* Replace the launchers of csrc/cuda/attention.cu, kv_cache.cu and the
+ * embedding (wisp_engine.h:567-595), same signatures and semantics:
+ * embedding row -> fp32; neox rotary on [n_heads][head_stride] at rope_off;
+ * fp32 -> fp16 cache rows at pos; softmax(q.K * scale).V over seq_len
+ * positions, K [seq][kv_heads][k_dim], V [seq][kv_heads][v_dim] (V == K or
+ * NULL: the first v_dim dims of the key), score_scratch [n_heads][seq_len]
+ * floats (holds the per-chunk partial results). */
+void wisp_gpu_embed_lookup(const wisp_half* table, int token, float* x, int hidden,
+                           cudaStream_t s);
+void wisp_gpu_rope(float* x, int n_heads, int head_stride, int rope_off, int rope_dim,
+                   int pos, float theta, cudaStream_t s);
+void wisp_gpu_kv_append(wisp_half* K, wisp_half* V, const float* k, const float* v,
+                        int pos, int kv_heads, int k_dim, int v_dim, cudaStream_t s);
+void wisp_gpu_attention(const float* q, const wisp_half* Kcache, const wisp_half* Vcache,
+                        float* out, float* score_scratch, int seq_len, int n_heads,
+                        int kv_heads, int k_dim, int v_dim, float scale, cudaStream_t s);
+
+/* New: one GQA attention block fused for one token (run_attention's GQA
+ * branch, wisp_engine.c:1328-1348, with the RMSNorm before it and the
+ * residual after it): x[H] += o_proj(attn(rope(q), cache)) with q, k, v the
+ * projections of rmsnorm(x; input_norm), k and v stored at `pos` of the
+ * layer's cache [max_seq][n_kv_heads][head_dim] (fp16) first.  Weights
+ * fp16 row-major, 16-byte aligned; head_dim a multiple of 16 (<= 576);
+ * hidden a multiple of 8. */
+typedef struct WispAttnLayer {
+    const wisp_half* input_norm; /* [H] (NULL: ones) */
+    const wisp_half* q_proj;     /* [n_heads * head_dim, H] */
+    const wisp_half* k_proj;     /* [n_kv_heads * head_dim, H] */
+    const wisp_half* v_proj;     /* [n_kv_heads * head_dim, H] */
+    const wisp_half* o_proj;     /* [H, n_heads * head_dim] */
+    int hidden, n_heads, n_kv_heads, head_dim;
+    float rope_theta, rms_eps;
+} WispAttnLayer;
+size_t wisp_attn_workspace_bytes(const WispAttnLayer* layer, int max_seq);
+WispError wisp_attn_decode(const WispAttnLayer* layer, float* x, wisp_half* k_cache,
+                           wisp_half* v_cache, int pos, int max_seq, void* workspace,
+                           size_t workspace_bytes, cudaStream_t s, WispErrCtx* err);
+/* New: logits[vocab] = lm_head . rmsnorm(x; final_norm) (decode_step's tail,
+ * wisp_engine.c:1575-1579); workspace of hidden floats. */
+WispError wisp_lm_head_forward(const wisp_half* final_norm, const wisp_half* lm_head,
+                               const float* x, float* logits, int vocab, int hidden, float eps,
+                               void* workspace, size_t workspace_bytes, cudaStream_t s,
+                               WispErrCtx* err);
+
+/* ====================================================================== *
  * 3. Engine ABI (reference: csrc/core/wisp_engine.h:472-543)
  * ====================================================================== */
 typedef struct WispEngine WispEngine;
@@ -481,6 +528,41 @@ cudaStream_t wisp_engine_stream(WispEngine* eng);
 /* New: hidden size, experts per layer, top-k, layers (for callers). */
 void wisp_engine_dims(WispEngine* eng, int* hidden, int* n_experts,
                       int* top_k, int* n_layers);
+
+/* ---------------------------------------------------------------------- *
+ * The decoder step around the MoE block (GQA models).  The engine loads the
+ * dense file's embed_tokens, final_norm, lm_head and per-layer input_norm /
+ * attn.{q,k,v,o}_proj (loader wisp_engine.c:1698-1760); MLA and KDA models
+ * are refused by these calls (WISP_ERR_MODEL).
+ * ---------------------------------------------------------------------- */
+typedef struct WispKVCache WispKVCache;
+
+/* Replaces wisp_kv_cache_alloc (wisp_engine.c:2191-2232): an fp16 K and V
+ * cache of max_seq_len positions per layer on the engine's device, layout
+ * [layer][pos][n_kv_heads][head_dim]. */
+WispKVCache* wisp_kv_cache_alloc(WispEngine* eng, int max_seq_len, WispErrCtx* err);
+/* Replace wisp_kv_cache_free / _clear / _rollback (wisp_engine.c:2234-2259). */
+void wisp_kv_cache_free(WispEngine* eng, WispKVCache* kv);
+void wisp_kv_cache_clear(WispEngine* eng, WispKVCache* kv);
+void wisp_kv_cache_rollback(WispEngine* eng, WispKVCache* kv, int n_tokens);
+/* New: positions held by the cache. */
+int wisp_kv_cache_len(const WispKVCache* kv);
+
+/* Replace wisp_prefill / wisp_decode_one / wisp_verify_tokens
+ * (wisp_engine.c:2263-2303) and their decode_step (:1537-1595): embed the
+ * token, per layer x += attention(rmsnorm(x)) and x += FFN(rmsnorm(x)) (the
+ * MoE block through the tiers, or the dense MLP), then the logits of
+ * rmsnorm(x) through lm_head, copied to the host array out_logits [vocab]
+ * (prefill: the last token's; verify: one row per token).  Tokens out of
+ * [0, vocab) and a full cache are refused with WISP_ERR_INVALID_ARG. */
+WispError wisp_prefill(WispEngine* eng, const int* token_ids, int n_tokens,
+                       WispKVCache* kv, float* out_logits, WispErrCtx* err);
+WispError wisp_decode_one(WispEngine* eng, int token_id, WispKVCache* kv,
+                          float* out_logits, WispErrCtx* err);
+WispError wisp_verify_tokens(WispEngine* eng, const int* token_ids, int n_tokens,
+                             WispKVCache* kv, float* out_logits, WispErrCtx* err);
+/* New: vocabulary size of the engine's model (0 without a decoder). */
+int wisp_engine_vocab(WispEngine* eng);
 
 /* Replace wisp_cache_stats / wisp_cache_clear_all / wisp_ram_trim /
  * wisp_drain_expert_log / wisp_vram_used / wisp_ram_used / wisp_tok_per_sec

@@ -74,6 +74,8 @@ def ref_lib() -> C.CDLL | None:
                                    C.c_void_p, C.c_void_p]
         _ref.ref_probe.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_void_p]
         _ref.ref_cache_stats.argtypes = [C.c_void_p, C.c_void_p]
+        _ref.ref_vocab.argtypes = [C.c_void_p]
+        _ref.ref_decode.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
     return _ref
 
 
@@ -288,6 +290,17 @@ class RefEngine:
         if rc:
             raise RuntimeError(f"reference stack failed: {rc}")
         return x, idx, w
+
+    def decode(self, tokens, max_seq: int) -> np.ndarray:
+        """The reference decoder step for each token in turn from an empty KV cache:
+        logits [n, vocab] (wisp_verify_tokens)."""
+        ids = np.ascontiguousarray(tokens, dtype=np.int32)
+        vocab = int(self.lib.ref_vocab(self.h))
+        out = np.zeros((len(ids), vocab), np.float32)
+        rc = self.lib.ref_decode(self.h, _ptr(ids), len(ids), max_seq, _ptr(out))
+        if rc:
+            raise RuntimeError(f"reference decode failed: {rc}")
+        return out
 
     def cache_stats(self):
         out = np.zeros(3, np.uint64)

@@ -111,3 +111,19 @@ int ref_probe(const char* path, int mat, int n, float* out) {
     memset(&err, 0, sizeof(err));
     return (int)wisp_debug_expert_probe(path, mat, n, out, &meta, &err);
 }
+
+/* The reference's whole decoder step (decode_step, wisp_engine.c:1537-1595)
+ * for n tokens from an empty KV cache of max_seq positions: logits [n][vocab]
+ * (wisp_verify_tokens, :2288-2303).  Returns the WispError code. */
+int ref_vocab(void* h) { return ((WispEngine*)h)->cfg.vocab; }
+
+int ref_decode(void* h, const int* tokens, int n, int max_seq, float* logits) {
+    WispEngine* eng = (WispEngine*)h;
+    WispErrCtx err;
+    memset(&err, 0, sizeof(err));
+    WispKVCache* kv = wisp_kv_cache_alloc(eng, max_seq, &err);
+    if (!kv) return (int)err.code;
+    WispError e = wisp_verify_tokens(eng, tokens, n, kv, logits, &err);
+    wisp_kv_cache_free(eng, kv);
+    return (int)e;
+}

@@ -115,8 +115,10 @@ def test_core_mirror_surface():
                  "drain_expert_log", "expert_prefetch_hint", "get_vram_used_bytes",
                  "get_ram_used_bytes", "get_tok_per_sec", "_selftest_lru",
                  "_selftest_double_buffer", "_debug_expert_probe", "prefill", "decode_one",
-                 "verify_tokens", "kv_cache_alloc", "moe_forward", "moe_stack"):
+                 "verify_tokens", "kv_cache_alloc", "kv_cache_free", "kv_cache_clear",
+                 "kv_cache_rollback", "moe_forward", "moe_stack"):
         assert callable(getattr(core, name)), name
     assert core.__version__ and core.cuda_enabled is True
-    with pytest.raises(RuntimeError, match="MoE block path only"):
-        core.decode_one(1, 0, 0)
+    # unknown handles are refused before any engine call, as in the reference
+    with pytest.raises(ValueError, match="invalid wisp engine handle"):
+        core.decode_one(123456, 0, 0)

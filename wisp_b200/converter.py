@@ -301,7 +301,7 @@ def make_dense_ffn(hidden: int, inter: int, layer: int, seed: int, tag: int,
 def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias: bool = False,
                     zipf_s: float | None = None, shared_int4: bool = True, vocab: int = 16,
                     shared_form: str = "int4", dense_layers=(), dense_inter: int = 0,
-                    missing=()) -> Path:
+                    missing=(), attention: dict | None = None) -> Path:
     """Write a converted-model directory (manifest, dense safetensors, expert blobs).
 
     The dense file carries what the reference loader requires (``embed_tokens``,
@@ -319,6 +319,10 @@ def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias
     ``dense_layers``: layers written without a router whose FFN is an fp16-dense
     SwiGLU of ``dense_inter`` rows under ``layers.i.shared.*`` (the reference's
     dense-MLP layers).  ``missing``: (layer, expert) pairs whose blob is not written.
+    ``attention``: ``{"n_heads", "n_kv_heads", "rope_theta", "max_pos"}`` writes a GQA
+    attention block per layer (``attn.{q,k,v,o}_proj`` seeded normal, ``input_norm``
+    near 1) so the directory serves the whole decoder step; without it the attention
+    tensors are the loader's minimum (``attn.o_proj`` only).
     """
     root = Path(path)
     (root / "experts").mkdir(parents=True, exist_ok=True)
@@ -332,9 +336,26 @@ def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias
     blob_bytes = 0
     missing = {tuple(m) for m in missing}
     for layer in range(shape.n_layers):
-        dense[f"layers.{layer}.input_norm"] = torch.ones(H, dtype=torch.float16)
-        dense[f"layers.{layer}.post_norm"] = torch.ones(H, dtype=torch.float16)
-        dense[f"layers.{layer}.attn.o_proj"] = torch.zeros(1, 1, dtype=torch.float16)
+        if attention:
+            nh, nkv = attention["n_heads"], attention["n_kv_heads"]
+            hd = H // nh
+            base = seed + 1000 * (layer + 1)
+            dense[f"layers.{layer}.input_norm"] = (
+                1.0 + _normal((H,), 0.1, base, "cpu")).half()
+            dense[f"layers.{layer}.post_norm"] = (
+                1.0 + _normal((H,), 0.1, base + 1, "cpu")).half()
+            dense[f"layers.{layer}.attn.q_proj"] = _normal((nh * hd, H), 0.5 / H ** 0.5, base + 2,
+                                                           "cpu").half()
+            dense[f"layers.{layer}.attn.k_proj"] = _normal((nkv * hd, H), 0.5 / H ** 0.5,
+                                                           base + 3, "cpu").half()
+            dense[f"layers.{layer}.attn.v_proj"] = _normal((nkv * hd, H), 1.0 / H ** 0.5,
+                                                           base + 4, "cpu").half()
+            dense[f"layers.{layer}.attn.o_proj"] = _normal((H, nh * hd), 0.5 / (nh * hd) ** 0.5,
+                                                           base + 5, "cpu").half()
+        else:
+            dense[f"layers.{layer}.input_norm"] = torch.ones(H, dtype=torch.float16)
+            dense[f"layers.{layer}.post_norm"] = torch.ones(H, dtype=torch.float16)
+            dense[f"layers.{layer}.attn.o_proj"] = torch.zeros(1, 1, dtype=torch.float16)
         if layer in dense_layers:
             for name, t in make_dense_ffn(H, dense_inter, layer, seed, 2).items():
                 dense[f"layers.{layer}.shared.{name}"] = t
@@ -374,10 +395,11 @@ def write_model_dir(path: str | Path, shape: MoEShape, seed: int, *, router_bias
             "vocab_size": vocab,
             "moe_intermediate_size": shape.inter,
             "intermediate_size": shape.shared_inter or shape.inter,
-            "num_attention_heads": 1,
-            "num_kv_heads": 1,
+            "num_attention_heads": attention["n_heads"] if attention else 1,
+            "num_kv_heads": attention["n_kv_heads"] if attention else 1,
+            "rope_theta": attention.get("rope_theta", 10000.0) if attention else 10000.0,
             "rms_norm_eps": shape.rms_eps,
-            "max_position_embeddings": 16,
+            "max_position_embeddings": attention.get("max_pos", 256) if attention else 16,
         },
         "quantization": {"weight_dtype": "int4", "scale_dtype": "float16",
                          "zero_dtype": "float16", "group_size": shape.group_size},

@@ -6,8 +6,10 @@ The calls go through ``libwisp_b200.so``'s C ABI.
 
 Coverage: the engine lifecycle, expert tiers, statistics, the expert access log,
 prefetch hints, self-tests and the byte-layout probe behave as in the reference.
-``prefill`` / ``decode_one`` / ``verify_tokens`` / ``kv_cache_*`` belong to the
-attention half of a decode step, which this build does not contain; they raise.
+``prefill`` / ``decode_one`` / ``verify_tokens`` / ``kv_cache_*`` run the whole
+decoder step on the GPU for GQA / MHA models (embedding, attention over an fp16 KV
+cache, the MoE block, logits); a model without those weights, or with MLA
+attention, raises ``wisp engine error [6]`` naming what is missing.
 New entry points for the MoE path: ``moe_forward``, ``moe_stack``, ``pin_experts``,
 ``engine_stream``, ``engine_dims``.
 """
@@ -176,10 +178,84 @@ def engine_dims(handle: int) -> dict:
     return {"hidden": h.value, "n_experts": e.value, "top_k": k.value, "n_layers": l.value}
 
 
-def _no_attention(*_a, **_k):
-    raise RuntimeError("wisp engine error [4]: this build implements the MoE block path only; "
-                       "attention, KV cache and logits are not part of it")
+# --- the decoder step (wisp_bindings.cpp:115-218): KV caches are integer
+# handles in a registry, logits come back as Python lists of vocab floats.
+_kv: dict[int, int] = {}
+_next_kv = [1]
 
 
-prefill = decode_one = verify_tokens = _no_attention
-kv_cache_alloc = kv_cache_free = kv_cache_clear = kv_cache_rollback = _no_attention
+def _kv_of(kv_cache_ptr: int) -> int:
+    with _reg_lock:
+        p = _kv.get(kv_cache_ptr)
+    if p is None:
+        raise ValueError(f"invalid kv cache handle {kv_cache_ptr}")
+    return p
+
+
+def _vocab(handle: int) -> int:
+    return int(lib().wisp_engine_vocab(_engine(handle)))
+
+
+def kv_cache_alloc(handle: int, max_seq_len: int) -> int:
+    err = WispErrCtx()
+    p = lib().wisp_kv_cache_alloc(_engine(handle), int(max_seq_len), C.byref(err))
+    if not p:
+        _raise(err)
+    with _reg_lock:
+        h = _next_kv[0]
+        _next_kv[0] += 1
+        _kv[h] = p
+    return h
+
+
+def kv_cache_free(handle: int, kv_cache_ptr: int) -> None:
+    with _reg_lock:
+        p = _kv.pop(kv_cache_ptr, None)
+    if p is not None:
+        lib().wisp_kv_cache_free(_engine(handle), p)
+
+
+def kv_cache_clear(handle: int, kv_cache_ptr: int) -> None:
+    lib().wisp_kv_cache_clear(_engine(handle), _kv_of(kv_cache_ptr))
+
+
+def kv_cache_rollback(handle: int, kv_cache_ptr: int, n_tokens: int) -> None:
+    lib().wisp_kv_cache_rollback(_engine(handle), _kv_of(kv_cache_ptr), int(n_tokens))
+
+
+def kv_cache_len(kv_cache_ptr: int) -> int:
+    """New: positions held by the cache."""
+    return int(lib().wisp_kv_cache_len(_kv_of(kv_cache_ptr)))
+
+
+def prefill(handle: int, token_ids: list[int], kv_cache_ptr: int) -> list[float]:
+    e, kv = _engine(handle), _kv_of(kv_cache_ptr)
+    ids = (C.c_int * max(1, len(token_ids)))(*token_ids)
+    out = (C.c_float * max(1, _vocab(handle)))()
+    err = WispErrCtx()
+    rc = lib().wisp_prefill(e, ids, len(token_ids), kv, out, C.byref(err))
+    if rc:
+        _raise(err, rc)
+    return list(out)
+
+
+def decode_one(handle: int, token_id: int, kv_cache_ptr: int) -> list[float]:
+    e, kv = _engine(handle), _kv_of(kv_cache_ptr)
+    out = (C.c_float * max(1, _vocab(handle)))()
+    err = WispErrCtx()
+    rc = lib().wisp_decode_one(e, int(token_id), kv, out, C.byref(err))
+    if rc:
+        _raise(err, rc)
+    return list(out)
+
+
+def verify_tokens(handle: int, token_ids: list[int], kv_cache_ptr: int) -> list[list[float]]:
+    e, kv = _engine(handle), _kv_of(kv_cache_ptr)
+    n, vocab = len(token_ids), _vocab(handle)
+    ids = (C.c_int * max(1, n))(*token_ids)
+    flat = (C.c_float * max(1, n * vocab))()
+    err = WispErrCtx()
+    rc = lib().wisp_verify_tokens(e, ids, n, kv, flat, C.byref(err))
+    if rc:
+        _raise(err, rc)
+    return [list(flat[i * vocab:(i + 1) * vocab]) for i in range(n)]

@@ -40,6 +40,8 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <tuple>
+#include <utility>
 #include <vector>
 
 #include "dense_ffn.h"
@@ -92,6 +94,12 @@ const char* json_find(const char* js, const char* key) {
 double json_num(const char* js, const char* key, double dflt) {
     const char* p = json_find(js, key);
     return p ? strtod(p, nullptr) : dflt;
+}
+std::string json_str(const char* js, const char* key) {
+    const char* p = json_find(js, key);
+    if (!p || *p != '"') return std::string();
+    const char* q = strchr(p + 1, '"');
+    return q ? std::string(p + 1, q) : std::string();
 }
 
 // Minimal safetensors reader: locate a tensor by exact name in the header.
@@ -172,6 +180,12 @@ struct LayerDev {
     wisp_half* shared_down = nullptr;
     int shared_inter = 0;
     bool dense_mlp = false;       // no router: the layer's FFN is shared.* alone
+    // the decoder step's attention (layers.i.input_norm, attn.{q,k,v,o}_proj)
+    wisp_half* input_norm = nullptr;
+    wisp_half* q_proj = nullptr;
+    wisp_half* k_proj = nullptr;
+    wisp_half* v_proj = nullptr;
+    wisp_half* o_proj = nullptr;
     void** d_table = nullptr;     // device [E]
     std::vector<void*> h_table;   // host mirror
     std::vector<uint8_t> in_vram; // expert is VRAM-resident (not ring-served)
@@ -196,6 +210,7 @@ struct WispEngine {
     int ring_pos = 0;
     void* staging = nullptr;  // pinned SSD staging (one expert)
     char* d_stage = nullptr;  // device staging slot: .bin blobs are tiled from here
+    size_t stage_cap = 0;     // its capacity (bytes)
     std::mutex fetch_mu;
     // workspace of the fused kernels
     void* ws = nullptr;
@@ -230,6 +245,28 @@ struct WispEngine {
     uint64_t log_dropped = 0;
     uint64_t tok_ns[32] = {0};
     int tok_head = 0, tok_count = 0;
+    // decoder step (GQA / MHA models whose dense file holds the attention
+    // projections): embedding, final norm, lm_head and per-token buffers
+    bool has_decoder = false;
+    std::string no_decoder;  // why not, for the error message
+    int vocab = 0, n_heads = 0, n_kv = 0, head_dim = 0;
+    float rope_theta = 10000.f;
+    wisp_half* embed = nullptr;
+    wisp_half* final_norm = nullptr;
+    wisp_half* lm_head = nullptr;
+    float* d_x = nullptr;       // [H] the token's hidden state
+    float* d_logits = nullptr;  // [vocab]
+    float* d_lmws = nullptr;    // [H] normalised input of lm_head
+};
+
+struct WispKVCache {
+    int max_seq = 0, len = 0;
+    size_t layer_elems = 0;  // max_seq * n_kv * head_dim
+    wisp_half* k = nullptr;  // [layers][max_seq][n_kv][head_dim]
+    wisp_half* v = nullptr;
+    void* ws = nullptr;      // attention workspace (wisp_attn_workspace_bytes)
+    size_t ws_bytes = 0;
+    int device = 0;
 };
 
 namespace {
@@ -375,6 +412,10 @@ bool put_tiled(WispEngine* e, void* dst, const void* src, size_t n, WispErrCtx* 
     cudaError_t ce;
     if (m.tiled) {
         ce = cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, e->transfer);
+    } else if (n > e->stage_cap) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "expert blob of %zu bytes exceeds the staging slot (%zu)",
+                   n, e->stage_cap);
+        return false;
     } else {
         ce = cudaMemcpyAsync(e->d_stage, src, n, cudaMemcpyHostToDevice, e->transfer);
         if (ce == cudaSuccess && wisp_expert_tile(&m, e->d_stage, dst, e->transfer, err) != WISP_OK)
@@ -696,11 +737,31 @@ WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
     WispExpertMeta m{};
     WispError r = wisp_expert_parse_header(blob.data(), blob.size(), &m, err);
     if (r != WISP_OK) return r;
+    // the fused block runs an int4 shared expert as one more tile of the routed
+    // experts' shape; a shared expert of another width runs from its fp16-dense
+    // copy (layers.i.shared.*) instead
+    if ((int)m.rows[0] != e->inter || (int)m.cols[0] != e->H) return WISP_OK;
+    // the shared expert may be wider than the routed ones (manifest
+    // expert_size_bytes): grow the staging slot to hold it (engine creation,
+    // nothing else is in flight on the transfer stream)
+    if (blob.size() > e->stage_cap) {
+        WB_CUDA_RET(cudaStreamSynchronize(e->transfer), err);
+        cudaFree(e->d_stage - 8);
+        e->d_stage = nullptr;
+        char* p = nullptr;
+        WB_CUDA_RET(cudaMalloc(&p, blob.size() + 264), err);
+        e->d_stage = p + 8;
+        e->stage_cap = blob.size();
+    }
     // place at (256-aligned) + 8 so the sections are 16-byte aligned
     char* base = nullptr;
     WB_CUDA_RET(cudaMalloc(&base, blob.size() + 264), err);
     void* dst = base + 8;
-    if (!put_tiled(e, dst, blob.data(), blob.size(), err)) return WISP_ERR_CUDA;
+    if (!put_tiled(e, dst, blob.data(), blob.size(), err)) {
+        cudaFree(base);
+        return err->code ? err->code : WISP_ERR_CUDA;
+    }
+    drain_uploads(e);  // `blob` is freed on return
     m.tiled = 1;
     e->L[l].shared_blob = dst;
     e->L[l].shared_meta = m;
@@ -708,6 +769,83 @@ WispError load_shared(WispEngine* e, int l, WispErrCtx* err) {
 }
 
 }  // namespace
+
+// The decoder step's weights (load_dense, wisp_engine.c:1698-1760, GQA/MHA
+// names): embed_tokens [vocab, H], final_norm [H], lm_head [vocab, H], and per
+// layer input_norm [H], attn.q_proj [nh*hd, H], attn.k_proj / v_proj
+// [nkv*hd, H], attn.o_proj [H, nh*hd] (hd = H / nh, as the reference derives
+// it).  A model without them (or with MLA attention) still serves the MoE
+// entry points; the decoder calls then report why.
+static WispError load_decoder(WispEngine* e, const StFile& st, const char* manifest,
+                              WispErrCtx* err) {
+    const std::string attn = json_str(manifest, "attention_type");
+    e->vocab = (int)json_num(manifest, "vocab_size", 0);
+    e->n_heads = (int)json_num(manifest, "num_attention_heads", 128);
+    e->n_kv = (int)json_num(manifest, "num_kv_heads", e->n_heads);
+    e->rope_theta = (float)json_num(manifest, "rope_theta", 10000.0);
+    if (attn != "GQA" && attn != "MHA") {
+        e->no_decoder = "attention type '" + attn + "' (the decoder step supports GQA and MHA)";
+        return WISP_OK;
+    }
+    if (e->n_heads <= 0 || e->n_kv <= 0 || e->n_heads % e->n_kv || e->H % e->n_heads ||
+        e->vocab <= 0) {
+        e->no_decoder = "manifest heads / kv heads / vocab do not describe a GQA model";
+        return WISP_OK;
+    }
+    e->head_dim = e->H / e->n_heads;
+    const int64_t H = e->H, nh = e->n_heads, nkv = e->n_kv, hd = e->head_dim;
+    std::vector<int64_t> sh;
+    auto want = [&](const std::string& name, wisp_half** out, std::vector<int64_t> shape) -> int {
+        WispError r = load_half(e, st, name, out, false, err, &sh);
+        if (r != WISP_OK) return -1;
+        if (!*out) return 0;
+        if (sh != shape) {
+            cudaFree(*out);
+            *out = nullptr;
+            if (e->no_decoder.empty()) e->no_decoder = "tensor " + name + " has an unexpected shape";
+            return 0;
+        }
+        return 1;
+    };
+    int ok = 1;
+    for (auto [name, out, shape] : {std::make_tuple(std::string("embed_tokens"), &e->embed,
+                                                    std::vector<int64_t>{e->vocab, H}),
+                                    std::make_tuple(std::string("final_norm"), &e->final_norm,
+                                                    std::vector<int64_t>{H}),
+                                    std::make_tuple(std::string("lm_head"), &e->lm_head,
+                                                    std::vector<int64_t>{e->vocab, H})}) {
+        const int r = want(name, out, shape);
+        if (r < 0) return err->code;
+        ok &= r;
+    }
+    for (int l = 0; l < e->n_layers && ok; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        LayerDev& d = e->L[l];
+        const std::pair<std::string, std::pair<wisp_half**, std::vector<int64_t>>> t[] = {
+            {p + "input_norm", {&d.input_norm, {H}}},
+            {p + "attn.q_proj", {&d.q_proj, {nh * hd, H}}},
+            {p + "attn.k_proj", {&d.k_proj, {nkv * hd, H}}},
+            {p + "attn.v_proj", {&d.v_proj, {nkv * hd, H}}},
+            {p + "attn.o_proj", {&d.o_proj, {H, nh * hd}}}};
+        for (const auto& it : t) {
+            const int r = want(it.first, it.second.first, it.second.second);
+            if (r < 0) return err->code;
+            if (r == 0 && it.first != p + "input_norm") {
+                ok = 0;
+                if (e->no_decoder.empty()) e->no_decoder = "tensor " + it.first + " missing";
+            }
+        }
+    }
+    if (!ok) {
+        if (e->no_decoder.empty()) e->no_decoder = "embed_tokens / final_norm / lm_head missing";
+        return WISP_OK;
+    }
+    WB_CUDA_RET(cudaMalloc(&e->d_x, (size_t)H * sizeof(float)), err);
+    WB_CUDA_RET(cudaMalloc(&e->d_lmws, (size_t)H * sizeof(float)), err);
+    WB_CUDA_RET(cudaMalloc(&e->d_logits, (size_t)e->vocab * sizeof(float)), err);
+    e->has_decoder = true;
+    return WISP_OK;
+}
 
 extern "C" size_t wisp_read_expert_file(const char* path, void* dst, size_t cap, int* direct,
                                         WispErrCtx* err) {
@@ -842,6 +980,7 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
     if (ce == cudaSuccess) ce = cudaHostAlloc(&e->staging, e->max_expert_bytes, 0);
     if (ce == cudaSuccess) ce = cudaMalloc(&e->d_stage, e->max_expert_bytes + 264);
     if (ce == cudaSuccess) e->d_stage += 8;  // blob at 8 (mod 16), like every slot
+    e->stage_cap = e->max_expert_bytes;
     if (ce != cudaSuccess) {
         WB_SET_ERR(err, WISP_ERR_CUDA, "stream/staging setup: %s", cudaGetErrorString(ce));
         wisp_engine_destroy(e.release());
@@ -889,6 +1028,10 @@ extern "C" WispEngine* wisp_engine_create(const char* model_path, size_t vram_bu
             return nullptr;
         }
     }
+    if (load_decoder(e.get(), st, j, err) != WISP_OK) {
+        wisp_engine_destroy(e.release());
+        return nullptr;
+    }
     // tiers
     e->ram.set_capacity(ram_budget);
     e->vram_budget = vram_budget;
@@ -935,7 +1078,18 @@ extern "C" void wisp_engine_destroy(WispEngine* e) {
         cudaFree(d.shared_up);
         cudaFree(d.shared_down);
         cudaFree(d.d_table);
+        cudaFree(d.input_norm);
+        cudaFree(d.q_proj);
+        cudaFree(d.k_proj);
+        cudaFree(d.v_proj);
+        cudaFree(d.o_proj);
     }
+    cudaFree(e->embed);
+    cudaFree(e->final_norm);
+    cudaFree(e->lm_head);
+    cudaFree(e->d_x);
+    cudaFree(e->d_lmws);
+    cudaFree(e->d_logits);
     if (e->ws) cudaFree(e->ws);
     cudaFree(e->d_idx);
     cudaFree(e->d_w);
@@ -1266,3 +1420,178 @@ extern "C" double wisp_tok_per_sec(WispEngine* e) {
 
 // wisp_b200_version() is generated at build time (wisp_b200/build.py): it carries
 // a hash of the sources the library was built from.
+
+// ------------------------------------------------------------------------
+// The decoder step (decode_step, wisp_engine.c:1537-1595) on the device:
+// embedding, per layer x += attention(rmsnorm(x)) (wisp_attn_decode) and
+// x += FFN(rmsnorm(x)) (the MoE block through the tiers, or the dense MLP),
+// then lm_head over rmsnorm(x) when logits are wanted.
+// ------------------------------------------------------------------------
+extern "C" int wisp_engine_vocab(WispEngine* e) { return e && e->has_decoder ? e->vocab : 0; }
+
+static bool decoder_ready(WispEngine* e, WispErrCtx* err, const char* what) {
+    if (!e) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "%s: NULL engine", what);
+        return false;
+    }
+    if (!e->has_decoder) {
+        WB_SET_ERR(err, WISP_ERR_MODEL, "%s: the model has no decoder step this build runs: %s",
+                   what, e->no_decoder.c_str());
+        return false;
+    }
+    return true;
+}
+
+static WispAttnLayer attn_desc(WispEngine* e, int l) {
+    const LayerDev& d = e->L[l];
+    WispAttnLayer a{};
+    a.input_norm = d.input_norm;
+    a.q_proj = d.q_proj;
+    a.k_proj = d.k_proj;
+    a.v_proj = d.v_proj;
+    a.o_proj = d.o_proj;
+    a.hidden = e->H;
+    a.n_heads = e->n_heads;
+    a.n_kv_heads = e->n_kv;
+    a.head_dim = e->head_dim;
+    a.rope_theta = e->rope_theta;
+    a.rms_eps = e->eps;
+    return a;
+}
+
+extern "C" WispKVCache* wisp_kv_cache_alloc(WispEngine* e, int max_seq_len, WispErrCtx* err) {
+    if (!decoder_ready(e, err, "kv_cache_alloc")) return nullptr;
+    if (max_seq_len <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "max_seq_len must be > 0, got %d", max_seq_len);
+        return nullptr;
+    }
+    cudaSetDevice(e->device);
+    std::unique_ptr<WispKVCache> kv(new WispKVCache());
+    kv->max_seq = max_seq_len;
+    kv->device = e->device;
+    kv->layer_elems = (size_t)max_seq_len * e->n_kv * e->head_dim;
+    const size_t bytes = (size_t)e->n_layers * kv->layer_elems * sizeof(wisp_half);
+    const WispAttnLayer a = attn_desc(e, 0);
+    kv->ws_bytes = wisp_attn_workspace_bytes(&a, max_seq_len);
+    cudaError_t ce = cudaMalloc(&kv->k, bytes);
+    if (ce == cudaSuccess) ce = cudaMalloc(&kv->v, bytes);
+    if (ce == cudaSuccess) ce = cudaMalloc(&kv->ws, kv->ws_bytes);
+    if (ce != cudaSuccess) {
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+        cudaFree(kv->ws);
+        WB_SET_ERR(err, WISP_ERR_OOM, "kv cache of %d positions (%zu bytes): %s", max_seq_len,
+                   2 * bytes, cudaGetErrorString(ce));
+        return nullptr;
+    }
+    return kv.release();
+}
+
+extern "C" void wisp_kv_cache_free(WispEngine* e, WispKVCache* kv) {
+    if (!kv) return;
+    if (e && e->compute) cudaStreamSynchronize(e->compute);
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    cudaFree(kv->ws);
+    delete kv;
+}
+
+extern "C" void wisp_kv_cache_clear(WispEngine* e, WispKVCache* kv) {
+    (void)e;
+    if (kv) kv->len = 0;
+}
+
+extern "C" void wisp_kv_cache_rollback(WispEngine* e, WispKVCache* kv, int n_tokens) {
+    (void)e;
+    if (!kv || n_tokens <= 0) return;
+    kv->len = kv->len >= n_tokens ? kv->len - n_tokens : 0;
+}
+
+extern "C" int wisp_kv_cache_len(const WispKVCache* kv) { return kv ? kv->len : 0; }
+
+static WispError decode_step(WispEngine* e, WispKVCache* kv, int token, float* out_logits,
+                             WispErrCtx* err) {
+    if (!decoder_ready(e, err, "decode")) return err->code;
+    if (!kv) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "decode: NULL kv cache");
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (token < 0 || token >= e->vocab) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "token id %d out of range [0, %d)", token, e->vocab);
+        return WISP_ERR_INVALID_ARG;
+    }
+    if (kv->len >= kv->max_seq) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "KV cache full (%d tokens)", kv->max_seq);
+        return WISP_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(e->device);
+    cudaStream_t s = e->compute;
+    order_after_compute(e, s);
+    wait_uploads(e, s);
+    WispError r = ensure_bufs(e, 1, 0, err);
+    if (r != WISP_OK) return r;
+    wisp_gpu_embed_lookup(e->embed, token, e->d_x, e->H, s);
+    WB_CUDA_RET(cudaGetLastError(), err);
+    for (int l = 0; l < e->n_layers; ++l) {
+        const WispAttnLayer a = attn_desc(e, l);
+        r = wisp_attn_decode(&a, e->d_x, kv->k + (size_t)l * kv->layer_elems,
+                             kv->v + (size_t)l * kv->layer_elems, kv->len, kv->max_seq, kv->ws,
+                             kv->ws_bytes, s, err);
+        if (r != WISP_OK) return r;
+        WB_CUDA_RET(wb::launch_rmsnorm_rows(e->d_x,
+                                            reinterpret_cast<const __half*>(e->L[l].post_norm),
+                                            e->d_xn, e->H, e->eps, 1, s),
+                    err);
+        r = moe_forward_impl(e, l, e->d_xn, e->d_ffn, 1, s, err);
+        if (r != WISP_OK) return r;
+        WB_CUDA_RET(wb::launch_add_rows(e->d_x, e->d_ffn, (size_t)e->H, s), err);
+    }
+    kv->len++;
+    if (out_logits) {
+        r = wisp_lm_head_forward(e->final_norm, e->lm_head, e->d_x, e->d_logits, e->vocab, e->H,
+                                 e->eps, e->d_lmws, (size_t)e->H * sizeof(float), s, err);
+        if (r != WISP_OK) return r;
+        WB_CUDA_RET(cudaMemcpyAsync(out_logits, e->d_logits, (size_t)e->vocab * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s),
+                    err);
+        WB_CUDA_RET(cudaStreamSynchronize(s), err);
+    }
+    std::lock_guard<std::mutex> g(e->stats_mu);
+    e->tok_ns[e->tok_head] = now_ns();
+    e->tok_head = (e->tok_head + 1) % 32;
+    if (e->tok_count < 32) e->tok_count++;
+    return WISP_OK;
+}
+
+extern "C" WispError wisp_decode_one(WispEngine* e, int token_id, WispKVCache* kv,
+                                     float* out_logits, WispErrCtx* err) {
+    return decode_step(e, kv, token_id, out_logits, err);
+}
+
+extern "C" WispError wisp_prefill(WispEngine* e, const int* token_ids, int n_tokens,
+                                  WispKVCache* kv, float* out_logits, WispErrCtx* err) {
+    if (!token_ids || n_tokens <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "prefill: empty prompt");
+        return WISP_ERR_INVALID_ARG;
+    }
+    for (int i = 0; i < n_tokens; ++i) {
+        const bool want = i == n_tokens - 1 && out_logits;
+        const WispError r = decode_step(e, kv, token_ids[i], want ? out_logits : nullptr, err);
+        if (r != WISP_OK) return r;
+    }
+    return WISP_OK;
+}
+
+extern "C" WispError wisp_verify_tokens(WispEngine* e, const int* token_ids, int n_tokens,
+                                        WispKVCache* kv, float* out_logits, WispErrCtx* err) {
+    if (!out_logits || !token_ids || n_tokens < 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "verify: NULL output buffer or tokens");
+        return WISP_ERR_INVALID_ARG;
+    }
+    for (int i = 0; i < n_tokens; ++i) {
+        const WispError r = decode_step(e, kv, token_ids[i],
+                                        out_logits + (size_t)i * (e ? e->vocab : 0), err);
+        if (r != WISP_OK) return r;
+    }
+    return WISP_OK;
+}

@@ -31,6 +31,13 @@ class WispExpertMeta(C.Structure):
                 ("total_bytes", C.c_size_t), ("valid", C.c_int), ("tiled", C.c_int)]
 
 
+class WispAttnLayer(C.Structure):
+    _fields_ = [("input_norm", C.c_void_p), ("q_proj", C.c_void_p), ("k_proj", C.c_void_p),
+                ("v_proj", C.c_void_p), ("o_proj", C.c_void_p), ("hidden", C.c_int),
+                ("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float)]
+
+
 class WispMoeLayer(C.Structure):
     _fields_ = [("meta", WispExpertMeta), ("expert_blobs", C.c_void_p), ("router_w", C.c_void_p),
                 ("router_bias", C.c_void_p), ("norm_w", C.c_void_p), ("shared_blob", C.c_void_p),
@@ -90,6 +97,34 @@ _SIGS = {
                                          C.POINTER(WispErrCtx)]),
     "wisp_stream_stats": (None, [C.c_void_p, C.c_void_p]),
     "wisp_stream_reset": (None, [C.c_void_p]),
+    # the decoder step
+    "wisp_kv_cache_alloc": (C.c_void_p, [C.c_void_p, C.c_int, C.POINTER(WispErrCtx)]),
+    "wisp_kv_cache_free": (None, [C.c_void_p, C.c_void_p]),
+    "wisp_kv_cache_clear": (None, [C.c_void_p, C.c_void_p]),
+    "wisp_kv_cache_rollback": (None, [C.c_void_p, C.c_void_p, C.c_int]),
+    "wisp_kv_cache_len": (C.c_int, [C.c_void_p]),
+    "wisp_decode_one": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                  C.POINTER(WispErrCtx)]),
+    "wisp_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                               C.POINTER(WispErrCtx)]),
+    "wisp_verify_tokens": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                     C.POINTER(WispErrCtx)]),
+    "wisp_engine_vocab": (C.c_int, [C.c_void_p]),
+    "wisp_attn_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
+    "wisp_attn_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_int, C.c_void_p, C.c_size_t, C.c_void_p,
+                                   C.POINTER(WispErrCtx)]),
+    "wisp_lm_head_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                       C.c_int, C.c_float, C.c_void_p, C.c_size_t, C.c_void_p,
+                                       C.POINTER(WispErrCtx)]),
+    "wisp_gpu_embed_lookup": (None, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
+    "wisp_gpu_rope": (None, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                             C.c_void_p]),
+    "wisp_gpu_kv_append": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                  C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "wisp_gpu_attention": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                  C.c_void_p]),
     "wisp_moe_prefill_routed_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int, C.c_int]),
     "wisp_moe_prefill_routed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
