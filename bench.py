@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--skip-cpu", action="store_true")
     p.add_argument("--skip-extra", action="store_true", help="no per-batch / e2e / profile legs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--decoder-pos", type=int, default=1023,
+                   help="KV position of the decoder-step leg (0: skip the leg)")
     p.add_argument("--config3-layers", type=int, default=4,
                    help="resident DeepSeek-shaped layers of the config-3 leg (0 = skip)")
     p.add_argument("--c3-experts", type=int, default=256,
@@ -325,6 +327,14 @@ def run_single(args, dev) -> dict:
                           "frac_of_measured_hbm": round(gbs / peaks()["hbm_gbs"], 4)}
         del g0
 
+    if not args.skip_extra and args.decoder_pos > 0:
+        # an extra leg: its failure is recorded, not fatal to the headline line
+        try:
+            out["decoder_step"] = run_decoder(args, dev, stack, shape, s)
+        except Exception as e:  # noqa: BLE001
+            out["decoder_step"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
+
     if not args.skip_extra and args.config3_layers > 0:
         # an extra leg: its failure is recorded, not fatal to the headline line
         try:
@@ -364,6 +374,99 @@ def run_single(args, dev) -> dict:
     out["gpu_launches_per_step"] = len(seq) * args.layers + 2
     del g
     return out
+
+
+def run_decoder(args, dev, stack, shape, s) -> dict:
+    """The whole decoder step at batch 1 on the config-1 stack: per layer the fused GQA
+    attention block (Mixtral-8x7B shapes: 32 heads over 8 kv heads of 128, rotary,
+    fp16 KV cache holding `decoder_pos` earlier positions) + RMSNorm + the MoE block +
+    the residual, then the logits over a 32000-token vocabulary; one CUDA graph per
+    token, every weight resident (random fp16 attention / embedding / lm_head weights:
+    no checkpoint is available)."""
+    import ctypes as C
+    import torch
+    from wisp_b200.lib import WispAttnLayer, WispErrCtx, check, lib
+    H, L, nh, nkv, hd, vocab = shape.hidden, args.layers, 32, 8, 128, 32000
+    pos, max_seq = args.decoder_pos, args.decoder_pos + 1
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 11)
+
+    def w(*sz, std):
+        return (torch.randn(*sz, generator=g, device=dev) * std).half()
+
+    attn = []
+    for _ in range(L):
+        attn.append({"input_norm": torch.ones(H, dtype=torch.float16, device=dev),
+                     "q": w(nh * hd, H, std=0.5 / H ** 0.5), "k": w(nkv * hd, H, std=0.5 / H ** 0.5),
+                     "v": w(nkv * hd, H, std=1.0 / H ** 0.5),
+                     "o": w(H, nh * hd, std=0.5 / (nh * hd) ** 0.5)})
+    embed, lm_head = w(vocab, H, std=0.02), w(vocab, H, std=0.02)
+    final_norm = torch.ones(H, dtype=torch.float16, device=dev)
+    Kc = w(L, max_seq, nkv, hd, std=1.0)
+    Vc = w(L, max_seq, nkv, hd, std=1.0)
+    layers = [WispAttnLayer(a["input_norm"].data_ptr(), a["q"].data_ptr(), a["k"].data_ptr(),
+                            a["v"].data_ptr(), a["o"].data_ptr(), H, nh, nkv, hd, 500000.0,
+                            shape.rms_eps) for a in attn]
+    n_ws = int(lib().wisp_attn_workspace_bytes(C.byref(layers[0]), max_seq))
+    ws = torch.zeros(n_ws, dtype=torch.uint8, device=dev)  # zero before first use
+    x = torch.empty((1, H), dtype=torch.float32, device=dev)
+    xn, y = torch.empty_like(x), torch.empty_like(x)
+    logits = torch.empty(vocab, dtype=torch.float32, device=dev)
+    lws = torch.empty(H, dtype=torch.float32, device=dev)
+    stack.workspace(max(args.batch, 1))
+    err = WispErrCtx()
+
+    def step(with_moe=True):
+        cs = torch.cuda.current_stream().cuda_stream
+        lib().wisp_gpu_embed_lookup(embed.data_ptr(), 7, x.data_ptr(), H, cs)
+        for l in range(L):
+            check(lib().wisp_attn_decode(C.byref(layers[l]), x.data_ptr(), Kc[l].data_ptr(),
+                                         Vc[l].data_ptr(), pos, max_seq, ws.data_ptr(), n_ws, cs,
+                                         C.byref(err)), err)
+            if with_moe:
+                lib().wisp_gpu_rmsnorm(x.data_ptr(), stack.layer_c(l).norm_w, xn.data_ptr(), H,
+                                       C.c_float(shape.rms_eps), cs)
+                stack.block(l, xn, y)
+                lib().wisp_gpu_residual_add(x.data_ptr(), y.data_ptr(), H, cs)
+        check(lib().wisp_lm_head_forward(final_norm.data_ptr(), lm_head.data_ptr(), x.data_ptr(),
+                                         logits.data_ptr(), vocab, H, C.c_float(shape.rms_eps),
+                                         lws.data_ptr(), lws.numel() * 4, cs, C.byref(err)), err)
+
+    def timed(with_moe):
+        with torch.cuda.stream(s):
+            step(with_moe)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step(with_moe)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(10, args.steps // 2)
+        e0.record()
+        for _ in range(n):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del gr
+        return e0.elapsed_time(e1) / n
+
+    ms = timed(True)
+    ms_attn = timed(False)  # embedding + attention blocks + logits only
+    assert stack.status() == 0, "kernel status flag set"
+    assert bool(torch.isfinite(logits).all()), "non-finite logits"
+    # bytes the attention half must read: its weights, the KV cache up to pos, the
+    # embedding row and lm_head
+    attn_bytes = L * ((2 * nh * hd * H + 2 * nkv * hd * H) * 2 + 2 * max_seq * nkv * hd * 2) \
+        + vocab * H * 2 + H * 2
+    return {"workload": f"Mixtral-8x7B-shaped decoder step at batch 1: {L} x (GQA attention "
+                        f"32/8 heads x 128, KV position {pos} + MoE block) + logits over {vocab}",
+            "ms_per_token": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 1),
+            "attention_and_logits_ms": round(ms_attn, 4),
+            "attention_hbm_gbs": round(attn_bytes / ms_attn / 1e6, 1),
+            "attention_frac_of_measured_hbm": round(attn_bytes / ms_attn / 1e6 / peaks()["hbm_gbs"], 4),
+            "attention_alg_bytes": int(attn_bytes)}
 
 
 def run_config3(args, dev, k: int) -> dict:
@@ -496,7 +599,8 @@ def main_ours(args):
         "gpu_launches": r["gpu_launches_per_step"] * args.steps,
         "step_hbm_gbs": round(r["step_gbs"], 1), "kernel_ms_mean": r["kernel_ms_mean"],
     }
-    for k in ("e2e", "per_batch", "config0", "config3", "config4", "cpu_baseline", "parity"):
+    for k in ("e2e", "per_batch", "config0", "decoder_step", "config3", "config4", "cpu_baseline",
+              "parity"):
         if k in r:
             line[k] = r[k]
     q = r.get("per_batch", {}).get(str(max(1, args.batch // 4)))

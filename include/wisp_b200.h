@@ -446,7 +446,9 @@ void wisp_gpu_attention(const float* q, const wisp_half* Kcache, const wisp_half
  * projections of rmsnorm(x; input_norm), k and v stored at `pos` of the
  * layer's cache [max_seq][n_kv_heads][head_dim] (fp16) first.  Weights
  * fp16 row-major, 16-byte aligned; head_dim a multiple of 16 (<= 576);
- * hidden a multiple of 8. */
+ * hidden a multiple of 8.  The workspace (wisp_attn_workspace_bytes) must be
+ * zero-filled before its first use: it holds the counters of the split
+ * projections, which every call leaves at zero. */
 typedef struct WispAttnLayer {
     const wisp_half* input_norm; /* [H] (NULL: ones) */
     const wisp_half* q_proj;     /* [n_heads * head_dim, H] */

@@ -152,7 +152,8 @@ def test_attention_launcher_with_values_aliased_to_keys(cuda, seq):
     assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
 
 
-@pytest.mark.parametrize("H,nh,nkv,pos", [(512, 8, 2, 0), (512, 8, 2, 517), (1024, 8, 8, 300)])
+@pytest.mark.parametrize("H,nh,nkv,pos", [(512, 8, 2, 0), (512, 8, 2, 517), (1024, 8, 8, 300),
+                                          (384, 6, 2, 45)])  # the last: the non-tensor-core path
 def test_attn_decode_layer_matches_the_restatement(cuda, H, nh, nkv, pos):
     hd, max_seq, eps, theta = H // nh, 600, 1e-5, 10000.0
     rng = np.random.default_rng(H + pos)
@@ -171,7 +172,7 @@ def test_attn_decode_layer_matches_the_restatement(cuda, H, nh, nkv, pos):
                       dw["k_proj"].data_ptr(), dw["v_proj"].data_ptr(), dw["o_proj"].data_ptr(),
                       H, nh, nkv, hd, theta, eps)
     n = int(lib().wisp_attn_workspace_bytes(C.byref(L), max_seq))
-    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")  # zero before first use
     err = WispErrCtx()
     rc = lib().wisp_attn_decode(C.byref(L), xd.data_ptr(), Kd.data_ptr(), Vd.data_ptr(), pos,
                                 max_seq, ws.data_ptr(), n,

@@ -16,17 +16,20 @@
 // Kernels (all HBM- or latency-bound at one token; every one waits on its
 // predecessor with griddepcontrol.wait before reading its output):
 //   embed_kernel        x = fp32(embed[token])
-//   qkv_rope_kernel     RMSNorm of x (each CTA recomputes it: H floats from L2),
-//                       the q / k / v rows of one head as warp-per-row-pair GEMVs
-//                       (a rotary pair i, i + d/2 lands in one warp), the
-//                       rotation, and k / v stored as fp16 into the cache at pos
+//   proj_split_kernel   q / k / v (with the RMSNorm, the rotation and the fp16
+//                       cache stores) and o_proj (with the residual) on the
+//                       tensor cores, each 16-row tile split over column slices
+//                       (see the comment at the kernel)
 //   attn_part_kernel    flash-decoding: CTA (kv head, up to 8 of its query heads,
 //                       a chunk of positions): scores with one lane per position
 //                       (the K row read once for all the CTA's heads), the
 //                       chunk's max and sum, and P.V with one thread per output
 //                       dimension (V rows read coalesced)
 //   attn_merge_kernel   the chunks' (max, sum, output) merged per head
-//   rows_gemv_kernel    y = W x or y += W x (o_proj with the residual, lm_head)
+//   rows_gemv_kernel    y = W x or y += W x, warp per row (lm_head; o_proj of
+//                       shapes the split kernel does not take)
+//   qkv_rope_kernel     q / k / v warp per rotary row pair (shapes the split
+//                       kernel does not take)
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -50,6 +53,13 @@ constexpr int kMaxHeadDim = 576;  // k_dim / v_dim limit of the attention kernel
 __device__ __forceinline__ void dec_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void dec_pdl_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Warm L2 with `bytes` (a multiple of 16) at the 16-byte aligned p: issued
+// before griddepcontrol.wait for weights and cache rows this kernel will
+// read, so their DRAM reads overlap the previous kernel's tail.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ float dot8(const uint4& wv, const float* x) {
@@ -118,11 +128,24 @@ __device__ __forceinline__ float2 row_pair_dot(const __half* __restrict__ W, int
     const int lane = threadIdx.x & 31;
     const uint4* a = reinterpret_cast<const uint4*>(W + (size_t)r0 * H);
     const uint4* b = reinterpret_cast<const uint4*>(W + (size_t)r1 * H);
+    // kLoads 16-byte loads of each row in flight per lane before any is used
+    constexpr int kLoads = 4;
+    const int n = H / 8;
     float s0 = 0.f, s1 = 0.f;
-    for (int c = lane; c < H / 8; c += 32) {
-        const uint4 wa = __ldg(a + c), wb = __ldg(b + c);
-        s0 += dot8(wa, xs + c * 8);
-        s1 += dot8(wb, xs + c * 8);
+    for (int c0 = lane; c0 < n; c0 += 32 * kLoads) {
+        uint4 wa[kLoads], wb[kLoads];
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int c = c0 + 32 * u;
+            wa[u] = c < n ? __ldg(a + c) : make_uint4(0, 0, 0, 0);
+            wb[u] = c < n ? __ldg(b + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int c = min(c0 + 32 * u, n - 1);
+            s0 += dot8(wa[u], xs + c * 8);
+            s1 += dot8(wb[u], xs + c * 8);
+        }
     }
     return make_float2(warp_sum(s0), warp_sum(s1));
 }
@@ -218,6 +241,16 @@ attn_part_kernel(const float* __restrict__ q, const __half* __restrict__ Kc,
     const int t0 = split * chunk, tn = min(seq, t0 + chunk) - t0;
     float* qs = sm;                        // [kAttnHeads][k_dim]
     float* sc = sm + kAttnHeads * k_dim;   // [kAttnHeads][chunk]
+    if (hb == 0) {  // one CTA of the kv head's query-head blocks warms the chunk's rows
+        // (value rows only when they are 16-byte aligned pieces of whole 16 bytes)
+        const bool v_ok = Vc != Kc && v_stride % 8 == 0 && v_dim % 8 == 0 &&
+                          (reinterpret_cast<uintptr_t>(Vc) & 15u) == 0;
+        for (int t = tid; t < tn; t += kDecThreads) {
+            prefetch_l2(Kc + ((size_t)(t0 + t) * nkv + kvh) * k_dim, (uint32_t)k_dim * 2);
+            if (v_ok)
+                prefetch_l2(Vc + ((size_t)(t0 + t) * nkv + kvh) * v_stride, (uint32_t)v_dim * 2);
+        }
+    }
     dec_pdl_wait();
     dec_pdl_launch();
     for (int i = tid; i < ng * k_dim; i += kDecThreads) qs[i] = q[(size_t)h0 * k_dim + i];
@@ -231,11 +264,19 @@ attn_part_kernel(const float* __restrict__ q, const __half* __restrict__ Kc,
         float acc[kAttnHeads];
 #pragma unroll
         for (int g = 0; g < kAttnHeads; ++g) acc[g] = 0.f;
-        for (int c = 0; c < k_dim / 8; ++c) {
-            const uint4 kv = __ldg(kr + c);
+        constexpr int kLoads = 8;  // the key row's 16-byte pieces in flight together
+        for (int c0 = 0; c0 < k_dim / 8; c0 += kLoads) {
+            uint4 kv[kLoads];
 #pragma unroll
-            for (int g = 0; g < kAttnHeads; ++g)
-                if (g < ng) acc[g] = dot8_chain(kv, qs + g * k_dim + c * 8, acc[g]);
+            for (int u = 0; u < kLoads; ++u)
+                kv[u] = c0 + u < k_dim / 8 ? __ldg(kr + c0 + u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < kLoads; ++u) {
+                if (c0 + u >= k_dim / 8) break;
+#pragma unroll
+                for (int g = 0; g < kAttnHeads; ++g)
+                    if (g < ng) acc[g] = dot8_chain(kv[u], qs + g * k_dim + (c0 + u) * 8, acc[g]);
+            }
         }
 #pragma unroll
         for (int g = 0; g < kAttnHeads; ++g)
@@ -288,6 +329,7 @@ attn_part_kernel(const float* __restrict__ q, const __half* __restrict__ Kc,
         const __half* vcol = Vc + (size_t)kvh * v_stride + d;
         const size_t vstep = (size_t)nkv * v_stride;
         float acc = 0.f;
+#pragma unroll 8
         for (int t = 0; t < tn; ++t) acc = fmaf(p[t], __half2float(vcol[(size_t)(t0 + t) * vstep]), acc);
         const int h = h0 + g;
         if (nsplit == 1) {
@@ -307,21 +349,255 @@ attn_part_kernel(const float* __restrict__ q, const __half* __restrict__ Kc,
 __global__ void __launch_bounds__(kDecThreads)
 attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                   float* __restrict__ out, int nsplit, int v_dim) {
+    extern __shared__ float s_e[];  // [nsplit] e^(m_i - M)
+    __shared__ float s_inv;
     const int h = blockIdx.x;
     dec_pdl_wait();
     dec_pdl_launch();
     const float* ml = part_ml + (size_t)h * nsplit * 2;
-    float M = -1e30f;
-    for (int i = 0; i < nsplit; ++i) M = fmaxf(M, ml[2 * i]);
-    float L = 0.f;
-    for (int i = 0; i < nsplit; ++i) L += ml[2 * i + 1] * expf(ml[2 * i] - M);
-    const float inv = 1.f / (L > 0.f ? L : 1.f);
+    if (threadIdx.x < 32) {
+        float M = -1e30f;
+        for (int i = threadIdx.x; i < nsplit; i += 32) M = fmaxf(M, ml[2 * i]);
+        M = warp_max(M);
+        float L = 0.f;
+        for (int i = threadIdx.x; i < nsplit; i += 32) {
+            const float e = expf(ml[2 * i] - M);
+            s_e[i] = e;
+            L += ml[2 * i + 1] * e;
+        }
+        L = warp_sum(L);
+        if (threadIdx.x == 0) s_inv = 1.f / (L > 0.f ? L : 1.f);
+    }
+    __syncthreads();
+    const float inv = s_inv;
     for (int d = threadIdx.x; d < v_dim; d += kDecThreads) {
+        const float* po = part_o + (size_t)h * nsplit * v_dim + d;
         float acc = 0.f;
-        for (int i = 0; i < nsplit; ++i)
-            acc = fmaf(part_o[((size_t)h * nsplit + i) * v_dim + d], expf(ml[2 * i] - M), acc);
+#pragma unroll 8
+        for (int i = 0; i < nsplit; ++i) acc = fmaf(po[(size_t)i * v_dim], s_e[i], acc);
         out[(size_t)h * v_dim + d] = acc * inv;
     }
+}
+
+// ------------------------------------------------------------------------
+// q / k / v and o projections on the tensor cores, split over the columns.
+// A CTA computes one 16-row tile (one rotary tile pair for q / k / v) over a
+// 1/J slice of the columns: the layer's weights spread over many small CTAs,
+// each warp with a single round of 16-byte loads in flight.  mma.sync
+// m16n8k16 (fp16 x fp16 -> fp32) takes the weights as A; the input vector is
+// split into fp16 hi and lo parts (x ~= hi + lo to about 2^-22) in columns 0
+// and 1 of B, so the products carry fp32-level precision and row r's result
+// is column 0 + column 1; the 16 rows of a tile share every input fragment.
+// Each lane loads 16 contiguous bytes of its two rows per 32-column block;
+// the K order inside a block is permuted identically for the weights and the
+// input (a dot product is order-free).  The J partial tiles are summed in
+// slice order by the last CTA to finish (a counter per tile, left at zero),
+// which also applies the rotation and the cache stores, or the residual.
+// With `norm`, each CTA computes cpu_rmsnorm's scale over the whole input
+// and applies it on the way in.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+                 : "memory");
+    return old;
+}
+
+struct ProjArgs {
+    const __half* W[3];    // q, k, v projections (QKV) or the matrix
+    const float* x;        // fp32 input [K] (written by the previous kernel)
+    const __half* norm_w;  // with `norm`: the input is rmsnorm(x; norm_w, eps) (NULL: ones)
+    float eps;
+    int norm;
+    float* part;    // [tiles][J][32] partial rows
+    int* counters;  // [tiles], zero on entry, left zero
+    int K, J, rows;
+    int nh, nkv, hd;  // QKV
+    float* y;         // rows mode: y[r] += W[r] . x
+    float* q_out;     // QKV outputs
+    __half* Kc;
+    __half* Vc;
+    int pos;
+    float theta;
+};
+
+// 8 consecutive inputs at k (normalised when `norm`: (x * scale) * w, as
+// cpu_rmsnorm rounds it) as the fp16 hi or lo part: this lane's B pieces.
+__device__ __forceinline__ uint4 x_frag(const float* __restrict__ x, int k, bool lo, bool norm,
+                                        float scale, const __half* __restrict__ w) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(x + k));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(x + k + 4));
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (norm) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = v[i] * scale * (w ? __half2float(w[k + i]) : 1.0f);
+    }
+    uint32_t r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half h0 = __float2half_rn(v[2 * i]), h1 = __float2half_rn(v[2 * i + 1]);
+        if (lo) {
+            h0 = __float2half_rn(v[2 * i] - __half2float(h0));
+            h1 = __float2half_rn(v[2 * i + 1] - __half2float(h1));
+        }
+        const __half2 h2 = __halves2half2(h0, h1);
+        r[i] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+template <bool QKV>
+__global__ void __launch_bounds__(kDecThreads)
+proj_split_kernel(ProjArgs P) {
+    __shared__ float part[kDecWarps][2][32][4];
+    __shared__ int s_last;
+    __shared__ double s_red[kDecWarps];
+    __shared__ float s_scale;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    const int j = blockIdx.x, u = blockIdx.y, J = P.J, K = P.K;
+    const __half* W = P.W[0];
+    int rA, rB = 0, rows;
+    if (QKV) {
+        const int per = P.hd / 32, head = u / per, t = u - head * per, half = P.hd / 2;
+        int r0;
+        if (head < P.nh) {
+            r0 = head * P.hd;
+        } else if (head < P.nh + P.nkv) {
+            W = P.W[1];
+            r0 = (head - P.nh) * P.hd;
+        } else {
+            W = P.W[2];
+            r0 = (head - P.nh - P.nkv) * P.hd;
+        }
+        rA = r0 + t * 16;
+        rB = r0 + half + t * 16;
+        rows = r0 + P.hd;
+    } else {
+        rA = u * 16;
+        rows = P.rows;
+    }
+    constexpr int kT = QKV ? 2 : 1;
+    const int ks = K / J, kc0 = j * ks;
+    if (threadIdx.x < 16 * kT) {  // this CTA's weight slice, warmed before the wait
+        const int r = threadIdx.x < 16 ? rA + threadIdx.x : rB + threadIdx.x - 16;
+        if (r < rows) prefetch_l2(W + (size_t)r * K + kc0, (uint32_t)ks * 2);
+    }
+    dec_pdl_wait();
+    dec_pdl_launch();
+    float scale = 1.f;
+    if (P.norm) {
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < K; i += kDecThreads) {
+            const double v = (double)__ldcg(P.x + i);
+            ss += v * v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+        if (lane == 0) s_red[warp] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int i = 0; i < kDecWarps; ++i) t += s_red[i];
+            s_scale = (float)(1.0 / sqrt(t / (double)K + (double)P.eps));
+        }
+        __syncthreads();
+        scale = s_scale;
+    }
+    const int kw = ks / kDecWarps, k0 = kc0 + warp * kw, k1 = k0 + kw;
+    const int ra[2] = {min(rA + g, rows - 1), min(rB + g, rows - 1)};
+    const int rb[2] = {min(rA + g + 8, rows - 1), min(rB + g + 8, rows - 1)};
+    float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    constexpr int kU = 4;
+    for (int kb = k0; kb < k1; kb += 32 * kU) {
+        uint4 wa[kT][kU], wb[kT][kU];
+#pragma unroll
+        for (int tt = 0; tt < kT; ++tt)
+#pragma unroll
+            for (int v = 0; v < kU; ++v) {
+                const bool in = kb + 32 * v < k1;
+                const size_t c = (size_t)(kb + 32 * v) + 8 * q;
+                wa[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)ra[tt] * K + c))
+                               : make_uint4(0, 0, 0, 0);
+                wb[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)rb[tt] * K + c))
+                               : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+        for (int v = 0; v < kU; ++v) {
+            if (kb + 32 * v >= k1) break;
+            const uint4 xv = g < 2 ? x_frag(P.x, kb + 32 * v + 8 * q, g == 1, P.norm != 0, scale,
+                                            P.norm_w)
+                                   : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int tt = 0; tt < kT; ++tt) {
+                mma_f16(d[tt], wa[tt][v].x, wb[tt][v].x, wa[tt][v].y, wb[tt][v].y, xv.x, xv.y);
+                mma_f16(d[tt], wa[tt][v].z, wb[tt][v].z, wa[tt][v].w, wb[tt][v].w, xv.z, xv.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[warp][tt][lane][i] = d[tt][i];
+    __syncthreads();
+    // this slice's rows, summed over the warps in order, to the slice record
+    if (warp == 0 && q == 0) {
+#pragma unroll
+        for (int tt = 0; tt < kT; ++tt) {
+            float a = 0.f, b = 0.f;
+            for (int w = 0; w < kDecWarps; ++w) {
+                a += part[w][tt][lane][0] + part[w][tt][lane][1];
+                b += part[w][tt][lane][2] + part[w][tt][lane][3];
+            }
+            float* dst = P.part + ((size_t)u * J + j) * 32 + tt * 16;
+            dst[g] = a;
+            dst[g + 8] = b;
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomic_add_acq_rel(P.counters + u, 1) == J - 1;
+    __syncthreads();
+    if (!s_last) return;
+    // the last slice: the tile's rows over all slices in order, then the epilogue
+    if (threadIdx.x < 16) {
+        const int i = threadIdx.x;
+        float a = 0.f, b = 0.f;
+        for (int jj = 0; jj < J; ++jj) {
+            const float* src = P.part + ((size_t)u * J + jj) * 32;
+            a += __ldcg(src + i);
+            if (QKV) b += __ldcg(src + 16 + i);
+        }
+        if (QKV) {
+            const int per = P.hd / 32, head = u / per, t = u - head * per, half = P.hd / 2;
+            const int pi = t * 16 + i;  // rotary pair (pi, pi + half)
+            if (head < P.nh) {
+                const float2 r = rope_pair(a, b, pi, P.hd, P.pos, P.theta);
+                P.q_out[head * P.hd + pi] = r.x;
+                P.q_out[head * P.hd + pi + half] = r.y;
+            } else if (head < P.nh + P.nkv) {
+                const float2 r = rope_pair(a, b, pi, P.hd, P.pos, P.theta);
+                __half* dst = P.Kc + ((size_t)P.pos * P.nkv + (head - P.nh)) * P.hd;
+                dst[pi] = __float2half_rn(r.x);
+                dst[pi + half] = __float2half_rn(r.y);
+            } else {
+                __half* dst = P.Vc + ((size_t)P.pos * P.nkv + (head - P.nh - P.nkv)) * P.hd;
+                dst[pi] = __float2half_rn(a);
+                dst[pi + half] = __float2half_rn(b);
+            }
+        } else if (rA + i < rows) {
+            P.y[rA + i] += a;
+        }
+    }
+    if (threadIdx.x == 0) P.counters[u] = 0;  // ready for the next call
 }
 
 // y[r] (= or +=) W[r] . x for rows r, one warp per row; x staged in dynamic
@@ -339,8 +615,19 @@ rows_gemv_kernel(const __half* __restrict__ W, const float* __restrict__ x, floa
     const int r = blockIdx.x * kDecWarps + (threadIdx.x >> 5);
     if (r >= rows) return;
     const uint4* w = reinterpret_cast<const uint4*>(W + (size_t)r * cols);
+    constexpr int kLoads = 8;  // 16-byte loads in flight per lane
+    const int n = cols / 8;
     float s = 0.f;
-    for (int c = lane; c < cols / 8; c += 32) s += dot8(__ldg(w + c), xs + c * 8);
+    for (int c0 = lane; c0 < n; c0 += 32 * kLoads) {
+        uint4 wv[kLoads];
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int c = c0 + 32 * u;
+            wv[u] = c < n ? __ldg(w + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) s += dot8(wv[u], xs + min(c0 + 32 * u, n - 1) * 8);
+    }
     s = warp_sum(s);
     if (lane == 0) y[r] = ACC ? y[r] + s : s;
 }
@@ -382,6 +669,17 @@ namespace {
 // partial result (v_dim + 2 floats), so the reference launcher's score
 // scratch ([n_heads][seq] floats) holds every chunk's partials.
 int attn_chunk(int v_dim) { return std::max(kAttnChunk, 2 * (v_dim + 2)); }
+
+// Chunk of the fused decode (its own workspace, sized for chunks of at least
+// kMinChunk): enough chunks for about two CTAs per SM, 32-position multiples,
+// at most kMaxChunk positions (shared memory).
+constexpr int kMinChunk = 32, kMaxChunk = 4096;
+int decode_chunk(int seq, int ctas_per_chunk) {
+    const int want = std::max(1, (2 * sm_count() + ctas_per_chunk - 1) / ctas_per_chunk);
+    int c = (seq + want - 1) / want;
+    c = (std::max(c, kMinChunk) + 31) / 32 * 32;
+    return std::min(c, kMaxChunk);
+}
 size_t attn_smem(int k_dim, int chunk) { return (size_t)kAttnHeads * (k_dim + chunk) * sizeof(float); }
 
 // Dynamic shared memory above the 48 KB default needs the kernel's opt-in
@@ -396,8 +694,7 @@ bool set_smem_once(const void* kern, size_t bytes) {
 
 cudaError_t launch_attention(const float* q, const __half* K, const __half* V, float* out,
                              float* part_o, float* part_ml, int seq, int nh, int nkv, int k_dim,
-                             int v_dim, int v_stride, float scale, cudaStream_t s) {
-    const int chunk = attn_chunk(v_dim);
+                             int v_dim, int v_stride, float scale, int chunk, cudaStream_t s) {
     const int nsplit = (seq + chunk - 1) / chunk;
     const int group = nh / nkv, hblocks = (group + kAttnHeads - 1) / kAttnHeads;
     const size_t smem = attn_smem(k_dim, chunk);
@@ -407,7 +704,7 @@ cudaError_t launch_attention(const float* q, const __half* K, const __half* V, f
                                s, q, K, V, out, part_o, part_ml, seq, nh, nkv, k_dim, v_dim,
                                v_stride, scale, chunk);
     if (e != cudaSuccess || nsplit == 1) return e;
-    return launch_pdl(attn_merge_kernel, dim3(nh), dim3(kDecThreads), 0, s,
+    return launch_pdl(attn_merge_kernel, dim3(nh), dim3(kDecThreads), (size_t)nsplit * 4, s,
                       (const float*)part_o, (const float*)part_ml, out, nsplit, v_dim);
 }
 
@@ -418,15 +715,31 @@ using namespace wb;
 namespace {
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Column slices of a split projection: the most of 4 / 2 / 1 that leaves each
+// warp a whole number of 32-column blocks.
+int split_of(int K) {
+    for (int J = 4; J > 1; J /= 2)
+        if (K % (256 * J) == 0) return J;
+    return 1;
+}
+
 struct AttnWs {
-    float *q, *attn, *part_ml, *part_o;
+    float *q, *attn, *part_ml, *part_o, *pq, *po;
+    int* counters;
+    bool split;          // tensor-core split projections (else warp-per-row kernels)
+    int jq, jo, uq, uo;  // slices and tiles of the q/k/v and o projections
     size_t bytes;
 };
 AttnWs attn_ws_layout(const WispAttnLayer* L, int max_seq, void* base) {
-    const int nh = L->n_heads, hd = L->head_dim;
-    const int nsplit = (max_seq + attn_chunk(hd) - 1) / attn_chunk(hd);
+    const int nh = L->n_heads, nkv = L->n_kv_heads, hd = L->head_dim, H = L->hidden;
+    const int nsplit = (max_seq + kMinChunk - 1) / kMinChunk;
     auto up = [](size_t v) { return (v + 63) / 64 * 64; };
     AttnWs w{};
+    w.split = H % 256 == 0 && hd % 32 == 0 && (nh * hd) % 256 == 0;
+    w.jq = split_of(H);
+    w.jo = split_of(nh * hd);
+    w.uq = (nh + 2 * nkv) * (hd / 32);
+    w.uo = (H + 15) / 16;
     size_t o = 0;
     char* b = static_cast<char*>(base);
     w.q = reinterpret_cast<float*>(b + o);
@@ -437,6 +750,12 @@ AttnWs attn_ws_layout(const WispAttnLayer* L, int max_seq, void* base) {
     o += up((size_t)nh * nsplit * 2 * 4);
     w.part_o = reinterpret_cast<float*>(b + o);
     o += up((size_t)nh * nsplit * hd * 4);
+    w.pq = reinterpret_cast<float*>(b + o);
+    o += up((size_t)w.uq * w.jq * 32 * 4);
+    w.po = reinterpret_cast<float*>(b + o);
+    o += up((size_t)w.uo * w.jo * 32 * 4);
+    w.counters = reinterpret_cast<int*>(b + o);
+    o += up((size_t)(w.uq + w.uo) * 4);
     w.bytes = o;
     return w;
 }
@@ -480,7 +799,8 @@ extern "C" void wisp_gpu_attention(const float* q, const wisp_half* Kcache, cons
     const bool same = Vcache == Kcache || Vcache == nullptr;
     launch_attention(q, reinterpret_cast<const __half*>(Kcache),
                      reinterpret_cast<const __half*>(same ? Kcache : Vcache), out, part_o, part_ml,
-                     seq_len, n_heads, kv_heads, k_dim, v_dim, same ? k_dim : v_dim, scale, s);
+                     seq_len, n_heads, kv_heads, k_dim, v_dim, same ? k_dim : v_dim, scale, chunk,
+                     s);
 }
 
 extern "C" size_t wisp_attn_workspace_bytes(const WispAttnLayer* layer, int max_seq) {
@@ -518,31 +838,78 @@ extern "C" WispError wisp_attn_decode(const WispAttnLayer* L, float* x, wisp_hal
                    workspace_bytes, w.bytes);
         return WISP_ERR_INVALID_ARG;
     }
-    const size_t xs_bytes = (size_t)std::max(H, nh * hd) * sizeof(float);
-    if (!set_smem_once(reinterpret_cast<const void*>(qkv_rope_kernel), (size_t)H * 4) ||
-        !set_smem_once(reinterpret_cast<const void*>(rows_gemv_kernel<true>), xs_bytes)) {
-        WB_SET_ERR(err, WISP_ERR_CUDA, "attn_decode: shared memory attribute refused");
-        return WISP_ERR_CUDA;
-    }
     const __half* Kc = reinterpret_cast<const __half*>(k_cache);
     const __half* Vc = reinterpret_cast<const __half*>(v_cache);
-    WB_CUDA_RET(launch_pdl(qkv_rope_kernel, dim3((hd / 2 + kDecWarps - 1) / kDecWarps, nh + 2 * nkv),
-                           dim3(kDecThreads), (size_t)H * 4, s, (const float*)x,
-                           reinterpret_cast<const __half*>(L->input_norm), L->rms_eps,
-                           reinterpret_cast<const __half*>(L->q_proj),
-                           reinterpret_cast<const __half*>(L->k_proj),
-                           reinterpret_cast<const __half*>(L->v_proj), w.q,
-                           reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache),
-                           pos, nh, nkv, hd, H, L->rope_theta),
-                err);
+    // q / k / v: tensor-core split-K projections when the shapes split evenly
+    // (H and the head width multiples of 256, head_dim of 32), else warp-per-row
+    // fused multiply-adds
+    if (w.split) {
+        ProjArgs P{};
+        P.W[0] = reinterpret_cast<const __half*>(L->q_proj);
+        P.W[1] = reinterpret_cast<const __half*>(L->k_proj);
+        P.W[2] = reinterpret_cast<const __half*>(L->v_proj);
+        P.x = x;
+        P.norm = 1;
+        P.norm_w = reinterpret_cast<const __half*>(L->input_norm);
+        P.eps = L->rms_eps;
+        P.part = w.pq;
+        P.counters = w.counters;
+        P.K = H;
+        P.J = w.jq;
+        P.nh = nh;
+        P.nkv = nkv;
+        P.hd = hd;
+        P.q_out = w.q;
+        P.Kc = reinterpret_cast<__half*>(k_cache);
+        P.Vc = reinterpret_cast<__half*>(v_cache);
+        P.pos = pos;
+        P.theta = L->rope_theta;
+        WB_CUDA_RET(launch_pdl(proj_split_kernel<true>, dim3(w.jq, w.uq), dim3(kDecThreads), 0, s, P),
+                    err);
+    } else {
+        if (!set_smem_once(reinterpret_cast<const void*>(qkv_rope_kernel), (size_t)H * 4)) {
+            WB_SET_ERR(err, WISP_ERR_CUDA, "attn_decode: shared memory attribute refused");
+            return WISP_ERR_CUDA;
+        }
+        WB_CUDA_RET(launch_pdl(qkv_rope_kernel, dim3((hd / 2 + kDecWarps - 1) / kDecWarps, nh + 2 * nkv),
+                               dim3(kDecThreads), (size_t)H * 4, s, (const float*)x,
+                               reinterpret_cast<const __half*>(L->input_norm), L->rms_eps,
+                               reinterpret_cast<const __half*>(L->q_proj),
+                               reinterpret_cast<const __half*>(L->k_proj),
+                               reinterpret_cast<const __half*>(L->v_proj), w.q,
+                               reinterpret_cast<__half*>(k_cache),
+                               reinterpret_cast<__half*>(v_cache), pos, nh, nkv, hd, H,
+                               L->rope_theta),
+                    err);
+    }
+    const int hblocks = (nh / nkv + kAttnHeads - 1) / kAttnHeads;
     WB_CUDA_RET(launch_attention(w.q, Kc, Vc, w.attn, w.part_o, w.part_ml, pos + 1, nh, nkv, hd, hd,
-                                 hd, 1.0f / sqrtf((float)hd), s),
+                                 hd, 1.0f / sqrtf((float)hd), decode_chunk(pos + 1, nkv * hblocks),
+                                 s),
                 err);
-    WB_CUDA_RET(launch_pdl(rows_gemv_kernel<true>, dim3((H + kDecWarps - 1) / kDecWarps),
-                           dim3(kDecThreads), (size_t)nh * hd * 4, s,
-                           reinterpret_cast<const __half*>(L->o_proj), (const float*)w.attn, x, H,
-                           nh * hd),
-                err);
+    if (w.split) {
+        ProjArgs P{};
+        P.W[0] = reinterpret_cast<const __half*>(L->o_proj);
+        P.x = w.attn;
+        P.part = w.po;
+        P.counters = w.counters + w.uq;
+        P.K = nh * hd;
+        P.J = w.jo;
+        P.rows = H;
+        P.y = x;
+        WB_CUDA_RET(launch_pdl(proj_split_kernel<false>, dim3(w.jo, w.uo), dim3(kDecThreads), 0, s, P),
+                    err);
+    } else {
+        if (!set_smem_once(reinterpret_cast<const void*>(rows_gemv_kernel<true>), (size_t)nh * hd * 4)) {
+            WB_SET_ERR(err, WISP_ERR_CUDA, "attn_decode: shared memory attribute refused");
+            return WISP_ERR_CUDA;
+        }
+        WB_CUDA_RET(launch_pdl(rows_gemv_kernel<true>, dim3((H + kDecWarps - 1) / kDecWarps),
+                               dim3(kDecThreads), (size_t)nh * hd * 4, s,
+                               reinterpret_cast<const __half*>(L->o_proj), (const float*)w.attn, x,
+                               H, nh * hd),
+                    err);
+    }
     return WISP_OK;
 }
 

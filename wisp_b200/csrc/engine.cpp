@@ -1476,6 +1476,7 @@ extern "C" WispKVCache* wisp_kv_cache_alloc(WispEngine* e, int max_seq_len, Wisp
     cudaError_t ce = cudaMalloc(&kv->k, bytes);
     if (ce == cudaSuccess) ce = cudaMalloc(&kv->v, bytes);
     if (ce == cudaSuccess) ce = cudaMalloc(&kv->ws, kv->ws_bytes);
+    if (ce == cudaSuccess) ce = cudaMemset(kv->ws, 0, kv->ws_bytes);  // the split-K counters
     if (ce != cudaSuccess) {
         cudaFree(kv->k);
         cudaFree(kv->v);
