@@ -1496,11 +1496,11 @@ __device__ __forceinline__ void load_act_inplace(WarpAct<NPG, NG, MT>& A, float2
 
 // This warp's partial dot products of a unit: acc[h].x = MMA row g (block A),
 // acc[h].y = row g+8 (block B), for token slot 4h + q.  `st`: the stage
-// (shared address); groups g0 .. g0+NG-1 of the unit's range (those past the
-// range are read at the range's last group and contribute 0); kp: shared
+// (shared address); groups g0 .. g0+n-1 of the unit's range (n <= NG; the
+// masked groups past n would add exactly 0 and are skipped); kp: shared
 // address of this warp's (k/254, S) pairs.
 template <int NPG, int NG, int MT, int NQ>
-__device__ __forceinline__ void mma_unit(uint32_t st, const Geo& geo, int g0,
+__device__ __forceinline__ void mma_unit(uint32_t st, const Geo& geo, int g0, int n,
                                          const WarpAct<NPG, NG, MT>& A, uint32_t kp,
                                          float2 (&acc)[MT / 4]) {
     static_assert(NQ >= 1 && NQ <= MT / 4, "active token quads");
@@ -1513,7 +1513,8 @@ __device__ __forceinline__ void mma_unit(uint32_t st, const Geo& geo, int g0,
     for (int h = 0; h < MT / 4; ++h) acc[h] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int G = 0; G < NG; ++G) {
-        const uint32_t gg = (uint32_t)min(g0 + G, geo.ng - 1);
+        if (G >= n) break;  // warp-uniform
+        const uint32_t gg = (uint32_t)(g0 + G);
         const Words<NPG> wl = lds_w<NPG>(a_lo + gg * kGroupCode);
         const Words<NPG> wh = lds_w<NPG>(a_lo + geo.bbytes + gg * kGroupCode);
         const uint32_t pl = lds32(z_lo + gg * 32), ph = lds32(z_lo + geo.bbytes + gg * 32);
@@ -1607,11 +1608,11 @@ __device__ void consume(const StreamSmem& S, const Ws& W, const Geo& geo, int up
         if (!(uf & kSkip)) {
             if constexpr (MT > kMT) {
                 if (nq == 2)
-                    mma_unit<NPG, NG, MT, 2>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+                    mma_unit<NPG, NG, MT, 2>(st0 + s * S.stage_bytes, geo, g0, n, A, kp, part);
                 else
-                    mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+                    mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, n, A, kp, part);
             } else {
-                mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, A, kp, part);
+                mma_unit<NPG, NG, MT, 1>(st0 + s * S.stage_bytes, geo, g0, n, A, kp, part);
             }
         }
         float2* red = S.red + ((size_t)s * kNcw + cw) * 32 * (MT / 4);
