@@ -102,6 +102,9 @@ struct LayerArgs {
     int act_slots;  // token slots of the staged activation tile (min(T, kMT))
     int mt;         // tokens per expert tile of the plan (1, 4 or 8)
     int gating;     // WISP_GATING_* of the layer
+    int tiles_hint; // the plan's likely tile count (exact for one token), so the
+                    // streaming kernels can fetch their first tile record
+                    // while the actual count is still in flight
 };
 
 struct Ws {
@@ -455,6 +458,31 @@ __host__ __device__ inline size_t prep_smem_bytes(int H, int cs, int E) {
 }
 constexpr int kProbeSlots = 5;  // experts 0..E (E <= 1024) over 256 threads
 
+// Partial router logit of expert e over a CTA's slice of the row (n4 float4s
+// in shared memory, starting at float4 i0 of the row), reduced over the warp.
+// With `pre`, this lane's first two 16-byte words of the row are rw0 / rw1
+// (loaded before the PDL wait).
+__device__ __forceinline__ float router_dot(const LayerArgs& L, const float4* sx4, int n4, int i0,
+                                            int e, int lane, bool pre, uint4 rw0, uint4 rw1) {
+    const uint4* row =
+        reinterpret_cast<const uint4*>(L.router_w) + ((size_t)e * L.H + (size_t)i0 * 4) / 8;
+    float acc = 0.f;
+    for (int c = lane; c < n4 / 2; c += 32) {
+        const uint4 wv = pre && c < lane + 64 ? (c == lane ? rw0 : rw1) : __ldg(row + c);
+        const float4 a = sx4[2 * c], b = sx4[2 * c + 1];
+        const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+        float2 f = __half22float2(w2[0]);
+        acc = fmaf(f.x, a.x, acc); acc = fmaf(f.y, a.y, acc);
+        f = __half22float2(w2[1]);
+        acc = fmaf(f.x, a.z, acc); acc = fmaf(f.y, a.w, acc);
+        f = __half22float2(w2[2]);
+        acc = fmaf(f.x, b.x, acc); acc = fmaf(f.y, b.y, acc);
+        f = __half22float2(w2[3]);
+        acc = fmaf(f.x, b.z, acc); acc = fmaf(f.y, b.w, acc);
+    }
+    return warp_sum(acc);
+}
+
 __global__ void __launch_bounds__(kPrepThreads)
 prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, int prevK,
             int prev_shared, int prev_kp, int mt) {
@@ -509,6 +537,10 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
     // reading; the first remote store waits for this arrival of every CTA of
     // the cluster, i.e. for all of them to have started.
     const bool remote = cs > 1 && (flags & (P_NORM | P_ROUTE));
+    // With the router, the norm's scale is applied after the router's dot
+    // products and the quantisation after the one cluster barrier.
+    const bool fold = (flags & P_ROUTE) != 0;
+    const bool norm = (flags & P_NORM) != 0;
     if (remote) cluster_arrive_relaxed();
     pdl_wait();
 #pragma unroll
@@ -573,11 +605,74 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             }
             if (y) reinterpret_cast<float4*>(y + (size_t)t * H)[i0 + i] = v;
         }
-        sx4[i] = v;
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        if (fold && norm && L.norm_w) {
+            uint2 nv = nwv;  // prefetched for the first float4
+            if (i != tid) nv = *reinterpret_cast<const uint2*>(
+                              reinterpret_cast<const __half2*>(L.norm_w) + 2 * (i0 + i));
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&nv.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&nv.y));
+            v.x *= a.x; v.y *= a.y; v.z *= b.x; v.w *= b.y;
+        }
+        sx4[i] = v;
     }
     if (!(flags & (P_NORM | P_QUANT | P_ROUTE))) return;
-    if (flags & P_NORM) {
+    if (fold) {
+        // RMSNorm scales the whole row by one factor, so the router's partial
+        // dot products are taken on the weighted, unscaled slice and scaled once
+        // the sum of squares is known: both partial sums cross the cluster in
+        // one barrier, and the slice is normalised and quantised after it.
+        if (norm) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+        }
+        __syncthreads();
+        const float lgp = warp < E ? router_dot(L, sx4, n4, i0, warp, lane, true, rw0, rw1) : 0.f;
+        if (remote) cluster_wait();  // peers started (the arrival at entry)
+        if (norm && tid < cs) {
+            float v = 0.f;
+            for (int w = 0; w < nw; ++w) v += red[w];
+            *cl.map_shared_rank(&s_ssv[rank], tid) = v;  // into CTA tid's copy
+        }
+        if (warp < E && lane == 0) *cl.map_shared_rank(&s_lg[rank * E + warp], 0) = lgp;
+        for (int e = warp + nw; e < E; e += nw) {  // experts past the warp count
+            const float v = router_dot(L, sx4, n4, i0, e, lane, false, rw0, rw1);
+            if (lane == 0) *cl.map_shared_rank(&s_lg[rank * E + e], 0) = v;
+        }
+        cl.sync();  // every CTA holds every sum of squares, rank 0 every partial logit
+        float sc = 1.f;
+        if (norm) {
+            float tot = 0.f;
+            for (int r = 0; r < cs; ++r) tot += s_ssv[r];
+            sc = 1.0f / sqrtf(tot / (float)H + eps);
+        }
+        if (rank == 0)
+            for (int e = tid; e < E; e += kPrepThreads) {
+                float v = 0.f;
+                for (int r = 0; r < cs; ++r) v += s_lg[r * E + e];
+                s_scr[2 * E + e] = __float_as_int(norm ? v * sc : v);
+            }
+        // the normalised slice and its two-digit form; rank 0 leaves warp 0 to
+        // the top-k and the plan
+        const int w0 = rank == 0 ? 1 : 0, nws = nw - w0;
+        if (warp >= w0) {
+            float4* xn = reinterpret_cast<float4*>(W.xn + (size_t)t * H) + i0;
+            for (int base = (warp - w0) * 128; norm && base < n4 * 4; base += nws * 128) {
+                const int i = base / 4 + lane;
+                if (i < n4) {
+                    float4 v = sx4[i];
+                    v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+                    sx4[i] = v;
+                    xn[i] = v;
+                }
+            }
+            __syncwarp();
+            if (flags & P_QUANT)
+                quantize_row(sx4, n4 * 4, L.gs, warp - w0, nws,
+                             W.xq + ((size_t)t * (H / kChunk) + (size_t)i0 * 4 / kChunk) * 4,
+                             W.xqp + (size_t)t * (H / L.gs) + (size_t)i0 * 4 / L.gs);
+        }
+    } else if (flags & P_NORM) {
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
@@ -607,46 +702,19 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             xn[i] = v;
         }
     }
-    __syncthreads();
-    if (flags & P_QUANT)
-        quantize_row(sx4, n4 * 4, L.gs, warp, nw,
-                     W.xq + ((size_t)t * (H / kChunk) + (size_t)i0 * 4 / kChunk) * 4,
-                     W.xqp + (size_t)t * (H / L.gs) + (size_t)i0 * 4 / L.gs);
-    if (flags & P_ROUTE) {
-        if (remote && !(flags & P_NORM)) cluster_wait();  // peers started
-        // partial logits of this slice: warp per expert
-        const uint4* wr = reinterpret_cast<const uint4*>(L.router_w);
-        for (int e = warp; e < E; e += nw) {
-            const uint4* row = wr + ((size_t)e * H + (size_t)i0 * 4) / 8;
-            float acc = 0.f;
-            for (int c = lane; c < n4 / 2; c += 32) {
-                // the first expert's first two words were prefetched
-                const uint4 wv = e == warp && c < lane + 64 ? (c == lane ? rw0 : rw1)
-                                                             : __ldg(row + c);
-                const float4 a = sx4[2 * c], b = sx4[2 * c + 1];
-                const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
-                float2 f = __half22float2(w2[0]);
-                acc = fmaf(f.x, a.x, acc); acc = fmaf(f.y, a.y, acc);
-                f = __half22float2(w2[1]);
-                acc = fmaf(f.x, a.z, acc); acc = fmaf(f.y, a.w, acc);
-                f = __half22float2(w2[2]);
-                acc = fmaf(f.x, b.x, acc); acc = fmaf(f.y, b.y, acc);
-                f = __half22float2(w2[3]);
-                acc = fmaf(f.x, b.z, acc); acc = fmaf(f.y, b.w, acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) *cl.map_shared_rank(&s_lg[rank * E + e], 0) = acc;  // to rank 0
-        }
-        cl.sync();  // rank 0 holds every CTA's partial logits; the others may leave
-        if (rank == 0)
-            for (int e = tid; e < E; e += kPrepThreads) {
-                float v = 0.f;
-                for (int r = 0; r < cs; ++r) v += s_lg[r * E + e];
-                s_scr[2 * E + e] = __float_as_int(v);
-            }
+    if (!fold) {
+        __syncthreads();
+        if (flags & P_QUANT)  // the two-digit form of the slice for the gate/up stream
+            quantize_row(sx4, n4 * 4, L.gs, warp, nw,
+                         W.xq + ((size_t)t * (H / kChunk) + (size_t)i0 * 4 / kChunk) * 4,
+                         W.xqp + (size_t)t * (H / L.gs) + (size_t)i0 * 4 / L.gs);
     }
     if (!(flags & P_ROUTE) || rank != 0) return;
-    if (planner) {
+    // With the router and at most 31 experts, warp 0 holds every logit and
+    // every probe, so the top-k and a one-token plan do not wait for the other
+    // warps (which are still writing the slice's two-digit form).
+    const bool w0only = fold && E + 1 <= 32;
+    if (planner && (!w0only || warp == 0)) {
 #pragma unroll
         for (int i = 0; i < kProbeSlots; ++i) {
             const int e = tid + i * kPrepThreads;
@@ -656,7 +724,10 @@ prep_kernel(LayerArgs L, Ws W, int T, int flags, float* x, float* y, float eps, 
             }
         }
     }
-    __syncthreads();
+    if (w0only)
+        __syncwarp();
+    else
+        __syncthreads();
     const bool one = T == 1 && L.K + 1 <= 32;  // the one-token plan
     if (warp == 0) {
         const float* lg = reinterpret_cast<const float*>(s_scr + 2 * E);
@@ -1103,7 +1174,8 @@ constexpr int kPrePdlStages = 2;
 template <int MT>
 __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end, int upt,
                         int ntiles, const Geo& geo, const ActSrc& as, bool act_after_pdl,
-                        const UnitAddr& ua, bool first_act_elsewhere = false) {
+                        const UnitAddr& ua, bool first_act_elsewhere = false,
+                        const TileView<MT>* pre = nullptr, int pre_ti = -1) {
     const int lane = threadIdx.x & 31;
     const uint32_t tx = 2 * geo.bbytes, zb = (uint32_t)geo.ng * 32u;
     const bool f32 = as.xf != nullptr;
@@ -1116,8 +1188,19 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
     const size_t coff = lane < 4 ? ua.coff[lane] : 0;
     int ti = u_begin / upt, r = u_begin - ti * upt;
     TileView<MT> cur, nxt;
-    if (u_begin < u_end) load_tile(W.tiles + ti, cur);
-    if (ti + 1 < ntiles) load_tile(W.tiles + ti + 1, nxt);
+    if (u_begin < u_end) {
+        if (pre && pre_ti == ti)
+            cur = *pre;
+        else
+            load_tile(W.tiles + ti, cur);
+    }
+    // with a pre-loaded first record (gate/up) the next one is read once the
+    // first copies are on their way
+    bool nxt_due = ti + 1 < ntiles;
+    if (!pre && nxt_due) {
+        load_tile(W.tiles + ti + 1, nxt);
+        nxt_due = false;
+    }
     const unsigned char* p = nullptr;
     bool tile_ok = false;
     // per tile: the lane's source pointer and whether the tile's copies are usable
@@ -1222,6 +1305,10 @@ __device__ void produce(const StreamSmem& S, const Ws& W, int u_begin, int u_end
         if (tile_ok && lane < 4)
             bulk_g2s(S.stages + (size_t)s * S.stage_bytes + dst_off, p, csize, &S.full[s], pol);
         ++issued;
+        if (nxt_due) {
+            load_tile(W.tiles + ti + 1, nxt);
+            nxt_due = false;
+        }
         p += ua.ustride;
         ++r;
         if (first_act_elsewhere && !waited_pdl && it + 1 >= kPrePdlStages) {
@@ -1649,6 +1736,18 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
 
     if (warp == 0) {
         {
+            // the record of the first tile if the plan has tiles_hint tiles, read
+            // alongside the tile count (both come from the previous kernel)
+            TileView<MT> spec;
+            int spec_ti = -1;
+            if (L.tiles_hint > 0) {
+                const long long th = (long long)L.tiles_hint * rbs;
+                spec_ti = (int)(th * blockIdx.x / gridDim.x / rbs);
+                if (spec_ti < W.max_tiles)
+                    load_tile(W.tiles + spec_ti, spec);
+                else
+                    spec_ti = -1;
+            }
             const int b = (int)(total * blockIdx.x / gridDim.x);
             const int e = (int)(total * (blockIdx.x + 1) / gridDim.x);
             const size_t bb = block_bytes_of(H, gs);
@@ -1656,7 +1755,8 @@ gateup_kernel(LayerArgs L, Ws W, int n_stages, uint32_t stage_bytes) {
             const ActSrc as{reinterpret_cast<const uint8_t*>(W.xq), W.xqp, nullptr, H / kChunk,
                             H / gs, 0, NPG, gs, H, false};
             const UnitAddr ua{off_g, bb, {0, 4 * (size_t)H, off_u - off_g, off_u - off_g + 4 * (size_t)H}};
-            produce<MT>(S, W, b, e, rbs, ntiles, geo, as, false, ua);
+            produce<MT>(S, W, b, e, rbs, ntiles, geo, as, false, ua, false,
+                        spec_ti >= 0 ? &spec : nullptr, spec_ti);
         }
         return;
     }
@@ -2009,6 +2109,7 @@ LayerArgs layer_args(const WispMoeLayer* ly, int T, int ctas) {
     a.act_slots = std::min(T, kMT);
     const long long tiles = std::min<long long>((long long)ly->n_experts, (long long)T * a.K) +
                             (a.has_shared == 1 ? (T + a.mt - 1) / a.mt : 0);
+    a.tiles_hint = (int)std::min<long long>(tiles, (long long)T * a.K + a.E + T + 1);
     a.kp = down_parts(a.I, a.gs, tiles * (a.H / 16), ctas, a.act_slots, a.mt);
     if (a.mt == kMaxTile && ng_bucket(npg, a.I / a.gs / a.kp) > kWideMaxNg) {
         a.mt = kMT;
