@@ -186,32 +186,41 @@ ExpertBatch* DoubleBuffer::tick(ExpertBatch* current, ExpertBatch* next) {
 }  // namespace wb
 
 // ------------------------------------------------------------- self-tests
+// The scenario exercises what the engine relies on: a byte budget over blobs of
+// different sizes, recency across two layers, the hit counter that drives RAM ->
+// VRAM promotion, eviction that spares the current layer's experts, and a clear
+// that hands every blob back to its owner.
 extern "C" int wisp_selftest_lru(void) {
     using wb::Lru;
-    static int payload[8];
-    Lru c(3 * sizeof(int));
-    for (uint32_t i = 0; i < 3; ++i) c.put(0, i, &payload[i], sizeof(int));
-    if (c.count() != 3) return 0;
+    static unsigned char blob[4][64];
+    Lru c(160);
+    c.put(2, 10, blob[0], 64);  // layer 2: two experts of 64 bytes
+    c.put(2, 11, blob[1], 64);
+    c.put(3, 40, blob[2], 16);  // layer 3: a small one
+    if (c.count() != 3 || c.used() != 144) return 0;
+    if (!c.would_overflow(32) || c.would_overflow(16)) return 0;
+    // Hits counted per entry; the third one is the promotion threshold.
+    if (c.touch(2, 10) != 1 || c.touch(2, 10) != 2 || c.touch(2, 10) != 3) return 0;
+    if (c.touch(9, 9) != 0) return 0;  // a miss counts nothing
+    // Recency (MRU first): (2,10), (3,40), (2,11).  Keeping layer 2's experts
+    // skips (2,11) and takes (3,40).
+    std::vector<uint64_t> keep = {Lru::key(2, 10), Lru::key(2, 11)};
+    std::sort(keep.begin(), keep.end());
     Lru::Entry e;
-    if (!c.get(0, 0, &e) || e.expert != 0) return 0;
-    c.touch(0, 0);  // expert 0 -> MRU; LRU is now expert 1
-    if (c.get(0, 99, nullptr) || c.get(7, 0, nullptr)) return 0;
-    if (!c.evict(&e) || e.expert != 1) return 0;
-    if (c.count() != 2) return 0;
-    if (c.would_overflow(sizeof(int))) return 0;  // 2/3 used
-    c.put(1, 5, &payload[3], sizeof(int));
-    if (!c.would_overflow(sizeof(int))) return 0;  // 3/3 used
-    if (c.used() != 3 * sizeof(int)) return 0;
-    c.put(1, 5, &payload[4], sizeof(int));  // duplicate put replaces
-    if (c.count() != 3) return 0;
-    if (!c.get(1, 5, &e) || e.data != &payload[4]) return 0;
-    // recency: MRU=(1,5), then (0,0), tail=(0,2)
-    if (!c.evict(&e) || !(e.layer == 0 && e.expert == 2)) return 0;
-    // promotion counter
-    if (c.touch(0, 0) != 2 || c.touch(0, 0) != 3) return 0;
-    c.clear([](const Lru::Entry&) {});
-    if (c.count() != 0 || c.used() != 0 || c.get(0, 0, nullptr)) return 0;
-    return 1;
+    if (!c.evict_except(keep, &e) || e.layer != 3 || e.expert != 40 || e.bytes != 16) return 0;
+    if (c.evict_except(keep, &e)) return 0;  // nothing left outside `keep`
+    // Re-inserting a key replaces its blob, keeps one entry, refreshes recency.
+    c.put(2, 11, blob[3], 32);
+    if (c.count() != 2 || c.used() != 96) return 0;
+    if (!c.get(2, 11, &e) || e.data != blob[3] || e.bytes != 32) return 0;
+    if (!c.evict(&e) || e.expert != 10 || e.hits != 3) return 0;  // (2,10) is LRU now
+    if (!c.remove(2, 11, &e) || c.remove(2, 11, &e) || c.count() != 0) return 0;
+    c.put(5, 1, blob[0], 48);
+    c.put(5, 2, blob[1], 48);
+    size_t handed = 0, bytes = 0;
+    c.clear([&](const Lru::Entry& x) { ++handed; bytes += x.bytes; });
+    if (handed != 2 || bytes != 96 || c.count() != 0 || c.used() != 0) return 0;
+    return c.get(5, 1, nullptr) ? 0 : 1;
 }
 
 extern "C" int wisp_selftest_double_buffer(void) {
