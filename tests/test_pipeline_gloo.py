@@ -1,4 +1,4 @@
-"""The layer pipeline's ring protocol on CPU: world_size-2 gloo ranks, a stand-in
+"""The layer pipeline's ring protocol on CPU: world_size-2 and -4 gloo ranks, a stand-in
 for each rank's layers (an affine map per rank), and the same LayerPipeline the GPU
 bench drives.  After K decode steps every micro-batch must equal the composition of
 all ranks' maps applied K times, in rank order -- which checks the send/receive
@@ -42,7 +42,9 @@ def _rank_main(rank, world, port, steps, M, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,M,steps", [(2, 2, 3), (2, 3, 2)])
+# (4, 4, 2): config 1's four micro-batches at four stages; (4, 2, 3): fewer
+# micro-batches than stages, as at eight GPUs
+@pytest.mark.parametrize("world,M,steps", [(2, 2, 3), (2, 3, 2), (4, 4, 2), (4, 2, 3)])
 def test_ring_applies_every_rank_in_order(world, M, steps):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()

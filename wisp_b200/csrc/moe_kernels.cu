@@ -2726,8 +2726,9 @@ extern "C" WispError wisp_moe_ep_combine(float* y, const float* rows, const int*
 // Every call on a device shares the one array, so two calls whose kernels
 // overlap on the GPU (different streams, or different host threads without
 // ordering) race and corrupt each other's results.  Each call clears what
-// must start at zero (the status word and the kernels' counters, by
-// cudaMemsetAsync on the call's stream).
+// must start at zero (the status word and the kernels' counters) with a
+// one-CTA zeroing kernel on the call's stream, as wisp_moe_block_forward does
+// for a caller's workspace.
 // ------------------------------------------------------------------------
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_block_scratch[kStaticScratchBytes];
