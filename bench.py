@@ -410,7 +410,6 @@ def run_decoder(args, dev, stack, shape, s) -> dict:
     n_ws = int(lib().wisp_attn_workspace_bytes(C.byref(layers[0]), max_seq))
     ws = torch.zeros(n_ws, dtype=torch.uint8, device=dev)  # zero before first use
     x = torch.empty((1, H), dtype=torch.float32, device=dev)
-    xn, y = torch.empty_like(x), torch.empty_like(x)
     logits = torch.empty(vocab, dtype=torch.float32, device=dev)
     lws = torch.empty(H, dtype=torch.float32, device=dev)
     stack.workspace(max(args.batch, 1))
@@ -423,11 +422,8 @@ def run_decoder(args, dev, stack, shape, s) -> dict:
             check(lib().wisp_attn_decode(C.byref(layers[l]), x.data_ptr(), Kc[l].data_ptr(),
                                          Vc[l].data_ptr(), pos, max_seq, ws.data_ptr(), n_ws, cs,
                                          C.byref(err)), err)
-            if with_moe:
-                lib().wisp_gpu_rmsnorm(x.data_ptr(), stack.layer_c(l).norm_w, xn.data_ptr(), H,
-                                       C.c_float(shape.rms_eps), cs)
-                stack.block(l, xn, y)
-                lib().wisp_gpu_residual_add(x.data_ptr(), y.data_ptr(), H, cs)
+            if with_moe:  # x += MoE_l(rmsnorm(x)): the fused one-layer stack
+                stack.stack(x, layers=1, layer0=l)
         check(lib().wisp_lm_head_forward(final_norm.data_ptr(), lm_head.data_ptr(), x.data_ptr(),
                                          logits.data_ptr(), vocab, H, C.c_float(shape.rms_eps),
                                          lws.data_ptr(), lws.numel() * 4, cs, C.byref(err)), err)

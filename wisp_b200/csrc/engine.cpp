@@ -1307,16 +1307,13 @@ extern "C" WispError wisp_moe_decode(WispEngine* e, int layer, const float* x, f
     return wisp_moe_forward(e, layer, x, y, 1, stream, err);
 }
 
-extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, int T,
-                                    cudaStream_t stream, WispErrCtx* err) {
-    if (!e || layer0 < 0 || n <= 0 || layer0 + n > e->n_layers || !x || T <= 0) {
-        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_stack: bad arguments");
-        return WISP_ERR_INVALID_ARG;
-    }
-    cudaSetDevice(e->device);
-    cudaStream_t s = stream ? stream : e->compute;
-    order_after_compute(e, s);
-    wait_uploads(e, s);
+// x <- x + FFN_l(rmsnorm(x; post_norm_l)) for the layers [layer0, layer0 + n) on
+// stream s (the FFN half of decode_step, wisp_engine.c:1563-1570).  A run of
+// VRAM-resident MoE layers is one fused stack (the norm in the router kernel, the
+// residual in the final combine); a layer on the miss path or a dense MLP runs
+// as norm, FFN and residual add.
+static WispError ffn_layers(WispEngine* e, int layer0, int n, float* x, int T, cudaStream_t s,
+                            WispErrCtx* err) {
     WispError r = WISP_OK;
     for (int l = layer0; l < layer0 + n && r == WISP_OK;) {
         // a run of VRAM-resident MoE layers: one fused stack, no host synchronisation
@@ -1342,6 +1339,20 @@ extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, 
         if (r == WISP_OK) WB_CUDA_RET(wb::launch_add_rows(x, e->d_ffn, (size_t)T * e->H, s), err);
         ++l;
     }
+    return r;
+}
+
+extern "C" WispError wisp_moe_stack(WispEngine* e, int layer0, int n, float* x, int T,
+                                    cudaStream_t stream, WispErrCtx* err) {
+    if (!e || layer0 < 0 || n <= 0 || layer0 + n > e->n_layers || !x || T <= 0) {
+        WB_SET_ERR(err, WISP_ERR_INVALID_ARG, "moe_stack: bad arguments");
+        return WISP_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(e->device);
+    cudaStream_t s = stream ? stream : e->compute;
+    order_after_compute(e, s);
+    wait_uploads(e, s);
+    const WispError r = ffn_layers(e, layer0, n, x, T, s, err);
     std::lock_guard<std::mutex> g(e->stats_mu);
     e->tok_ns[e->tok_head] = now_ns();
     e->tok_head = (e->tok_head + 1) % 32;
@@ -1539,13 +1550,8 @@ static WispError decode_step(WispEngine* e, WispKVCache* kv, int token, float* o
                              kv->v + (size_t)l * kv->layer_elems, kv->len, kv->max_seq, kv->ws,
                              kv->ws_bytes, s, err);
         if (r != WISP_OK) return r;
-        WB_CUDA_RET(wb::launch_rmsnorm_rows(e->d_x,
-                                            reinterpret_cast<const __half*>(e->L[l].post_norm),
-                                            e->d_xn, e->H, e->eps, 1, s),
-                    err);
-        r = moe_forward_impl(e, l, e->d_xn, e->d_ffn, 1, s, err);
+        r = ffn_layers(e, l, 1, e->d_x, 1, s, err);
         if (r != WISP_OK) return r;
-        WB_CUDA_RET(wb::launch_add_rows(e->d_x, e->d_ffn, (size_t)e->H, s), err);
     }
     kv->len++;
     if (out_logits) {

@@ -262,10 +262,14 @@ class MoEStack:
         return int(lib().wisp_moe_status(ws.data_ptr() + off,
                                          torch.cuda.current_stream().cuda_stream))
 
-    def stack(self, x: torch.Tensor, routing: bool = False, layers: int | None = None):
-        """x <- x + MoE_l(rmsnorm(x)) for every layer, in place, on the current stream."""
+    def stack(self, x: torch.Tensor, routing: bool = False, layers: int | None = None,
+              layer0: int = 0):
+        """x <- x + MoE_l(rmsnorm(x)) for `layers` layers from `layer0` (default: every
+        layer), in place, on the current stream."""
         T = x.shape[0]
-        n = layers or self.L
+        n = layers or self.L - layer0
+        if layer0 < 0 or layer0 + n > self.L:
+            raise ValueError(f"layers [{layer0}, {layer0 + n}) outside the stack of {self.L}")
         idx = w = None
         if routing:
             idx = torch.empty((n, T, self.shape.top_k), dtype=torch.int32, device=self.device)
@@ -273,7 +277,8 @@ class MoEStack:
         ws = self.workspace(T)
         err = WispErrCtx()
         rc = lib().wisp_moe_stack_forward(
-            C.byref(self._c_layers), n, self.shape.rms_eps, x.data_ptr(), T,
+            C.byref(self._c_layers, layer0 * C.sizeof(WispMoeLayer)), n, self.shape.rms_eps,
+            x.data_ptr(), T,
             idx.data_ptr() if routing else None, w.data_ptr() if routing else None,
             ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream, C.byref(err))
         check(rc, err)
