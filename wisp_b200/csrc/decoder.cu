@@ -486,11 +486,33 @@ proj_split_kernel(ProjArgs P) {
         rows = P.rows;
     }
     constexpr int kT = QKV ? 2 : 1;
+    constexpr int kU = 4;
     const int ks = K / J, kc0 = j * ks;
-    if (threadIdx.x < 16 * kT) {  // this CTA's weight slice, warmed before the wait
+    const int kw = ks / kDecWarps, k0 = kc0 + warp * kw, k1 = k0 + kw;
+    const int ra[2] = {min(rA + g, rows - 1), min(rB + g, rows - 1)};
+    const int rb[2] = {min(rA + g + 8, rows - 1), min(rB + g + 8, rows - 1)};
+    uint4 wa[kT][kU], wb[kT][kU];
+    // this lane's 16-byte weight pieces of kU 32-column blocks from kb on
+    auto load_w = [&](int kb) {
+#pragma unroll
+        for (int tt = 0; tt < kT; ++tt)
+#pragma unroll
+            for (int v = 0; v < kU; ++v) {
+                const bool in = kb + 32 * v < k1;
+                const size_t c = (size_t)(kb + 32 * v) + 8 * q;
+                wa[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)ra[tt] * K + c))
+                               : make_uint4(0, 0, 0, 0);
+                wb[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)rb[tt] * K + c))
+                               : make_uint4(0, 0, 0, 0);
+            }
+    };
+    if (kw > 32 * kU && threadIdx.x < 16 * kT) {  // a slice longer than one round: warm it
         const int r = threadIdx.x < 16 ? rA + threadIdx.x : rB + threadIdx.x - 16;
         if (r < rows) prefetch_l2(W + (size_t)r * K + kc0, (uint32_t)ks * 2);
     }
+    // the weights do not depend on the previous kernel: the first round of loads
+    // is in flight through the dependency wait and the RMSNorm
+    load_w(k0);
     dec_pdl_wait();
     dec_pdl_launch();
     float scale = 1.f;
@@ -512,24 +534,9 @@ proj_split_kernel(ProjArgs P) {
         __syncthreads();
         scale = s_scale;
     }
-    const int kw = ks / kDecWarps, k0 = kc0 + warp * kw, k1 = k0 + kw;
-    const int ra[2] = {min(rA + g, rows - 1), min(rB + g, rows - 1)};
-    const int rb[2] = {min(rA + g + 8, rows - 1), min(rB + g + 8, rows - 1)};
     float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    constexpr int kU = 4;
     for (int kb = k0; kb < k1; kb += 32 * kU) {
-        uint4 wa[kT][kU], wb[kT][kU];
-#pragma unroll
-        for (int tt = 0; tt < kT; ++tt)
-#pragma unroll
-            for (int v = 0; v < kU; ++v) {
-                const bool in = kb + 32 * v < k1;
-                const size_t c = (size_t)(kb + 32 * v) + 8 * q;
-                wa[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)ra[tt] * K + c))
-                               : make_uint4(0, 0, 0, 0);
-                wb[tt][v] = in ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)rb[tt] * K + c))
-                               : make_uint4(0, 0, 0, 0);
-            }
+        if (kb != k0) load_w(kb);
 #pragma unroll
         for (int v = 0; v < kU; ++v) {
             if (kb + 32 * v >= k1) break;
