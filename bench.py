@@ -887,7 +887,7 @@ def main_reference(args):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int4xf32", "data": "synthetic",
         "config": {"workload": "config1: Mixtral-8x7B-shaped 32-block stack decode, sampled "
                                "as 1 token x 1 block per step, x32 blocks"},
