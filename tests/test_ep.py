@@ -1,5 +1,5 @@
-"""Expert parallelism (config 2).  On CPU: the dispatch bookkeeping and a 2-rank gloo
-round trip of dispatch -> per-owner expert compute -> return -> top-k-ordered combine,
+"""Expert parallelism (config 2).  On CPU: the dispatch bookkeeping and 2- and 4-rank gloo
+round trips of dispatch -> per-owner expert compute -> return -> top-k-ordered combine,
 with stand-in experts.  On one GPU: the expert-parallel layer (world size 1, every
 expert local) against the fused block and against the oracle."""
 
@@ -46,11 +46,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_rank(rank, world, port, out):
+def _ep_rank(rank, world, port, out, idle_last=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    per, E, K, B, H = 3, 6, 2, 5, 4
+    per, K, B, H = 3, 2, 5, 4
+    # idle_last: no token routes to the last rank's experts, so it receives no rows
+    E = per * (world - 1) if idle_last else per * world
     g = torch.Generator().manual_seed(100 + rank)
     x = torch.randn(B, H, generator=g)
     idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(B)]).int()
@@ -74,22 +76,28 @@ def _ep_rank(rank, world, port, out):
             e = int(idx[t, j])
             if e >= 0:
                 want[t] += w[t, j] * ((e + 1) * x[t] + e)
-    out.put((rank, float((y - want).abs().max())))
+    out.put((rank, float((y - want).abs().max()), sum(d.recv_counts)))
     dist.destroy_process_group()
 
 
-def test_two_rank_dispatch_compute_return_combine():
+# (2, False): config 2's exchange at two ranks; (4, True): four ranks, the last one
+# owning experts no token chose (it sends its own tokens' rows and receives none)
+@pytest.mark.parametrize("world,idle_last", [(2, False), (4, True)])
+def test_dispatch_compute_return_combine(world, idle_last):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, world, port, out, idle_last))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [out.get(timeout=120) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert all(err < 1e-5 for _, err in res), res
+    assert all(err < 1e-5 for _, err, _ in res), res
+    if idle_last:
+        assert [n for r, _, n in res if r == world - 1] == [0]
 
 
 @pytest.mark.gpu
