@@ -223,37 +223,79 @@ extern "C" int wisp_selftest_lru(void) {
     return c.get(5, 1, nullptr) ? 0 : 1;
 }
 
+// The scenario checks what the staging path relies on: reservations packed back to
+// back up to the exact capacity and refused past it or past the entry limit, a tick
+// handing the consumer the filled side intact while new reservations land in the
+// other buffer, and, with a producer thread, batches that only ever hold whole
+// rounds of fills with their bytes where the entries say.
 extern "C" int wisp_selftest_double_buffer(void) {
+    using wb::ExpertBatch;
+    constexpr size_t kCap = 1024;
     wb::DoubleBuffer db;
-    if (db.init(4096, nullptr, /*pinned=*/false) != cudaSuccess) return 0;
-    void* p0 = db.reserve(1, 10, 1000);
-    void* p1 = db.reserve(1, 11, 1000);
-    if (!p0 || !p1) return 0;
-    if (static_cast<char*>(p1) - static_cast<char*>(p0) != 1000) return 0;
-    if (db.reserve(1, 12, 4096) != nullptr) return 0;  // capacity respected
+    if (db.init(kCap, nullptr, /*pinned=*/false) != cudaSuccess) return 0;
+    const size_t sizes[4] = {256, 512, 128, 128};
+    char* base = nullptr;
+    for (uint32_t e = 0; e < 4; ++e) {
+        char* p = static_cast<char*>(db.reserve(3, e, sizes[e]));
+        if (!p) return 0;
+        if (e == 0) base = p;
+        memset(p, 0x40 + (int)e, sizes[e]);
+    }
+    if (db.reserve(3, 9, 1) != nullptr) return 0;  // exactly full
     db.fill_done();
-    wb::ExpertBatch cur, nxt;
-    wb::ExpertBatch* active = db.tick(&cur, &nxt);
-    if (!active || active->count != 2 || cur.count != 2 || nxt.count != 0) return 0;
-    if (active->expert[0] != 10 || active->expert[1] != 11) return 0;
-    int produced = 0;
+    const int before = db.active();
+    ExpertBatch cur, nxt;
+    ExpertBatch* got = db.tick(&cur, &nxt);
+    if (db.active() == before || got->count != 4 || cur.count != 4 || nxt.count != 0) return 0;
+    const size_t want_off[4] = {0, 256, 768, 896};
+    for (int i = 0; i < 4; ++i) {
+        if (got->layer[i] != 3 || got->expert[i] != (uint32_t)i || got->offset[i] != want_off[i] ||
+            got->size[i] != sizes[i])
+            return 0;
+        const char* d = static_cast<const char*>(db.buffer(db.active())) + got->offset[i];
+        for (size_t k = 0; k < got->size[i]; ++k)
+            if (d[k] != (char)(0x40 + i)) return 0;
+    }
+    if (base != db.buffer(db.active())) return 0;
+    // the next fill goes to the other buffer, outside what the consumer reads
+    char* q = static_cast<char*>(db.reserve(4, 0, 64));
+    const char* act = static_cast<const char*>(db.buffer(db.active()));
+    if (!q || (q >= act && q < act + kCap)) return 0;
+    for (int i = 1; i < ExpertBatch::kMax; ++i)
+        if (!db.reserve(4, (uint32_t)i, 1)) return 0;
+    if (db.reserve(4, 99, 1) != nullptr) return 0;  // entry limit
+    db.fill_done();
+    db.tick(nullptr, nullptr);
+    db.tick(nullptr, nullptr);  // both sides empty again
+    // producer thread: 6 rounds of 4 fills of 32 bytes, one layer per round
+    constexpr int kRounds = 6, kPer = 4;
+    constexpr size_t kSz = 32;
     std::thread producer([&] {
-        for (int r = 0; r < 8; ++r) {
-            for (uint32_t e = 0; e < 4; ++e) {
-                void* dst = db.reserve(0, e, 256);
-                if (dst) {
-                    memset(dst, (int)(e + 1), 256);
-                    ++produced;
-                }
+        for (int r = 0; r < kRounds; ++r) {
+            for (int e = 0; e < kPer; ++e) {
+                char* d = static_cast<char*>(db.reserve((uint32_t)r, (uint32_t)e, kSz));
+                if (d) memset(d, r * kPer + e + 1, kSz);
             }
             db.fill_done();
         }
     });
-    for (int r = 0; r < 8; ++r) db.tick(nullptr, nullptr);
+    int seen = 0;
+    bool ok = true;
+    auto check = [&](const ExpertBatch* bt) {
+        if (bt->count % kPer) ok = false;
+        const char* buf = static_cast<const char*>(db.buffer(db.active()));
+        for (int i = 0; i < bt->count; ++i) {
+            if (bt->expert[i] != (uint32_t)(i % kPer) || bt->layer[i] != bt->layer[i - i % kPer])
+                ok = false;
+            const char want = (char)(bt->layer[i] * kPer + bt->expert[i] + 1);
+            for (size_t k = 0; k < kSz; ++k)
+                if (buf[bt->offset[i] + k] != want) ok = false;
+        }
+        seen += bt->count;
+    };
+    for (int r = 0; r < kRounds; ++r) check(db.tick(nullptr, nullptr));
     producer.join();
-    if (produced == 0) return 0;
-    wb::ExpertBatch* last = db.tick(nullptr, nullptr);
-    for (int i = 0; i < last->count; ++i)
-        if (last->offset[i] + last->size[i] > db.bytes()) return 0;
-    return 1;
+    check(db.tick(nullptr, nullptr));
+    check(db.tick(nullptr, nullptr));
+    return ok && seen == kRounds * kPer ? 1 : 0;
 }
