@@ -385,18 +385,25 @@ void drain_uploads(WispEngine* e) {
     e->uploads_pending = false;
 }
 
-void ram_put(WispEngine* e, uint32_t layer, uint32_t expert, void* data, size_t n) {
-    if (n > e->ram.capacity()) {
-        drain_uploads(e);
-        cudaFreeHost(data);
-        return;
+// Insert a pinned host blob into the RAM tier, evicting its least recently used
+// entries, except the keys in `keep` (sorted), until it fits.  A blob that cannot
+// fit is freed instead and false is returned: the caller must not use `data` then.
+bool ram_put(WispEngine* e, uint32_t layer, uint32_t expert, void* data, size_t n,
+             const std::vector<uint64_t>& keep = {}) {
+    if (n <= e->ram.capacity()) {
+        wb::Lru::Entry v;
+        while (e->ram.would_overflow(n) && e->ram.evict_except(keep, &v)) {
+            drain_uploads(e);  // an upload or write-back may still use the victim's buffer
+            cudaFreeHost(v.data);
+        }
+        if (!e->ram.would_overflow(n)) {
+            e->ram.put(layer, expert, data, n);
+            return true;
+        }
     }
-    wb::Lru::Entry v;
-    while (e->ram.would_overflow(n) && e->ram.evict(&v)) {
-        drain_uploads(e);  // an upload or write-back may still use the victim's buffer
-        cudaFreeHost(v.data);
-    }
-    e->ram.put(layer, expert, data, n);
+    drain_uploads(e);  // a write-back into `data` may still be in flight
+    cudaFreeHost(data);
+    return false;
 }
 
 // Host blob -> device slot in the tiled layout the kernels stream, on the
@@ -443,8 +450,11 @@ void* scratch_serve(WispEngine* e, const void* src, size_t n, WispErrCtx* err) {
 }
 
 // A VRAM slot, evicting the VRAM LRU (copied back to the RAM tier) until
-// one is free.  `keep` lists keys that must not be evicted (sorted).
-void* vram_alloc_evicting(WispEngine* e, size_t n, const std::vector<uint64_t>& keep) {
+// one is free.  `keep` lists keys that must not be evicted (sorted); `ram_keep`
+// lists RAM-tier entries the write-backs must not push out (sorted: the blob
+// being promoted, whose buffer is the next upload's source).
+void* vram_alloc_evicting(WispEngine* e, size_t n, const std::vector<uint64_t>& keep,
+                          const std::vector<uint64_t>& ram_keep) {
     if (e->arena.n_slots() == 0) return nullptr;
     for (;;) {
         if (!e->vram.would_overflow(n)) {
@@ -465,7 +475,7 @@ void* vram_alloc_evicting(WispEngine* e, size_t n, const std::vector<uint64_t>& 
                     cudaSuccess) {
                     cudaEventRecord(e->up_ev, e->transfer);
                     e->uploads_pending = true;
-                    ram_put(e, v.layer, v.expert, host, v.bytes);
+                    ram_put(e, v.layer, v.expert, host, v.bytes, ram_keep);
                 } else {
                     cudaFreeHost(host);
                 }
@@ -521,7 +531,7 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
             if (p) set_table(e, layer, expert, p, false);
             return p;
         }
-        void* slot = vram_alloc_evicting(e, ent.bytes, keep);
+        void* slot = vram_alloc_evicting(e, ent.bytes, keep, {wb::Lru::key(layer, expert)});
         if (!slot) {
             void* p = scratch_serve(e, ent.data, ent.bytes, err);
             if (p) set_table(e, layer, expert, p, false);
@@ -543,9 +553,9 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
     // the RAM-tier copy is the upload's source, so the staging buffer is free for
     // the next read at once; without one, the upload from staging is waited for
     void* host = nullptr;
-    if (cudaHostAlloc(&host, n, cudaHostAllocDefault) == cudaSuccess) {
+    if (n <= e->ram.capacity() && cudaHostAlloc(&host, n, cudaHostAllocDefault) == cudaSuccess) {
         memcpy(host, e->staging, n);
-        ram_put(e, layer, expert, host, n);
+        if (!ram_put(e, layer, expert, host, n)) host = nullptr;  // freed: upload from staging
     }
     const void* src = host ? host : e->staging;
     void* slot = nullptr;
