@@ -75,9 +75,12 @@ void* take_slot(WispStreamCache* c, const std::vector<uint64_t>& keep, cudaStrea
     wb::Lru::Entry v;
     if (!c->lru.evict_except(hold, &v)) return nullptr;
     // kernels already queued may still read the victim (through the table and
-    // the slot): the transfer stream waits for them before touching either
+    // the slot): the transfer stream waits for them before touching either; and
+    // the victim's own fill may still be in flight on the other transfer stream
+    // (a prefetch nobody read yet): the new copy waits for it too
     const int si = c->slot_index(v.data);
     if (c->last_use[si] >= 0) cudaStreamWaitEvent(s, c->use_ev[c->last_use[si]], 0);
+    cudaStreamWaitEvent(s, c->ready[si], 0);
     const size_t ti = (size_t)v.layer * c->E + v.expert;
     c->h_tables[ti] = nullptr;
     cudaMemcpyAsync(c->d_tables + ti, &c->h_tables[ti], sizeof(void*), cudaMemcpyHostToDevice, s);
