@@ -46,11 +46,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_rank(rank, world, port, out, idle_last=False):
+def _ep_rank(rank, world, port, out, idle_last=False, uneven=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    per, K, B, H = 3, 2, 5, 4
+    per, K, H = 3, 2, 4
+    # uneven: rank r holds 5 + r tokens, and every rank passes the largest count
+    B = 5 + rank if uneven else 5
+    max_tokens = 5 + world - 1 if uneven else None
     # idle_last: no token routes to the last rank's experts, so it receives no rows
     E = per * (world - 1) if idle_last else per * world
     g = torch.Generator().manual_seed(100 + rank)
@@ -58,7 +61,7 @@ def _ep_rank(rank, world, port, out, idle_last=False):
     idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(B)]).int()
     idx[1, 1] = -1  # an unrouted slot
     w = torch.rand(B, K, generator=g)
-    d = Dispatch(x, idx, per, world)
+    d = Dispatch(x, idx, per, world, max_tokens=max_tokens)
     # stand-in expert e (global id rank*per + local): y = (e + 1) * x + e
     ge = d.eids.view(-1).float() + rank * per
     rows = d.rows * (ge + 1).view(-1, 1) + ge.view(-1, 1)
@@ -80,14 +83,15 @@ def _ep_rank(rank, world, port, out, idle_last=False):
     dist.destroy_process_group()
 
 
-# (2, False): config 2's exchange at two ranks; (4, True): four ranks, the last one
-# owning experts no token chose (it sends its own tokens' rows and receives none)
-@pytest.mark.parametrize("world,idle_last", [(2, False), (4, True)])
-def test_dispatch_compute_return_combine(world, idle_last):
+# (2, False, False): config 2's exchange at two ranks; (4, True, True): four ranks
+# holding 5..8 tokens, the last one owning experts no token chose (it sends its own
+# tokens' rows and receives none)
+@pytest.mark.parametrize("world,idle_last,uneven", [(2, False, False), (4, True, True)])
+def test_dispatch_compute_return_combine(world, idle_last, uneven):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, world, port, out, idle_last))
+    procs = [ctx.Process(target=_ep_rank, args=(r, world, port, out, idle_last, uneven))
              for r in range(world)]
     for p in procs:
         p.start()

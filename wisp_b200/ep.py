@@ -99,12 +99,20 @@ class Dispatch:
     count/expert-id table, the rows out, the rows back) and one small device-to-host
     read (both count vectors, which the variable all-to-alls need on the host)."""
 
-    def __init__(self, x, idx, per: int, world: int, group=None):
+    def __init__(self, x, idx, per: int, world: int, group=None, max_tokens: int | None = None):
+        """`max_tokens`: the most tokens any rank of the group dispatches in this call;
+        every rank must pass the same value (the count table has a fixed size).  The
+        default, this rank's own token count, is right when every rank has as many."""
         import torch
         B, K = idx.shape
+        if max_tokens is None:
+            max_tokens = B
+        if B > max_tokens:
+            raise ValueError(f"{B} tokens on this rank, above max_tokens={max_tokens}")
+        cap = max_tokens * K
         self.world, self.group = world, group
         _, counts, tokens, local_eid, owner, self.row_idx = dispatch_plan(idx, per, world)
-        table = exchange_counts(counts, owner, local_eid, world, B * K, group)
+        table = exchange_counts(counts, owner, local_eid, world, cap, group)
         both = torch.stack([counts.int(), table[:, 0]]).cpu()  # the one host read
         self.send_counts = [int(c) for c in both[0]]
         self.recv_counts = [int(c) for c in both[1]]
@@ -119,7 +127,7 @@ class Dispatch:
         end = torch.cumsum(rc, 0)
         j = torch.arange(n_recv, device=x.device)
         src = torch.searchsorted(end, j, right=True)
-        sel = src * (1 + B * K) + 1 + (j - (end - rc)[src])
+        sel = src * (1 + cap) + 1 + (j - (end - rc)[src])
         self.eids = table.view(-1)[sel].view(-1, 1)
 
     def back(self, out_rows):
@@ -240,13 +248,15 @@ class EPLayer:
                                             C.byref(err)), err)
         return y
 
-    def forward(self, x):
-        """y [B, H] for this rank's tokens x [B, H] (fp32, on this rank's GPU)."""
+    def forward(self, x, max_tokens: int | None = None):
+        """y [B, H] for this rank's tokens x [B, H] (fp32, on this rank's GPU).  When the
+        ranks hold different numbers of tokens, every rank passes the largest of them as
+        `max_tokens` (see Dispatch)."""
         import torch
         from .lib import WispErrCtx, check, lib
         B, H = x.shape
         idx, w = self.route(x)
-        dsp = Dispatch(x, idx, self.per, self.world, self.group)
+        dsp = Dispatch(x, idx, self.per, self.world, self.group, max_tokens)
         self.last_counts = dsp.send_counts
         wt = torch.ones((dsp.rows.shape[0], 1), dtype=torch.float32, device=self.device)
         rows = self.experts(self.expert_layer, dsp.rows.contiguous(), dsp.eids.contiguous(), wt)
