@@ -578,6 +578,9 @@ void* fetch_locked(WispEngine* e, uint32_t layer, uint32_t expert,
 }
 
 void prefetch_loop(WispEngine* e) {
+    // the RAM-tier buffers this thread pins belong to the engine's device context
+    // (a new thread starts on device 0)
+    cudaSetDevice(e->device);
     std::vector<char> buf;
     for (;;) {
         std::pair<uint32_t, uint32_t> item;
