@@ -48,7 +48,7 @@ struct WispStreamCache {
     std::vector<uint64_t> slot_key;   // (layer, expert) key of the slot's expert
     std::vector<cudaEvent_t> use_ev;  // ring of "layer kernels done" events
     int use_head = 0;
-    std::vector<std::vector<int>> layer_slots;  // slots of the last ensure per layer
+    std::vector<std::vector<int>> layer_slots;  // per layer: slots held until its layer_done
     uint64_t hits = 0, misses = 0, prefetched = 0, prefetch_used = 0, bytes = 0;
     std::mutex mu;
 
@@ -236,8 +236,10 @@ extern "C" WispError wisp_stream_ensure(WispStreamCache* c, int layer, const int
     for (int e : u) keep.push_back(wb::Lru::key((uint32_t)layer, (uint32_t)e));
     std::sort(keep.begin(), keep.end());
     int h = 0, m = 0;
+    // the layer's slots stay held until its layer_done; an ensure repeated before it
+    // adds to the held set instead of replacing it (the earlier call's kernels may be
+    // queued already)
     std::vector<int>& used = c->layer_slots[layer];
-    used.clear();
     for (int e : u) {
         wb::Lru::Entry ent;
         void* slot = nullptr;
@@ -257,7 +259,7 @@ extern "C" WispError wisp_stream_ensure(WispStreamCache* c, int layer, const int
         }
         const int si = c->slot_index(slot);
         cudaStreamWaitEvent(compute, c->ready[si], 0);
-        used.push_back(si);
+        if (!c->pending[si]) used.push_back(si);
         c->pending[si] = 1;
     }
     c->hits += (uint64_t)h;
@@ -301,6 +303,7 @@ extern "C" WispError wisp_stream_layer_done(WispStreamCache* c, int layer, cudaS
         c->last_use[si] = i;
         c->pending[si] = 0;
     }
+    c->layer_slots[layer].clear();
     return WISP_OK;
 }
 
